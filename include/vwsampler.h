@@ -1,0 +1,152 @@
+/*
+ * vwsampler.h -- C ABI of the B200 (sm_100a) token sampler for voxwerk's Qwen3-TTS generation loop.
+ *
+ * The library replaces, with one batched GPU call, the per-row sampling block that voxwerk runs on the CPU:
+ *
+ *   talker rows (codebook 0, V = 3072)       src/Voxwerk/Talker/TalkerGenerator.cs:369-373 (GenerateBatch)
+ *                                            src/Voxwerk/Talker/TalkerGenerator.cs:246-249 (Generate)
+ *     Sampler.ApplyRepetitionPenalty(lg, history, RepetitionPenalty)   Sampler.cs:25-33
+ *     suppress ids [V-1024, V) except EOS; EOS too while t < 2         TalkerGenerator.cs:247-248 / :371-372
+ *     Sampler.Select(lg, options.Talker)                               Sampler.cs:35-88
+ *   sub-talker rows (codebooks 1..15, V = 2048)
+ *     Sampler.Select(cpLogits[row], options.SubTalker)                 TalkerGenerator.cs:420 / :268
+ *
+ * The reference has no FFI for this path (Sampler is a sealed C# class called directly); the entry points
+ * below are what its P/Invoke layer would bind.  Every struct is plain-old-data and blittable.
+ *
+ * Random numbers stay with the caller: each sampled row takes one uniform, the value the reference's
+ * Sampler._rng.NextDouble() would return at Sampler.cs:77 (talker rows from Random(Seed), sub-talker rows from
+ * Random(Seed + 1), TalkerGenerator.cs:217-218 / :345-346).  Greedy rows take no draw and ignore their slot.
+ *
+ * Threading: a handle is bound to one CUDA device and must not be used by two host threads at once (like
+ * Sampler, whose System.Random is not thread-safe).  Use one handle per GPU per host thread.
+ */
+#ifndef VWSAMPLER_H
+#define VWSAMPLER_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VW_ABI_VERSION 1
+
+/* Status codes.  No C++ exception crosses the ABI. */
+typedef enum vw_status {
+    VW_OK = 0,
+    VW_ERR_INVALID_ARG = 1,  /* bad pointer, size, dtype, option (e.g. Temperature <= 0 with DoSample) */
+    VW_ERR_OUT_OF_RANGE = 2, /* a history id outside [0, V): the reference throws at Sampler.cs:30 */
+    VW_ERR_CUDA = 3,         /* a CUDA runtime error; see vw_last_error() */
+    VW_ERR_TIMEOUT = 4,      /* a bounded wait inside the kernel gave up; results are not valid */
+    VW_ERR_NO_DEVICE = 5     /* no CUDA device with that ordinal, or not an sm_100 device */
+} vw_status;
+
+typedef enum vw_dtype { VW_F32 = 0, VW_BF16 = 1 } vw_dtype;
+
+/* Row kinds.  TALKER rows get the repetition penalty and the suppress mask; SUB rows get neither. */
+typedef enum vw_row_kind { VW_ROWS_TALKER = 0, VW_ROWS_SUB = 1 } vw_row_kind;
+
+/* Where the pointers of a call live.  DEVICE: every array is device memory on the handle's device and the call
+ * is stream-ordered.  HOST: every array is host memory; the library copies inputs to the device and the ids
+ * back, and returns when they are written. */
+typedef enum vw_mem { VW_MEM_DEVICE = 0, VW_MEM_HOST = 1 } vw_mem;
+
+/* One stage's decoding settings: SamplingOptions (Sampler.cs:4-13) plus GenerationOptions.RepetitionPenalty
+ * (TalkerGenerator.cs:11), which only talker rows use.  Defaults: {1, 50, 1.0f, 0.9f, 1.05f}. */
+typedef struct vw_options {
+    int32_t do_sample;          /* SamplingOptions.DoSample (0 = argmax, Sampler.cs:37) */
+    int32_t top_k;              /* SamplingOptions.TopK; <= 0 or >= V disables the cut (Sampler.cs:42) */
+    float top_p;                /* SamplingOptions.TopP; >= 1 disables the cut (Sampler.cs:62) */
+    float temperature;          /* SamplingOptions.Temperature; must be > 0 when do_sample */
+    float repetition_penalty;   /* GenerationOptions.RepetitionPenalty; 1.0f disables (Sampler.cs:27) */
+} vw_options;
+
+/* A block of rows that share vocabulary size, dtype and kind.  A call takes up to VW_MAX_SEGMENTS segments, so
+ * one launch can hold the talker rows and the sub-talker rows of a frame. */
+#define VW_MAX_SEGMENTS 8
+
+typedef struct vw_segment {
+    const void* logits;          /* [n_rows, row_stride] elements of `dtype`; read-only */
+    int64_t row_stride;          /* elements between consecutive rows (>= vocab) */
+    int32_t n_rows;
+    int32_t vocab;               /* V: 3072 talker (Qwen3TtsConfig.cs:28), 2048 code predictor (:49) */
+    int32_t dtype;               /* vw_dtype */
+    int32_t kind;                /* vw_row_kind */
+    /* ---- talker rows only (ignored for SUB rows) ---- */
+    const int64_t* hist_offsets; /* [n_rows + 1] CSR offsets into hist_ids; NULL = every history empty */
+    const int32_t* hist_ids;     /* ids generated so far by each row's sequence (Active.History) */
+    const int32_t* steps;        /* [n_rows] generation step t (Active.Step); NULL = every row at t >= min_new_tokens */
+    int32_t suppress_lo;         /* ids [suppress_lo, suppress_hi) except eos_id become -inf; voxwerk: V - 1024 */
+    int32_t suppress_hi;         /* voxwerk: V */
+    int32_t eos_id;              /* codec EOS, Qwen3TtsConfig.cs:34: 2150 */
+    int32_t min_new_tokens;      /* EOS is suppressed while t < min_new_tokens; voxwerk: 2 */
+    int32_t max_hist_len;        /* optional hint: the longest history in the segment (0 = unknown) */
+    /* ---- all rows ---- */
+    const int32_t* opt_index;    /* [n_rows] index into the options table; NULL = options[0] for every row */
+    const double* uniforms;      /* [n_rows] NextDouble() per row; may be NULL only if every row is greedy */
+    int32_t* out_ids;            /* [n_rows] sampled token ids */
+    double* out_probs;           /* optional [n_rows, vocab]: the probabilities the draw scanned (after top-k,
+                                    softmax, top-p and renormalisation), 0 for every other id; NULL = none */
+} vw_segment;
+
+typedef struct vw_handle vw_handle;
+
+/* Library version string, e.g. "vwsampler 1.0 (sm_100a)". */
+const char* vw_version(void);
+
+/* Human-readable name of a status code. */
+const char* vw_status_string(vw_status status);
+
+/* Creates a handle on CUDA device `device`.  Replaces `new Sampler(seed)` (Sampler.cs:21) as the per-worker
+ * object; the RNG stays with the caller. */
+vw_status vw_create(int32_t device, vw_handle** out_handle);
+
+/* Frees the handle and all device memory it owns.  Safe on NULL. */
+vw_status vw_destroy(vw_handle* handle);
+
+/* Message of the last error on this handle ("" if none).  Valid until the next call on the handle. */
+const char* vw_last_error(const vw_handle* handle);
+
+/*
+ * Samples one token id for every row of every segment.  Replaces, for a whole batch, the per-row sequence
+ * ApplyRepetitionPenalty -> suppress mask -> Select of TalkerGenerator.cs:366-385 (talker rows) and the per-row
+ * SubSampler.Select of TalkerGenerator.cs:419-420 (sub-talker rows); results are the ids those loops return.
+ *
+ * options / n_options: host array (always host memory), indexed by each row's opt_index.
+ * mem: VW_MEM_DEVICE or VW_MEM_HOST (see vw_mem).
+ * stream: a cudaStream_t for VW_MEM_DEVICE calls, or NULL.  With NULL the call runs on the handle's stream and
+ *   returns after the ids are written, reporting device-side errors.  With a stream the call is enqueued and
+ *   returns at once; device-side errors (history id out of range, timeout) are reported by the next
+ *   vw_synchronize() on that stream.  VW_MEM_HOST calls are always synchronous.
+ */
+vw_status vw_sample(vw_handle* handle, const vw_segment* segments, int32_t n_segments,
+                    const vw_options* options, int32_t n_options, int32_t mem, void* stream);
+
+/* Waits for work enqueued on `stream` (NULL = the handle's stream) and returns, then clears, any device-side
+ * error latched by earlier calls. */
+vw_status vw_synchronize(vw_handle* handle, void* stream);
+
+/*
+ * Single-row mirrors of the reference's Sampler methods, for callers that keep the reference's call shape.
+ * Pointers follow `mem`; the calls are synchronous.
+ */
+
+/* Sampler.ApplyRepetitionPenalty (Sampler.cs:25-33): in place on `logits[0..vocab)`; each distinct id in
+ * `history` is divided (logit >= 0) or multiplied (logit < 0) by `penalty` once. */
+vw_status vw_apply_repetition_penalty(vw_handle* handle, float* logits, int32_t vocab, const int32_t* history,
+                                      int64_t history_len, float penalty, int32_t mem);
+
+/* Sampler.Select (Sampler.cs:35-88) on one fp32 row, without penalty or mask.  `uniform` is the NextDouble()
+ * draw (ignored when options->do_sample == 0).  Unlike the reference, `logits` is not modified. */
+vw_status vw_select(vw_handle* handle, const float* logits, int32_t vocab, const vw_options* options,
+                    double uniform, int32_t mem, int32_t* out_id);
+
+/* Sampler.ArgMax (Sampler.cs:90-95): first index of the maximum. */
+vw_status vw_argmax(vw_handle* handle, const float* logits, int32_t vocab, int32_t mem, int32_t* out_id);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VWSAMPLER_H */

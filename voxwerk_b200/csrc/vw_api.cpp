@@ -1,0 +1,545 @@
+// vw_api.cpp -- C ABI of the sampler (include/vwsampler.h): argument checks, device-memory staging for host
+// callers, launch planning and error reporting.  No C++ exception crosses the boundary.
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "../../include/vwsampler.h"
+#include "vw_internal.h"
+
+#define VW_EXPORT extern "C" __attribute__((visibility("default")))
+
+struct vw_handle {
+    int device = -1;
+    cudaStream_t stream = nullptr;
+    int sm_count = 0;
+    unsigned* d_err = nullptr;      // device error word (kErr* bits)
+    unsigned* h_err = nullptr;      // pinned mirror
+    char* d_scratch = nullptr;      // general-path scratch, one slice per CTA
+    size_t scratch_bytes = 0;
+    char* d_stage = nullptr;        // VW_MEM_HOST: device copies of the caller's arrays
+    size_t stage_bytes = 0;
+    vw::DevOptions* d_opts = nullptr;
+    vw::DevOptions* h_opts = nullptr;   // pinned upload buffer for option tables > kInlineOptions
+    size_t opts_cap = 0;
+    cudaEvent_t opts_done = nullptr;
+    std::string last_error;
+};
+
+namespace {
+
+// Restores the caller's current device on scope exit.
+class DeviceGuard {
+  public:
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev_) != cudaSuccess) prev_ = -1;
+        ok_ = cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        if (prev_ >= 0) cudaSetDevice(prev_);
+    }
+    bool ok() const { return ok_; }
+
+  private:
+    int prev_ = -1;
+    bool ok_ = false;
+};
+
+vw_status fail(vw_handle* h, vw_status s, const std::string& msg) {
+    if (h) h->last_error = msg;
+    return s;
+}
+
+vw_status cuda_fail(vw_handle* h, cudaError_t e, const char* where) {
+    return fail(h, VW_ERR_CUDA, std::string(where) + ": " + cudaGetErrorString(e));
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Elements of a row that the kernel stages: everything outside the suppressed span, 16-byte vectors.
+int staged_elems(const vw_segment& s) {
+    const int vw = s.dtype == VW_F32 ? 4 : 8;
+    if (s.kind == VW_ROWS_TALKER) {
+        const int lo = std::clamp(s.suppress_lo, 0, s.vocab);
+        const int hi = std::clamp(s.suppress_hi, 0, s.vocab);
+        if (lo < hi) {
+            const int la = (lo + vw - 1) / vw * vw;
+            const int ha = hi / vw * vw;
+            if (la < ha) return la + (s.vocab - ha);
+        }
+    }
+    return s.vocab;
+}
+
+vw_status grow(vw_handle* h, char** buf, size_t* cap, size_t need, const char* what) {
+    if (need <= *cap) return VW_OK;
+    if (*buf) {
+        cudaError_t e = cudaStreamSynchronize(h->stream);
+        if (e != cudaSuccess) return cuda_fail(h, e, what);
+        cudaFree(*buf);
+        *buf = nullptr;
+        *cap = 0;
+    }
+    const size_t n = round_up(need + need / 4, 1 << 20);
+    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(buf), n);
+    if (e != cudaSuccess) return cuda_fail(h, e, what);
+    *cap = n;
+    return VW_OK;
+}
+
+vw_status check_options(vw_handle* h, const vw_options* opts, int32_t n_opts, bool* any_sample) {
+    *any_sample = false;
+    if (n_opts < 1 || !opts) return fail(h, VW_ERR_INVALID_ARG, "options: at least one entry is required");
+    for (int i = 0; i < n_opts; ++i) {
+        if (opts[i].do_sample) {
+            *any_sample = true;
+            if (!(opts[i].temperature > 0.0f))
+                return fail(h, VW_ERR_INVALID_ARG,
+                            "options[" + std::to_string(i) + "]: temperature must be > 0 when do_sample");
+        }
+    }
+    return VW_OK;
+}
+
+vw_status check_segment(vw_handle* h, const vw_segment& s, int i, int32_t n_opts, bool any_sample, int mem) {
+    const std::string w = "segment " + std::to_string(i) + ": ";
+    if (s.n_rows < 0) return fail(h, VW_ERR_INVALID_ARG, w + "n_rows < 0");
+    if (s.vocab < 1) return fail(h, VW_ERR_INVALID_ARG, w + "vocab < 1");
+    if (s.dtype != VW_F32 && s.dtype != VW_BF16) return fail(h, VW_ERR_INVALID_ARG, w + "unknown dtype");
+    if (s.kind != VW_ROWS_TALKER && s.kind != VW_ROWS_SUB) return fail(h, VW_ERR_INVALID_ARG, w + "unknown kind");
+    if (s.n_rows == 0) return VW_OK;
+    const size_t es = s.dtype == VW_F32 ? 4 : 2;
+    if (!s.logits || !aligned(s.logits, es)) return fail(h, VW_ERR_INVALID_ARG, w + "logits NULL or misaligned");
+    if (s.row_stride < s.vocab) return fail(h, VW_ERR_INVALID_ARG, w + "row_stride < vocab");
+    if (!s.out_ids || !aligned(s.out_ids, 4)) return fail(h, VW_ERR_INVALID_ARG, w + "out_ids NULL or misaligned");
+    if (s.out_probs && !aligned(s.out_probs, 8)) return fail(h, VW_ERR_INVALID_ARG, w + "out_probs misaligned");
+    if (any_sample && !s.uniforms) return fail(h, VW_ERR_INVALID_ARG, w + "uniforms NULL with sampling options");
+    if (s.uniforms && !aligned(s.uniforms, 8)) return fail(h, VW_ERR_INVALID_ARG, w + "uniforms misaligned");
+    if (s.opt_index && !aligned(s.opt_index, 4)) return fail(h, VW_ERR_INVALID_ARG, w + "opt_index misaligned");
+    if (s.kind == VW_ROWS_TALKER) {
+        if (s.hist_offsets && (!aligned(s.hist_offsets, 8) || !s.hist_ids || !aligned(s.hist_ids, 4)))
+            return fail(h, VW_ERR_INVALID_ARG, w + "hist_offsets / hist_ids NULL or misaligned");
+        if (s.steps && !aligned(s.steps, 4)) return fail(h, VW_ERR_INVALID_ARG, w + "steps misaligned");
+    }
+    if (staged_elems(s) * es > static_cast<size_t>(vw::kMaxStageLogitBytes))
+        return fail(h, VW_ERR_INVALID_ARG, w + "vocab too large for one row stage");
+    if (mem == VW_MEM_HOST) {
+        if (s.opt_index)
+            for (int r = 0; r < s.n_rows; ++r)
+                if (s.opt_index[r] < 0 || s.opt_index[r] >= n_opts)
+                    return fail(h, VW_ERR_INVALID_ARG, w + "opt_index out of range at row " + std::to_string(r));
+        if (s.kind == VW_ROWS_TALKER && s.hist_offsets) {
+            if (s.hist_offsets[0] < 0) return fail(h, VW_ERR_INVALID_ARG, w + "hist_offsets[0] < 0");
+            for (int r = 0; r < s.n_rows; ++r)
+                if (s.hist_offsets[r + 1] < s.hist_offsets[r])
+                    return fail(h, VW_ERR_INVALID_ARG, w + "hist_offsets decrease at row " + std::to_string(r));
+        }
+    }
+    return VW_OK;
+}
+
+// Copies one host array into the staging buffer at *off (256-byte aligned); returns the device pointer.
+template <typename T>
+T* stage_copy(vw_handle* h, const T* src, size_t count, size_t* off, cudaStream_t st, cudaError_t* err) {
+    if (!src || count == 0) return nullptr;
+    *off = round_up(*off, 256);
+    T* dst = reinterpret_cast<T*>(h->d_stage + *off);
+    *off += count * sizeof(T);
+    if (*err == cudaSuccess) *err = cudaMemcpyAsync(dst, src, count * sizeof(T), cudaMemcpyHostToDevice, st);
+    return dst;
+}
+
+struct HostStaging {
+    std::vector<vw_segment> dev;           // device-side view of each segment
+    std::vector<std::vector<int64_t>> offsets;   // re-based history offsets
+};
+
+// VW_MEM_HOST: copies every input to the device; outputs get device buffers (copied back afterwards).
+vw_status stage_host_inputs(vw_handle* h, const vw_segment* segs, int n, cudaStream_t st, HostStaging* hs) {
+    hs->dev.assign(segs, segs + n);
+    hs->offsets.resize(n);
+    size_t need = 0;
+    for (int i = 0; i < n; ++i) {
+        const vw_segment& s = segs[i];
+        if (s.n_rows == 0) continue;
+        const size_t es = s.dtype == VW_F32 ? 4 : 2;
+        need += round_up((static_cast<size_t>(s.n_rows - 1) * s.row_stride + s.vocab) * es, 256) + 256;
+        if (s.kind == VW_ROWS_TALKER && s.hist_offsets) {
+            need += round_up(static_cast<size_t>(s.n_rows + 1) * 8, 256) + 256;
+            need += round_up(static_cast<size_t>(s.hist_offsets[s.n_rows] - s.hist_offsets[0]) * 4, 256) + 256;
+        }
+        if (s.kind == VW_ROWS_TALKER && s.steps) need += round_up(static_cast<size_t>(s.n_rows) * 4, 256) + 256;
+        if (s.opt_index) need += round_up(static_cast<size_t>(s.n_rows) * 4, 256) + 256;
+        if (s.uniforms) need += round_up(static_cast<size_t>(s.n_rows) * 8, 256) + 256;
+        need += round_up(static_cast<size_t>(s.n_rows) * 4, 256) + 256;
+        if (s.out_probs) need += round_up(static_cast<size_t>(s.n_rows) * s.vocab * 8, 256) + 256;
+    }
+    vw_status r = grow(h, &h->d_stage, &h->stage_bytes, need, "staging buffer");
+    if (r != VW_OK) return r;
+    size_t off = 0;
+    cudaError_t e = cudaSuccess;
+    for (int i = 0; i < n; ++i) {
+        const vw_segment& s = segs[i];
+        vw_segment& d = hs->dev[i];
+        if (s.n_rows == 0) continue;
+        const size_t es = s.dtype == VW_F32 ? 4 : 2;
+        const size_t nel = static_cast<size_t>(s.n_rows - 1) * s.row_stride + s.vocab;
+        d.logits = stage_copy(h, static_cast<const unsigned char*>(s.logits), nel * es, &off, st, &e);
+        if (s.kind == VW_ROWS_TALKER && s.hist_offsets) {
+            auto& ofs = hs->offsets[i];
+            ofs.resize(static_cast<size_t>(s.n_rows) + 1);
+            for (int k = 0; k <= s.n_rows; ++k) ofs[k] = s.hist_offsets[k] - s.hist_offsets[0];
+            d.hist_offsets = stage_copy(h, ofs.data(), ofs.size(), &off, st, &e);
+            const size_t nh = static_cast<size_t>(s.hist_offsets[s.n_rows] - s.hist_offsets[0]);
+            d.hist_ids = nh ? stage_copy(h, s.hist_ids + s.hist_offsets[0], nh, &off, st, &e) : nullptr;
+            if (!d.hist_ids) {
+                off = round_up(off, 256);
+                d.hist_ids = reinterpret_cast<int32_t*>(h->d_stage + off);   // never read: every history empty
+            }
+        } else {
+            d.hist_offsets = nullptr;
+            d.hist_ids = nullptr;
+        }
+        d.steps = (s.kind == VW_ROWS_TALKER) ? stage_copy(h, s.steps, s.steps ? s.n_rows : 0, &off, st, &e) : nullptr;
+        d.opt_index = stage_copy(h, s.opt_index, s.opt_index ? s.n_rows : 0, &off, st, &e);
+        d.uniforms = stage_copy(h, s.uniforms, s.uniforms ? s.n_rows : 0, &off, st, &e);
+        off = round_up(off, 256);
+        d.out_ids = reinterpret_cast<int32_t*>(h->d_stage + off);
+        off += static_cast<size_t>(s.n_rows) * 4;
+        if (s.out_probs) {
+            off = round_up(off, 256);
+            d.out_probs = reinterpret_cast<double*>(h->d_stage + off);
+            off += static_cast<size_t>(s.n_rows) * s.vocab * 8;
+        }
+    }
+    if (e != cudaSuccess) return cuda_fail(h, e, "host-to-device copy");
+    return VW_OK;
+}
+
+vw_status read_device_error(vw_handle* h, cudaStream_t st) {
+    cudaError_t e = cudaMemcpyAsync(h->h_err, h->d_err, sizeof(unsigned), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_fail(h, e, "synchronize");
+    const unsigned bits = *h->h_err;
+    if (bits) {
+        cudaMemsetAsync(h->d_err, 0, sizeof(unsigned), st);
+        cudaStreamSynchronize(st);
+    }
+    if (bits & vw::kErrTimeout) return fail(h, VW_ERR_TIMEOUT, "a bounded wait in the sampler kernel gave up");
+    if (bits & vw::kErrHistRange) return fail(h, VW_ERR_OUT_OF_RANGE, "a history id is outside [0, vocab)");
+    if (bits & vw::kErrBadOption) return fail(h, VW_ERR_INVALID_ARG, "a row's opt_index is outside the options table");
+    return VW_OK;
+}
+
+vw_status sample_impl(vw_handle* h, const vw_segment* segs, int32_t n_segs, const vw_options* opts, int32_t n_opts,
+                      int32_t mem, void* stream) {
+    if (!h) return VW_ERR_INVALID_ARG;
+    h->last_error.clear();
+    if (!segs || n_segs < 1 || n_segs > vw::kMaxSegments)
+        return fail(h, VW_ERR_INVALID_ARG, "n_segments must be in [1, VW_MAX_SEGMENTS]");
+    if (mem != VW_MEM_DEVICE && mem != VW_MEM_HOST) return fail(h, VW_ERR_INVALID_ARG, "unknown memory kind");
+    if (mem == VW_MEM_HOST && stream) return fail(h, VW_ERR_INVALID_ARG, "VW_MEM_HOST calls take no stream");
+    bool any_sample = false;
+    vw_status r = check_options(h, opts, n_opts, &any_sample);
+    if (r != VW_OK) return r;
+    int64_t total = 0;
+    for (int i = 0; i < n_segs; ++i) {
+        r = check_segment(h, segs[i], i, n_opts, any_sample, mem);
+        if (r != VW_OK) return r;
+        total += segs[i].n_rows;
+    }
+    if (total > INT32_MAX) return fail(h, VW_ERR_INVALID_ARG, "more than 2^31 - 1 rows");
+    if (total == 0) return VW_OK;
+
+    DeviceGuard guard(h->device);
+    if (!guard.ok()) return fail(h, VW_ERR_CUDA, "cudaSetDevice failed");
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+    const bool sync = (stream == nullptr);
+
+    HostStaging hs;
+    const vw_segment* run = segs;
+    if (mem == VW_MEM_HOST) {
+        r = stage_host_inputs(h, segs, n_segs, st, &hs);
+        if (r != VW_OK) return r;
+        run = hs.dev.data();
+    }
+
+    vw::LaunchParams p;
+    std::memset(&p, 0, sizeof p);
+    int row_begin = 0, vmax = 1, logit_bytes = 16, hist_cap = 0;
+    bool any_pen = false;
+    for (int i = 0; i < n_opts; ++i) any_pen |= opts[i].repetition_penalty != 1.0f;
+    int nd = 0;
+    for (int i = 0; i < n_segs; ++i) {
+        const vw_segment& s = run[i];
+        if (s.n_rows == 0) continue;
+        vw::DevSegment& d = p.seg[nd++];
+        d.logits = s.logits;
+        d.hist_offsets = s.kind == VW_ROWS_TALKER ? s.hist_offsets : nullptr;
+        d.hist_ids = s.kind == VW_ROWS_TALKER ? s.hist_ids : nullptr;
+        d.steps = s.kind == VW_ROWS_TALKER ? s.steps : nullptr;
+        d.opt_index = s.opt_index;
+        d.uniforms = s.uniforms;
+        d.out_ids = s.out_ids;
+        d.out_probs = s.out_probs;
+        d.row_stride = s.row_stride;
+        d.row_begin = row_begin;
+        d.n_rows = s.n_rows;
+        d.vocab = s.vocab;
+        d.dtype = s.dtype;
+        d.kind = s.kind;
+        d.sup_lo = s.kind == VW_ROWS_TALKER ? std::clamp(s.suppress_lo, 0, s.vocab) : 0;
+        d.sup_hi = s.kind == VW_ROWS_TALKER ? std::clamp(s.suppress_hi, 0, s.vocab) : 0;
+        if (d.sup_hi < d.sup_lo) d.sup_hi = d.sup_lo;
+        d.eos = s.kind == VW_ROWS_TALKER ? s.eos_id : -1;
+        d.min_new = s.kind == VW_ROWS_TALKER ? s.min_new_tokens : 0;
+        const size_t es = s.dtype == VW_F32 ? 4 : 2;
+        d.bulk_ok = aligned(s.logits, 16) && (s.row_stride * es) % 16 == 0 && (s.vocab * es) % 16 == 0;
+        d.hist_aligned = d.hist_ids ? aligned(d.hist_ids, 16) : 0;
+        row_begin += s.n_rows;
+        vmax = std::max(vmax, s.vocab);
+        const int vwe = s.dtype == VW_F32 ? 4 : 8;
+        logit_bytes = std::max(logit_bytes, (staged_elems(s) + vwe - 1) / vwe * 16);
+        if (s.kind == VW_ROWS_TALKER && s.hist_offsets && any_pen) {
+            int hint = s.max_hist_len;
+            if (hint <= 0 && mem == VW_MEM_HOST) {
+                for (int k = 0; k < s.n_rows; ++k)
+                    hint = static_cast<int>(std::min<int64_t>(
+                        std::max<int64_t>(hint, segs[i].hist_offsets[k + 1] - segs[i].hist_offsets[k]), vw::kMaxHistStage));
+            }
+            if (hint <= 0) hint = 1024;
+            hist_cap = std::max(hist_cap, static_cast<int>(round_up(std::min(hint, vw::kMaxHistStage), 4)));
+        }
+    }
+    p.n_segs = nd;
+    p.total_rows = row_begin;
+    p.n_opts = n_opts;
+    if (n_opts <= vw::kInlineOptions) {
+        std::memcpy(p.inl_opts, opts, sizeof(vw_options) * n_opts);
+    } else {
+        if (static_cast<size_t>(n_opts) > h->opts_cap) {
+            cudaStreamSynchronize(st);
+            if (h->d_opts) cudaFree(h->d_opts);
+            if (h->h_opts) cudaFreeHost(h->h_opts);
+            h->d_opts = nullptr;
+            h->h_opts = nullptr;
+            h->opts_cap = 0;
+            cudaError_t e = cudaMalloc(&h->d_opts, sizeof(vw::DevOptions) * n_opts);
+            if (e == cudaSuccess) e = cudaMallocHost(&h->h_opts, sizeof(vw::DevOptions) * n_opts);
+            if (e != cudaSuccess) return cuda_fail(h, e, "options table");
+            h->opts_cap = n_opts;
+        } else {
+            cudaEventSynchronize(h->opts_done);   // the previous upload has left the pinned buffer
+        }
+        std::memcpy(h->h_opts, opts, sizeof(vw_options) * n_opts);
+        cudaError_t e = cudaMemcpyAsync(h->d_opts, h->h_opts, sizeof(vw::DevOptions) * n_opts,
+                                        cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess) e = cudaEventRecord(h->opts_done, st);
+        if (e != cudaSuccess) return cuda_fail(h, e, "options upload");
+        p.dev_opts = h->d_opts;
+    }
+    p.stage_logit_bytes = logit_bytes;
+    p.stage_hist_cap = hist_cap;
+    p.bitmap_words = (vmax + 31) / 32;
+    p.vmax = vmax;
+    p.err = h->d_err;
+
+    int ctas = 0;
+    size_t smem = 0;
+    for (int stages = vw::kStages; stages >= 2 && ctas == 0; --stages) {
+        p.n_stages = stages;
+        smem = vw::sampler_smem_bytes(p);
+        ctas = vw::sampler_ctas_per_sm(smem);
+    }
+    if (ctas == 0) return fail(h, VW_ERR_INVALID_ARG, "rows too large for shared memory");
+    const int grid = static_cast<int>(std::min<int64_t>(p.total_rows, static_cast<int64_t>(h->sm_count) * ctas));
+    p.gscratch_stride = vw::sampler_gscratch_stride(vmax);
+    r = grow(h, &h->d_scratch, &h->scratch_bytes, static_cast<size_t>(grid) * p.gscratch_stride, "scratch");
+    if (r != VW_OK) return r;
+    p.gscratch = h->d_scratch;
+
+    cudaError_t e = cudaSuccess;
+    if (sync) e = cudaMemsetAsync(h->d_err, 0, sizeof(unsigned), st);
+    if (e == cudaSuccess) e = vw::launch_sampler(p, grid, smem, st);
+    if (e != cudaSuccess) return cuda_fail(h, e, "sampler launch");
+    if (mem == VW_MEM_HOST) {
+        for (int i = 0; i < n_segs && e == cudaSuccess; ++i) {
+            const vw_segment& s = segs[i];
+            if (s.n_rows == 0) continue;
+            e = cudaMemcpyAsync(s.out_ids, hs.dev[i].out_ids, static_cast<size_t>(s.n_rows) * 4,
+                                cudaMemcpyDeviceToHost, st);
+            if (e == cudaSuccess && s.out_probs)
+                e = cudaMemcpyAsync(s.out_probs, hs.dev[i].out_probs, static_cast<size_t>(s.n_rows) * s.vocab * 8,
+                                    cudaMemcpyDeviceToHost, st);
+        }
+        if (e != cudaSuccess) return cuda_fail(h, e, "device-to-host copy");
+    }
+    if (sync) return read_device_error(h, st);
+    return VW_OK;
+}
+
+}  // namespace
+
+VW_EXPORT const char* vw_version(void) { return "vwsampler 1.0 (sm_100a)"; }
+
+VW_EXPORT const char* vw_status_string(vw_status s) {
+    switch (s) {
+        case VW_OK: return "ok";
+        case VW_ERR_INVALID_ARG: return "invalid argument";
+        case VW_ERR_OUT_OF_RANGE: return "history id out of range";
+        case VW_ERR_CUDA: return "CUDA error";
+        case VW_ERR_TIMEOUT: return "device wait timed out";
+        case VW_ERR_NO_DEVICE: return "no usable CUDA device";
+    }
+    return "unknown status";
+}
+
+VW_EXPORT vw_status vw_create(int32_t device, vw_handle** out) {
+    if (!out) return VW_ERR_INVALID_ARG;
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return VW_ERR_NO_DEVICE;
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess || prop.major != 10) return VW_ERR_NO_DEVICE;
+    DeviceGuard guard(device);
+    if (!guard.ok()) return VW_ERR_NO_DEVICE;
+    vw_handle* h = new (std::nothrow) vw_handle;
+    if (!h) return VW_ERR_CUDA;
+    h->device = device;
+    h->sm_count = prop.multiProcessorCount;
+    cudaError_t e = cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaMalloc(&h->d_err, sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMallocHost(&h->h_err, sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMemset(h->d_err, 0, sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->opts_done, cudaEventDisableTiming);
+    if (e != cudaSuccess) {
+        vw_destroy(h);
+        return VW_ERR_CUDA;
+    }
+    *out = h;
+    return VW_OK;
+}
+
+VW_EXPORT vw_status vw_destroy(vw_handle* h) {
+    if (!h) return VW_OK;
+    {
+        DeviceGuard guard(h->device);
+        if (h->stream) cudaStreamSynchronize(h->stream);
+        if (h->d_scratch) cudaFree(h->d_scratch);
+        if (h->d_stage) cudaFree(h->d_stage);
+        if (h->d_opts) cudaFree(h->d_opts);
+        if (h->h_opts) cudaFreeHost(h->h_opts);
+        if (h->d_err) cudaFree(h->d_err);
+        if (h->h_err) cudaFreeHost(h->h_err);
+        if (h->opts_done) cudaEventDestroy(h->opts_done);
+        if (h->stream) cudaStreamDestroy(h->stream);
+    }
+    delete h;
+    return VW_OK;
+}
+
+VW_EXPORT const char* vw_last_error(const vw_handle* h) { return h ? h->last_error.c_str() : ""; }
+
+VW_EXPORT vw_status vw_sample(vw_handle* h, const vw_segment* segs, int32_t n_segs, const vw_options* opts,
+                              int32_t n_opts, int32_t mem, void* stream) {
+    return sample_impl(h, segs, n_segs, opts, n_opts, mem, stream);
+}
+
+VW_EXPORT vw_status vw_synchronize(vw_handle* h, void* stream) {
+    if (!h) return VW_ERR_INVALID_ARG;
+    DeviceGuard guard(h->device);
+    if (!guard.ok()) return fail(h, VW_ERR_CUDA, "cudaSetDevice failed");
+    return read_device_error(h, stream ? static_cast<cudaStream_t>(stream) : h->stream);
+}
+
+VW_EXPORT vw_status vw_apply_repetition_penalty(vw_handle* h, float* logits, int32_t vocab, const int32_t* history,
+                                                int64_t history_len, float penalty, int32_t mem) {
+    if (!h) return VW_ERR_INVALID_ARG;
+    h->last_error.clear();
+    if (!logits || vocab < 1 || history_len < 0 || (history_len > 0 && !history))
+        return fail(h, VW_ERR_INVALID_ARG, "bad logits / history arguments");
+    if (mem != VW_MEM_DEVICE && mem != VW_MEM_HOST) return fail(h, VW_ERR_INVALID_ARG, "unknown memory kind");
+    if (penalty == 1.0f || history_len == 0) return VW_OK;   // Sampler.cs:27
+    DeviceGuard guard(h->device);
+    if (!guard.ok()) return fail(h, VW_ERR_CUDA, "cudaSetDevice failed");
+    cudaStream_t st = h->stream;
+    float* d_logits = logits;
+    const int32_t* d_hist = history;
+    cudaError_t e = cudaSuccess;
+    if (mem == VW_MEM_HOST) {
+        const size_t need = round_up(static_cast<size_t>(vocab) * 4, 256) + static_cast<size_t>(history_len) * 4 + 256;
+        vw_status r = grow(h, &h->d_stage, &h->stage_bytes, need, "staging buffer");
+        if (r != VW_OK) return r;
+        d_logits = reinterpret_cast<float*>(h->d_stage);
+        int32_t* dh = reinterpret_cast<int32_t*>(h->d_stage + round_up(static_cast<size_t>(vocab) * 4, 256));
+        e = cudaMemcpyAsync(d_logits, logits, static_cast<size_t>(vocab) * 4, cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(dh, history, static_cast<size_t>(history_len) * 4, cudaMemcpyHostToDevice, st);
+        d_hist = dh;
+    }
+    if (e == cudaSuccess) e = cudaMemsetAsync(h->d_err, 0, sizeof(unsigned), st);
+    if (e == cudaSuccess) e = vw::launch_apply_penalty(d_logits, vocab, d_hist, history_len, penalty, h->d_err, st);
+    if (e == cudaSuccess && mem == VW_MEM_HOST)
+        e = cudaMemcpyAsync(logits, d_logits, static_cast<size_t>(vocab) * 4, cudaMemcpyDeviceToHost, st);
+    if (e != cudaSuccess) return cuda_fail(h, e, "apply_repetition_penalty");
+    return read_device_error(h, st);
+}
+
+VW_EXPORT vw_status vw_select(vw_handle* h, const float* logits, int32_t vocab, const vw_options* options,
+                              double uniform, int32_t mem, int32_t* out_id) {
+    if (!h) return VW_ERR_INVALID_ARG;
+    if (!out_id || !options) return fail(h, VW_ERR_INVALID_ARG, "NULL out_id / options");
+    vw_segment s;
+    std::memset(&s, 0, sizeof s);
+    s.logits = logits;
+    s.row_stride = vocab;
+    s.n_rows = 1;
+    s.vocab = vocab;
+    s.dtype = VW_F32;
+    s.kind = VW_ROWS_SUB;
+    double u = uniform;
+    if (mem == VW_MEM_HOST) {
+        s.uniforms = &u;
+        s.out_ids = out_id;
+        return sample_impl(h, &s, 1, options, 1, mem, nullptr);
+    }
+    // device logits: the scalar uniform and the id still live on the host
+    s.uniforms = nullptr;
+    vw_options o = *options;
+    double* d_u = nullptr;
+    int32_t* d_id = nullptr;
+    DeviceGuard guard(h->device);
+    if (!guard.ok()) return fail(h, VW_ERR_CUDA, "cudaSetDevice failed");
+    vw_status r = grow(h, &h->d_stage, &h->stage_bytes, 512, "staging buffer");
+    if (r != VW_OK) return r;
+    d_u = reinterpret_cast<double*>(h->d_stage);
+    d_id = reinterpret_cast<int32_t*>(h->d_stage + 256);
+    cudaError_t e = cudaMemcpyAsync(d_u, &u, sizeof u, cudaMemcpyHostToDevice, h->stream);
+    if (e != cudaSuccess) return cuda_fail(h, e, "select");
+    s.uniforms = d_u;
+    s.out_ids = d_id;
+    r = sample_impl(h, &s, 1, &o, 1, VW_MEM_DEVICE, nullptr);
+    if (r != VW_OK) return r;
+    e = cudaMemcpy(out_id, d_id, sizeof(int32_t), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(h, e, "select");
+    return VW_OK;
+}
+
+VW_EXPORT vw_status vw_argmax(vw_handle* h, const float* logits, int32_t vocab, int32_t mem, int32_t* out_id) {
+    vw_options o;
+    o.do_sample = 0;
+    o.top_k = 0;
+    o.top_p = 1.0f;
+    o.temperature = 1.0f;
+    o.repetition_penalty = 1.0f;
+    return vw_select(h, logits, vocab, &o, 0.0, mem, out_id);
+}

@@ -1,0 +1,88 @@
+// vw_internal.h -- launch-parameter layout shared by the C-ABI host code (vw_api.cpp) and the sampler kernel
+// (vw_sampler.cu).  Not part of the public ABI.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+#include <cuda_runtime.h>
+
+namespace vw {
+
+constexpr int kMaxSegments = 8;        // == VW_MAX_SEGMENTS
+constexpr int kInlineOptions = 32;     // option tables up to this size travel in the kernel parameters
+constexpr int kThreads = 128;          // one warp-group per logits row
+constexpr int kWarps = kThreads / 32;
+constexpr int kRegElems = 24;          // elements per thread held in registers: rows of <= 3072 active ids
+constexpr int kSmallK = 64;            // top-k <= kSmallK uses the candidate path
+constexpr int kCandCap = 128;          // candidate buffer entries (one warp sorts 4 per lane)
+constexpr int kSmallSurvivors = 64;    // survivors handled by the one-warp exact chain (2 per lane)
+constexpr int kMaxStageLogitBytes = 64 * 1024;
+constexpr int kMaxHistStage = 4096;    // history ids staged per row; longer histories stream the rest
+constexpr int kStages = 3;
+
+// Error bits latched in the device error word.
+enum : unsigned {
+    kErrHistRange = 1u,   // a history id outside [0, V)
+    kErrTimeout = 2u,     // an mbarrier wait gave up
+    kErrBadOption = 4u,   // a row's option index outside the table
+};
+
+struct DevOptions {       // same layout as vw_options
+    int32_t do_sample;
+    int32_t top_k;
+    float top_p;
+    float temperature;
+    float rep_penalty;
+};
+
+struct DevSegment {
+    const void* logits;
+    const int64_t* hist_offsets;
+    const int32_t* hist_ids;
+    const int32_t* steps;
+    const int32_t* opt_index;
+    const double* uniforms;
+    int32_t* out_ids;
+    double* out_probs;
+    int64_t row_stride;   // elements
+    int32_t row_begin;    // first global row of the segment
+    int32_t n_rows;
+    int32_t vocab;
+    int32_t dtype;        // 0 f32, 1 bf16
+    int32_t kind;         // 0 talker, 1 sub
+    int32_t sup_lo, sup_hi, eos, min_new;   // talker suppress mask (clamped to [0, vocab]); lo == hi: none
+    int32_t bulk_ok;      // rows are 16-byte aligned with 16-byte multiple sizes: bulk copies allowed
+    int32_t hist_aligned; // hist_ids is 16-byte aligned
+};
+
+struct LaunchParams {
+    DevSegment seg[kMaxSegments];
+    DevOptions inl_opts[kInlineOptions];
+    const DevOptions* dev_opts;   // used when n_opts > kInlineOptions
+    int32_t n_opts;
+    int32_t n_segs;
+    int32_t total_rows;
+    int32_t n_stages;
+    int32_t stage_logit_bytes;    // multiple of 16
+    int32_t stage_hist_cap;       // ids per stage, multiple of 4
+    int32_t bitmap_words;         // vmax / 32 rounded up
+    int32_t vmax;
+    unsigned* err;
+    char* gscratch;               // large-path scratch, gscratch_stride bytes per CTA
+    int64_t gscratch_stride;
+};
+
+// Dynamic shared memory the sampler kernel needs for `p`.
+size_t sampler_smem_bytes(const LaunchParams& p);
+// Global scratch bytes per CTA for rows of up to `vmax` ids.
+int64_t sampler_gscratch_stride(int vmax);
+// Resident CTAs per SM at that shared-memory size (0 if it does not fit).
+int sampler_ctas_per_sm(size_t smem);
+cudaError_t launch_sampler(const LaunchParams& p, int grid, size_t smem, cudaStream_t stream);
+
+// Sampler.ApplyRepetitionPenalty on one device row, in place.
+cudaError_t launch_apply_penalty(float* logits, int vocab, const int32_t* hist, int64_t hist_len, float penalty,
+                                 unsigned* err, cudaStream_t stream);
+
+}  // namespace vw
