@@ -65,7 +65,8 @@ bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) %
 
 size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-// Elements of a row that the kernel stages: everything outside the suppressed span, 16-byte vectors.
+// Elements of a row that the kernel stages: everything outside the suppressed span plus the 16-byte vector
+// holding EOS, in index order.
 int staged_elems(const vw_segment& s) {
     const int vw = s.dtype == VW_F32 ? 4 : 8;
     if (s.kind == VW_ROWS_TALKER) {
@@ -74,7 +75,7 @@ int staged_elems(const vw_segment& s) {
         if (lo < hi) {
             const int la = (lo + vw - 1) / vw * vw;
             const int ha = hi / vw * vw;
-            if (la < ha) return la + (s.vocab - ha);
+            if (la < ha) return la + vw + (s.vocab - ha);
         }
     }
     return s.vocab;

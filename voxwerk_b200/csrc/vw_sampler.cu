@@ -1,27 +1,35 @@
 // vw_sampler.cu -- fused token-sampling kernel for sm_100a (B200).
 //
-// One warp-group (128 threads, "compute warps") samples one logits row at a time; a fifth "producer" warp
-// streams the next rows into a shared-memory ring with cp.async.bulk (TMA bulk copies) completing on mbarriers,
-// so HBM reads overlap the per-row work.  CTAs are persistent: CTA b takes rows b, b + grid, b + 2 grid, ...
+// Persistent CTAs of six warps, specialised by role:
+//   * producer warp: plans each of the CTA's rows (CTA b takes rows b, b + grid, ...) and streams its logits and
+//     history into a shared-memory ring with cp.async.bulk (TMA bulk copies) completing on mbarriers, so HBM reads
+//     run ahead of the work.  The suppressed span of talker rows is never read.
+//   * four element warps (one warp-group per row): repetition penalty, suppress mask, temperature, greedy argmax,
+//     and the top-k candidate filter; rows the chain warp cannot take are finished here (general path).
+//   * chain warp: top-k select, softmax, top-p and the inverse-CDF draw on the <= 128 candidates of a row, while
+//     the element warps already work on the next row.
 //
 // Per row, in the order of the reference (src/Voxwerk/Talker/Sampler.cs, TalkerGenerator.cs):
 //   1. repetition penalty (talker rows; Sampler.cs:25-33): history ids -> a V-bit shared bitmap (Distinct());
 //      each element whose bit is set becomes s < 0 ? s * p : s / p in fp32.  The IEEE quotient s / p is formed
-//      as fp32(fp64(s) * RN64(1/p)); the fp64 product is within 2^-52 relative of s/p while no fp32 rounding
+//      as fp32(fp64(s) * RN64(1/p)): the fp64 product is within 2^-52 relative of s/p while no fp32 rounding
 //      midpoint lies closer than 2^-49 relative to a quotient of two fp32 values, so both round the same way.
 //   2. suppress mask (talker rows; TalkerGenerator.cs:247-248): ids [lo, hi) except EOS, and EOS while
-//      t < min_new_tokens, become -inf.  The suppressed span is never read from HBM.
+//      t < min_new_tokens, become -inf.
 //   3. greedy rows: first index of the maximum (Sampler.cs:90-95).
 //   4. temperature: x * fp32(1/T) (Sampler.cs:39-40).
-//   5. top-k (Sampler.cs:42-49): every value >= the K-th largest survives (ties kept).  Candidates are the
-//      values >= tau, where tau = min over the 4 warps of the ceil(K/4)-th largest lane maximum (so >= K values
-//      are >= tau and the K-th largest is >= tau); one warp sorts the candidates (bitonic, 4 per lane).
-//   6. softmax in fp64 over the survivors, the fp64 sum taken sequentially in index order (Sampler.cs:51-60),
-//      top-p over the (prob, index)-ascending order with the reference's cumulative rule (:62-75) and the
-//      inverse-CDF draw against the caller's uniform (:77-87).  These sums are order-dependent roundings, so
-//      one warp replays them in the reference's order (every lane runs the same chain on shuffled values).
-// Rows the small path cannot take (top-k off or K > 64, > 128 candidates, > 64 survivors, > 3072 active ids)
-// take the general path: the same steps over the whole row in per-CTA global scratch.
+//   5. top-k (Sampler.cs:42-49): every value >= the K-th largest survives (ties kept).  For K <= 64 the
+//      candidates are the values >= tau, tau = min over the 4 element warps of the ceil(K/4)-th largest lane
+//      maximum (>= K values are >= tau, so the K-th largest is too); the chain warp sorts them (bitonic).
+//      Otherwise a block radix select over order-preserving keys finds the K-th largest.
+//   6. softmax in fp64, top-p cut over the (prob, index)-ascending order and the inverse-CDF draw
+//      (Sampler.cs:51-88).  The reference's sums are sequential fp64 roundings.  Here they are formed in
+//      parallel; every decision they feed (which ids top-p removes, where the draw lands) is taken only when the
+//      parallel value is farther from the threshold than a proven bound on the difference between the two
+//      (eta = (4n + 128) 2^-53 of the total for n survivors, covering both exp implementations' 1-ulp error,
+//      the reference's n-term sequential roundings and this code's tree roundings).  A row with any decision
+//      inside that band is replayed with the reference's exact sequential order (exact paths below), so the
+//      ids equal the reference's in every case.
 //
 // Compile with -fmad=false: no multiply-add may be contracted; every rounding step is explicit (_rn
 // intrinsics) to match the reference's separately rounded fp32 / fp64 operations.
@@ -36,8 +44,11 @@ namespace {
 
 constexpr unsigned kFull = 0xffffffffu;
 constexpr int kMetaBytes = 128;
-constexpr int kKeepBytes = 16;
-constexpr uint64_t kWaitLimitNs = 2000000000ull;   // bounded mbarrier waits: 2 s
+constexpr uint64_t kWaitLimitNs = 2000000000ull;   // bounded mbarrier waits: 2 s without progress
+constexpr double kU = 1.1102230246251565e-16;      // 2^-53
+constexpr int kChainWarp = kWarps;                 // warp 4
+constexpr int kProducerWarp = kWarps + 1;          // warp 5
+constexpr int kBlockThreads = (kWarps + 2) * 32;   // 192
 
 struct RowMeta {
     double uniform;
@@ -45,33 +56,44 @@ struct RowMeta {
     int32_t row;          // global row index
     int32_t seg, local, step, hist_len;
     int32_t hs_lo, hs_hi; // history ids [hs_lo, hs_hi) (relative to hist_begin) are staged in shared memory
-    int32_t lo_al, hi_al; // staged logits: ids [0, lo_al) then [hi_al, V), packed
-    int32_t keep;         // the 16-byte vector holding EOS is staged separately
-    int32_t direct;       // logits were not bulk-copied: the compute warps load them
+    int32_t lo_al, hi_al; // staged logits: ids [0, lo_al) | kvw ids from kbase (the EOS vector) | [hi_al, V)
+    int32_t kvw, kbase;
+    int32_t direct;       // logits were not bulk-copied: the element warps load them
     int32_t pen_on;       // repetition penalty active
     int32_t opt_ok;       // option index valid
     DevOptions opt;
 };
 static_assert(sizeof(RowMeta) <= kMetaBytes, "RowMeta too large");
 
-struct SmemMisc {
-    float tau_w[kWarps];
-    float red_v[kWarps];
-    int32_t red_i[kWarps];
-    uint32_t cand_count;
-    int32_t decision;     // small path result (>= 0) or -1: take the general path
-    int32_t issued;       // rows the producer has issued (for the timeout drain)
-    int32_t pad;
-    double bcast_d;
-    int32_t bcast_i;
-    int32_t pad2;
-    uint32_t hist256[256];
-    int32_t flags[kSmallSurvivors];
-};
-
 struct Cand {
     float x;
     int32_t idx;
+};
+
+// One row handed from the element warps to the chain warp.
+struct ChainSlot {
+    Cand cand[kCandCap];
+    uint32_t count;       // candidates written (atomic); the chain warp resets it
+    int32_t cmd;          // 0: a row, 1: no more rows
+    int32_t K, V, seg, local;
+    DevOptions opt;
+    double uniform;
+};
+
+struct SmemMisc {
+    float tau_w[kWarps];
+    float red_f[8][kWarps];
+    int32_t red_i[8][kWarps];
+    double red_d[8][kWarps];
+    unsigned long long red_u[4][kWarps];
+    double red_v[kWarps][8];
+    int32_t issued;       // rows the producer has issued (timeout drain)
+    uint32_t progress;    // rows finished by the element warps (extends the chain warp's wait bound)
+    int32_t bc_i[4];
+    double bc_d[4];
+    uint32_t chist[256];
+    double mhist[256];
+    int32_t flags[kCandCap];   // chain warp scratch
 };
 
 // ---------------------------------------------------------------- PTX helpers
@@ -104,12 +126,21 @@ __device__ __forceinline__ uint64_t global_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
-// Waits for the phase with `parity` to complete; gives up after kWaitLimitNs and returns false.
-__device__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+// Waits for the phase with `parity` to complete; gives up after kWaitLimitNs without progress and returns
+// false.  `progress` (nullable) is a counter whose change restarts the clock.
+__device__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, const volatile uint32_t* progress = nullptr) {
     if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = global_ns();
+    uint64_t t0 = global_ns();
+    uint32_t last = progress ? *progress : 0u;
     for (;;) {
         if (mbar_try_wait(bar, parity)) return true;
+        if (progress) {
+            const uint32_t now = *progress;
+            if (now != last) {
+                last = now;
+                t0 = global_ns();
+            }
+        }
         if (global_ns() - t0 > kWaitLimitNs) return false;
     }
 }
@@ -127,7 +158,7 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
-// Barrier among the 128 compute threads (named barrier 1; the producer warp never joins it).
+// Barrier among the 128 element threads (named barrier 1; the chain and producer warps never join it).
 __device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 __device__ __forceinline__ bool cbar_or(bool v) {
     uint32_t r;
@@ -144,6 +175,7 @@ __device__ __forceinline__ bool cbar_or(bool v) {
 
 // ---------------------------------------------------------------- value helpers
 __device__ __forceinline__ float neg_inf() { return __int_as_float(0xff800000); }
+__device__ __forceinline__ float pos_inf() { return __int_as_float(0x7f800000); }
 __device__ __forceinline__ bool is_neg_inf(float x) { return __float_as_uint(x) == 0xff800000u; }
 
 // Order-preserving uint32 key of a float; -0 is folded onto +0 (they compare equal in every rule here).
@@ -154,6 +186,10 @@ __device__ __forceinline__ uint32_t okey(float x) {
 }
 __device__ __forceinline__ float okey_inv(uint32_t k) {
     return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+// exp(fp64(fp32(x - mx))), Sampler.cs:57
+__device__ __forceinline__ double softmax_num(float x, float mx) {
+    return exp(static_cast<double>(__fsub_rn(x, mx)));
 }
 
 __device__ __forceinline__ uint64_t shfl_xor_u64(uint64_t v, int m) { return __shfl_xor_sync(kFull, v, m); }
@@ -236,6 +272,123 @@ __device__ __forceinline__ void warp_sort_pair(uint64_t (&k)[P], uint32_t (&t)[P
     }
 }
 
+// Warp reductions; results are the same in every lane (lane 0's value is broadcast where rounding is involved).
+__device__ __forceinline__ float warp_max_f(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
+    return v;
+}
+__device__ __forceinline__ float warp_min_f(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(kFull, v, o));
+    return v;
+}
+__device__ __forceinline__ int warp_sum_i(int v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+    return v;
+}
+__device__ __forceinline__ int warp_max_i(int v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(kFull, v, o));
+    return v;
+}
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __dadd_rn(v, __shfl_xor_sync(kFull, v, o));
+    return __shfl_sync(kFull, v, 0);
+}
+// Inclusive / exclusive prefix sums across the 32 lanes.
+__device__ __forceinline__ double warp_incl_d(double v, int lane) {
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const double y = __shfl_up_sync(kFull, v, o);
+        if (lane >= o) v = __dadd_rn(v, y);
+    }
+    return v;
+}
+__device__ __forceinline__ double warp_excl_from_incl_d(double incl, int lane) {
+    const double y = __shfl_up_sync(kFull, incl, 1);
+    return lane == 0 ? 0.0 : y;
+}
+
+// ---------------------------------------------------------------- block reductions (128 element threads)
+// Each call site passes its own `slot`; a slot is reused only after at least one more cbar.
+__device__ __forceinline__ float block_max_f(float v, SmemMisc& m, int slot, int lane, int warp) {
+    v = warp_max_f(v);
+    if (lane == 0) m.red_f[slot][warp] = v;
+    cbar();
+    float r = m.red_f[slot][0];
+#pragma unroll
+    for (int w = 1; w < kWarps; ++w) r = fmaxf(r, m.red_f[slot][w]);
+    return r;
+}
+__device__ __forceinline__ int block_sum_i(int v, SmemMisc& m, int slot, int lane, int warp) {
+    v = warp_sum_i(v);
+    if (lane == 0) m.red_i[slot][warp] = v;
+    cbar();
+    int r = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) r += m.red_i[slot][w];
+    return r;
+}
+__device__ __forceinline__ int block_max_i(int v, SmemMisc& m, int slot, int lane, int warp) {
+    v = warp_max_i(v);
+    if (lane == 0) m.red_i[slot][warp] = v;
+    cbar();
+    int r = m.red_i[slot][0];
+#pragma unroll
+    for (int w = 1; w < kWarps; ++w) r = max(r, m.red_i[slot][w]);
+    return r;
+}
+__device__ __forceinline__ double block_sum_d(double v, SmemMisc& m, int slot, int lane, int warp) {
+    v = warp_sum_d(v);
+    if (lane == 0) m.red_d[slot][warp] = v;
+    cbar();
+    double r = m.red_d[slot][0];
+#pragma unroll
+    for (int w = 1; w < kWarps; ++w) r = __dadd_rn(r, m.red_d[slot][w]);
+    return r;
+}
+// max of a and min of b in one barrier (slots `slot` of red_f for a and `slot + 1` for b)
+__device__ __forceinline__ void block_max_min_f(float& a, float& b, SmemMisc& m, int slot, int lane, int warp) {
+    a = warp_max_f(a);
+    b = warp_min_f(b);
+    if (lane == 0) {
+        m.red_f[slot][warp] = a;
+        m.red_f[slot + 1][warp] = b;
+    }
+    cbar();
+    a = m.red_f[slot][0];
+    b = m.red_f[slot + 1][0];
+#pragma unroll
+    for (int w = 1; w < kWarps; ++w) {
+        a = fmaxf(a, m.red_f[slot][w]);
+        b = fminf(b, m.red_f[slot + 1][w]);
+    }
+}
+// Exclusive scan of a uint64 over the 128 element threads in thread order; `total` is the sum over all.
+__device__ __forceinline__ void block_scan_u64(unsigned long long v, SmemMisc& m, int slot, int lane, int warp,
+                                               unsigned long long& excl, unsigned long long& total) {
+    unsigned long long incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long y = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31) m.red_u[slot][warp] = incl;
+    cbar();
+    unsigned long long base = 0, tot = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+        const unsigned long long t = m.red_u[slot][w];
+        if (w < warp) base += t;
+        tot += t;
+    }
+    excl = base + incl - v;
+    total = tot;
+}
+
 // ---------------------------------------------------------------- per-row element transform
 struct RowCtx {
     int vocab;
@@ -248,6 +401,17 @@ struct RowCtx {
     bool sample;
     float inv_t;         // fp32(1 / T)
     const uint32_t* bitmap;
+};
+
+// Staged position -> vocabulary id: [0, lo_al) | kvw ids from kbase | [hi_al, V)
+struct RowMap {
+    int lo_al, kvw, kbase, hi_al;
+    __device__ __forceinline__ int idx(int q) const {
+        if (q < lo_al) return q;
+        q -= lo_al;
+        if (q < kvw) return kbase + q;
+        return q - kvw + hi_al;
+    }
 };
 
 // penalty (Sampler.cs:31) -> mask (TalkerGenerator.cs:247-248) -> temperature (Sampler.cs:40)
@@ -290,68 +454,55 @@ __device__ __forceinline__ float load_elem(const unsigned char* base, int i, int
     return __uint_as_float(static_cast<uint32_t>(reinterpret_cast<const uint16_t*>(base)[i]) << 16);
 }
 
-// ---------------------------------------------------------------- block reductions (compute warps)
-// Max over the 128 compute threads.  Uses misc.red_v; one cbar.
-__device__ float block_max(float v, SmemMisc& misc, int lane, int warp) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
-    if (lane == 0) misc.red_v[warp] = v;
-    cbar();
-    float r = misc.red_v[0];
-#pragma unroll
-    for (int w = 1; w < kWarps; ++w) r = fmaxf(r, misc.red_v[w]);
-    return r;
-}
-
-// ---------------------------------------------------------------- general path (all 128 compute threads)
-// gx[0, V) holds the transformed row (suppressed ids = -inf).  Returns the sampled id in every thread.
-__device__ int general_path(const RowCtx& c, const DevOptions& o, double r, float mx, float* gx, double* gp,
-                            uint4* gs, int sort_n, double* out_probs, SmemMisc& misc, int tid) {
+// ---------------------------------------------------------------- exact block path (all 128 element threads)
+// The reference's operations in its own order over gx[0, V) (per-CTA global scratch; suppressed ids = -inf).
+// Runs for rows whose parallel decisions are inside the error band, and for rows of more than 3072 active ids.
+__device__ int exact_block_path(const RowCtx& c, const DevOptions& o, double r, float mx, float* gx, double* gp,
+                                uint4* gs, int sort_n, double* out_probs, SmemMisc& misc, int tid) {
     const int V = c.vocab;
     if (is_neg_inf(mx)) {
         // Every logit is -inf: the reference's probabilities are 0/0 = NaN, the draw never fires and it
         // returns the last index (Sampler.cs:80-87).
         if (out_probs)
             for (int i = tid; i < V; i += kThreads) out_probs[i] = 0.0;
+        cbar();
         return V - 1;
     }
-    // ---- top-k threshold: the K-th largest of the V values (radix select over order-preserving keys)
     float kth = neg_inf();
     const int K = o.top_k;
-    if (K > 0 && K < V) {
+    if (K > 0 && K < V) {   // the K-th largest of the V values
         uint32_t prefix = 0, pmask = 0;
         int need = K;
         for (int shift = 24; shift >= 0; shift -= 8) {
-            for (int b = tid; b < 256; b += kThreads) misc.hist256[b] = 0;
+            for (int b = tid; b < 256; b += kThreads) misc.chist[b] = 0;
             cbar();
             for (int i = tid; i < V; i += kThreads) {
                 const uint32_t k = okey(gx[i]);
-                if ((k & pmask) == prefix) atomicAdd(&misc.hist256[(k >> shift) & 255u], 1u);
+                if ((k & pmask) == prefix) atomicAdd(&misc.chist[(k >> shift) & 255u], 1u);
             }
             cbar();
             if (tid == 0) {
                 int d = 255;
                 for (; d > 0; --d) {
-                    const int h = static_cast<int>(misc.hist256[d]);
+                    const int h = static_cast<int>(misc.chist[d]);
                     if (need <= h) break;
                     need -= h;
                 }
-                misc.bcast_i = d;
-                misc.bcast_d = static_cast<double>(need);
+                misc.bc_i[0] = d;
+                misc.bc_i[1] = need;
             }
             cbar();
-            const uint32_t d = static_cast<uint32_t>(misc.bcast_i);
-            need = static_cast<int>(misc.bcast_d);
+            const uint32_t d = static_cast<uint32_t>(misc.bc_i[0]);
+            need = misc.bc_i[1];
             prefix |= d << shift;
             pmask |= 255u << shift;
             cbar();
         }
         kth = okey_inv(prefix);
     }
-    // ---- softmax numerators (Sampler.cs:55-58): exp(fp64(fp32(x - max))) for survivors, 0 otherwise
-    for (int i = tid; i < V; i += kThreads) {
+    for (int i = tid; i < V; i += kThreads) {   // Sampler.cs:55-57
         const float x = gx[i];
-        gp[i] = (!is_neg_inf(x) && x >= kth) ? exp(static_cast<double>(__fsub_rn(x, mx))) : 0.0;
+        gp[i] = (!is_neg_inf(x) && x >= kth) ? softmax_num(x, mx) : 0.0;
     }
     cbar();
     if (tid == 0) {   // sequential fp64 sum in index order (Sampler.cs:58)
@@ -360,11 +511,11 @@ __device__ int general_path(const RowCtx& c, const DevOptions& o, double r, floa
             const double v = gp[i];
             if (v != 0.0) s = __dadd_rn(s, v);
         }
-        misc.bcast_d = s;
+        misc.bc_d[0] = s;
     }
     cbar();
     {
-        const double s1 = misc.bcast_d;
+        const double s1 = misc.bc_d[0];
         for (int i = tid; i < V; i += kThreads) gp[i] = __ddiv_rn(gp[i], s1);   // :60
     }
     cbar();
@@ -374,7 +525,8 @@ __device__ int general_path(const RowCtx& c, const DevOptions& o, double r, floa
             uint4 it;
             if (i < V) {
                 const unsigned long long b = static_cast<unsigned long long>(__double_as_longlong(gp[i]));
-                it = make_uint4(static_cast<uint32_t>(b), static_cast<uint32_t>(b >> 32), static_cast<uint32_t>(i), 0u);
+                it = make_uint4(static_cast<uint32_t>(b), static_cast<uint32_t>(b >> 32), static_cast<uint32_t>(i),
+                                0u);
             } else {
                 it = make_uint4(0xffffffffu, 0xffffffffu, 0xffffffffu, 0u);
             }
@@ -405,7 +557,8 @@ __device__ int general_path(const RowCtx& c, const DevOptions& o, double r, floa
             int m = V - 1;
             for (int j = 0; j < V - 1; ++j) {
                 const uint4 it = gs[j];
-                const double v = __longlong_as_double(static_cast<long long>((static_cast<uint64_t>(it.y) << 32) | it.x));
+                const double v =
+                    __longlong_as_double(static_cast<long long>((static_cast<uint64_t>(it.y) << 32) | it.x));
                 if (v == 0.0) continue;   // adds 0 and removes an id that is already 0
                 cum = __dadd_rn(cum, v);
                 if (!(cum <= thr)) {
@@ -413,11 +566,11 @@ __device__ int general_path(const RowCtx& c, const DevOptions& o, double r, floa
                     break;
                 }
             }
-            misc.bcast_i = m;
+            misc.bc_i[0] = m;
         }
         cbar();
         {
-            const int m = misc.bcast_i;
+            const int m = misc.bc_i[0];
             for (int j = tid; j < m; j += kThreads) gp[gs[j].z] = 0.0;
         }
         cbar();
@@ -427,11 +580,11 @@ __device__ int general_path(const RowCtx& c, const DevOptions& o, double r, floa
                 const double v = gp[i];
                 if (v != 0.0) s = __dadd_rn(s, v);
             }
-            misc.bcast_d = s;
+            misc.bc_d[0] = s;
         }
         cbar();
         {
-            const double s2 = misc.bcast_d;
+            const double s2 = misc.bc_d[0];
             for (int i = tid; i < V; i += kThreads) gp[i] = __ddiv_rn(gp[i], s2);   // :74
         }
         cbar();
@@ -449,167 +602,621 @@ __device__ int general_path(const RowCtx& c, const DevOptions& o, double r, floa
                 break;
             }
         }
-        misc.bcast_i = res < 0 ? last : res;
+        misc.bc_i[0] = res < 0 ? last : res;
     }
     if (out_probs)
         for (int i = tid; i < V; i += kThreads) out_probs[i] = gp[i];
     cbar();
-    const int res = misc.bcast_i;
+    const int res = misc.bc_i[0];
     cbar();
     return res;
 }
 
-// ---------------------------------------------------------------- small path (one warp)
-// Candidates (x, idx) in `cand[0, C)`, C <= kCandCap.  Returns the sampled id, or -1 if the survivors
-// exceed kSmallSurvivors.  Runs on warp 0 only.
-__device__ int small_path(const Cand* cand, int C, const DevOptions& o, double r, double* out_probs,
-                          SmemMisc& misc, int lane) {
-    // descending value, ascending index
+// ---------------------------------------------------------------- general path, parallel (element threads)
+// x[g * VW + e] is staged position (tid + 128 g) * VW + e, valid while (tid + 128 g) < nvec; the staged order is
+// the index order.  Returns the sampled id, or -1 when a decision lies inside the error band.
+// `ecache` (nullable, shared memory, kRegElems * 128 doubles) keeps each survivor's softmax numerator at
+// [j * 128 + tid]; without it they are recomputed.
+template <int VW>
+__device__ int general_parallel(const float (&x)[kRegElems], int nvec, const RowMap& mp, int V,
+                                const DevOptions& o, double r, float mx, double* out_probs, double* ecache,
+                                SmemMisc& m, int tid, int lane, int warp) {
+    constexpr int G = kRegElems / VW;
+    constexpr int FB = VW == 4 ? 10 : 11;           // bits per packed count field
+    if (is_neg_inf(mx)) return -1;                  // all -inf: the exact path reproduces the NaN behaviour
+    // ---- top-k threshold
+    float kth = neg_inf();
+    const int K = o.top_k;
+    if (K > 0 && K < V) {
+        int fin = 0;
+#pragma unroll
+        for (int j = 0; j < kRegElems; ++j) fin += is_neg_inf(x[j]) ? 0 : 1;
+        fin = block_sum_i(fin, m, 0, lane, warp);
+        if (K <= fin) {   // else the K-th largest is -inf and the cut keeps every finite value
+            uint32_t prefix = 0, pmask = 0;
+            int need = K;
+            for (int pass = 0; pass < 4; ++pass) {
+                const int shift = 24 - 8 * pass;
+                for (int b = tid; b < 256; b += kThreads) m.chist[b] = 0;
+                cbar();
+#pragma unroll
+                for (int j = 0; j < kRegElems; ++j) {
+                    if (!is_neg_inf(x[j])) {
+                        const uint32_t k = okey(x[j]);
+                        if ((k & pmask) == prefix) atomicAdd(&m.chist[(k >> shift) & 255u], 1u);
+                    }
+                }
+                cbar();
+                if (warp == 0) {   // the need-th largest: suffix counts from the top bin
+                    int c[8], loc = 0;
+#pragma unroll
+                    for (int b = 0; b < 8; ++b) {
+                        c[b] = static_cast<int>(m.chist[lane * 8 + b]);
+                        loc += c[b];
+                    }
+                    int suf = loc;   // sum over lanes >= lane
+#pragma unroll
+                    for (int off = 1; off < 32; off <<= 1) {
+                        const int y = __shfl_down_sync(kFull, suf, off);
+                        if (lane + off < 32) suf += y;
+                    }
+                    int above = suf - loc;   // lanes above this one
+                    if (above < need && need <= suf) {
+#pragma unroll
+                        for (int b = 7; b >= 0; --b) {
+                            if (need <= above + c[b]) {
+                                m.bc_i[0] = lane * 8 + b;
+                                m.bc_i[1] = need - above;
+                                break;
+                            }
+                            above += c[b];
+                        }
+                    }
+                }
+                cbar();
+                prefix |= static_cast<uint32_t>(m.bc_i[0]) << shift;
+                need = m.bc_i[1];
+                pmask |= 255u << shift;
+                cbar();
+            }
+            kth = okey_inv(prefix);
+        }
+    }
+    // ---- softmax numerators of the survivors, total and count
+    auto ev = [&](int j) -> double {
+        if (is_neg_inf(x[j]) || !(x[j] >= kth)) return 0.0;
+        return ecache ? ecache[j * kThreads + tid] : softmax_num(x[j], mx);
+    };
+    double lsum = 0.0;
+    int lcnt = 0;
+#pragma unroll
+    for (int j = 0; j < kRegElems; ++j) {
+        const bool s = !is_neg_inf(x[j]) && x[j] >= kth;
+        const double ej = s ? softmax_num(x[j], mx) : 0.0;
+        if (ecache) ecache[j * kThreads + tid] = ej;
+        lsum = __dadd_rn(lsum, ej);
+        lcnt += s ? 1 : 0;
+    }
+    const double total = block_sum_d(lsum, m, 0, lane, warp);
+    const int nsurv = block_sum_i(lcnt, m, 1, lane, warp);
+    const double eta = (4.0 * nsurv + 128.0) * kU;
+    uint32_t removed = 0;   // bit j: element j removed by top-p
+    if (o.top_p < 1.0f) {
+        const double thr = static_cast<double>(__fsub_rn(1.0f, o.top_p));
+        const double T = __dmul_rn(thr, total);
+        const double before_last = __dsub_rn(total, 1.0);   // mass of every survivor but one max (e(max) = 1)
+        const double band = __dmul_rn(eta, total);
+        if (__dsub_rn(T, before_last) > band) {
+            // the cut never fires before the last element: every survivor but the last of the order goes.  The
+            // last is the max with the highest index; survivors below the max must have a strictly smaller
+            // probability in the reference too.
+            int li = -1;
+            float below = neg_inf();
+#pragma unroll
+            for (int j = 0; j < kRegElems; ++j) {
+                const int qv = tid + (j / VW) * kThreads;
+                if (!is_neg_inf(x[j]) && x[j] >= kth) {
+                    if (x[j] == mx) li = max(li, mp.idx(qv * VW + (j % VW)));
+                    else below = fmaxf(below, x[j]);
+                }
+            }
+            li = block_max_i(li, m, 0, lane, warp);
+            below = block_max_f(below, m, 0, lane, warp);
+            if (!is_neg_inf(below) && !(softmax_num(below, mx) < 1.0 - 32.0 * kU)) return -1;
+#pragma unroll
+            for (int j = 0; j < kRegElems; ++j) {
+                const int qv = tid + (j / VW) * kThreads;
+                const bool s = !is_neg_inf(x[j]) && x[j] >= kth;
+                if (s && mp.idx(qv * VW + (j % VW)) != li) removed |= 1u << j;
+            }
+        } else if (__dsub_rn(before_last, T) > band) {
+            // mass radix select over ascending keys: the group x* holding the break element
+            uint32_t prefix = 0, pmask = 0;
+            double below = 0.0;
+            int ng = 0;
+            for (int pass = 0; pass < 4; ++pass) {
+                const int shift = 24 - 8 * pass;
+                for (int b = tid; b < 256; b += kThreads) {
+                    m.chist[b] = 0;
+                    m.mhist[b] = 0.0;
+                }
+                cbar();
+#pragma unroll
+                for (int j = 0; j < kRegElems; ++j) {
+                    if (!is_neg_inf(x[j]) && x[j] >= kth) {
+                        const uint32_t k = okey(x[j]);
+                        if ((k & pmask) == prefix) {
+                            atomicAdd(&m.chist[(k >> shift) & 255u], 1u);
+                            atomicAdd(&m.mhist[(k >> shift) & 255u], ev(j));
+                        }
+                    }
+                }
+                cbar();
+                if (warp == 0) {
+                    double mb[8], loc = 0.0;
+#pragma unroll
+                    for (int b = 0; b < 8; ++b) {
+                        mb[b] = m.mhist[lane * 8 + b];
+                        loc = __dadd_rn(loc, mb[b]);
+                    }
+                    const double incl = warp_incl_d(loc, lane);
+                    double acc = __dadd_rn(below, __dsub_rn(incl, loc));
+                    int found = -1;
+                    double acc_before = 0.0;
+                    if (__dadd_rn(below, incl) > T && !(acc > T)) {
+#pragma unroll
+                        for (int b = 0; b < 8; ++b) {
+                            const double nxt = __dadd_rn(acc, mb[b]);
+                            if (found < 0 && nxt > T) {
+                                found = lane * 8 + b;
+                                acc_before = acc;
+                            }
+                            acc = nxt;
+                        }
+                    }
+                    const unsigned who = __ballot_sync(kFull, found >= 0);
+                    if (lane == 0) m.bc_i[0] = who ? 1 : 0;
+                    if (who) {
+                        const int src = __ffs(who) - 1;
+                        const int d = __shfl_sync(kFull, found, src);
+                        const double ab = shfl_d(acc_before, src);
+                        if (lane == 0) {
+                            m.bc_i[1] = d;
+                            m.bc_i[2] = static_cast<int>(m.chist[d]);
+                            m.bc_d[0] = ab;
+                        }
+                    }
+                }
+                cbar();
+                if (!m.bc_i[0]) return -1;   // rounding put the crossing outside every bin
+                prefix |= static_cast<uint32_t>(m.bc_i[1]) << shift;
+                pmask |= 255u << shift;
+                below = m.bc_d[0];
+                ng = m.bc_i[2];
+                cbar();
+            }
+            const float xs = okey_inv(prefix);
+            const double es = softmax_num(xs, mx);
+            const double q = __ddiv_rn(__dsub_rn(T, below), es);
+            if (!(q >= 0.0) || !(q < static_cast<double>(ng))) return -1;
+            const int jrem = static_cast<int>(floor(q));   // group members removed (lowest ids first)
+            const double last_removed = __dadd_rn(below, __dmul_rn(static_cast<double>(jrem), es));
+            const double brk = __dadd_rn(below, __dmul_rn(static_cast<double>(jrem + 1), es));
+            if (!(__dsub_rn(brk, T) > band)) return -1;
+            if (last_removed > 0.0 && !(__dsub_rn(T, last_removed) > band)) return -1;
+            // neighbours: the reference orders by probability, so the groups next to x* must be strictly apart
+            float lo_n = neg_inf(), hi_n = pos_inf();
+#pragma unroll
+            for (int j = 0; j < kRegElems; ++j) {
+                if (!is_neg_inf(x[j]) && x[j] >= kth) {
+                    if (x[j] < xs) lo_n = fmaxf(lo_n, x[j]);
+                    if (x[j] > xs) hi_n = fminf(hi_n, x[j]);
+                }
+            }
+            block_max_min_f(lo_n, hi_n, m, 2, lane, warp);
+            if (!is_neg_inf(lo_n) && !(softmax_num(lo_n, mx) < es * (1.0 - 32.0 * kU))) return -1;
+            if (jrem > 0 && hi_n != pos_inf() && !(softmax_num(hi_n, mx) > es * (1.0 + 32.0 * kU))) return -1;
+            // rank of each x* member in index order (packed per-vector counts, one block scan)
+            unsigned long long packed = 0;
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                unsigned cg = 0;
+#pragma unroll
+                for (int t = 0; t < VW; ++t) {
+                    const int j = g * VW + t;
+                    cg += (!is_neg_inf(x[j]) && x[j] >= kth && x[j] == xs) ? 1u : 0u;
+                }
+                packed |= static_cast<unsigned long long>(cg) << (FB * g);
+            }
+            unsigned long long pex, ptot;
+            block_scan_u64(packed, m, 0, lane, warp, pex, ptot);
+            const unsigned long long fmask = (1ull << FB) - 1;
+            unsigned base_g = 0;
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                unsigned rk = base_g + static_cast<unsigned>((pex >> (FB * g)) & fmask);
+#pragma unroll
+                for (int t = 0; t < VW; ++t) {
+                    const int j = g * VW + t;
+                    const bool s = !is_neg_inf(x[j]) && x[j] >= kth;
+                    if (s && (x[j] < xs || (x[j] == xs && rk < static_cast<unsigned>(jrem)))) removed |= 1u << j;
+                    if (s && x[j] == xs) ++rk;
+                }
+                base_g += static_cast<unsigned>((ptot >> (FB * g)) & fmask);
+            }
+        } else {
+            return -1;
+        }
+    }
+    // ---- inverse-CDF draw over the kept ids in index order
+    double c[G];
+    double lk = 0.0;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        c[g] = 0.0;
+#pragma unroll
+        for (int t = 0; t < VW; ++t) {
+            const int j = g * VW + t;
+            if (!((removed >> j) & 1u)) c[g] = __dadd_rn(c[g], ev(j));
+        }
+        lk = __dadd_rn(lk, c[g]);
+    }
+    // per-vector exclusive prefix across threads, and the per-vector totals
+    double ex[G], tot[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const double incl = warp_incl_d(c[g], lane);
+        ex[g] = warp_excl_from_incl_d(incl, lane);
+        if (lane == 31) m.red_v[warp][g] = incl;
+    }
+    cbar();
+    double B = 0.0;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        double base = 0.0, t = 0.0;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) {
+            const double v = m.red_v[w][g];
+            if (w < warp) base = __dadd_rn(base, v);
+            t = __dadd_rn(t, v);
+        }
+        ex[g] = __dadd_rn(ex[g], base);
+        tot[g] = t;
+        B = __dadd_rn(B, t);
+    }
+    const double rB = __dmul_rn(r, B);
+    const double bandB = __dmul_rn(eta, B);
+    int hit = -1, hits = 0;
+    bool unsure = false;
+    double run = 0.0;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        double pre = __dadd_rn(run, ex[g]);
+#pragma unroll
+        for (int t = 0; t < VW; ++t) {
+            const int j = g * VW + t;
+            const double ej = ((removed >> j) & 1u) ? 0.0 : ev(j);
+            if (ej > 0.0) {
+                const double inc = __dadd_rn(pre, ej);
+                if (inc > rB && !(pre > rB)) {
+                    ++hits;
+                    hit = mp.idx((tid + g * kThreads) * VW + t);
+                    if (!(__dsub_rn(inc, rB) > bandB)) unsure = true;
+                    if (pre > 0.0 && !(__dsub_rn(rB, pre) > bandB)) unsure = true;
+                }
+                pre = inc;
+            }
+        }
+        run = __dadd_rn(run, tot[g]);
+    }
+    hits = block_sum_i(hits, m, 2, lane, warp);
+    const bool any_unsure = cbar_or(unsure);
+    if (hits != 1 || any_unsure) return -1;
+    hit = block_max_i(hit, m, 3, lane, warp);
+    if (out_probs) {
+        for (int i = tid; i < V; i += kThreads) out_probs[i] = 0.0;
+        cbar();
+#pragma unroll
+        for (int j = 0; j < kRegElems; ++j) {
+            const int qv = tid + (j / VW) * kThreads;
+            if (qv < nvec) {
+                const int i = mp.idx(qv * VW + (j % VW));
+                if (i < V) out_probs[i] = ((removed >> j) & 1u) ? 0.0 : __ddiv_rn(ev(j), B);
+            }
+        }
+        cbar();
+    }
+    return hit;
+}
+
+// ---------------------------------------------------------------- chain warp: parallel path
+// Candidates cand[0, C) (C <= 128, every survivor among them).  Returns the id, or -1 when a decision is inside
+// the error band.
+__device__ int chain_parallel(const ChainSlot& sl, double* out_probs, int lane) {
+    const int C = static_cast<int>(sl.count);
+    const int K = sl.K;
+    // ascending (value, index); padding (key 0) sorts first, so real entries sit at positions [128 - C, 128)
     uint64_t key[4];
 #pragma unroll
     for (int s = 0; s < 4; ++s) {
         const int e = s * 32 + lane;
-        if (e < C) {
-            const Cand cd = cand[e];
-            key[s] = (static_cast<uint64_t>(~okey(cd.x)) << 32) | static_cast<uint32_t>(cd.idx);
-        } else {
-            key[s] = ~0ull;
-        }
+        key[s] = e < C ? ((static_cast<uint64_t>(okey(sl.cand[e].x)) << 32) | static_cast<uint32_t>(sl.cand[e].idx))
+                       : 0ull;
     }
     warp_sort<4>(key, lane);
-    const int K = o.top_k;
-    const int ks = (K - 1) >> 5, kl = (K - 1) & 31;
+    const int kp = kCandCap - K;   // position of the K-th largest
     uint64_t kk = 0;
 #pragma unroll
     for (int s = 0; s < 4; ++s) {
-        const uint64_t v = shfl_u64(key[s], kl);
-        if (s == ks) kk = v;
+        const uint64_t v = shfl_u64(key[s], kp & 31);
+        if (s == (kp >> 5)) kk = v;
+    }
+    const uint32_t kth_key = static_cast<uint32_t>(kk >> 32);
+    const float mx = okey_inv(static_cast<uint32_t>(shfl_u64(key[3], 31) >> 32));
+    bool surv[4];
+    float xv[4];
+    double e[4];
+    int S = 0;
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+        surv[s] = key[s] != 0ull && static_cast<uint32_t>(key[s] >> 32) >= kth_key;
+        xv[s] = okey_inv(static_cast<uint32_t>(key[s] >> 32));
+        e[s] = surv[s] ? softmax_num(xv[s], mx) : 0.0;
+        S += __popc(__ballot_sync(kFull, surv[s]));
+    }
+    const double total = warp_sum_d(__dadd_rn(__dadd_rn(e[0], e[1]), __dadd_rn(e[2], e[3])));
+    const double eta = (4.0 * S + 128.0) * kU;
+    bool removed[4] = {false, false, false, false};
+    const DevOptions& o = sl.opt;
+    if (o.top_p < 1.0f) {
+        const double thr = static_cast<double>(__fsub_rn(1.0f, o.top_p));
+        const double T = __dmul_rn(thr, total);
+        const double band = __dmul_rn(eta, total);
+        // prefix sums in ascending order (positions slot-major)
+        double incl[4], excl[4], base = 0.0;
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+            const double in = warp_incl_d(e[s], lane);
+            excl[s] = __dadd_rn(base, warp_excl_from_incl_d(in, lane));
+            incl[s] = __dadd_rn(base, in);
+            base = __dadd_rn(base, shfl_d(in, 31));
+        }
+        // the break element: a survivor at position <= 126 (the last one is never removed) crossing T
+        unsigned bm[4];
+        int nb = 0;
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+            const int pos = s * 32 + lane;
+            bm[s] = __ballot_sync(kFull, surv[s] && pos <= kCandCap - 2 && incl[s] > T && !(excl[s] > T));
+            nb += __popc(bm[s]);
+        }
+        int pb;   // survivors at positions < pb are removed
+        if (nb == 1) {
+            int bs = 0;
+#pragma unroll
+            for (int s = 0; s < 4; ++s)
+                if (bm[s]) bs = s;
+            const int bl = __ffs(bm[bs]) - 1;
+            pb = bs * 32 + bl;
+            double bi = 0.0, be = 0.0;
+            float bx = 0.0f;
+#pragma unroll
+            for (int s = 0; s < 4; ++s) {
+                const double a = shfl_d(incl[s], bl), b = shfl_d(excl[s], bl);
+                const float xx = __shfl_sync(kFull, xv[s], bl);
+                if (s == bs) {
+                    bi = a;
+                    be = b;
+                    bx = xx;
+                }
+            }
+            if (!(__dsub_rn(bi, T) > band)) return -1;
+            if (be > 0.0 && !(__dsub_rn(T, be) > band)) return -1;
+            // groups next to the break value must be strictly apart in probability
+            float lo_n = neg_inf(), hi_n = pos_inf();
+            bool cut_inside = false;
+#pragma unroll
+            for (int s = 0; s < 4; ++s) {
+                const int pos = s * 32 + lane;
+                if (surv[s]) {
+                    if (xv[s] < bx) lo_n = fmaxf(lo_n, xv[s]);
+                    if (xv[s] > bx) hi_n = fminf(hi_n, xv[s]);
+                    if (xv[s] == bx && pos < pb) cut_inside = true;
+                }
+            }
+            lo_n = warp_max_f(lo_n);
+            hi_n = warp_min_f(hi_n);
+            cut_inside = __any_sync(kFull, cut_inside);
+            const double eb = softmax_num(bx, mx);
+            if (!is_neg_inf(lo_n) && !(softmax_num(lo_n, mx) < eb * (1.0 - 32.0 * kU))) return -1;
+            if (cut_inside && hi_n != pos_inf() && !(softmax_num(hi_n, mx) > eb * (1.0 + 32.0 * kU))) return -1;
+        } else if (nb == 0) {
+            // no crossing before the last survivor: all but the last go, if certainly below T
+            const double at126 = shfl_d(incl[3], 30);
+            if (S > 1 && !(__dsub_rn(T, at126) > band)) return -1;
+            pb = kCandCap - 1;
+            float lo_n = neg_inf();
+#pragma unroll
+            for (int s = 0; s < 4; ++s)
+                if (surv[s] && xv[s] < mx) lo_n = fmaxf(lo_n, xv[s]);
+            lo_n = warp_max_f(lo_n);
+            if (!is_neg_inf(lo_n) && !(softmax_num(lo_n, mx) < 1.0 - 32.0 * kU)) return -1;
+        } else {
+            return -1;
+        }
+#pragma unroll
+        for (int s = 0; s < 4; ++s) removed[s] = surv[s] && (s * 32 + lane) < pb;
+    }
+    // ---- kept ids in index order, then the draw
+    uint64_t k2[4];
+#pragma unroll
+    for (int s = 0; s < 4; ++s)
+        k2[s] = (surv[s] && !removed[s]) ? ((static_cast<uint64_t>(static_cast<uint32_t>(key[s])) << 32) |
+                                            static_cast<uint32_t>(key[s] >> 32))
+                                         : ~0ull;
+    warp_sort<4>(k2, lane);
+    double e2[4];
+    double b4 = 0.0;
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+        e2[s] = k2[s] != ~0ull ? softmax_num(okey_inv(static_cast<uint32_t>(k2[s])), mx) : 0.0;
+        b4 = __dadd_rn(b4, e2[s]);
+    }
+    const double B = warp_sum_d(b4);
+    const double rB = __dmul_rn(sl.uniform, B);
+    const double bandB = __dmul_rn(eta, B);
+    double base = 0.0;
+    int hits = 0, hit = -1;
+    bool unsure = false;
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+        const double in = warp_incl_d(e2[s], lane);
+        const double inc = __dadd_rn(base, in);
+        const double exc = __dadd_rn(base, warp_excl_from_incl_d(in, lane));
+        const bool h = e2[s] > 0.0 && inc > rB && !(exc > rB);
+        if (h) {
+            hit = static_cast<int>(k2[s] >> 32);
+            if (!(__dsub_rn(inc, rB) > bandB)) unsure = true;
+            if (exc > 0.0 && !(__dsub_rn(rB, exc) > bandB)) unsure = true;
+        }
+        hits += __popc(__ballot_sync(kFull, h));
+        base = __dadd_rn(base, shfl_d(in, 31));
+    }
+    if (hits != 1 || __any_sync(kFull, unsure)) return -1;
+    hit = warp_max_i(hit);
+    if (out_probs) {
+        for (int i = lane; i < sl.V; i += 32) out_probs[i] = 0.0;
+        __syncwarp();
+#pragma unroll
+        for (int s = 0; s < 4; ++s)
+            if (k2[s] != ~0ull) out_probs[k2[s] >> 32] = __ddiv_rn(e2[s], B);
+    }
+    return hit;
+}
+
+// ---------------------------------------------------------------- chain warp: exact path
+// The reference's sequential operations on the candidates (<= 128 survivors), every lane running the same chain
+// on shuffled values.
+__device__ int chain_exact(const ChainSlot& sl, double* out_probs, int* flags, int lane) {
+    const int C = static_cast<int>(sl.count);
+    const int K = sl.K;
+    const DevOptions& o = sl.opt;
+    uint64_t key[4];   // descending value, ascending index
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+        const int e = s * 32 + lane;
+        key[s] = e < C ? ((static_cast<uint64_t>(~okey(sl.cand[e].x)) << 32) |
+                          static_cast<uint32_t>(sl.cand[e].idx))
+                       : ~0ull;
+    }
+    warp_sort<4>(key, lane);
+    uint64_t kk = 0;
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+        const uint64_t v = shfl_u64(key[s], (K - 1) & 31);
+        if (s == ((K - 1) >> 5)) kk = v;
     }
     const uint32_t kth_key = ~static_cast<uint32_t>(kk >> 32);
     int S = 0;
 #pragma unroll
-    for (int s = 0; s < 4; ++s) {
-        const bool surv = key[s] != ~0ull && (~static_cast<uint32_t>(key[s] >> 32)) >= kth_key;
-        S += __popc(__ballot_sync(kFull, surv));
-    }
-    if (S > kSmallSurvivors) return -1;
+    for (int s = 0; s < 4; ++s)
+        S += __popc(__ballot_sync(kFull, key[s] != ~0ull && (~static_cast<uint32_t>(key[s] >> 32)) >= kth_key));
     const float mx = okey_inv(~static_cast<uint32_t>(shfl_u64(key[0], 0) >> 32));
-
-    // survivors (positions [0, S)) re-sorted by index, carrying the value key
-    uint64_t k2[2];
+    // survivors are positions [0, S); re-sort them by index
+    uint64_t k2[4];
 #pragma unroll
-    for (int s = 0; s < 2; ++s) {
-        const int e = s * 32 + lane;
-        k2[s] = e < S ? ((static_cast<uint64_t>(static_cast<uint32_t>(key[s])) << 32) | ~static_cast<uint32_t>(key[s] >> 32))
-                      : ~0ull;
-    }
-    warp_sort<2>(k2, lane);
-    int idx[2];
-    double p[2];
+    for (int s = 0; s < 4; ++s)
+        k2[s] = (s * 32 + lane) < S ? ((static_cast<uint64_t>(static_cast<uint32_t>(key[s])) << 32) |
+                                       ~static_cast<uint32_t>(key[s] >> 32))
+                                    : ~0ull;
+    warp_sort<4>(k2, lane);
+    int idx[4];
+    double p[4];
 #pragma unroll
-    for (int s = 0; s < 2; ++s) {
-        const int e = s * 32 + lane;
+    for (int s = 0; s < 4; ++s) {
         idx[s] = static_cast<int>(k2[s] >> 32);
-        const float x = okey_inv(static_cast<uint32_t>(k2[s]));
-        p[s] = e < S ? exp(static_cast<double>(__fsub_rn(x, mx))) : 0.0;   // Sampler.cs:57
+        p[s] = (s * 32 + lane) < S ? softmax_num(okey_inv(static_cast<uint32_t>(k2[s])), mx) : 0.0;
     }
-    // sequential fp64 sum in index order (Sampler.cs:58)
-    double s1 = 0.0;
-    {
-        const int n0 = S < 32 ? S : 32;
-        for (int j = 0; j < n0; ++j) s1 = __dadd_rn(s1, shfl_d(p[0], j));
-        for (int j = 32; j < S; ++j) s1 = __dadd_rn(s1, shfl_d(p[1], j - 32));
-    }
+    double s1 = 0.0;   // Sampler.cs:58
 #pragma unroll
-    for (int s = 0; s < 2; ++s) p[s] = __ddiv_rn(p[s], s1);   // :60 (0 / s1 = 0 on padding)
-
-    if (o.top_p < 1.0f) {   // Sampler.cs:62-75
+    for (int s = 0; s < 4; ++s)
+        for (int l = 0; l < 32 && s * 32 + l < S; ++l) s1 = __dadd_rn(s1, shfl_d(p[s], l));
+#pragma unroll
+    for (int s = 0; s < 4; ++s) p[s] = __ddiv_rn(p[s], s1);   // :60
+    if (o.top_p < 1.0f) {   // :62-75
         const double thr = static_cast<double>(__fsub_rn(1.0f, o.top_p));
-        uint64_t pk[2];
-        uint32_t tag[2];
+        uint64_t pk[4];
+        uint32_t tag[4];
 #pragma unroll
-        for (int s = 0; s < 2; ++s) {
+        for (int s = 0; s < 4; ++s) {
             const int e = s * 32 + lane;
             pk[s] = e < S ? static_cast<uint64_t>(__double_as_longlong(p[s])) : ~0ull;
-            tag[s] = static_cast<uint32_t>(e);   // index-order position; the order of positions is the index order
+            tag[s] = static_cast<uint32_t>(e);   // index-order position
         }
-        warp_sort_pair<2>(pk, tag, lane);
+        warp_sort_pair<4>(pk, tag, lane);
         double cum = 0.0;
         int m = S - 1;
-        {
-            const int n0 = (S - 1) < 32 ? (S - 1) : 32;
-            bool done = false;
-            for (int j = 0; j < n0; ++j) {
-                cum = __dadd_rn(cum, __longlong_as_double(static_cast<long long>(shfl_u64(pk[0], j))));
-                if (!(cum <= thr)) {
-                    m = j;
+        bool done = false;
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+            for (int l = 0; l < 32 && !done; ++l) {
+                const int j = s * 32 + l;
+                if (j >= S - 1) {
                     done = true;
                     break;
                 }
-            }
-            if (!done)
-                for (int j = 32; j < S - 1; ++j) {
-                    cum = __dadd_rn(cum, __longlong_as_double(static_cast<long long>(shfl_u64(pk[1], j - 32))));
-                    if (!(cum <= thr)) {
-                        m = j;
-                        break;
-                    }
+                cum = __dadd_rn(cum, __longlong_as_double(static_cast<long long>(shfl_u64(pk[s], l))));
+                if (!(cum <= thr)) {
+                    m = j;
+                    done = true;
                 }
+            }
         }
 #pragma unroll
-        for (int s = 0; s < 2; ++s) {
+        for (int s = 0; s < 4; ++s) {
             const int j = s * 32 + lane;
-            if (j < S) misc.flags[tag[s]] = j < m ? 1 : 0;
+            if (j < S) flags[tag[s]] = j < m ? 1 : 0;
         }
         __syncwarp();
 #pragma unroll
-        for (int s = 0; s < 2; ++s) {
+        for (int s = 0; s < 4; ++s) {
             const int e = s * 32 + lane;
-            if (e < S && misc.flags[e]) p[s] = 0.0;
+            if (e < S && flags[e]) p[s] = 0.0;
         }
         __syncwarp();
         double s2 = 0.0;   // probs.Sum() (:73)
-        {
-            const int n0 = S < 32 ? S : 32;
-            for (int j = 0; j < n0; ++j) s2 = __dadd_rn(s2, shfl_d(p[0], j));
-            for (int j = 32; j < S; ++j) s2 = __dadd_rn(s2, shfl_d(p[1], j - 32));
-        }
 #pragma unroll
-        for (int s = 0; s < 2; ++s) p[s] = __ddiv_rn(p[s], s2);   // :74
+        for (int s = 0; s < 4; ++s)
+            for (int l = 0; l < 32 && s * 32 + l < S; ++l) s2 = __dadd_rn(s2, shfl_d(p[s], l));
+#pragma unroll
+        for (int s = 0; s < 4; ++s) p[s] = __ddiv_rn(p[s], s2);   // :74
     }
-    // inverse-CDF draw (Sampler.cs:77-87)
-    double acc = 0.0;
+    double acc = 0.0;   // inverse-CDF draw (:77-87)
     int last = 0, res = -1;
-    {
-        const int n0 = S < 32 ? S : 32;
-        for (int j = 0; j < n0 && res < 0; ++j) {
-            const double v = shfl_d(p[0], j);
-            const int id = __shfl_sync(kFull, idx[0], j);
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+        for (int l = 0; l < 32 && s * 32 + l < S && res < 0; ++l) {
+            const double v = shfl_d(p[s], l);
+            const int id = __shfl_sync(kFull, idx[s], l);
             if (v <= 0.0) continue;
             acc = __dadd_rn(acc, v);
             last = id;
-            if (r < acc) res = id;
-        }
-        for (int j = 32; j < S && res < 0; ++j) {
-            const double v = shfl_d(p[1], j - 32);
-            const int id = __shfl_sync(kFull, idx[1], j - 32);
-            if (v <= 0.0) continue;
-            acc = __dadd_rn(acc, v);
-            last = id;
-            if (r < acc) res = id;
+            if (sl.uniform < acc) res = id;
         }
     }
     if (out_probs) {
+        for (int i = lane; i < sl.V; i += 32) out_probs[i] = 0.0;
+        __syncwarp();
 #pragma unroll
-        for (int s = 0; s < 2; ++s)
+        for (int s = 0; s < 4; ++s)
             if (s * 32 + lane < S) out_probs[idx[s]] = p[s];
     }
     return res < 0 ? last : res;
 }
 
-// ---------------------------------------------------------------- the kernel
+// ---------------------------------------------------------------- element pass
 template <int VW>
-__device__ __forceinline__ void process_vectors(const unsigned char* sl, int nvec, int lo_al, int hi_al,
+__device__ __forceinline__ void process_vectors(const unsigned char* sl, int nvec, const RowMap& mp,
                                                 const RowCtx& c, int tid, float (&x)[kRegElems],
                                                 float& tmax, float& bestv, int& besti) {
     constexpr int G = kRegElems / VW;
@@ -619,8 +1226,7 @@ __device__ __forceinline__ void process_vectors(const unsigned char* sl, int nve
         if (qv < nvec) {
             float v[VW];
             load_vec<VW>(sl, qv, v);
-            const int q0 = qv * VW;
-            const int i0 = q0 < lo_al ? q0 : q0 - lo_al + hi_al;
+            const int i0 = mp.idx(qv * VW);
             const uint32_t bits = c.pen_on ? c.bitmap[i0 >> 5] : 0u;
 #pragma unroll
             for (int e = 0; e < VW; ++e) {
@@ -639,19 +1245,48 @@ __device__ __forceinline__ void process_vectors(const unsigned char* sl, int nve
     }
 }
 
-__global__ void __launch_bounds__(kThreads + 32) sampler_kernel(const __grid_constant__ LaunchParams p) {
+// Greedy: first index of the maximum over the 128 element threads (Sampler.cs:90-95).
+__device__ int block_argmax(float bestv, int besti, SmemMisc& m, int lane, int warp) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const float ov = __shfl_xor_sync(kFull, bestv, off);
+        const int oi = __shfl_xor_sync(kFull, besti, off);
+        if (ov > bestv || (ov == bestv && oi < besti)) {
+            bestv = ov;
+            besti = oi;
+        }
+    }
+    if (lane == 0) {
+        m.red_f[7][warp] = bestv;
+        m.red_i[7][warp] = besti;
+    }
+    cbar();
+    float bv = m.red_f[7][0];
+    int bi = m.red_i[7][0];
+    for (int w = 1; w < kWarps; ++w)
+        if (m.red_f[7][w] > bv || (m.red_f[7][w] == bv && m.red_i[7][w] < bi)) {
+            bv = m.red_f[7][w];
+            bi = m.red_i[7][w];
+        }
+    return is_neg_inf(bv) ? 0 : bi;   // all -inf: the reference's scan never moves off index 0
+}
+
+// ---------------------------------------------------------------- the kernel
+__global__ void __launch_bounds__(kBlockThreads, 4) sampler_kernel(const __grid_constant__ LaunchParams p) {
     extern __shared__ __align__(128) unsigned char smem[];
     const int tid = threadIdx.x;
     const int lane = tid & 31;
     const int warp = tid >> 5;
     const int S_ = p.n_stages;
-    const int stage_bytes = kMetaBytes + kKeepBytes + p.stage_logit_bytes + p.stage_hist_cap * 4;
+    const int stage_bytes = kMetaBytes + p.stage_logit_bytes + p.stage_hist_cap * 4;
     unsigned char* stages = smem;
     uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(S_) * stage_bytes);
     uint64_t* empty_bar = full_bar + S_;
-    uint32_t* bitmap = reinterpret_cast<uint32_t*>(empty_bar + S_);
-    Cand* cand = reinterpret_cast<Cand*>(bitmap + ((p.bitmap_words + 1) & ~1));
-    SmemMisc& misc = *reinterpret_cast<SmemMisc*>(cand + kCandCap);
+    uint64_t* slot_full = empty_bar + S_;
+    uint64_t* slot_empty = slot_full + 2;
+    uint32_t* bitmap = reinterpret_cast<uint32_t*>(slot_empty + 2);
+    ChainSlot* slots = reinterpret_cast<ChainSlot*>(bitmap + ((p.bitmap_words + 3) & ~3));
+    SmemMisc& misc = *reinterpret_cast<SmemMisc*>(slots + 2);
 
     const int first = blockIdx.x;
     const int gstride = gridDim.x;
@@ -662,14 +1297,20 @@ __global__ void __launch_bounds__(kThreads + 32) sampler_kernel(const __grid_con
             mbar_init(&full_bar[s], 1);
             mbar_init(&empty_bar[s], 1);
         }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&slot_full[s], 1);
+            mbar_init(&slot_empty[s], 1);
+            slots[s].count = 0;
+            slots[s].cmd = 0;
+        }
         fence_mbar_init();
-        misc.cand_count = 0;
         misc.issued = 0;
+        misc.progress = 0;
     }
     for (int i = tid; i < p.bitmap_words; i += blockDim.x) bitmap[i] = 0u;
     __syncthreads();
 
-    if (warp == kWarps) {
+    if (warp == kProducerWarp) {
         // ================= producer warp: plans rows and issues the bulk copies =================
         bool alive = true;
         for (int k0 = 0; k0 < n_my && alive; k0 += 32) {
@@ -720,7 +1361,10 @@ __global__ void __launch_bounds__(kThreads + 32) sampler_kernel(const __grid_con
                         m.hi_al = ha;
                     }
                 }
-                m.keep = (sg->kind == 0 && sg->eos >= m.lo_al && sg->eos < m.hi_al && m.step >= sg->min_new) ? 1 : 0;
+                const bool keep =
+                    sg->kind == 0 && sg->eos >= m.lo_al && sg->eos < m.hi_al && m.step >= sg->min_new;
+                m.kvw = keep ? VWe : 0;
+                m.kbase = keep ? sg->eos / VWe * VWe : 0;
                 m.direct = sg->bulk_ok ? 0 : 1;
                 m.hs_lo = 0;
                 m.hs_hi = 0;
@@ -735,7 +1379,7 @@ __global__ void __launch_bounds__(kThreads + 32) sampler_kernel(const __grid_con
                 }
                 row_ptr = static_cast<const unsigned char*>(sg->logits) +
                           static_cast<int64_t>(local) * sg->row_stride * esize;
-                if (!m.direct) bytes += static_cast<uint32_t>((m.lo_al + V - m.hi_al) * esize) + (m.keep ? 16u : 0u);
+                if (!m.direct) bytes += static_cast<uint32_t>((m.lo_al + m.kvw + V - m.hi_al) * esize);
                 bytes += static_cast<uint32_t>(m.hs_hi - m.hs_lo) * 4u;
             }
             const int nb = (n_my - k0) < 32 ? (n_my - k0) : 32;
@@ -745,26 +1389,26 @@ __global__ void __launch_bounds__(kThreads + 32) sampler_kernel(const __grid_con
                     const int k = k0 + j;
                     const int s = k % S_;
                     const int n = k / S_;
-                    if (n > 0) ok = mbar_wait_bounded(&empty_bar[s], static_cast<uint32_t>((n - 1) & 1));
+                    if (n > 0)
+                        ok = mbar_wait_bounded(&empty_bar[s], static_cast<uint32_t>((n - 1) & 1), &misc.progress);
                     if (ok) {
                         unsigned char* st = stages + static_cast<size_t>(s) * stage_bytes;
                         *reinterpret_cast<RowMeta*>(st) = m;
-                        unsigned char* keep_dst = st + kMetaBytes;
-                        unsigned char* log_dst = keep_dst + kKeepBytes;
+                        unsigned char* log_dst = st + kMetaBytes;
                         unsigned char* hist_dst = log_dst + p.stage_logit_bytes;
                         fence_proxy_async();
                         mbar_arrive_expect_tx(&full_bar[s], bytes);
                         if (!m.direct) {
                             const int V = sg->vocab;
-                            if (m.lo_al > 0) bulk_g2s(log_dst, row_ptr, static_cast<uint32_t>(m.lo_al * esize), &full_bar[s]);
+                            if (m.lo_al > 0)
+                                bulk_g2s(log_dst, row_ptr, static_cast<uint32_t>(m.lo_al * esize), &full_bar[s]);
+                            if (m.kvw > 0)
+                                bulk_g2s(log_dst + m.lo_al * esize, row_ptr + static_cast<int64_t>(m.kbase) * esize,
+                                         16u, &full_bar[s]);
                             if (V > m.hi_al)
-                                bulk_g2s(log_dst + m.lo_al * esize, row_ptr + static_cast<int64_t>(m.hi_al) * esize,
+                                bulk_g2s(log_dst + (m.lo_al + m.kvw) * esize,
+                                         row_ptr + static_cast<int64_t>(m.hi_al) * esize,
                                          static_cast<uint32_t>((V - m.hi_al) * esize), &full_bar[s]);
-                            if (m.keep) {
-                                const int VWe = 16 / esize;
-                                bulk_g2s(keep_dst, row_ptr + static_cast<int64_t>(sg->eos / VWe * VWe) * esize, 16u,
-                                         &full_bar[s]);
-                            }
                         }
                         if (m.hs_hi > m.hs_lo)
                             bulk_g2s(hist_dst, sg->hist_ids + m.hist_begin + m.hs_lo,
@@ -784,30 +1428,56 @@ __global__ void __launch_bounds__(kThreads + 32) sampler_kernel(const __grid_con
         return;
     }
 
-    // ================= compute warps =================
+    if (warp == kChainWarp) {
+        // ================= chain warp: candidate rows handed over by the element warps =================
+        for (uint32_t n = 0;; ++n) {
+            const int s = n & 1;
+            if (!mbar_wait_bounded(&slot_full[s], (n >> 1) & 1u, &misc.progress)) {
+                if (lane == 0) atomicOr(p.err, kErrTimeout);
+                return;
+            }
+            ChainSlot& cs = slots[s];
+            if (cs.cmd == 1) return;
+            const DevSegment& g = p.seg[cs.seg];
+            double* probs = g.out_probs ? g.out_probs + static_cast<int64_t>(cs.local) * cs.V : nullptr;
+            int res = chain_parallel(cs, probs, lane);
+            if (res < 0) res = chain_exact(cs, probs, misc.flags, lane);
+            __syncwarp();
+            if (lane == 0) {
+                g.out_ids[cs.local] = res;
+                cs.count = 0;
+                mbar_arrive(&slot_empty[s]);
+            }
+            __syncwarp();
+        }
+    }
+
+    // ================= element warps =================
+    uint32_t h = 0;   // rows handed to the chain warp
     for (int k = 0; k < n_my; ++k) {
         const int s = k % S_;
         unsigned char* st = stages + static_cast<size_t>(s) * stage_bytes;
         const bool ok = mbar_wait_bounded(&full_bar[s], static_cast<uint32_t>((k / S_) & 1));
         if (cbar_or(!ok)) {
-            if (tid == 0) atomicOr(p.err, kErrTimeout);
-            // drain: wait (bounded) for every copy the producer issued after this row
             if (tid == 0) {
+                atomicOr(p.err, kErrTimeout);
+                // drain: wait (bounded) for every copy the producer issued after this row
                 const int issued = *reinterpret_cast<volatile int*>(&misc.issued);
-                for (int kk = k; kk < issued; ++kk) mbar_wait_bounded(&full_bar[kk % S_], static_cast<uint32_t>((kk / S_) & 1));
+                for (int kk = k; kk < issued; ++kk)
+                    mbar_wait_bounded(&full_bar[kk % S_], static_cast<uint32_t>((kk / S_) & 1));
             }
             cbar();
-            return;
+            break;
         }
         const RowMeta m = *reinterpret_cast<const RowMeta*>(st);
         const DevSegment& g = p.seg[m.seg];
-        const unsigned char* keep_src = st + kMetaBytes;
-        unsigned char* sl = st + kMetaBytes + kKeepBytes;
+        unsigned char* sl = st + kMetaBytes;
         const int32_t* sh = reinterpret_cast<const int32_t*>(sl + p.stage_logit_bytes);
         const int V = g.vocab;
         const int dtype = g.dtype;
         const int VWe = dtype == 0 ? 4 : 8;
-        const int NA = m.lo_al + (V - m.hi_al);
+        const RowMap mp{m.lo_al, m.kvw, m.kbase, m.hi_al};
+        const int NA = m.lo_al + m.kvw + (V - m.hi_al);
         const int nvec = (NA + VWe - 1) / VWe;   // bulk-copied rows have NA % VWe == 0
         double* out_probs = g.out_probs ? g.out_probs + static_cast<int64_t>(m.local) * V : nullptr;
 
@@ -817,17 +1487,20 @@ __global__ void __launch_bounds__(kThreads + 32) sampler_kernel(const __grid_con
                 g.out_ids[m.local] = -1;
             }
             cbar();
-            if (tid == 0) mbar_arrive(&empty_bar[s]);
+            if (tid == 0) {
+                mbar_arrive(&empty_bar[s]);
+                ++misc.progress;
+            }
             continue;
         }
         const DevOptions o = m.opt;
 
-        // ---- unaligned rows: the compute warps stage the active ids themselves
+        // ---- unaligned rows: the element warps stage the active ids themselves
         if (m.direct) {
             const unsigned char* row = static_cast<const unsigned char*>(g.logits) +
                                        static_cast<int64_t>(m.local) * g.row_stride * (dtype == 0 ? 4 : 2);
             for (int q = tid; q < nvec * VWe; q += kThreads) {
-                const int i = q < m.lo_al ? q : q - m.lo_al + m.hi_al;
+                const int i = mp.idx(q);
                 if (dtype == 0)
                     reinterpret_cast<float*>(sl)[q] = i < V ? reinterpret_cast<const float*>(row)[i] : neg_inf();
                 else   // padding past V reads as bf16 -inf
@@ -836,8 +1509,8 @@ __global__ void __launch_bounds__(kThreads + 32) sampler_kernel(const __grid_con
         }
 
         // ---- repetition-penalty bitmap: Distinct() over the history (Sampler.cs:28)
-        bool bad = false;
         if (m.pen_on) {
+            bool bad = false;
             const int32_t* gh = g.hist_ids + m.hist_begin;
             const int nst = m.hs_hi - m.hs_lo;
             for (int c4 = tid; c4 < nst / 4; c4 += kThreads) {
@@ -880,105 +1553,113 @@ __global__ void __launch_bounds__(kThreads + 32) sampler_kernel(const __grid_con
         c.inv_t = __fdiv_rn(1.0f, o.temperature);
         c.bitmap = bitmap;
 
+        char* gbase = p.gscratch + static_cast<int64_t>(blockIdx.x) * p.gscratch_stride;
+        const int vpad = (p.vmax + 31) & ~31;
+        float* gx = reinterpret_cast<float*>(gbase);
+        double* gp = reinterpret_cast<double*>(gbase + static_cast<int64_t>(vpad) * 4);
+        uint4* gs = reinterpret_cast<uint4*>(gbase + static_cast<int64_t>(vpad) * 12);
+        int sort_n = 1;
+        while (sort_n < V) sort_n <<= 1;
+
         const bool big = nvec > kThreads * (kRegElems / VWe);
+        if (big) {
+            // ---- rows with more than 3072 active ids: transform into global scratch, exact path
+            float tmax = neg_inf(), bestv = neg_inf();
+            int besti = 0x7fffffff;
+            for (int i = tid; i < V; i += kThreads) gx[i] = neg_inf();
+            cbar();
+            for (int qv = tid; qv < nvec; qv += kThreads) {
+                const int q0 = qv * VWe;
+                const int i0 = mp.idx(q0);
+                const uint32_t bits = c.pen_on ? bitmap[i0 >> 5] : 0u;
+                for (int e = 0; e < VWe && i0 + e < V; ++e) {
+                    const float t = transform(load_elem(sl, q0 + e, dtype), i0 + e, bits, c);
+                    gx[i0 + e] = t;
+                    tmax = fmaxf(tmax, t);
+                    if (t > bestv) {
+                        bestv = t;
+                        besti = i0 + e;
+                    }
+                }
+            }
+            cbar();
+            if (tid == 0) mbar_arrive(&empty_bar[s]);
+            if (m.pen_on)
+                for (int i = tid; i < p.bitmap_words; i += kThreads) bitmap[i] = 0u;
+            int res;
+            if (!c.sample) {
+                res = block_argmax(bestv, besti, misc, lane, warp);
+                if (out_probs)
+                    for (int i = tid; i < V; i += kThreads) out_probs[i] = 0.0;
+            } else {
+                const float mx = block_max_f(tmax, misc, 0, lane, warp);
+                res = exact_block_path(c, o, m.uniform, mx, gx, gp, gs, sort_n, out_probs, misc, tid);
+            }
+            if (tid == 0) {
+                g.out_ids[m.local] = res;
+                ++misc.progress;
+            }
+            cbar();
+            continue;
+        }
+
         float x[kRegElems];
         float tmax = neg_inf();
         float bestv = neg_inf();
         int besti = 0x7fffffff;
-        float xk = neg_inf();   // EOS when staged separately (thread 0)
-        if (!big) {
-            if (dtype == 0)
-                process_vectors<4>(sl, nvec, m.lo_al, m.hi_al, c, tid, x, tmax, bestv, besti);
-            else
-                process_vectors<8>(sl, nvec, m.lo_al, m.hi_al, c, tid, x, tmax, bestv, besti);
-        }
-        if (m.keep && tid == 0) {
-            float v;
-            if (m.direct) {
-                const unsigned char* row = static_cast<const unsigned char*>(g.logits) +
-                                           static_cast<int64_t>(m.local) * g.row_stride * (dtype == 0 ? 4 : 2);
-                v = load_elem(row, g.eos, dtype);
-            } else {
-                v = load_elem(keep_src, g.eos % VWe, dtype);
+        if (dtype == 0)
+            process_vectors<4>(sl, nvec, mp, c, tid, x, tmax, bestv, besti);
+        else
+            process_vectors<8>(sl, nvec, mp, c, tid, x, tmax, bestv, besti);
+        cbar();   // the stage has been read
+        if (m.pen_on)
+            for (int i = tid; i < p.bitmap_words; i += kThreads) bitmap[i] = 0u;
+        bool released = false;
+        auto release = [&]() {   // hand the stage back to the producer (after a cbar)
+            if (!released && tid == 0) mbar_arrive(&empty_bar[s]);
+            released = true;
+        };
+
+        if (!c.sample) {
+            release();
+            const int res = block_argmax(bestv, besti, misc, lane, warp);
+            if (out_probs)
+                for (int i = tid; i < V; i += kThreads) out_probs[i] = 0.0;
+            if (tid == 0) {
+                g.out_ids[m.local] = res;
+                ++misc.progress;
             }
-            const uint32_t bits = c.pen_on ? bitmap[g.eos >> 5] : 0u;
-            xk = transform(v, g.eos, bits, c);
-            tmax = fmaxf(tmax, xk);
-            if (xk > bestv || (xk == bestv && g.eos < besti)) {
-                bestv = xk;
-                besti = g.eos;
-            }
+            continue;
         }
 
-        int result = -1;
-        bool general = false;
-        if (big) {
-            general = true;   // handled below, after the stage is copied out
-        } else if (!c.sample) {
-            // ---- greedy (Sampler.cs:37, 90-95): first index of the maximum
+        const int K = o.top_k;
+        bool handed = false;
+        if (K > 0 && K < V && K <= kSmallK) {
+            release();   // the candidate path no longer reads the stage
+            // tau_w = ceil(K/4)-th largest lane maximum of this warp
+            const int cw = (K + kWarps - 1) / kWarps;
+            uint64_t lk[1] = {static_cast<uint64_t>(~okey(tmax))};
+            warp_sort<1>(lk, lane);
+            const float tw = okey_inv(~static_cast<uint32_t>(__shfl_sync(kFull, lk[0], cw - 1)));
+            if (lane == 0) misc.tau_w[warp] = tw;
+            cbar();
+            float tau = misc.tau_w[0];
 #pragma unroll
-            for (int off = 16; off > 0; off >>= 1) {
-                const float ov = __shfl_xor_sync(kFull, bestv, off);
-                const int oi = __shfl_xor_sync(kFull, besti, off);
-                if (ov > bestv || (ov == bestv && oi < besti)) {
-                    bestv = ov;
-                    besti = oi;
+            for (int w = 1; w < kWarps; ++w) tau = fminf(tau, misc.tau_w[w]);
+            if (!is_neg_inf(tau)) {
+                const int sidx = h & 1;
+                const uint32_t use = h >> 1;
+                bool got = true;
+                if (use > 0) got = mbar_wait_bounded(&slot_empty[sidx], (use - 1) & 1u);
+                if (cbar_or(!got)) {
+                    if (tid == 0) atomicOr(p.err, kErrTimeout);
+                    break;
                 }
-            }
-            if (lane == 0) {
-                misc.red_v[warp] = bestv;
-                misc.red_i[warp] = besti;
-            }
-            cbar();
-            if (tid == 0) {
-                float bv = misc.red_v[0];
-                int bi = misc.red_i[0];
-                for (int w = 1; w < kWarps; ++w)
-                    if (misc.red_v[w] > bv || (misc.red_v[w] == bv && misc.red_i[w] < bi)) {
-                        bv = misc.red_v[w];
-                        bi = misc.red_i[w];
-                    }
-                // all -inf: the reference's scan never moves off index 0
-                g.out_ids[m.local] = is_neg_inf(bv) ? 0 : bi;
-                mbar_arrive(&empty_bar[s]);
-            }
-            if (out_probs)
-                for (int i = tid; i < V; i += kThreads) out_probs[i] = 0.0;
-            if (m.pen_on)
-                for (int i = tid; i < p.bitmap_words; i += kThreads) bitmap[i] = 0u;
-            cbar();
-            continue;
-        } else {
-            const int K = o.top_k;
-            const bool small_ok = K > 0 && K < V && K <= kSmallK;
-            float tau = neg_inf();
-            if (small_ok) {
-                // tau_w = ceil(K/4)-th largest lane maximum of this warp
-                const int cw = (K + kWarps - 1) / kWarps;
-                uint64_t lk[1] = {static_cast<uint64_t>(~okey(tmax))};
-                warp_sort<1>(lk, lane);
-                const float tw = okey_inv(~static_cast<uint32_t>(__shfl_sync(kFull, lk[0], cw - 1)));
-                if (lane == 0) misc.tau_w[warp] = tw;
-            }
-            if (out_probs)
-                for (int i = tid; i < V; i += kThreads) out_probs[i] = 0.0;
-            cbar();   // tau_w visible; the stage has been read: hand it back to the producer
-            if (tid == 0) mbar_arrive(&empty_bar[s]);
-            if (m.pen_on)
-                for (int i = tid; i < p.bitmap_words; i += kThreads) bitmap[i] = 0u;
-            if (small_ok) {
-                tau = misc.tau_w[0];
-#pragma unroll
-                for (int w = 1; w < kWarps; ++w) tau = fminf(tau, misc.tau_w[w]);
-            }
-            if (!small_ok || is_neg_inf(tau)) {
-                general = true;
-            } else {
-                // ---- candidates x >= tau -> shared buffer (warp-scan positions, one atomic per warp)
+                ChainSlot& cs = slots[sidx];
+                // ---- candidates x >= tau -> the chain slot (warp-scan positions, one atomic per warp)
                 int cnt = 0;
 #pragma unroll
                 for (int e = 0; e < kRegElems; ++e) cnt += (x[e] >= tau) ? 1 : 0;
-                if (tid == 0 && m.keep && xk >= tau) ++cnt;
                 int incl = cnt;
 #pragma unroll
                 for (int off = 1; off < 32; off <<= 1) {
@@ -986,128 +1667,87 @@ __global__ void __launch_bounds__(kThreads + 32) sampler_kernel(const __grid_con
                     if (lane >= off) incl += y;
                 }
                 uint32_t base = 0;
-                if (lane == 31) base = atomicAdd(&misc.cand_count, static_cast<uint32_t>(incl));
+                if (lane == 31) base = atomicAdd(&cs.count, static_cast<uint32_t>(incl));
                 base = __shfl_sync(kFull, base, 31);
                 int pos = static_cast<int>(base) + incl - cnt;
                 if (cnt > 0) {
-                    const int VWl = VWe;
 #pragma unroll
                     for (int e = 0; e < kRegElems; ++e) {
                         if (x[e] >= tau) {
                             if (pos < kCandCap) {
-                                const int gg = e / VWl;
+                                const int gg = e / VWe;
                                 const int qv = tid + gg * kThreads;
-                                const int q = qv * VWl + (e - gg * VWl);
-                                const int i = q < m.lo_al ? q : q - m.lo_al + m.hi_al;
-                                cand[pos] = Cand{x[e], i};
+                                cs.cand[pos] = Cand{x[e], mp.idx(qv * VWe + (e - gg * VWe))};
                             }
                             ++pos;
                         }
                     }
-                    if (tid == 0 && m.keep && xk >= tau) {
-                        if (pos < kCandCap) cand[pos] = Cand{xk, g.eos};
-                        ++pos;
-                    }
                 }
                 cbar();
-                if (warp == 0) {
-                    const int C = static_cast<int>(misc.cand_count);
-                    int res = -1;
-                    if (C <= kCandCap) res = small_path(cand, C, o, m.uniform, out_probs, misc, lane);
-                    if (lane == 0) {
-                        misc.decision = res;
-                        if (res >= 0) g.out_ids[m.local] = res;
-                        misc.cand_count = 0;
+                const uint32_t C = cs.count;
+                if (C <= static_cast<uint32_t>(kCandCap)) {
+                    if (tid == 0) {
+                        cs.cmd = 0;
+                        cs.K = K;
+                        cs.V = V;
+                        cs.seg = m.seg;
+                        cs.local = m.local;
+                        cs.opt = o;
+                        cs.uniform = m.uniform;
+                        mbar_arrive(&slot_full[sidx]);
                     }
+                    ++h;
+                    handed = true;
+                } else {
+                    cbar();   // every thread has read the count
+                    if (tid == 0) cs.count = 0;
                 }
-                cbar();
-                result = misc.decision;
-                general = result < 0;
             }
         }
-
-        if (general) {
-            // ================= general path over per-CTA global scratch =================
-            char* gbase = p.gscratch + static_cast<int64_t>(blockIdx.x) * p.gscratch_stride;
-            const int vpad = (p.vmax + 31) & ~31;
-            float* gx = reinterpret_cast<float*>(gbase);
-            double* gp = reinterpret_cast<double*>(gbase + static_cast<int64_t>(vpad) * 4);
-            uint4* gs = reinterpret_cast<uint4*>(gbase + static_cast<int64_t>(vpad) * 12);
-            int sort_n = 1;
-            while (sort_n < V) sort_n <<= 1;
-            for (int i = tid; i < V; i += kThreads) gx[i] = neg_inf();
+        if (!handed) {
+            const float mx = block_max_f(tmax, misc, 0, lane, warp);
+            // the consumed stage doubles as the numerator cache when it is large enough
+            const int used = ((nvec + kThreads - 1) / kThreads) * VWe;
+            double* ecache = (!released && (stage_bytes - kMetaBytes) >= used * kThreads * 8)
+                                 ? reinterpret_cast<double*>(sl) : nullptr;
+            if (!ecache) release();
+            int res = dtype == 0 ? general_parallel<4>(x, nvec, mp, V, o, m.uniform, mx, out_probs, ecache, misc, tid, lane, warp)
+                                 : general_parallel<8>(x, nvec, mp, V, o, m.uniform, mx, out_probs, ecache, misc, tid, lane, warp);
             cbar();
-            if (!big) {
+            release();
+            if (res < 0) {
+                for (int i = tid; i < V; i += kThreads) gx[i] = neg_inf();
+                cbar();
                 const int G = kRegElems / VWe;
                 for (int gg = 0; gg < G; ++gg) {
                     const int qv = tid + gg * kThreads;
                     if (qv < nvec) {
                         for (int e = 0; e < VWe; ++e) {
-                            const int q = qv * VWe + e;
-                            const int i = q < m.lo_al ? q : q - m.lo_al + m.hi_al;
+                            const int i = mp.idx(qv * VWe + e);
                             if (i < V) gx[i] = x[gg * VWe + e];
                         }
                     }
                 }
-            } else {
-                // rows with more than 3072 active ids: transform straight from the stage
-                for (int qv = tid; qv < nvec; qv += kThreads) {
-                    const int q0 = qv * VWe;
-                    const int i0 = q0 < m.lo_al ? q0 : q0 - m.lo_al + m.hi_al;
-                    const uint32_t bits = c.pen_on ? bitmap[i0 >> 5] : 0u;
-                    for (int e = 0; e < VWe && i0 + e < V; ++e) {
-                        const float t = transform(load_elem(sl, q0 + e, dtype), i0 + e, bits, c);
-                        gx[i0 + e] = t;
-                        tmax = fmaxf(tmax, t);
-                        if (t > bestv) {
-                            bestv = t;
-                            besti = i0 + e;
-                        }
-                    }
-                }
-            }
-            if (tid == 0 && m.keep) gx[g.eos] = xk;
-            if (big) {
-                if (out_probs)
-                    for (int i = tid; i < V; i += kThreads) out_probs[i] = 0.0;
                 cbar();
-                if (tid == 0) mbar_arrive(&empty_bar[s]);
-                if (m.pen_on)
-                    for (int i = tid; i < p.bitmap_words; i += kThreads) bitmap[i] = 0u;
+                res = exact_block_path(c, o, m.uniform, mx, gx, gp, gs, sort_n, out_probs, misc, tid);
             }
-            cbar();
-            if (big && !c.sample) {
-#pragma unroll
-                for (int off = 16; off > 0; off >>= 1) {
-                    const float ov = __shfl_xor_sync(kFull, bestv, off);
-                    const int oi = __shfl_xor_sync(kFull, besti, off);
-                    if (ov > bestv || (ov == bestv && oi < besti)) {
-                        bestv = ov;
-                        besti = oi;
-                    }
-                }
-                if (lane == 0) {
-                    misc.red_v[warp] = bestv;
-                    misc.red_i[warp] = besti;
-                }
-                cbar();
-                if (tid == 0) {
-                    float bv = misc.red_v[0];
-                    int bi = misc.red_i[0];
-                    for (int w = 1; w < kWarps; ++w)
-                        if (misc.red_v[w] > bv || (misc.red_v[w] == bv && misc.red_i[w] < bi)) {
-                            bv = misc.red_v[w];
-                            bi = misc.red_i[w];
-                        }
-                    g.out_ids[m.local] = is_neg_inf(bv) ? 0 : bi;
-                }
-                cbar();
-                continue;
-            }
-            const float mx = block_max(tmax, misc, lane, warp);
-            cbar();
-            const int res = general_path(c, o, m.uniform, mx, gx, gp, gs, sort_n, out_probs, misc, tid);
             if (tid == 0) g.out_ids[m.local] = res;
+        }
+        if (tid == 0) ++misc.progress;
+    }
+    // no more rows for the chain warp
+    {
+        const int sidx = h & 1;
+        const uint32_t use = h >> 1;
+        if (tid == 0) {
+            bool got = true;
+            if (use > 0) got = mbar_wait_bounded(&slot_empty[sidx], (use - 1) & 1u);
+            if (got) {
+                slots[sidx].cmd = 1;
+                mbar_arrive(&slot_full[sidx]);
+            } else {
+                atomicOr(p.err, kErrTimeout);
+            }
         }
     }
 }
@@ -1140,12 +1780,11 @@ __global__ void __launch_bounds__(256) penalty_kernel(float* logits, int vocab, 
 
 // ---------------------------------------------------------------- host-side launch helpers
 size_t sampler_smem_bytes(const LaunchParams& p) {
-    const size_t stage = kMetaBytes + kKeepBytes + static_cast<size_t>(p.stage_logit_bytes) +
-                         static_cast<size_t>(p.stage_hist_cap) * 4;
+    const size_t stage = kMetaBytes + static_cast<size_t>(p.stage_logit_bytes) + static_cast<size_t>(p.stage_hist_cap) * 4;
     size_t b = stage * p.n_stages;
-    b += 2 * sizeof(uint64_t) * p.n_stages;
-    b += sizeof(uint32_t) * ((p.bitmap_words + 1) & ~1);
-    b += sizeof(Cand) * kCandCap;
+    b += sizeof(uint64_t) * (2 * p.n_stages + 4);
+    b += sizeof(uint32_t) * ((p.bitmap_words + 3) & ~3);
+    b += sizeof(ChainSlot) * 2;
     b += sizeof(SmemMisc);
     return b;
 }
@@ -1167,13 +1806,13 @@ int sampler_ctas_per_sm(size_t smem) {
         configured = smem;
     }
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, sampler_kernel, kThreads + 32, smem) != cudaSuccess)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, sampler_kernel, kBlockThreads, smem) != cudaSuccess)
         return 0;
     return n;
 }
 
 cudaError_t launch_sampler(const LaunchParams& p, int grid, size_t smem, cudaStream_t stream) {
-    sampler_kernel<<<grid, kThreads + 32, smem, stream>>>(p);
+    sampler_kernel<<<grid, kBlockThreads, smem, stream>>>(p);
     return cudaGetLastError();
 }
 
