@@ -233,6 +233,7 @@ def main():
     for _ in range(2):
         graph.replay()
     torch.cuda.synchronize()
+    dev.stats(reset=True)
 
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
@@ -247,6 +248,7 @@ def main():
     torch.cuda.synchronize()
     elapsed_ms = ev0.elapsed_time(ev1)
     dev.synchronize(sp)   # raises if the kernel latched an error
+    paths = dev.stats(reset=True)
     t = torch.tensor([elapsed_ms], dtype=torch.float64, device="cuda")
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -324,6 +326,7 @@ def main():
             "clocks": clocks.summary(),
             "gpu_launches": args.steps,
             "parity": parity,
+            "rows_by_path": paths,
         }
         print(json.dumps(line), flush=True)
     del graph

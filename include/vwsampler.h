@@ -90,6 +90,20 @@ typedef struct vw_segment {
                                     softmax, top-p and renormalisation), 0 for every other id; NULL = none */
 } vw_segment;
 
+/* Rows sampled per path since the handle was created (or last reset).  Every path returns the reference's id;
+ * the counters show where the time goes.  "replayed" rows had a top-p or draw decision within the proven error
+ * band of the parallel sums and were recomputed in the reference's sequential order. */
+typedef struct vw_stats {
+    uint64_t rows_greedy;            /* DoSample == false: argmax */
+    uint64_t rows_fast;              /* top-k <= 64 rows decided from their candidates in parallel */
+    uint64_t rows_fast_replayed;     /* top-k <= 64 rows replayed in the reference's order */
+    uint64_t rows_general;           /* whole-row rows (top-k off / larger K / candidate overflow), parallel */
+    uint64_t rows_general_replayed;  /* whole-row rows replayed in the reference's order */
+    uint64_t rows_large;             /* rows of more than 3072 active ids (always replayed) */
+    uint64_t rows_overflow;          /* top-k <= 64 rows whose candidates overflowed (counted in rows_general*) */
+    uint64_t reserved;
+} vw_stats;
+
 typedef struct vw_handle vw_handle;
 
 /* Library version string, e.g. "vwsampler 1.0 (sm_100a)". */
@@ -126,6 +140,11 @@ vw_status vw_sample(vw_handle* handle, const vw_segment* segments, int32_t n_seg
 /* Waits for work enqueued on `stream` (NULL = the handle's stream) and returns, then clears, any device-side
  * error latched by earlier calls. */
 vw_status vw_synchronize(vw_handle* handle, void* stream);
+
+/* Copies the per-path row counters into *out (after any vw_synchronize the caller needs); `reset` != 0 clears
+ * them.  Setting the environment variable VW_FORCE_EXACT=1 before vw_create makes every sampled row take the
+ * sequential replay (a test hook; results are identical, only slower). */
+vw_status vw_get_stats(vw_handle* handle, vw_stats* out, int32_t reset);
 
 /*
  * Single-row mirrors of the reference's Sampler methods, for callers that keep the reference's call shape.

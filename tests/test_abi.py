@@ -47,6 +47,7 @@ def _c_layout():
 int main(void) {
   printf("vw_options %zu\n", sizeof(vw_options));
   printf("vw_segment %zu\n", sizeof(vw_segment));
+  printf("vw_stats %zu\n", sizeof(vw_stats));
   F(vw_options, do_sample) F(vw_options, top_k) F(vw_options, top_p) F(vw_options, temperature)
   F(vw_options, repetition_penalty)
   F(vw_segment, logits) F(vw_segment, row_stride) F(vw_segment, n_rows) F(vw_segment, vocab) F(vw_segment, dtype)
@@ -70,6 +71,7 @@ def test_ctypes_structs_match_c_layout():
     lay = _c_layout()
     assert lay["vw_options"] == ctypes.sizeof(_lib.VwOptions)
     assert lay["vw_segment"] == ctypes.sizeof(_lib.VwSegment)
+    assert lay["vw_stats"] == ctypes.sizeof(_lib.VwStats)
     for cls, cname in ((_lib.VwOptions, "vw_options"), (_lib.VwSegment, "vw_segment")):
         for fname, _ in cls._fields_:
             key = "eos_id" if fname == "eos_id" else fname

@@ -36,6 +36,7 @@ EXPORTED = (
     "vw_last_error",
     "vw_sample",
     "vw_synchronize",
+    "vw_get_stats",
     "vw_apply_repetition_penalty",
     "vw_select",
     "vw_argmax",
@@ -79,6 +80,24 @@ class VwSegment(ctypes.Structure):
     ]
 
 
+class VwStats(ctypes.Structure):
+    """vw_stats: rows sampled per path."""
+
+    _fields_ = [
+        ("rows_greedy", ctypes.c_uint64),
+        ("rows_fast", ctypes.c_uint64),
+        ("rows_fast_replayed", ctypes.c_uint64),
+        ("rows_general", ctypes.c_uint64),
+        ("rows_general_replayed", ctypes.c_uint64),
+        ("rows_large", ctypes.c_uint64),
+        ("rows_overflow", ctypes.c_uint64),
+        ("reserved", ctypes.c_uint64),
+    ]
+
+    def as_dict(self) -> dict:
+        return {name: int(getattr(self, name)) for name, _ in self._fields_ if name != "reserved"}
+
+
 class VwError(RuntimeError):
     """A non-zero vw_status.  `status` holds the code."""
 
@@ -117,6 +136,8 @@ def _load() -> ctypes.CDLL:
     lib.vw_sample.argtypes = [vp, ctypes.POINTER(VwSegment), i32, ctypes.POINTER(VwOptions), i32, i32, vp]
     lib.vw_synchronize.restype = ctypes.c_int
     lib.vw_synchronize.argtypes = [vp, vp]
+    lib.vw_get_stats.restype = ctypes.c_int
+    lib.vw_get_stats.argtypes = [vp, ctypes.POINTER(VwStats), i32]
     lib.vw_apply_repetition_penalty.restype = ctypes.c_int
     lib.vw_apply_repetition_penalty.argtypes = [vp, vp, i32, vp, i64, ctypes.c_float, i32]
     lib.vw_select.restype = ctypes.c_int

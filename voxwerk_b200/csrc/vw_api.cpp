@@ -4,6 +4,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -30,6 +31,8 @@ struct vw_handle {
     vw::DevOptions* h_opts = nullptr;   // pinned upload buffer for option tables > kInlineOptions
     size_t opts_cap = 0;
     cudaEvent_t opts_done = nullptr;
+    unsigned long long* d_stats = nullptr;   // vw::kNumStats per-path row counters
+    int force_exact = 0;                     // VW_FORCE_EXACT at creation
     std::string last_error;
 };
 
@@ -353,6 +356,8 @@ vw_status sample_impl(vw_handle* h, const vw_segment* segs, int32_t n_segs, cons
     p.bitmap_words = (vmax + 31) / 32;
     p.vmax = vmax;
     p.err = h->d_err;
+    p.stats = h->d_stats;
+    p.force_exact = h->force_exact;
 
     int ctas = 0;
     size_t smem = 0;
@@ -422,6 +427,11 @@ VW_EXPORT vw_status vw_create(int32_t device, vw_handle** out) {
     if (e == cudaSuccess) e = cudaMallocHost(&h->h_err, sizeof(unsigned));
     if (e == cudaSuccess) e = cudaMemset(h->d_err, 0, sizeof(unsigned));
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->opts_done, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaMalloc(&h->d_stats, sizeof(unsigned long long) * vw::kNumStats);
+    if (e == cudaSuccess) e = cudaMemset(h->d_stats, 0, sizeof(unsigned long long) * vw::kNumStats);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    const char* fe = std::getenv("VW_FORCE_EXACT");
+    h->force_exact = (fe && fe[0] == '1') ? 1 : 0;
     if (e != cudaSuccess) {
         vw_destroy(h);
         return VW_ERR_CUDA;
@@ -440,6 +450,7 @@ VW_EXPORT vw_status vw_destroy(vw_handle* h) {
         if (h->d_opts) cudaFree(h->d_opts);
         if (h->h_opts) cudaFreeHost(h->h_opts);
         if (h->d_err) cudaFree(h->d_err);
+        if (h->d_stats) cudaFree(h->d_stats);
         if (h->h_err) cudaFreeHost(h->h_err);
         if (h->opts_done) cudaEventDestroy(h->opts_done);
         if (h->stream) cudaStreamDestroy(h->stream);
@@ -460,6 +471,19 @@ VW_EXPORT vw_status vw_synchronize(vw_handle* h, void* stream) {
     DeviceGuard guard(h->device);
     if (!guard.ok()) return fail(h, VW_ERR_CUDA, "cudaSetDevice failed");
     return read_device_error(h, stream ? static_cast<cudaStream_t>(stream) : h->stream);
+}
+
+VW_EXPORT vw_status vw_get_stats(vw_handle* h, vw_stats* out, int32_t reset) {
+    if (!h) return VW_ERR_INVALID_ARG;
+    if (!out) return fail(h, VW_ERR_INVALID_ARG, "NULL out");
+    static_assert(sizeof(vw_stats) == sizeof(unsigned long long) * vw::kNumStats, "vw_stats layout");
+    DeviceGuard guard(h->device);
+    if (!guard.ok()) return fail(h, VW_ERR_CUDA, "cudaSetDevice failed");
+    cudaError_t e = cudaMemcpy(out, h->d_stats, sizeof(vw_stats), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && reset) e = cudaMemset(h->d_stats, 0, sizeof(vw_stats));
+    if (e == cudaSuccess && reset) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(h, e, "vw_get_stats");
+    return VW_OK;
 }
 
 VW_EXPORT vw_status vw_apply_repetition_penalty(vw_handle* h, float* logits, int32_t vocab, const int32_t* history,

@@ -16,10 +16,21 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kRegElems = 24;          // elements per thread held in registers: rows of <= 3072 active ids
 constexpr int kSmallK = 64;            // top-k <= kSmallK uses the candidate path
 constexpr int kCandCap = 128;          // candidate buffer entries (one warp sorts 4 per lane)
-constexpr int kSmallSurvivors = 64;    // survivors handled by the one-warp exact chain (2 per lane)
 constexpr int kMaxStageLogitBytes = 64 * 1024;
 constexpr int kMaxHistStage = 4096;    // history ids staged per row; longer histories stream the rest
 constexpr int kStages = 3;
+
+// Counters of rows by path (vw_stats field order).
+enum : int {
+    kStatGreedy = 0,
+    kStatFast = 1,             // candidate rows decided in parallel by the chain warp
+    kStatFastReplayed = 2,     // candidate rows replayed in the reference's order
+    kStatGeneral = 3,          // whole-row rows decided in parallel
+    kStatGeneralReplayed = 4,  // whole-row rows replayed in the reference's order
+    kStatLarge = 5,            // rows of more than 3072 active ids (always replayed)
+    kStatOverflow = 6,         // candidate-eligible rows that took the whole-row path
+    kNumStats = 8,
+};
 
 // Error bits latched in the device error word.
 enum : unsigned {
@@ -69,6 +80,8 @@ struct LaunchParams {
     int32_t bitmap_words;         // vmax / 32 rounded up
     int32_t vmax;
     unsigned* err;
+    unsigned long long* stats;    // kNumStats counters (nullable)
+    int32_t force_exact;          // replay every sampled row in the reference's order (test hook)
     char* gscratch;               // large-path scratch, gscratch_stride bytes per CTA
     int64_t gscratch_stride;
 };

@@ -46,6 +46,7 @@ constexpr unsigned kFull = 0xffffffffu;
 constexpr int kMetaBytes = 128;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;   // bounded mbarrier waits: 2 s without progress
 constexpr double kU = 1.1102230246251565e-16;      // 2^-53
+constexpr double kFix = 2251799813685248.0;         // 2^51: fixed-point scale of histogram masses (e <= 1)
 constexpr int kChainWarp = kWarps;                 // warp 4
 constexpr int kProducerWarp = kWarps + 1;          // warp 5
 constexpr int kBlockThreads = (kWarps + 2) * 32;   // 192
@@ -92,7 +93,7 @@ struct SmemMisc {
     int32_t bc_i[4];
     double bc_d[4];
     uint32_t chist[256];
-    double mhist[256];
+    unsigned long long mhist[256];   // masses in units of 2^-51 (exact integer sums, any order)
     int32_t flags[kCandCap];   // chain warp scratch
 };
 
@@ -699,7 +700,7 @@ __device__ int general_parallel(const float (&x)[kRegElems], int nvec, const Row
     }
     const double total = block_sum_d(lsum, m, 0, lane, warp);
     const int nsurv = block_sum_i(lcnt, m, 1, lane, warp);
-    const double eta = (4.0 * nsurv + 128.0) * kU;
+    const double eta = (8.0 * nsurv + 128.0) * kU;   // also covers the 2^-52-per-value histogram rounding
     uint32_t removed = 0;   // bit j: element j removed by top-p
     if (o.top_p < 1.0f) {
         const double thr = static_cast<double>(__fsub_rn(1.0f, o.top_p));
@@ -730,15 +731,18 @@ __device__ int general_parallel(const float (&x)[kRegElems], int nvec, const Row
                 if (s && mp.idx(qv * VW + (j % VW)) != li) removed |= 1u << j;
             }
         } else if (__dsub_rn(before_last, T) > band) {
-            // mass radix select over ascending keys: the group x* holding the break element
+            // mass radix select over ascending keys: the group x* holding the break element.  Masses are summed
+            // as integers (round(e * 2^51)); a row of <= 3072 values stays below 2^63.
+            const unsigned long long tfx =
+                static_cast<unsigned long long>(fmin(__dmul_rn(T, kFix), 9.2e18));
             uint32_t prefix = 0, pmask = 0;
-            double below = 0.0;
+            unsigned long long below_fx = 0;
             int ng = 0;
             for (int pass = 0; pass < 4; ++pass) {
                 const int shift = 24 - 8 * pass;
                 for (int b = tid; b < 256; b += kThreads) {
                     m.chist[b] = 0;
-                    m.mhist[b] = 0.0;
+                    m.mhist[b] = 0ull;
                 }
                 cbar();
 #pragma unroll
@@ -747,27 +751,32 @@ __device__ int general_parallel(const float (&x)[kRegElems], int nvec, const Row
                         const uint32_t k = okey(x[j]);
                         if ((k & pmask) == prefix) {
                             atomicAdd(&m.chist[(k >> shift) & 255u], 1u);
-                            atomicAdd(&m.mhist[(k >> shift) & 255u], ev(j));
+                            atomicAdd(&m.mhist[(k >> shift) & 255u], __double2ull_rn(__dmul_rn(ev(j), kFix)));
                         }
                     }
                 }
                 cbar();
                 if (warp == 0) {
-                    double mb[8], loc = 0.0;
+                    unsigned long long mb[8], loc = 0;
 #pragma unroll
                     for (int b = 0; b < 8; ++b) {
                         mb[b] = m.mhist[lane * 8 + b];
-                        loc = __dadd_rn(loc, mb[b]);
+                        loc += mb[b];
                     }
-                    const double incl = warp_incl_d(loc, lane);
-                    double acc = __dadd_rn(below, __dsub_rn(incl, loc));
+                    unsigned long long incl = loc;
+#pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const unsigned long long y = __shfl_up_sync(kFull, incl, o);
+                        if (lane >= o) incl += y;
+                    }
+                    unsigned long long acc = below_fx + incl - loc;
                     int found = -1;
-                    double acc_before = 0.0;
-                    if (__dadd_rn(below, incl) > T && !(acc > T)) {
+                    unsigned long long acc_before = 0;
+                    if (below_fx + incl > tfx && acc <= tfx) {
 #pragma unroll
                         for (int b = 0; b < 8; ++b) {
-                            const double nxt = __dadd_rn(acc, mb[b]);
-                            if (found < 0 && nxt > T) {
+                            const unsigned long long nxt = acc + mb[b];
+                            if (found < 0 && nxt > tfx) {
                                 found = lane * 8 + b;
                                 acc_before = acc;
                             }
@@ -779,22 +788,23 @@ __device__ int general_parallel(const float (&x)[kRegElems], int nvec, const Row
                     if (who) {
                         const int src = __ffs(who) - 1;
                         const int d = __shfl_sync(kFull, found, src);
-                        const double ab = shfl_d(acc_before, src);
+                        const unsigned long long ab = __shfl_sync(kFull, acc_before, src);
                         if (lane == 0) {
                             m.bc_i[1] = d;
                             m.bc_i[2] = static_cast<int>(m.chist[d]);
-                            m.bc_d[0] = ab;
+                            m.red_u[3][0] = ab;
                         }
                     }
                 }
                 cbar();
-                if (!m.bc_i[0]) return -1;   // rounding put the crossing outside every bin
+                if (!m.bc_i[0]) return -1;   // the crossing lies outside every bin (T at the very top)
                 prefix |= static_cast<uint32_t>(m.bc_i[1]) << shift;
                 pmask |= 255u << shift;
-                below = m.bc_d[0];
+                below_fx = m.red_u[3][0];
                 ng = m.bc_i[2];
                 cbar();
             }
+            const double below = __dmul_rn(static_cast<double>(below_fx), 1.0 / kFix);
             const float xs = okey_inv(prefix);
             const double es = softmax_num(xs, mx);
             const double q = __ddiv_rn(__dsub_rn(T, below), es);
@@ -1218,7 +1228,7 @@ __device__ int chain_exact(const ChainSlot& sl, double* out_probs, int* flags, i
 template <int VW>
 __device__ __forceinline__ void process_vectors(const unsigned char* sl, int nvec, const RowMap& mp,
                                                 const RowCtx& c, int tid, float (&x)[kRegElems],
-                                                float& tmax, float& bestv, int& besti) {
+                                                float& tmax, float& tmax2, float& bestv, int& besti) {
     constexpr int G = kRegElems / VW;
 #pragma unroll
     for (int g = 0; g < G; ++g) {
@@ -1232,7 +1242,12 @@ __device__ __forceinline__ void process_vectors(const unsigned char* sl, int nve
             for (int e = 0; e < VW; ++e) {
                 const float t = transform(v[e], i0 + e, bits, c);
                 x[g * VW + e] = t;
-                tmax = fmaxf(tmax, t);
+                if (t > tmax) {
+                    tmax2 = tmax;
+                    tmax = t;
+                } else if (t > tmax2) {
+                    tmax2 = t;
+                }
                 if (t > bestv) {
                     bestv = t;
                     besti = i0 + e;
@@ -1430,18 +1445,24 @@ __global__ void __launch_bounds__(kBlockThreads, 4) sampler_kernel(const __grid_
 
     if (warp == kChainWarp) {
         // ================= chain warp: candidate rows handed over by the element warps =================
+        uint32_t st_fast = 0, st_exact = 0;
         for (uint32_t n = 0;; ++n) {
             const int s = n & 1;
             if (!mbar_wait_bounded(&slot_full[s], (n >> 1) & 1u, &misc.progress)) {
                 if (lane == 0) atomicOr(p.err, kErrTimeout);
-                return;
+                break;
             }
             ChainSlot& cs = slots[s];
-            if (cs.cmd == 1) return;
+            if (cs.cmd == 1) break;
             const DevSegment& g = p.seg[cs.seg];
             double* probs = g.out_probs ? g.out_probs + static_cast<int64_t>(cs.local) * cs.V : nullptr;
-            int res = chain_parallel(cs, probs, lane);
-            if (res < 0) res = chain_exact(cs, probs, misc.flags, lane);
+            int res = p.force_exact ? -1 : chain_parallel(cs, probs, lane);
+            if (res < 0) {
+                res = chain_exact(cs, probs, misc.flags, lane);
+                ++st_exact;
+            } else {
+                ++st_fast;
+            }
             __syncwarp();
             if (lane == 0) {
                 g.out_ids[cs.local] = res;
@@ -1450,10 +1471,16 @@ __global__ void __launch_bounds__(kBlockThreads, 4) sampler_kernel(const __grid_
             }
             __syncwarp();
         }
+        if (lane == 0 && p.stats) {
+            if (st_fast) atomicAdd(&p.stats[kStatFast], static_cast<unsigned long long>(st_fast));
+            if (st_exact) atomicAdd(&p.stats[kStatFastReplayed], static_cast<unsigned long long>(st_exact));
+        }
+        return;
     }
 
     // ================= element warps =================
     uint32_t h = 0;   // rows handed to the chain warp
+    uint32_t st_greedy = 0, st_general = 0, st_general_exact = 0, st_large = 0, st_overflow = 0;
     for (int k = 0; k < n_my; ++k) {
         const int s = k % S_;
         unsigned char* st = stages + static_cast<size_t>(s) * stage_bytes;
@@ -1599,18 +1626,19 @@ __global__ void __launch_bounds__(kBlockThreads, 4) sampler_kernel(const __grid_
                 g.out_ids[m.local] = res;
                 ++misc.progress;
             }
+            ++st_large;
             cbar();
             continue;
         }
 
         float x[kRegElems];
-        float tmax = neg_inf();
+        float tmax = neg_inf(), tmax2 = neg_inf();   // the two largest values of this thread
         float bestv = neg_inf();
         int besti = 0x7fffffff;
         if (dtype == 0)
-            process_vectors<4>(sl, nvec, mp, c, tid, x, tmax, bestv, besti);
+            process_vectors<4>(sl, nvec, mp, c, tid, x, tmax, tmax2, bestv, besti);
         else
-            process_vectors<8>(sl, nvec, mp, c, tid, x, tmax, bestv, besti);
+            process_vectors<8>(sl, nvec, mp, c, tid, x, tmax, tmax2, bestv, besti);
         cbar();   // the stage has been read
         if (m.pen_on)
             for (int i = tid; i < p.bitmap_words; i += kThreads) bitmap[i] = 0u;
@@ -1629,6 +1657,7 @@ __global__ void __launch_bounds__(kBlockThreads, 4) sampler_kernel(const __grid_
                 g.out_ids[m.local] = res;
                 ++misc.progress;
             }
+            ++st_greedy;
             continue;
         }
 
@@ -1636,10 +1665,11 @@ __global__ void __launch_bounds__(kBlockThreads, 4) sampler_kernel(const __grid_
         bool handed = false;
         if (K > 0 && K < V && K <= kSmallK) {
             release();   // the candidate path no longer reads the stage
-            // tau_w = ceil(K/4)-th largest lane maximum of this warp
+            // tau_w = ceil(K/4)-th largest of the warp's 64 per-thread top-2 values: >= ceil(K/4) distinct
+            // elements of this warp are >= tau_w, so >= K elements of the row are >= min over warps
             const int cw = (K + kWarps - 1) / kWarps;
-            uint64_t lk[1] = {static_cast<uint64_t>(~okey(tmax))};
-            warp_sort<1>(lk, lane);
+            uint64_t lk[2] = {static_cast<uint64_t>(~okey(tmax)), static_cast<uint64_t>(~okey(tmax2))};
+            warp_sort<2>(lk, lane);
             const float tw = okey_inv(~static_cast<uint32_t>(__shfl_sync(kFull, lk[0], cw - 1)));
             if (lane == 0) misc.tau_w[warp] = tw;
             cbar();
@@ -1703,6 +1733,7 @@ __global__ void __launch_bounds__(kBlockThreads, 4) sampler_kernel(const __grid_
                     if (tid == 0) cs.count = 0;
                 }
             }
+            if (!handed) ++st_overflow;
         }
         if (!handed) {
             const float mx = block_max_f(tmax, misc, 0, lane, warp);
@@ -1711,11 +1742,15 @@ __global__ void __launch_bounds__(kBlockThreads, 4) sampler_kernel(const __grid_
             double* ecache = (!released && (stage_bytes - kMetaBytes) >= used * kThreads * 8)
                                  ? reinterpret_cast<double*>(sl) : nullptr;
             if (!ecache) release();
-            int res = dtype == 0 ? general_parallel<4>(x, nvec, mp, V, o, m.uniform, mx, out_probs, ecache, misc, tid, lane, warp)
+            int res = -1;
+            if (!p.force_exact)
+                res = dtype == 0 ? general_parallel<4>(x, nvec, mp, V, o, m.uniform, mx, out_probs, ecache, misc, tid, lane, warp)
                                  : general_parallel<8>(x, nvec, mp, V, o, m.uniform, mx, out_probs, ecache, misc, tid, lane, warp);
             cbar();
             release();
+            if (res >= 0) ++st_general;
             if (res < 0) {
+                ++st_general_exact;
                 for (int i = tid; i < V; i += kThreads) gx[i] = neg_inf();
                 cbar();
                 const int G = kRegElems / VWe;
@@ -1734,6 +1769,12 @@ __global__ void __launch_bounds__(kBlockThreads, 4) sampler_kernel(const __grid_
             if (tid == 0) g.out_ids[m.local] = res;
         }
         if (tid == 0) ++misc.progress;
+    }
+    if (tid == 0 && p.stats) {
+        const uint32_t v[5] = {st_greedy, st_general, st_general_exact, st_large, st_overflow};
+        const int idx[5] = {kStatGreedy, kStatGeneral, kStatGeneralReplayed, kStatLarge, kStatOverflow};
+        for (int i = 0; i < 5; ++i)
+            if (v[i]) atomicAdd(&p.stats[idx[i]], static_cast<unsigned long long>(v[i]));
     }
     // no more rows for the chain warp
     {

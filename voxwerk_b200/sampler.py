@@ -166,6 +166,12 @@ class Device:
         except Exception:
             pass
 
+    def stats(self, reset: bool = False) -> dict:
+        """vw_get_stats: rows sampled per path (call after synchronizing the work of interest)."""
+        st = _lib.VwStats()
+        check(lib.vw_get_stats(self.handle, ctypes.byref(st), 1 if reset else 0), self.handle)
+        return st.as_dict()
+
     def synchronize(self, stream: Optional[int] = None) -> None:
         """vw_synchronize: waits for `stream` and raises any device-side error latched by earlier calls."""
         check(lib.vw_synchronize(self.handle, ctypes.c_void_p(stream) if stream else None), self.handle)
