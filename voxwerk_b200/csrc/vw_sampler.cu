@@ -1,13 +1,10 @@
 // vw_sampler.cu -- fused token-sampling kernel for sm_100a (B200).
 //
-// Persistent CTAs of six warps, specialised by role:
-//   * producer warp: plans each of the CTA's rows (CTA b takes rows b, b + grid, ...) and streams its logits and
-//     history into a shared-memory ring with cp.async.bulk (TMA bulk copies) completing on mbarriers, so HBM reads
-//     run ahead of the work.  The suppressed span of talker rows is never read.
-//   * four element warps (one warp-group per row): repetition penalty, suppress mask, temperature, greedy argmax,
-//     and the top-k candidate filter; rows the chain warp cannot take are finished here (general path).
-//   * chain warp: top-k select, softmax, top-p and the inverse-CDF draw on the <= 128 candidates of a row, while
-//     the element warps already work on the next row.
+// Persistent CTAs of five warps:
+//   * a producer warp plans each of the CTA's rows (CTA b takes rows b, b + grid, ...) and streams their logits
+//     and histories into a shared-memory ring with cp.async.bulk (TMA bulk copies) completing on mbarriers, so
+//     HBM reads run ahead of the work.  The suppressed span of talker rows is never read.
+//   * four element warps (one warp-group per row) do the rest of the row.
 //
 // Per row, in the order of the reference (src/Voxwerk/Talker/Sampler.cs, TalkerGenerator.cs):
 //   1. repetition penalty (talker rows; Sampler.cs:25-33): history ids -> a V-bit shared bitmap (Distinct());
@@ -19,17 +16,17 @@
 //   3. greedy rows: first index of the maximum (Sampler.cs:90-95).
 //   4. temperature: x * fp32(1/T) (Sampler.cs:39-40).
 //   5. top-k (Sampler.cs:42-49): every value >= the K-th largest survives (ties kept).  For K <= 64 the
-//      candidates are the values >= tau, tau = min over the 4 element warps of the ceil(K/4)-th largest lane
-//      maximum (>= K values are >= tau, so the K-th largest is too); the chain warp sorts them (bitonic).
-//      Otherwise a block radix select over order-preserving keys finds the K-th largest.
+//      candidates are the values >= tau, tau = min over the 4 warps of the ceil(K/4)-th largest of each warp's
+//      per-thread top-2 values (so >= K values are >= tau, and so is the K-th largest); each candidate's exact
+//      rank is counted by its own thread.  Otherwise a binned select over the row finds the K-th largest.
 //   6. softmax in fp64, top-p cut over the (prob, index)-ascending order and the inverse-CDF draw
 //      (Sampler.cs:51-88).  The reference's sums are sequential fp64 roundings.  Here they are formed in
 //      parallel; every decision they feed (which ids top-p removes, where the draw lands) is taken only when the
 //      parallel value is farther from the threshold than a proven bound on the difference between the two
-//      (eta = (4n + 128) 2^-53 of the total for n survivors, covering both exp implementations' 1-ulp error,
-//      the reference's n-term sequential roundings and this code's tree roundings).  A row with any decision
-//      inside that band is replayed with the reference's exact sequential order (exact paths below), so the
-//      ids equal the reference's in every case.
+//      (eta = (4n + 128) 2^-53 of the total for n survivors, (8n + 128) 2^-53 where fixed-point histograms are
+//      involved, covering both exp implementations' 1-ulp error, the reference's n-term sequential roundings
+//      and this code's own roundings).  A row with any decision inside that band is replayed in the
+//      reference's exact sequential order (replay paths below), so the ids equal the reference's in every case.
 //
 // Compile with -fmad=false: no multiply-add may be contracted; every rounding step is explicit (_rn
 // intrinsics) to match the reference's separately rounded fp32 / fp64 operations.
@@ -47,9 +44,8 @@ constexpr int kMetaBytes = 128;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;   // bounded mbarrier waits: 2 s without progress
 constexpr double kU = 1.1102230246251565e-16;      // 2^-53
 constexpr double kFix = 2251799813685248.0;         // 2^51: fixed-point scale of histogram masses (e <= 1)
-constexpr int kChainWarp = kWarps;                 // warp 4
-constexpr int kProducerWarp = kWarps + 1;          // warp 5
-constexpr int kBlockThreads = (kWarps + 2) * 32;   // 192
+constexpr int kProducerWarp = kWarps;              // warp 4
+constexpr int kBlockThreads = (kWarps + 1) * 32;   // 160
 
 struct RowMeta {
     double uniform;
@@ -71,14 +67,22 @@ struct Cand {
     int32_t idx;
 };
 
-// One row handed from the element warps to the chain warp.
-struct ChainSlot {
-    Cand cand[kCandCap];
-    uint32_t count;       // candidates written (atomic); the chain warp resets it
-    int32_t cmd;          // 0: a row, 1: no more rows
-    int32_t K, V, seg, local;
-    DevOptions opt;
-    double uniform;
+// Candidate-path work area.
+struct CandWork {
+    double ae[kCandCap];   // survivors' softmax numerators in ascending (value, index) order
+    float ax[kCandCap];
+    int32_t ai[kCandCap];
+    double be[kCandCap];   // kept survivors' numerators in index order
+    int32_t bi[kCandCap];
+    float kth, mx;
+    int32_t S, cut, ambiguous, res;
+    double B;
+};
+
+// Binned-search histograms: counts and the three 20-bit chunks of fixed-point masses per bin.
+struct Bins {
+    uint32_t cnt[256];
+    uint32_t m[3][256];
 };
 
 struct SmemMisc {
@@ -89,12 +93,16 @@ struct SmemMisc {
     unsigned long long red_u[4][kWarps];
     double red_v[kWarps][8];
     int32_t issued;       // rows the producer has issued (timeout drain)
-    uint32_t progress;    // rows finished by the element warps (extends the chain warp's wait bound)
+    uint32_t progress;    // rows finished by the element warps (extends the producer's wait bound)
+    uint32_t cand_count;
     int32_t bc_i[4];
+    unsigned long long bc_u[2];
     double bc_d[4];
-    uint32_t chist[256];
-    unsigned long long mhist[256];   // masses in units of 2^-51 (exact integer sums, any order)
-    int32_t flags[kCandCap];   // chain warp scratch
+    union {
+        CandWork cw;      // candidate path
+        Bins bins;        // general path
+    } u;
+    int32_t flags[kCandCap];   // candidate replay scratch
 };
 
 // ---------------------------------------------------------------- PTX helpers
@@ -159,7 +167,7 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
-// Barrier among the 128 element threads (named barrier 1; the chain and producer warps never join it).
+// Barrier among the 128 element threads (named barrier 1; the producer warp never joins it).
 __device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 __device__ __forceinline__ bool cbar_or(bool v) {
     uint32_t r;
@@ -475,17 +483,17 @@ __device__ int exact_block_path(const RowCtx& c, const DevOptions& o, double r, 
         uint32_t prefix = 0, pmask = 0;
         int need = K;
         for (int shift = 24; shift >= 0; shift -= 8) {
-            for (int b = tid; b < 256; b += kThreads) misc.chist[b] = 0;
+            for (int b = tid; b < 256; b += kThreads) misc.u.bins.cnt[b] = 0;
             cbar();
             for (int i = tid; i < V; i += kThreads) {
                 const uint32_t k = okey(gx[i]);
-                if ((k & pmask) == prefix) atomicAdd(&misc.chist[(k >> shift) & 255u], 1u);
+                if ((k & pmask) == prefix) atomicAdd(&misc.u.bins.cnt[(k >> shift) & 255u], 1u);
             }
             cbar();
             if (tid == 0) {
                 int d = 255;
                 for (; d > 0; --d) {
-                    const int h = static_cast<int>(misc.chist[d]);
+                    const int h = static_cast<int>(misc.u.bins.cnt[d]);
                     if (need <= h) break;
                     need -= h;
                 }
@@ -613,93 +621,171 @@ __device__ int exact_block_path(const RowCtx& c, const DevOptions& o, double r, 
     return res;
 }
 
+// ---------------------------------------------------------------- binned search (element threads)
+// Ascending search over the values x[j] whose bit j is set in `live`: finds the value v* at which the running
+// weight, from the smallest value up, first exceeds `target` (weights: counts, or fixed-point masses
+// round(ev(j) * 2^51) when kMass).  On return `below` is the weight of the live values < v* and `cnt` the number
+// of live values equal to v*.  Each pass bins the live values linearly over [min, max] (monotone in the value),
+// keeps the bin holding the crossing, and stops when one value is left.  Returns false (the caller replays the
+// row) when the span is not a finite positive float or eight passes do not isolate a value.
+template <bool kMass, typename EvFn>
+__device__ bool binned_search(const float (&x)[kRegElems], uint32_t live, EvFn ev, unsigned long long target,
+                              SmemMisc& m, int tid, int lane, int warp, float& vstar, unsigned long long& below,
+                              int& cnt) {
+    float lo = pos_inf(), hi = neg_inf();
+    int n = 0;
+#pragma unroll
+    for (int j = 0; j < kRegElems; ++j) {
+        if ((live >> j) & 1u) {
+            lo = fminf(lo, x[j]);
+            hi = fmaxf(hi, x[j]);
+            ++n;
+        }
+    }
+    block_max_min_f(hi, lo, m, 4, lane, warp);
+    cnt = block_sum_i(n, m, 4, lane, warp);
+    below = 0;
+    for (int pass = 0; pass < 8; ++pass) {
+        if (lo == hi) {
+            vstar = lo;
+            return true;
+        }
+        const float scale = __fdiv_rn(256.0f, __fsub_rn(hi, lo));
+        if (!(scale > 0.0f) || !(scale < pos_inf())) return false;
+        uint32_t* bw = &m.u.bins.cnt[0];
+        for (int i = tid; i < 4 * 256; i += kThreads) bw[i] = 0u;
+        cbar();
+#pragma unroll
+        for (int j = 0; j < kRegElems; ++j) {
+            if ((live >> j) & 1u) {
+                const int b = min(255, static_cast<int>(__fmul_rn(__fsub_rn(x[j], lo), scale)));
+                atomicAdd(&m.u.bins.cnt[b], 1u);
+                if (kMass) {
+                    const unsigned long long f = __double2ull_rn(__dmul_rn(ev(j), kFix));
+                    atomicAdd(&m.u.bins.m[0][b], static_cast<uint32_t>(f & 0xfffffull));
+                    atomicAdd(&m.u.bins.m[1][b], static_cast<uint32_t>((f >> 20) & 0xfffffull));
+                    atomicAdd(&m.u.bins.m[2][b], static_cast<uint32_t>(f >> 40));
+                }
+            }
+        }
+        cbar();
+        if (warp == 0) {
+            unsigned long long w8[8], loc = 0;
+#pragma unroll
+            for (int b = 0; b < 8; ++b) {
+                const int bb = lane * 8 + b;
+                w8[b] = kMass ? (static_cast<unsigned long long>(m.u.bins.m[0][bb]) +
+                                 (static_cast<unsigned long long>(m.u.bins.m[1][bb]) << 20) +
+                                 (static_cast<unsigned long long>(m.u.bins.m[2][bb]) << 40))
+                              : static_cast<unsigned long long>(m.u.bins.cnt[bb]);
+                loc += w8[b];
+            }
+            unsigned long long incl = loc;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const unsigned long long y = __shfl_up_sync(kFull, incl, o);
+                if (lane >= o) incl += y;
+            }
+            unsigned long long acc = below + incl - loc;
+            int found = -1;
+            unsigned long long acc_before = 0;
+            if (below + incl > target && acc <= target) {
+#pragma unroll
+                for (int b = 0; b < 8; ++b) {
+                    const unsigned long long nxt = acc + w8[b];
+                    if (found < 0 && nxt > target) {
+                        found = lane * 8 + b;
+                        acc_before = acc;
+                    }
+                    acc = nxt;
+                }
+            }
+            const unsigned who = __ballot_sync(kFull, found >= 0);
+            if (lane == 0) m.bc_i[0] = who ? 1 : 0;
+            if (who) {
+                const int src = __ffs(who) - 1;
+                const int d = __shfl_sync(kFull, found, src);
+                const unsigned long long ab = __shfl_sync(kFull, acc_before, src);
+                if (lane == 0) {
+                    m.bc_i[1] = d;
+                    m.bc_i[2] = static_cast<int>(m.u.bins.cnt[d]);
+                    m.bc_u[0] = ab;
+                }
+            }
+        }
+        cbar();
+        if (!m.bc_i[0]) return false;   // target at or past the total: no crossing
+        const int bstar = m.bc_i[1];
+        below = m.bc_u[0];
+        cnt = m.bc_i[2];
+        float nlo = pos_inf(), nhi = neg_inf();
+#pragma unroll
+        for (int j = 0; j < kRegElems; ++j) {
+            if ((live >> j) & 1u) {
+                const int b = min(255, static_cast<int>(__fmul_rn(__fsub_rn(x[j], lo), scale)));
+                if (b != bstar) {
+                    live &= ~(1u << j);
+                } else {
+                    nlo = fminf(nlo, x[j]);
+                    nhi = fmaxf(nhi, x[j]);
+                }
+            }
+        }
+        block_max_min_f(nhi, nlo, m, 6, lane, warp);   // also orders this pass's reads before the next zeroing
+        lo = nlo;
+        hi = nhi;
+    }
+    return false;
+}
+
 // ---------------------------------------------------------------- general path, parallel (element threads)
 // x[g * VW + e] is staged position (tid + 128 g) * VW + e, valid while (tid + 128 g) < nvec; the staged order is
-// the index order.  Returns the sampled id, or -1 when a decision lies inside the error band.
-// `ecache` (nullable, shared memory, kRegElems * 128 doubles) keeps each survivor's softmax numerator at
-// [j * 128 + tid]; without it they are recomputed.
+// the index order.  `ecache` (nullable, shared memory, kRegElems * 128 doubles) keeps each survivor's softmax
+// numerator at [j * 128 + tid]; without it they are recomputed.  Returns the sampled id, or -1 when a decision
+// lies inside the error band.
 template <int VW>
 __device__ int general_parallel(const float (&x)[kRegElems], int nvec, const RowMap& mp, int V,
                                 const DevOptions& o, double r, float mx, double* out_probs, double* ecache,
                                 SmemMisc& m, int tid, int lane, int warp) {
     constexpr int G = kRegElems / VW;
     constexpr int FB = VW == 4 ? 10 : 11;           // bits per packed count field
-    if (is_neg_inf(mx)) return -1;                  // all -inf: the exact path reproduces the NaN behaviour
-    // ---- top-k threshold
+    if (is_neg_inf(mx)) return -1;                  // all -inf: the replay reproduces the NaN behaviour
+    uint32_t fin = 0;                               // bit j: finite value
+#pragma unroll
+    for (int j = 0; j < kRegElems; ++j)
+        if (!is_neg_inf(x[j])) fin |= 1u << j;
+    // ---- top-k threshold: the K-th largest value
     float kth = neg_inf();
     const int K = o.top_k;
     if (K > 0 && K < V) {
-        int fin = 0;
-#pragma unroll
-        for (int j = 0; j < kRegElems; ++j) fin += is_neg_inf(x[j]) ? 0 : 1;
-        fin = block_sum_i(fin, m, 0, lane, warp);
-        if (K <= fin) {   // else the K-th largest is -inf and the cut keeps every finite value
-            uint32_t prefix = 0, pmask = 0;
-            int need = K;
-            for (int pass = 0; pass < 4; ++pass) {
-                const int shift = 24 - 8 * pass;
-                for (int b = tid; b < 256; b += kThreads) m.chist[b] = 0;
-                cbar();
-#pragma unroll
-                for (int j = 0; j < kRegElems; ++j) {
-                    if (!is_neg_inf(x[j])) {
-                        const uint32_t k = okey(x[j]);
-                        if ((k & pmask) == prefix) atomicAdd(&m.chist[(k >> shift) & 255u], 1u);
-                    }
-                }
-                cbar();
-                if (warp == 0) {   // the need-th largest: suffix counts from the top bin
-                    int c[8], loc = 0;
-#pragma unroll
-                    for (int b = 0; b < 8; ++b) {
-                        c[b] = static_cast<int>(m.chist[lane * 8 + b]);
-                        loc += c[b];
-                    }
-                    int suf = loc;   // sum over lanes >= lane
-#pragma unroll
-                    for (int off = 1; off < 32; off <<= 1) {
-                        const int y = __shfl_down_sync(kFull, suf, off);
-                        if (lane + off < 32) suf += y;
-                    }
-                    int above = suf - loc;   // lanes above this one
-                    if (above < need && need <= suf) {
-#pragma unroll
-                        for (int b = 7; b >= 0; --b) {
-                            if (need <= above + c[b]) {
-                                m.bc_i[0] = lane * 8 + b;
-                                m.bc_i[1] = need - above;
-                                break;
-                            }
-                            above += c[b];
-                        }
-                    }
-                }
-                cbar();
-                prefix |= static_cast<uint32_t>(m.bc_i[0]) << shift;
-                need = m.bc_i[1];
-                pmask |= 255u << shift;
-                cbar();
-            }
-            kth = okey_inv(prefix);
+        const int F = block_sum_i(__popc(fin), m, 0, lane, warp);
+        if (K <= F) {   // else the K-th largest is -inf and the cut keeps every finite value
+            unsigned long long bl;
+            int cnt;
+            auto none = [](int) { return 0.0; };
+            if (!binned_search<false>(x, fin, none, static_cast<unsigned long long>(F - K), m, tid, lane, warp, kth,
+                                      bl, cnt))
+                return -1;
         }
     }
+    uint32_t surv = 0;
+#pragma unroll
+    for (int j = 0; j < kRegElems; ++j)
+        if (((fin >> j) & 1u) && x[j] >= kth) surv |= 1u << j;
     // ---- softmax numerators of the survivors, total and count
     auto ev = [&](int j) -> double {
-        if (is_neg_inf(x[j]) || !(x[j] >= kth)) return 0.0;
+        if (!((surv >> j) & 1u)) return 0.0;
         return ecache ? ecache[j * kThreads + tid] : softmax_num(x[j], mx);
     };
     double lsum = 0.0;
-    int lcnt = 0;
 #pragma unroll
     for (int j = 0; j < kRegElems; ++j) {
-        const bool s = !is_neg_inf(x[j]) && x[j] >= kth;
-        const double ej = s ? softmax_num(x[j], mx) : 0.0;
+        const double ej = ((surv >> j) & 1u) ? softmax_num(x[j], mx) : 0.0;
         if (ecache) ecache[j * kThreads + tid] = ej;
         lsum = __dadd_rn(lsum, ej);
-        lcnt += s ? 1 : 0;
     }
     const double total = block_sum_d(lsum, m, 0, lane, warp);
-    const int nsurv = block_sum_i(lcnt, m, 1, lane, warp);
+    const int nsurv = block_sum_i(__popc(surv), m, 1, lane, warp);
     const double eta = (8.0 * nsurv + 128.0) * kU;   // also covers the 2^-52-per-value histogram rounding
     uint32_t removed = 0;   // bit j: element j removed by top-p
     if (o.top_p < 1.0f) {
@@ -715,8 +801,8 @@ __device__ int general_parallel(const float (&x)[kRegElems], int nvec, const Row
             float below = neg_inf();
 #pragma unroll
             for (int j = 0; j < kRegElems; ++j) {
-                const int qv = tid + (j / VW) * kThreads;
-                if (!is_neg_inf(x[j]) && x[j] >= kth) {
+                if ((surv >> j) & 1u) {
+                    const int qv = tid + (j / VW) * kThreads;
                     if (x[j] == mx) li = max(li, mp.idx(qv * VW + (j % VW)));
                     else below = fmaxf(below, x[j]);
                 }
@@ -727,85 +813,16 @@ __device__ int general_parallel(const float (&x)[kRegElems], int nvec, const Row
 #pragma unroll
             for (int j = 0; j < kRegElems; ++j) {
                 const int qv = tid + (j / VW) * kThreads;
-                const bool s = !is_neg_inf(x[j]) && x[j] >= kth;
-                if (s && mp.idx(qv * VW + (j % VW)) != li) removed |= 1u << j;
+                if (((surv >> j) & 1u) && mp.idx(qv * VW + (j % VW)) != li) removed |= 1u << j;
             }
         } else if (__dsub_rn(before_last, T) > band) {
-            // mass radix select over ascending keys: the group x* holding the break element.  Masses are summed
-            // as integers (round(e * 2^51)); a row of <= 3072 values stays below 2^63.
-            const unsigned long long tfx =
-                static_cast<unsigned long long>(fmin(__dmul_rn(T, kFix), 9.2e18));
-            uint32_t prefix = 0, pmask = 0;
-            unsigned long long below_fx = 0;
-            int ng = 0;
-            for (int pass = 0; pass < 4; ++pass) {
-                const int shift = 24 - 8 * pass;
-                for (int b = tid; b < 256; b += kThreads) {
-                    m.chist[b] = 0;
-                    m.mhist[b] = 0ull;
-                }
-                cbar();
-#pragma unroll
-                for (int j = 0; j < kRegElems; ++j) {
-                    if (!is_neg_inf(x[j]) && x[j] >= kth) {
-                        const uint32_t k = okey(x[j]);
-                        if ((k & pmask) == prefix) {
-                            atomicAdd(&m.chist[(k >> shift) & 255u], 1u);
-                            atomicAdd(&m.mhist[(k >> shift) & 255u], __double2ull_rn(__dmul_rn(ev(j), kFix)));
-                        }
-                    }
-                }
-                cbar();
-                if (warp == 0) {
-                    unsigned long long mb[8], loc = 0;
-#pragma unroll
-                    for (int b = 0; b < 8; ++b) {
-                        mb[b] = m.mhist[lane * 8 + b];
-                        loc += mb[b];
-                    }
-                    unsigned long long incl = loc;
-#pragma unroll
-                    for (int o = 1; o < 32; o <<= 1) {
-                        const unsigned long long y = __shfl_up_sync(kFull, incl, o);
-                        if (lane >= o) incl += y;
-                    }
-                    unsigned long long acc = below_fx + incl - loc;
-                    int found = -1;
-                    unsigned long long acc_before = 0;
-                    if (below_fx + incl > tfx && acc <= tfx) {
-#pragma unroll
-                        for (int b = 0; b < 8; ++b) {
-                            const unsigned long long nxt = acc + mb[b];
-                            if (found < 0 && nxt > tfx) {
-                                found = lane * 8 + b;
-                                acc_before = acc;
-                            }
-                            acc = nxt;
-                        }
-                    }
-                    const unsigned who = __ballot_sync(kFull, found >= 0);
-                    if (lane == 0) m.bc_i[0] = who ? 1 : 0;
-                    if (who) {
-                        const int src = __ffs(who) - 1;
-                        const int d = __shfl_sync(kFull, found, src);
-                        const unsigned long long ab = __shfl_sync(kFull, acc_before, src);
-                        if (lane == 0) {
-                            m.bc_i[1] = d;
-                            m.bc_i[2] = static_cast<int>(m.chist[d]);
-                            m.red_u[3][0] = ab;
-                        }
-                    }
-                }
-                cbar();
-                if (!m.bc_i[0]) return -1;   // the crossing lies outside every bin (T at the very top)
-                prefix |= static_cast<uint32_t>(m.bc_i[1]) << shift;
-                pmask |= 255u << shift;
-                below_fx = m.red_u[3][0];
-                ng = m.bc_i[2];
-                cbar();
-            }
+            // the group x* holding the break element, by mass from the smallest value up
+            const unsigned long long tfx = __double2ull_rn(__dmul_rn(T, kFix));
+            float xs;
+            unsigned long long below_fx;
+            int ng;
+            if (!binned_search<true>(x, surv, ev, tfx, m, tid, lane, warp, xs, below_fx, ng)) return -1;
             const double below = __dmul_rn(static_cast<double>(below_fx), 1.0 / kFix);
-            const float xs = okey_inv(prefix);
             const double es = softmax_num(xs, mx);
             const double q = __ddiv_rn(__dsub_rn(T, below), es);
             if (!(q >= 0.0) || !(q < static_cast<double>(ng))) return -1;
@@ -818,7 +835,7 @@ __device__ int general_parallel(const float (&x)[kRegElems], int nvec, const Row
             float lo_n = neg_inf(), hi_n = pos_inf();
 #pragma unroll
             for (int j = 0; j < kRegElems; ++j) {
-                if (!is_neg_inf(x[j]) && x[j] >= kth) {
+                if ((surv >> j) & 1u) {
                     if (x[j] < xs) lo_n = fmaxf(lo_n, x[j]);
                     if (x[j] > xs) hi_n = fminf(hi_n, x[j]);
                 }
@@ -834,7 +851,7 @@ __device__ int general_parallel(const float (&x)[kRegElems], int nvec, const Row
 #pragma unroll
                 for (int t = 0; t < VW; ++t) {
                     const int j = g * VW + t;
-                    cg += (!is_neg_inf(x[j]) && x[j] >= kth && x[j] == xs) ? 1u : 0u;
+                    cg += (((surv >> j) & 1u) && x[j] == xs) ? 1u : 0u;
                 }
                 packed |= static_cast<unsigned long long>(cg) << (FB * g);
             }
@@ -848,9 +865,10 @@ __device__ int general_parallel(const float (&x)[kRegElems], int nvec, const Row
 #pragma unroll
                 for (int t = 0; t < VW; ++t) {
                     const int j = g * VW + t;
-                    const bool s = !is_neg_inf(x[j]) && x[j] >= kth;
-                    if (s && (x[j] < xs || (x[j] == xs && rk < static_cast<unsigned>(jrem)))) removed |= 1u << j;
-                    if (s && x[j] == xs) ++rk;
+                    if ((surv >> j) & 1u) {
+                        if (x[j] < xs || (x[j] == xs && rk < static_cast<unsigned>(jrem))) removed |= 1u << j;
+                        if (x[j] == xs) ++rk;
+                    }
                 }
                 base_g += static_cast<unsigned>((ptot >> (FB * g)) & fmask);
             }
@@ -860,7 +878,6 @@ __device__ int general_parallel(const float (&x)[kRegElems], int nvec, const Row
     }
     // ---- inverse-CDF draw over the kept ids in index order
     double c[G];
-    double lk = 0.0;
 #pragma unroll
     for (int g = 0; g < G; ++g) {
         c[g] = 0.0;
@@ -869,7 +886,6 @@ __device__ int general_parallel(const float (&x)[kRegElems], int nvec, const Row
             const int j = g * VW + t;
             if (!((removed >> j) & 1u)) c[g] = __dadd_rn(c[g], ev(j));
         }
-        lk = __dadd_rn(lk, c[g]);
     }
     // per-vector exclusive prefix across threads, and the per-vector totals
     double ex[G], tot[G];
@@ -939,184 +955,226 @@ __device__ int general_parallel(const float (&x)[kRegElems], int nvec, const Row
     return hit;
 }
 
-// ---------------------------------------------------------------- chain warp: parallel path
-// Candidates cand[0, C) (C <= 128, every survivor among them).  Returns the id, or -1 when a decision is inside
-// the error band.
-__device__ int chain_parallel(const ChainSlot& sl, double* out_probs, int lane) {
-    const int C = static_cast<int>(sl.count);
-    const int K = sl.K;
-    // ascending (value, index); padding (key 0) sorts first, so real entries sit at positions [128 - C, 128)
-    uint64_t key[4];
-#pragma unroll
-    for (int s = 0; s < 4; ++s) {
-        const int e = s * 32 + lane;
-        key[s] = e < C ? ((static_cast<uint64_t>(okey(sl.cand[e].x)) << 32) | static_cast<uint32_t>(sl.cand[e].idx))
-                       : 0ull;
+
+// ---------------------------------------------------------------- candidate path (top-k <= 64)
+// cand[0, C) (C <= 128) holds every value >= tau, so every survivor.  All 128 element threads: candidate t is
+// owned by thread t, which counts the candidates ahead of it for its exact rank.  Returns the id, or -1 when a
+// decision lies inside the error band (the caller replays the row).
+__device__ int cand_parallel(const Cand* cand, int C, int K, const DevOptions& o, double r, double* out_probs,
+                             int V, CandWork& w, int tid, int lane, int warp) {
+    const bool mine = tid < C;
+    float xt = 0.0f;
+    int it = 0, gt = 0, eq = 0, eqlt = 0;
+    if (mine) {
+        const Cand me = cand[tid];
+        xt = me.x;
+        it = me.idx;
+#pragma unroll 4
+        for (int j = 0; j < C; ++j) {
+            const Cand cj = cand[j];
+            gt += cj.x > xt ? 1 : 0;
+            const bool e = cj.x == xt;
+            eq += e ? 1 : 0;
+            eqlt += (e && cj.idx < it) ? 1 : 0;
+        }
+        const int rank = gt + eqlt;   // position in (value descending, index ascending) order
+        if (rank == K - 1) {
+            w.kth = xt;
+            w.S = gt + eq;            // values >= the K-th largest
+        }
+        if (rank == 0) w.mx = xt;
     }
-    warp_sort<4>(key, lane);
-    const int kp = kCandCap - K;   // position of the K-th largest
-    uint64_t kk = 0;
-#pragma unroll
-    for (int s = 0; s < 4; ++s) {
-        const uint64_t v = shfl_u64(key[s], kp & 31);
-        if (s == (kp >> 5)) kk = v;
+    if (out_probs)
+        for (int i = tid; i < V; i += kThreads) out_probs[i] = 0.0;
+    cbar();
+    const float kth = w.kth, mx = w.mx;
+    const int S = w.S;
+    const bool surv = mine && xt >= kth;
+    int pos = 0;
+    double et = 0.0;
+    if (surv) {
+        pos = (S - gt - eq) + eqlt;   // position in (value ascending, index ascending) order
+        et = softmax_num(xt, mx);
+        w.ae[pos] = et;
+        w.ax[pos] = xt;
+        w.ai[pos] = it;
     }
-    const uint32_t kth_key = static_cast<uint32_t>(kk >> 32);
-    const float mx = okey_inv(static_cast<uint32_t>(shfl_u64(key[3], 31) >> 32));
-    bool surv[4];
-    float xv[4];
-    double e[4];
-    int S = 0;
-#pragma unroll
-    for (int s = 0; s < 4; ++s) {
-        surv[s] = key[s] != 0ull && static_cast<uint32_t>(key[s] >> 32) >= kth_key;
-        xv[s] = okey_inv(static_cast<uint32_t>(key[s] >> 32));
-        e[s] = surv[s] ? softmax_num(xv[s], mx) : 0.0;
-        S += __popc(__ballot_sync(kFull, surv[s]));
-    }
-    const double total = warp_sum_d(__dadd_rn(__dadd_rn(e[0], e[1]), __dadd_rn(e[2], e[3])));
-    const double eta = (4.0 * S + 128.0) * kU;
-    bool removed[4] = {false, false, false, false};
-    const DevOptions& o = sl.opt;
-    if (o.top_p < 1.0f) {
-        const double thr = static_cast<double>(__fsub_rn(1.0f, o.top_p));
-        const double T = __dmul_rn(thr, total);
-        const double band = __dmul_rn(eta, total);
-        // prefix sums in ascending order (positions slot-major)
-        double incl[4], excl[4], base = 0.0;
+    cbar();
+    if (warp == 0) {
+        // ---- top-p cut over the ascending order (Sampler.cs:62-72)
+        double e[4];
+        float xv[4];
+        bool sv[4];
 #pragma unroll
         for (int s = 0; s < 4; ++s) {
-            const double in = warp_incl_d(e[s], lane);
-            excl[s] = __dadd_rn(base, warp_excl_from_incl_d(in, lane));
-            incl[s] = __dadd_rn(base, in);
+            const int p = s * 32 + lane;
+            sv[s] = p < S;
+            e[s] = sv[s] ? w.ae[p] : 0.0;
+            xv[s] = sv[s] ? w.ax[p] : 0.0f;
+        }
+        const double total = warp_sum_d(__dadd_rn(__dadd_rn(e[0], e[1]), __dadd_rn(e[2], e[3])));
+        const double eta = (4.0 * S + 128.0) * kU;
+        int pb = 0;   // survivors at ascending positions < pb are removed
+        bool amb = false;
+        if (o.top_p < 1.0f) {
+            const double thr = static_cast<double>(__fsub_rn(1.0f, o.top_p));
+            const double T = __dmul_rn(thr, total);
+            const double band = __dmul_rn(eta, total);
+            double incl[4], excl[4], base = 0.0;
+#pragma unroll
+            for (int s = 0; s < 4; ++s) {
+                const double in = warp_incl_d(e[s], lane);
+                excl[s] = __dadd_rn(base, warp_excl_from_incl_d(in, lane));
+                incl[s] = __dadd_rn(base, in);
+                base = __dadd_rn(base, shfl_d(in, 31));
+            }
+            // the break element: the first position <= S - 2 (the last is never removed) whose cum exceeds T
+            unsigned bm[4];
+            int nb = 0;
+#pragma unroll
+            for (int s = 0; s < 4; ++s) {
+                const int p = s * 32 + lane;
+                bm[s] = __ballot_sync(kFull, sv[s] && p <= S - 2 && incl[s] > T && !(excl[s] > T));
+                nb += __popc(bm[s]);
+            }
+            if (nb == 1) {
+                int bs = 0;
+#pragma unroll
+                for (int s = 0; s < 4; ++s)
+                    if (bm[s]) bs = s;
+                const int bl = __ffs(bm[bs]) - 1;
+                pb = bs * 32 + bl;
+                double bi = 0.0, be = 0.0;
+                float bx = 0.0f;
+#pragma unroll
+                for (int s = 0; s < 4; ++s) {
+                    const double a = shfl_d(incl[s], bl), b = shfl_d(excl[s], bl);
+                    const float xx = __shfl_sync(kFull, xv[s], bl);
+                    if (s == bs) {
+                        bi = a;
+                        be = b;
+                        bx = xx;
+                    }
+                }
+                if (!(__dsub_rn(bi, T) > band)) amb = true;
+                if (be > 0.0 && !(__dsub_rn(T, be) > band)) amb = true;
+                // the groups next to the break value must be strictly apart in probability
+                float lo_n = neg_inf(), hi_n = pos_inf();
+                bool cut_inside = false;
+#pragma unroll
+                for (int s = 0; s < 4; ++s) {
+                    const int p = s * 32 + lane;
+                    if (sv[s]) {
+                        if (xv[s] < bx) lo_n = fmaxf(lo_n, xv[s]);
+                        if (xv[s] > bx) hi_n = fminf(hi_n, xv[s]);
+                        if (xv[s] == bx && p < pb) cut_inside = true;
+                    }
+                }
+                lo_n = warp_max_f(lo_n);
+                hi_n = warp_min_f(hi_n);
+                cut_inside = __any_sync(kFull, cut_inside);
+                const double eb = softmax_num(bx, mx);
+                if (!is_neg_inf(lo_n) && !(softmax_num(lo_n, mx) < eb * (1.0 - 32.0 * kU))) amb = true;
+                if (cut_inside && hi_n != pos_inf() && !(softmax_num(hi_n, mx) > eb * (1.0 + 32.0 * kU))) amb = true;
+            } else if (nb == 0) {
+                // no crossing before the last survivor: all but the last go, if certainly below T
+                pb = S - 1;
+                if (S > 1) {
+                    const int q = S - 2;
+                    double at = 0.0;
+#pragma unroll
+                    for (int s = 0; s < 4; ++s) {
+                        const double a = shfl_d(incl[s], q & 31);
+                        if (s == (q >> 5)) at = a;
+                    }
+                    if (!(__dsub_rn(T, at) > band)) amb = true;
+                    float lo_n = neg_inf();
+#pragma unroll
+                    for (int s = 0; s < 4; ++s)
+                        if (sv[s] && xv[s] < mx) lo_n = fmaxf(lo_n, xv[s]);
+                    lo_n = warp_max_f(lo_n);
+                    if (!is_neg_inf(lo_n) && !(softmax_num(lo_n, mx) < 1.0 - 32.0 * kU)) amb = true;
+                }
+            } else {
+                amb = true;
+            }
+        }
+        if (lane == 0) {
+            w.cut = pb;
+            w.ambiguous = amb ? 1 : 0;
+        }
+    }
+    cbar();
+    if (w.ambiguous) return -1;
+    const int cut = w.cut;
+    const bool kept = surv && pos >= cut;
+    if (kept) {   // index-order position among the kept survivors
+        int pidx = 0;
+        for (int j = cut; j < S; ++j) pidx += w.ai[j] < it ? 1 : 0;
+        w.be[pidx] = et;
+        w.bi[pidx] = it;
+    }
+    cbar();
+    if (warp == 0) {
+        // ---- inverse-CDF draw over the kept ids in index order (Sampler.cs:73-87)
+        const int nk = S - cut;
+        double e2[4];
+        double b4 = 0.0;
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+            const int p = s * 32 + lane;
+            e2[s] = p < nk ? w.be[p] : 0.0;
+            b4 = __dadd_rn(b4, e2[s]);
+        }
+        const double B = warp_sum_d(b4);
+        const double eta = (4.0 * S + 128.0) * kU;
+        const double rB = __dmul_rn(r, B);
+        const double bandB = __dmul_rn(eta, B);
+        double base = 0.0;
+        int hits = 0, hit = -1;
+        bool unsure = false;
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+            const double in = warp_incl_d(e2[s], lane);
+            const double inc = __dadd_rn(base, in);
+            const double exc = __dadd_rn(base, warp_excl_from_incl_d(in, lane));
+            const bool h = e2[s] > 0.0 && inc > rB && !(exc > rB);
+            if (h) {
+                hit = w.bi[s * 32 + lane];
+                if (!(__dsub_rn(inc, rB) > bandB)) unsure = true;
+                if (exc > 0.0 && !(__dsub_rn(rB, exc) > bandB)) unsure = true;
+            }
+            hits += __popc(__ballot_sync(kFull, h));
             base = __dadd_rn(base, shfl_d(in, 31));
         }
-        // the break element: a survivor at position <= 126 (the last one is never removed) crossing T
-        unsigned bm[4];
-        int nb = 0;
-#pragma unroll
-        for (int s = 0; s < 4; ++s) {
-            const int pos = s * 32 + lane;
-            bm[s] = __ballot_sync(kFull, surv[s] && pos <= kCandCap - 2 && incl[s] > T && !(excl[s] > T));
-            nb += __popc(bm[s]);
+        const bool bad = hits != 1 || __any_sync(kFull, unsure);
+        hit = warp_max_i(hit);
+        if (lane == 0) {
+            w.res = bad ? -1 : hit;
+            w.B = B;
         }
-        int pb;   // survivors at positions < pb are removed
-        if (nb == 1) {
-            int bs = 0;
-#pragma unroll
-            for (int s = 0; s < 4; ++s)
-                if (bm[s]) bs = s;
-            const int bl = __ffs(bm[bs]) - 1;
-            pb = bs * 32 + bl;
-            double bi = 0.0, be = 0.0;
-            float bx = 0.0f;
-#pragma unroll
-            for (int s = 0; s < 4; ++s) {
-                const double a = shfl_d(incl[s], bl), b = shfl_d(excl[s], bl);
-                const float xx = __shfl_sync(kFull, xv[s], bl);
-                if (s == bs) {
-                    bi = a;
-                    be = b;
-                    bx = xx;
-                }
-            }
-            if (!(__dsub_rn(bi, T) > band)) return -1;
-            if (be > 0.0 && !(__dsub_rn(T, be) > band)) return -1;
-            // groups next to the break value must be strictly apart in probability
-            float lo_n = neg_inf(), hi_n = pos_inf();
-            bool cut_inside = false;
-#pragma unroll
-            for (int s = 0; s < 4; ++s) {
-                const int pos = s * 32 + lane;
-                if (surv[s]) {
-                    if (xv[s] < bx) lo_n = fmaxf(lo_n, xv[s]);
-                    if (xv[s] > bx) hi_n = fminf(hi_n, xv[s]);
-                    if (xv[s] == bx && pos < pb) cut_inside = true;
-                }
-            }
-            lo_n = warp_max_f(lo_n);
-            hi_n = warp_min_f(hi_n);
-            cut_inside = __any_sync(kFull, cut_inside);
-            const double eb = softmax_num(bx, mx);
-            if (!is_neg_inf(lo_n) && !(softmax_num(lo_n, mx) < eb * (1.0 - 32.0 * kU))) return -1;
-            if (cut_inside && hi_n != pos_inf() && !(softmax_num(hi_n, mx) > eb * (1.0 + 32.0 * kU))) return -1;
-        } else if (nb == 0) {
-            // no crossing before the last survivor: all but the last go, if certainly below T
-            const double at126 = shfl_d(incl[3], 30);
-            if (S > 1 && !(__dsub_rn(T, at126) > band)) return -1;
-            pb = kCandCap - 1;
-            float lo_n = neg_inf();
-#pragma unroll
-            for (int s = 0; s < 4; ++s)
-                if (surv[s] && xv[s] < mx) lo_n = fmaxf(lo_n, xv[s]);
-            lo_n = warp_max_f(lo_n);
-            if (!is_neg_inf(lo_n) && !(softmax_num(lo_n, mx) < 1.0 - 32.0 * kU)) return -1;
-        } else {
-            return -1;
-        }
-#pragma unroll
-        for (int s = 0; s < 4; ++s) removed[s] = surv[s] && (s * 32 + lane) < pb;
     }
-    // ---- kept ids in index order, then the draw
-    uint64_t k2[4];
-#pragma unroll
-    for (int s = 0; s < 4; ++s)
-        k2[s] = (surv[s] && !removed[s]) ? ((static_cast<uint64_t>(static_cast<uint32_t>(key[s])) << 32) |
-                                            static_cast<uint32_t>(key[s] >> 32))
-                                         : ~0ull;
-    warp_sort<4>(k2, lane);
-    double e2[4];
-    double b4 = 0.0;
-#pragma unroll
-    for (int s = 0; s < 4; ++s) {
-        e2[s] = k2[s] != ~0ull ? softmax_num(okey_inv(static_cast<uint32_t>(k2[s])), mx) : 0.0;
-        b4 = __dadd_rn(b4, e2[s]);
+    cbar();
+    const int res = w.res;
+    if (res >= 0 && out_probs) {
+        if (kept) out_probs[it] = __ddiv_rn(et, w.B);
+        cbar();
     }
-    const double B = warp_sum_d(b4);
-    const double rB = __dmul_rn(sl.uniform, B);
-    const double bandB = __dmul_rn(eta, B);
-    double base = 0.0;
-    int hits = 0, hit = -1;
-    bool unsure = false;
-#pragma unroll
-    for (int s = 0; s < 4; ++s) {
-        const double in = warp_incl_d(e2[s], lane);
-        const double inc = __dadd_rn(base, in);
-        const double exc = __dadd_rn(base, warp_excl_from_incl_d(in, lane));
-        const bool h = e2[s] > 0.0 && inc > rB && !(exc > rB);
-        if (h) {
-            hit = static_cast<int>(k2[s] >> 32);
-            if (!(__dsub_rn(inc, rB) > bandB)) unsure = true;
-            if (exc > 0.0 && !(__dsub_rn(rB, exc) > bandB)) unsure = true;
-        }
-        hits += __popc(__ballot_sync(kFull, h));
-        base = __dadd_rn(base, shfl_d(in, 31));
-    }
-    if (hits != 1 || __any_sync(kFull, unsure)) return -1;
-    hit = warp_max_i(hit);
-    if (out_probs) {
-        for (int i = lane; i < sl.V; i += 32) out_probs[i] = 0.0;
-        __syncwarp();
-#pragma unroll
-        for (int s = 0; s < 4; ++s)
-            if (k2[s] != ~0ull) out_probs[k2[s] >> 32] = __ddiv_rn(e2[s], B);
-    }
-    return hit;
+    return res;
 }
 
-// ---------------------------------------------------------------- chain warp: exact path
-// The reference's sequential operations on the candidates (<= 128 survivors), every lane running the same chain
-// on shuffled values.
-__device__ int chain_exact(const ChainSlot& sl, double* out_probs, int* flags, int lane) {
-    const int C = static_cast<int>(sl.count);
-    const int K = sl.K;
-    const DevOptions& o = sl.opt;
+
+// ---------------------------------------------------------------- candidate replay (warp 0)
+// The reference's sequential operations on the candidates (<= 128 survivors), every lane of one warp running the
+// same chain on shuffled values.
+__device__ int replay_candidates(const Cand* cand, int C, int K, const DevOptions& o, double uniform, int V,
+                                 double* out_probs, int* flags, int lane) {
     uint64_t key[4];   // descending value, ascending index
 #pragma unroll
     for (int s = 0; s < 4; ++s) {
         const int e = s * 32 + lane;
-        key[s] = e < C ? ((static_cast<uint64_t>(~okey(sl.cand[e].x)) << 32) |
-                          static_cast<uint32_t>(sl.cand[e].idx))
+        key[s] = e < C ? ((static_cast<uint64_t>(~okey(cand[e].x)) << 32) |
+                          static_cast<uint32_t>(cand[e].idx))
                        : ~0ull;
     }
     warp_sort<4>(key, lane);
@@ -1211,11 +1269,11 @@ __device__ int chain_exact(const ChainSlot& sl, double* out_probs, int* flags, i
             if (v <= 0.0) continue;
             acc = __dadd_rn(acc, v);
             last = id;
-            if (sl.uniform < acc) res = id;
+            if (uniform < acc) res = id;
         }
     }
     if (out_probs) {
-        for (int i = lane; i < sl.V; i += 32) out_probs[i] = 0.0;
+        for (int i = lane; i < V; i += 32) out_probs[i] = 0.0;
         __syncwarp();
 #pragma unroll
         for (int s = 0; s < 4; ++s)
@@ -1287,7 +1345,7 @@ __device__ int block_argmax(float bestv, int besti, SmemMisc& m, int lane, int w
 }
 
 // ---------------------------------------------------------------- the kernel
-__global__ void __launch_bounds__(kBlockThreads, 4) sampler_kernel(const __grid_constant__ LaunchParams p) {
+__global__ void __launch_bounds__(kBlockThreads, 5) sampler_kernel(const __grid_constant__ LaunchParams p) {
     extern __shared__ __align__(128) unsigned char smem[];
     const int tid = threadIdx.x;
     const int lane = tid & 31;
@@ -1297,11 +1355,9 @@ __global__ void __launch_bounds__(kBlockThreads, 4) sampler_kernel(const __grid_
     unsigned char* stages = smem;
     uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(S_) * stage_bytes);
     uint64_t* empty_bar = full_bar + S_;
-    uint64_t* slot_full = empty_bar + S_;
-    uint64_t* slot_empty = slot_full + 2;
-    uint32_t* bitmap = reinterpret_cast<uint32_t*>(slot_empty + 2);
-    ChainSlot* slots = reinterpret_cast<ChainSlot*>(bitmap + ((p.bitmap_words + 3) & ~3));
-    SmemMisc& misc = *reinterpret_cast<SmemMisc*>(slots + 2);
+    uint32_t* bitmap = reinterpret_cast<uint32_t*>(empty_bar + S_);
+    Cand* cand = reinterpret_cast<Cand*>(bitmap + ((p.bitmap_words + 3) & ~3));
+    SmemMisc& misc = *reinterpret_cast<SmemMisc*>(cand + kCandCap);
 
     const int first = blockIdx.x;
     const int gstride = gridDim.x;
@@ -1312,15 +1368,10 @@ __global__ void __launch_bounds__(kBlockThreads, 4) sampler_kernel(const __grid_
             mbar_init(&full_bar[s], 1);
             mbar_init(&empty_bar[s], 1);
         }
-        for (int s = 0; s < 2; ++s) {
-            mbar_init(&slot_full[s], 1);
-            mbar_init(&slot_empty[s], 1);
-            slots[s].count = 0;
-            slots[s].cmd = 0;
-        }
         fence_mbar_init();
         misc.issued = 0;
         misc.progress = 0;
+        misc.cand_count = 0;
     }
     for (int i = tid; i < p.bitmap_words; i += blockDim.x) bitmap[i] = 0u;
     __syncthreads();
@@ -1443,44 +1494,9 @@ __global__ void __launch_bounds__(kBlockThreads, 4) sampler_kernel(const __grid_
         return;
     }
 
-    if (warp == kChainWarp) {
-        // ================= chain warp: candidate rows handed over by the element warps =================
-        uint32_t st_fast = 0, st_exact = 0;
-        for (uint32_t n = 0;; ++n) {
-            const int s = n & 1;
-            if (!mbar_wait_bounded(&slot_full[s], (n >> 1) & 1u, &misc.progress)) {
-                if (lane == 0) atomicOr(p.err, kErrTimeout);
-                break;
-            }
-            ChainSlot& cs = slots[s];
-            if (cs.cmd == 1) break;
-            const DevSegment& g = p.seg[cs.seg];
-            double* probs = g.out_probs ? g.out_probs + static_cast<int64_t>(cs.local) * cs.V : nullptr;
-            int res = p.force_exact ? -1 : chain_parallel(cs, probs, lane);
-            if (res < 0) {
-                res = chain_exact(cs, probs, misc.flags, lane);
-                ++st_exact;
-            } else {
-                ++st_fast;
-            }
-            __syncwarp();
-            if (lane == 0) {
-                g.out_ids[cs.local] = res;
-                cs.count = 0;
-                mbar_arrive(&slot_empty[s]);
-            }
-            __syncwarp();
-        }
-        if (lane == 0 && p.stats) {
-            if (st_fast) atomicAdd(&p.stats[kStatFast], static_cast<unsigned long long>(st_fast));
-            if (st_exact) atomicAdd(&p.stats[kStatFastReplayed], static_cast<unsigned long long>(st_exact));
-        }
-        return;
-    }
-
     // ================= element warps =================
-    uint32_t h = 0;   // rows handed to the chain warp
-    uint32_t st_greedy = 0, st_general = 0, st_general_exact = 0, st_large = 0, st_overflow = 0;
+    uint32_t st_greedy = 0, st_fast = 0, st_fast_exact = 0, st_general = 0, st_general_exact = 0, st_large = 0,
+             st_overflow = 0;
     for (int k = 0; k < n_my; ++k) {
         const int s = k % S_;
         unsigned char* st = stages + static_cast<size_t>(s) * stage_bytes;
@@ -1677,16 +1693,7 @@ __global__ void __launch_bounds__(kBlockThreads, 4) sampler_kernel(const __grid_
 #pragma unroll
             for (int w = 1; w < kWarps; ++w) tau = fminf(tau, misc.tau_w[w]);
             if (!is_neg_inf(tau)) {
-                const int sidx = h & 1;
-                const uint32_t use = h >> 1;
-                bool got = true;
-                if (use > 0) got = mbar_wait_bounded(&slot_empty[sidx], (use - 1) & 1u);
-                if (cbar_or(!got)) {
-                    if (tid == 0) atomicOr(p.err, kErrTimeout);
-                    break;
-                }
-                ChainSlot& cs = slots[sidx];
-                // ---- candidates x >= tau -> the chain slot (warp-scan positions, one atomic per warp)
+                // ---- candidates x >= tau -> shared buffer (warp-scan positions, one atomic per warp)
                 int cnt = 0;
 #pragma unroll
                 for (int e = 0; e < kRegElems; ++e) cnt += (x[e] >= tau) ? 1 : 0;
@@ -1697,7 +1704,7 @@ __global__ void __launch_bounds__(kBlockThreads, 4) sampler_kernel(const __grid_
                     if (lane >= off) incl += y;
                 }
                 uint32_t base = 0;
-                if (lane == 31) base = atomicAdd(&cs.count, static_cast<uint32_t>(incl));
+                if (lane == 31) base = atomicAdd(&misc.cand_count, static_cast<uint32_t>(incl));
                 base = __shfl_sync(kFull, base, 31);
                 int pos = static_cast<int>(base) + incl - cnt;
                 if (cnt > 0) {
@@ -1707,30 +1714,32 @@ __global__ void __launch_bounds__(kBlockThreads, 4) sampler_kernel(const __grid_
                             if (pos < kCandCap) {
                                 const int gg = e / VWe;
                                 const int qv = tid + gg * kThreads;
-                                cs.cand[pos] = Cand{x[e], mp.idx(qv * VWe + (e - gg * VWe))};
+                                cand[pos] = Cand{x[e], mp.idx(qv * VWe + (e - gg * VWe))};
                             }
                             ++pos;
                         }
                     }
                 }
                 cbar();
-                const uint32_t C = cs.count;
-                if (C <= static_cast<uint32_t>(kCandCap)) {
-                    if (tid == 0) {
-                        cs.cmd = 0;
-                        cs.K = K;
-                        cs.V = V;
-                        cs.seg = m.seg;
-                        cs.local = m.local;
-                        cs.opt = o;
-                        cs.uniform = m.uniform;
-                        mbar_arrive(&slot_full[sidx]);
+                const int C = static_cast<int>(misc.cand_count);
+                cbar();   // every thread has read the count
+                if (tid == 0) misc.cand_count = 0;
+                if (C <= kCandCap) {
+                    int res = p.force_exact ? -1 : cand_parallel(cand, C, K, o, m.uniform, out_probs, V, misc.u.cw,
+                                                                tid, lane, warp);
+                    if (res < 0) {
+                        if (warp == 0) {
+                            const int rr = replay_candidates(cand, C, K, o, m.uniform, V, out_probs, misc.flags, lane);
+                            if (lane == 0) misc.bc_i[3] = rr;
+                        }
+                        cbar();
+                        res = misc.bc_i[3];
+                        ++st_fast_exact;
+                    } else {
+                        ++st_fast;
                     }
-                    ++h;
+                    if (tid == 0) g.out_ids[m.local] = res;
                     handed = true;
-                } else {
-                    cbar();   // every thread has read the count
-                    if (tid == 0) cs.count = 0;
                 }
             }
             if (!handed) ++st_overflow;
@@ -1771,25 +1780,11 @@ __global__ void __launch_bounds__(kBlockThreads, 4) sampler_kernel(const __grid_
         if (tid == 0) ++misc.progress;
     }
     if (tid == 0 && p.stats) {
-        const uint32_t v[5] = {st_greedy, st_general, st_general_exact, st_large, st_overflow};
-        const int idx[5] = {kStatGreedy, kStatGeneral, kStatGeneralReplayed, kStatLarge, kStatOverflow};
-        for (int i = 0; i < 5; ++i)
+        const uint32_t v[7] = {st_greedy, st_fast, st_fast_exact, st_general, st_general_exact, st_large, st_overflow};
+        const int idx[7] = {kStatGreedy, kStatFast, kStatFastReplayed, kStatGeneral, kStatGeneralReplayed,
+                            kStatLarge, kStatOverflow};
+        for (int i = 0; i < 7; ++i)
             if (v[i]) atomicAdd(&p.stats[idx[i]], static_cast<unsigned long long>(v[i]));
-    }
-    // no more rows for the chain warp
-    {
-        const int sidx = h & 1;
-        const uint32_t use = h >> 1;
-        if (tid == 0) {
-            bool got = true;
-            if (use > 0) got = mbar_wait_bounded(&slot_empty[sidx], (use - 1) & 1u);
-            if (got) {
-                slots[sidx].cmd = 1;
-                mbar_arrive(&slot_full[sidx]);
-            } else {
-                atomicOr(p.err, kErrTimeout);
-            }
-        }
     }
 }
 
@@ -1823,9 +1818,9 @@ __global__ void __launch_bounds__(256) penalty_kernel(float* logits, int vocab, 
 size_t sampler_smem_bytes(const LaunchParams& p) {
     const size_t stage = kMetaBytes + static_cast<size_t>(p.stage_logit_bytes) + static_cast<size_t>(p.stage_hist_cap) * 4;
     size_t b = stage * p.n_stages;
-    b += sizeof(uint64_t) * (2 * p.n_stages + 4);
+    b += sizeof(uint64_t) * (2 * p.n_stages);
     b += sizeof(uint32_t) * ((p.bitmap_words + 3) & ~3);
-    b += sizeof(ChainSlot) * 2;
+    b += sizeof(Cand) * kCandCap;
     b += sizeof(SmemMisc);
     return b;
 }
