@@ -31,6 +31,7 @@
 // Compile with -fmad=false: no multiply-add may be contracted; every rounding step is explicit (_rn
 // intrinsics) to match the reference's separately rounded fp32 / fp64 operations.
 
+#include <algorithm>
 #include <cstdint>
 #include <cuda_runtime.h>
 
@@ -740,9 +741,9 @@ __device__ bool binned_search(const float (&x)[kRegElems], uint32_t live, EvFn e
 
 // ---------------------------------------------------------------- general path, parallel (element threads)
 // x[g * VW + e] is staged position (tid + 128 g) * VW + e, valid while (tid + 128 g) < nvec; the staged order is
-// the index order.  `ecache` (nullable, shared memory, kRegElems * 128 doubles) keeps each survivor's softmax
-// numerator at [j * 128 + tid]; without it they are recomputed.  Returns the sampled id, or -1 when a decision
-// lies inside the error band.
+// the index order.  `ecache` (shared or global memory, kRegElems * 128 doubles) keeps each value's softmax
+// numerator at [j * 128 + tid] (0 for non-survivors).  Returns the sampled id, or -1 when a decision lies inside
+// the error band.
 template <int VW>
 __device__ int general_parallel(const float (&x)[kRegElems], int nvec, const RowMap& mp, int V,
                                 const DevOptions& o, double r, float mx, double* out_probs, double* ecache,
@@ -773,15 +774,12 @@ __device__ int general_parallel(const float (&x)[kRegElems], int nvec, const Row
     for (int j = 0; j < kRegElems; ++j)
         if (((fin >> j) & 1u) && x[j] >= kth) surv |= 1u << j;
     // ---- softmax numerators of the survivors, total and count
-    auto ev = [&](int j) -> double {
-        if (!((surv >> j) & 1u)) return 0.0;
-        return ecache ? ecache[j * kThreads + tid] : softmax_num(x[j], mx);
-    };
+    auto ev = [&](int j) -> double { return ecache[j * kThreads + tid]; };   // 0 for non-survivors
     double lsum = 0.0;
 #pragma unroll
     for (int j = 0; j < kRegElems; ++j) {
         const double ej = ((surv >> j) & 1u) ? softmax_num(x[j], mx) : 0.0;
-        if (ecache) ecache[j * kThreads + tid] = ej;
+        ecache[j * kThreads + tid] = ej;
         lsum = __dadd_rn(lsum, ej);
     }
     const double total = block_sum_d(lsum, m, 0, lane, warp);
@@ -1318,6 +1316,21 @@ __device__ __forceinline__ void process_vectors(const unsigned char* sl, int nve
     }
 }
 
+// Writes the register-resident row into gx[0, V) (every index into x is a compile-time constant, so x stays in
+// registers).
+template <int VW>
+__device__ __forceinline__ void scatter_row(const float (&x)[kRegElems], int nvec, const RowMap& mp, int V,
+                                            float* gx, int tid) {
+#pragma unroll
+    for (int j = 0; j < kRegElems; ++j) {
+        const int qv = tid + (j / VW) * kThreads;
+        if (qv < nvec) {
+            const int i = mp.idx(qv * VW + (j % VW));
+            if (i < V) gx[i] = x[j];
+        }
+    }
+}
+
 // Greedy: first index of the maximum over the 128 element threads (Sampler.cs:90-95).
 __device__ int block_argmax(float bestv, int besti, SmemMisc& m, int lane, int warp) {
 #pragma unroll
@@ -1597,7 +1610,7 @@ __global__ void __launch_bounds__(kBlockThreads, 5) sampler_kernel(const __grid_
         c.bitmap = bitmap;
 
         char* gbase = p.gscratch + static_cast<int64_t>(blockIdx.x) * p.gscratch_stride;
-        const int vpad = (p.vmax + 31) & ~31;
+        const int vpad = (max(p.vmax, kRegElems * kThreads) + 31) & ~31;
         float* gx = reinterpret_cast<float*>(gbase);
         double* gp = reinterpret_cast<double*>(gbase + static_cast<int64_t>(vpad) * 4);
         uint4* gs = reinterpret_cast<uint4*>(gbase + static_cast<int64_t>(vpad) * 12);
@@ -1746,11 +1759,10 @@ __global__ void __launch_bounds__(kBlockThreads, 5) sampler_kernel(const __grid_
         }
         if (!handed) {
             const float mx = block_max_f(tmax, misc, 0, lane, warp);
-            // the consumed stage doubles as the numerator cache when it is large enough
-            const int used = ((nvec + kThreads - 1) / kThreads) * VWe;
-            double* ecache = (!released && (stage_bytes - kMetaBytes) >= used * kThreads * 8)
-                                 ? reinterpret_cast<double*>(sl) : nullptr;
-            if (!ecache) release();
+            // numerator cache: the consumed stage when it is large enough, else this CTA's global scratch
+            const bool in_stage = !released && (stage_bytes - kMetaBytes) >= kRegElems * kThreads * 8;
+            double* ecache = in_stage ? reinterpret_cast<double*>(sl) : gp;
+            if (!in_stage) release();
             int res = -1;
             if (!p.force_exact)
                 res = dtype == 0 ? general_parallel<4>(x, nvec, mp, V, o, m.uniform, mx, out_probs, ecache, misc, tid, lane, warp)
@@ -1762,16 +1774,10 @@ __global__ void __launch_bounds__(kBlockThreads, 5) sampler_kernel(const __grid_
                 ++st_general_exact;
                 for (int i = tid; i < V; i += kThreads) gx[i] = neg_inf();
                 cbar();
-                const int G = kRegElems / VWe;
-                for (int gg = 0; gg < G; ++gg) {
-                    const int qv = tid + gg * kThreads;
-                    if (qv < nvec) {
-                        for (int e = 0; e < VWe; ++e) {
-                            const int i = mp.idx(qv * VWe + e);
-                            if (i < V) gx[i] = x[gg * VWe + e];
-                        }
-                    }
-                }
+                if (dtype == 0)
+                    scatter_row<4>(x, nvec, mp, V, gx, tid);
+                else
+                    scatter_row<8>(x, nvec, mp, V, gx, tid);
                 cbar();
                 res = exact_block_path(c, o, m.uniform, mx, gx, gp, gs, sort_n, out_probs, misc, tid);
             }
@@ -1826,7 +1832,7 @@ size_t sampler_smem_bytes(const LaunchParams& p) {
 }
 
 int64_t sampler_gscratch_stride(int vmax) {
-    const int64_t vpad = (vmax + 31) & ~31;
+    const int64_t vpad = (std::max(vmax, kRegElems * kThreads) + 31) & ~31;
     int64_t sort_n = 1;
     while (sort_n < vmax) sort_n <<= 1;
     int64_t b = vpad * 4 + vpad * 8 + sort_n * 16;
