@@ -241,6 +241,38 @@ __device__ __forceinline__ void warp_sort(uint64_t (&k)[P], int lane) {
     }
 }
 
+// Bitonic sort of 32*P uint32 keys held slot-major, ascending.
+template <int P>
+__device__ __forceinline__ void warp_sort32(uint32_t (&k)[P], int lane) {
+#pragma unroll
+    for (int size = 2; size <= 32 * P; size <<= 1) {
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            if (stride >= 32) {
+                const int ds = stride >> 5;
+#pragma unroll
+                for (int s = 0; s < P; ++s) {
+                    const int t = s ^ ds;
+                    if (t > s) {
+                        const bool up = (((s * 32 + lane) & size) == 0);
+                        const uint32_t a = k[s], b = k[t];
+                        k[s] = up ? min(a, b) : max(a, b);
+                        k[t] = up ? max(a, b) : min(a, b);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int s = 0; s < P; ++s) {
+                    const uint32_t o = __shfl_xor_sync(kFull, k[s], stride);
+                    const bool lower = (lane & stride) == 0;
+                    const bool up = (((s * 32 + lane) & size) == 0);
+                    k[s] = (lower == up) ? min(k[s], o) : max(k[s], o);
+                }
+            }
+        }
+    }
+}
+
 // Same network on (key, tag) pairs ordered lexicographically; tags are unique so the order is total.
 template <int P>
 __device__ __forceinline__ void warp_sort_pair(uint64_t (&k)[P], uint32_t (&t)[P], int lane) {
@@ -422,13 +454,24 @@ struct RowMap {
         if (q < kvw) return kbase + q;
         return q - kvw + hi_al;
     }
+    // vocabulary id -> staged position, or -1 for an id inside the unstaged (suppressed) span
+    __device__ __forceinline__ int pos(int id) const {
+        if (id < lo_al) return id;
+        if (id >= kbase && id < kbase + kvw) return lo_al + (id - kbase);
+        if (id >= hi_al) return lo_al + kvw + (id - hi_al);
+        return -1;
+    }
 };
 
+// Sampler.cs:31 in fp32: s < 0 ? s * p : s / p, the quotient as fp32(fp64(s) * RN64(1/p)) (see the file header).
+__device__ __forceinline__ float penalize(float s, float pen, double pen_rcp) {
+    return s < 0.0f ? __fmul_rn(s, pen) : __double2float_rn(__dmul_rn(static_cast<double>(s), pen_rcp));
+}
+
 // penalty (Sampler.cs:31) -> mask (TalkerGenerator.cs:247-248) -> temperature (Sampler.cs:40)
+// c.pen_on is set only where the penalty is applied per element (bf16 rows; fp32 rows take it in place).
 __device__ __forceinline__ float transform(float v, int idx, uint32_t bits, const RowCtx& c) {
-    if (c.pen_on && ((bits >> (idx & 31)) & 1u)) {
-        v = v < 0.0f ? __fmul_rn(v, c.pen) : __double2float_rn(__dmul_rn(static_cast<double>(v), c.pen_rcp));
-    }
+    if (c.pen_on && ((bits >> (idx & 31)) & 1u)) v = penalize(v, c.pen, c.pen_rcp);
     if (c.kind == 0) {
         const bool masked = (idx >= c.sup_lo && idx < c.sup_hi && idx != c.eos) || (idx == c.eos && c.eos_blocked);
         if (masked) v = neg_inf();
@@ -955,51 +998,43 @@ __device__ int general_parallel(const float (&x)[kRegElems], int nvec, const Row
 
 
 // ---------------------------------------------------------------- candidate path (top-k <= 64)
-// cand[0, C) (C <= 128) holds every value >= tau, so every survivor.  All 128 element threads: candidate t is
-// owned by thread t, which counts the candidates ahead of it for its exact rank.  Returns the id, or -1 when a
-// decision lies inside the error band (the caller replays the row).
-__device__ int cand_parallel(const Cand* cand, int C, int K, const DevOptions& o, double r, double* out_probs,
-                             int V, CandWork& w, int tid, int lane, int warp) {
+// key[0, C) (C <= 128) = okey(x) << 32 | id of every value >= tau, so of every survivor; keys are unique.  All 128
+// element threads: thread t counts the keys below key t, its position in (value, index)-ascending order.  `mx` is
+// the row maximum.  Returns the id, or -1 when a decision lies inside the error band (the caller replays the row).
+__device__ int cand_parallel(const unsigned long long* key, int C, int K, const DevOptions& o, double r, float mx,
+                             double* out_probs, int V, CandWork& w, int tid, int lane, int warp) {
     const bool mine = tid < C;
-    float xt = 0.0f;
-    int it = 0, gt = 0, eq = 0, eqlt = 0;
+    int lt = 0;
+    uint32_t it = 0;
     if (mine) {
-        const Cand me = cand[tid];
-        xt = me.x;
-        it = me.idx;
+        const unsigned long long kt = key[tid];
+        const ulonglong2* k2 = reinterpret_cast<const ulonglong2*>(key);
+        const int C2 = C >> 1;
 #pragma unroll 4
-        for (int j = 0; j < C; ++j) {
-            const Cand cj = cand[j];
-            gt += cj.x > xt ? 1 : 0;
-            const bool e = cj.x == xt;
-            eq += e ? 1 : 0;
-            eqlt += (e && cj.idx < it) ? 1 : 0;
+        for (int j = 0; j < C2; ++j) {
+            const ulonglong2 v = k2[j];
+            lt += (v.x < kt ? 1 : 0) + (v.y < kt ? 1 : 0);
         }
-        const int rank = gt + eqlt;   // position in (value descending, index ascending) order
-        if (rank == K - 1) {
-            w.kth = xt;
-            w.S = gt + eq;            // values >= the K-th largest
-        }
-        if (rank == 0) w.mx = xt;
+        if (C & 1) lt += key[C - 1] < kt ? 1 : 0;
+        const float xt = okey_inv(static_cast<uint32_t>(kt >> 32));
+        it = static_cast<uint32_t>(kt);
+        w.ax[lt] = xt;
+        w.ai[lt] = static_cast<int32_t>(it);
+        w.ae[lt] = softmax_num(xt, mx);
     }
     if (out_probs)
         for (int i = tid; i < V; i += kThreads) out_probs[i] = 0.0;
     cbar();
-    const float kth = w.kth, mx = w.mx;
-    const int S = w.S;
-    const bool surv = mine && xt >= kth;
-    int pos = 0;
-    double et = 0.0;
-    if (surv) {
-        pos = (S - gt - eq) + eqlt;   // position in (value ascending, index ascending) order
-        et = softmax_num(xt, mx);
-        w.ae[pos] = et;
-        w.ax[pos] = xt;
-        w.ai[pos] = it;
-    }
-    cbar();
     if (warp == 0) {
-        // ---- top-p cut over the ascending order (Sampler.cs:62-72)
+        // survivors: the values >= the K-th largest, i.e. positions [C - S, C)
+        const float kth = w.ax[C - K];
+        int S = 0;
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+            const int p = s * 32 + lane;
+            S += __popc(__ballot_sync(kFull, p < C && w.ax[p] >= kth));
+        }
+        const int base0 = C - S;
         double e[4];
         float xv[4];
         bool sv[4];
@@ -1007,14 +1042,14 @@ __device__ int cand_parallel(const Cand* cand, int C, int K, const DevOptions& o
         for (int s = 0; s < 4; ++s) {
             const int p = s * 32 + lane;
             sv[s] = p < S;
-            e[s] = sv[s] ? w.ae[p] : 0.0;
-            xv[s] = sv[s] ? w.ax[p] : 0.0f;
+            e[s] = sv[s] ? w.ae[base0 + p] : 0.0;
+            xv[s] = sv[s] ? w.ax[base0 + p] : 0.0f;
         }
         const double total = warp_sum_d(__dadd_rn(__dadd_rn(e[0], e[1]), __dadd_rn(e[2], e[3])));
         const double eta = (4.0 * S + 128.0) * kU;
-        int pb = 0;   // survivors at ascending positions < pb are removed
+        int pb = 0;   // survivors at positions < pb (counted from the smallest) are removed
         bool amb = false;
-        if (o.top_p < 1.0f) {
+        if (o.top_p < 1.0f) {   // Sampler.cs:62-72
             const double thr = static_cast<double>(__fsub_rn(1.0f, o.top_p));
             const double T = __dmul_rn(thr, total);
             const double band = __dmul_rn(eta, total);
@@ -1098,24 +1133,25 @@ __device__ int cand_parallel(const Cand* cand, int C, int K, const DevOptions& o
             }
         }
         if (lane == 0) {
-            w.cut = pb;
+            w.cut = base0 + pb;   // candidates at positions >= cut are kept
+            w.S = S;
             w.ambiguous = amb ? 1 : 0;
         }
     }
     cbar();
     if (w.ambiguous) return -1;
     const int cut = w.cut;
-    const bool kept = surv && pos >= cut;
+    const bool kept = mine && lt >= cut;
     if (kept) {   // index-order position among the kept survivors
         int pidx = 0;
-        for (int j = cut; j < S; ++j) pidx += w.ai[j] < it ? 1 : 0;
-        w.be[pidx] = et;
-        w.bi[pidx] = it;
+        for (int j = cut; j < C; ++j) pidx += w.ai[j] < static_cast<int32_t>(it) ? 1 : 0;
+        w.be[pidx] = w.ae[lt];
+        w.bi[pidx] = static_cast<int32_t>(it);
     }
     cbar();
     if (warp == 0) {
         // ---- inverse-CDF draw over the kept ids in index order (Sampler.cs:73-87)
-        const int nk = S - cut;
+        const int nk = C - cut;
         double e2[4];
         double b4 = 0.0;
 #pragma unroll
@@ -1125,7 +1161,7 @@ __device__ int cand_parallel(const Cand* cand, int C, int K, const DevOptions& o
             b4 = __dadd_rn(b4, e2[s]);
         }
         const double B = warp_sum_d(b4);
-        const double eta = (4.0 * S + 128.0) * kU;
+        const double eta = (4.0 * w.S + 128.0) * kU;
         const double rB = __dmul_rn(r, B);
         const double bandB = __dmul_rn(eta, B);
         double base = 0.0;
@@ -1155,24 +1191,23 @@ __device__ int cand_parallel(const Cand* cand, int C, int K, const DevOptions& o
     cbar();
     const int res = w.res;
     if (res >= 0 && out_probs) {
-        if (kept) out_probs[it] = __ddiv_rn(et, w.B);
+        if (kept) out_probs[it] = __ddiv_rn(w.ae[lt], w.B);
         cbar();
     }
     return res;
 }
 
-
 // ---------------------------------------------------------------- candidate replay (warp 0)
 // The reference's sequential operations on the candidates (<= 128 survivors), every lane of one warp running the
 // same chain on shuffled values.
-__device__ int replay_candidates(const Cand* cand, int C, int K, const DevOptions& o, double uniform, int V,
-                                 double* out_probs, int* flags, int lane) {
+__device__ int replay_candidates(const unsigned long long* ck, int C, int K, const DevOptions& o, double uniform,
+                                 int V, double* out_probs, int* flags, int lane) {
     uint64_t key[4];   // descending value, ascending index
 #pragma unroll
     for (int s = 0; s < 4; ++s) {
         const int e = s * 32 + lane;
-        key[s] = e < C ? ((static_cast<uint64_t>(~okey(cand[e].x)) << 32) |
-                          static_cast<uint32_t>(cand[e].idx))
+        key[s] = e < C ? ((static_cast<uint64_t>(~static_cast<uint32_t>(ck[e] >> 32)) << 32) |
+                          static_cast<uint32_t>(ck[e]))
                        : ~0ull;
     }
     warp_sort<4>(key, lane);
@@ -1281,7 +1316,10 @@ __device__ int replay_candidates(const Cand* cand, int C, int K, const DevOption
 }
 
 // ---------------------------------------------------------------- element pass
-template <int VW>
+// One pass over the staged row: transform every element into x[] (registers).  Sampling rows track each thread's
+// two largest values (tau); greedy rows the first maximum.  Vectors that no mask boundary, EOS rule or per-element
+// penalty touches take the short path (temperature only).
+template <int VW, bool kSample>
 __device__ __forceinline__ void process_vectors(const unsigned char* sl, int nvec, const RowMap& mp,
                                                 const RowCtx& c, int tid, float (&x)[kRegElems],
                                                 float& tmax, float& tmax2, float& bestv, int& besti) {
@@ -1294,17 +1332,25 @@ __device__ __forceinline__ void process_vectors(const unsigned char* sl, int nve
             load_vec<VW>(sl, qv, v);
             const int i0 = mp.idx(qv * VW);
             const uint32_t bits = c.pen_on ? c.bitmap[i0 >> 5] : 0u;
+            const bool slow = (c.pen_on && ((bits >> (i0 & 31)) & ((1u << VW) - 1u)) != 0u) ||
+                              (c.kind == 0 && ((i0 + VW > c.sup_lo && i0 < c.sup_hi) ||
+                                               (c.eos_blocked && c.eos >= i0 && c.eos < i0 + VW)));
 #pragma unroll
             for (int e = 0; e < VW; ++e) {
-                const float t = transform(v[e], i0 + e, bits, c);
+                float t;
+                if (slow)
+                    t = transform(v[e], i0 + e, bits, c);
+                else
+                    t = kSample ? __fmul_rn(v[e], c.inv_t) : v[e];
                 x[g * VW + e] = t;
-                if (t > tmax) {
-                    tmax2 = tmax;
-                    tmax = t;
-                } else if (t > tmax2) {
-                    tmax2 = t;
-                }
-                if (t > bestv) {
+                if (kSample) {
+                    if (t > tmax) {
+                        tmax2 = tmax;
+                        tmax = t;
+                    } else if (t > tmax2) {
+                        tmax2 = t;
+                    }
+                } else if (t > bestv) {
                     bestv = t;
                     besti = i0 + e;
                 }
@@ -1369,8 +1415,8 @@ __global__ void __launch_bounds__(kBlockThreads, 5) sampler_kernel(const __grid_
     uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(S_) * stage_bytes);
     uint64_t* empty_bar = full_bar + S_;
     uint32_t* bitmap = reinterpret_cast<uint32_t*>(empty_bar + S_);
-    Cand* cand = reinterpret_cast<Cand*>(bitmap + ((p.bitmap_words + 3) & ~3));
-    SmemMisc& misc = *reinterpret_cast<SmemMisc*>(cand + kCandCap);
+    unsigned long long* ckey = reinterpret_cast<unsigned long long*>(bitmap + ((p.bitmap_words + 3) & ~3));
+    SmemMisc& misc = *reinterpret_cast<SmemMisc*>(ckey + kCandCap);
 
     const int first = blockIdx.x;
     const int gstride = gridDim.x;
@@ -1564,33 +1610,38 @@ __global__ void __launch_bounds__(kBlockThreads, 5) sampler_kernel(const __grid_
             }
         }
 
-        // ---- repetition-penalty bitmap: Distinct() over the history (Sampler.cs:28)
+        // ---- repetition penalty (Sampler.cs:25-33): Distinct() through a V-bit bitmap.  fp32 rows take the penalty
+        //      in place in the stage, applied by the thread that first sets an id's bit; bf16 rows per element.
         if (m.pen_on) {
+            if (m.direct) cbar();   // the staged copy is complete before ids update it in place
+            const bool inplace = dtype == 0;
+            const float pen = o.rep_penalty;
+            const double pen_rcp = __drcp_rn(static_cast<double>(o.rep_penalty));
+            float* sf = reinterpret_cast<float*>(sl);
             bool bad = false;
+            auto visit = [&](int id) {
+                if (static_cast<unsigned>(id) >= static_cast<unsigned>(V)) {
+                    bad = true;
+                    return;
+                }
+                const uint32_t bit = 1u << (id & 31);
+                const uint32_t old = atomicOr(&bitmap[id >> 5], bit);
+                if (inplace && !(old & bit)) {
+                    const int q = mp.pos(id);
+                    if (q >= 0) sf[q] = penalize(sf[q], pen, pen_rcp);
+                }
+            };
             const int32_t* gh = g.hist_ids + m.hist_begin;
             const int nst = m.hs_hi - m.hs_lo;
             for (int c4 = tid; c4 < nst / 4; c4 += kThreads) {
                 const int4 v = reinterpret_cast<const int4*>(sh)[c4];
-                const int ids[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    if (static_cast<unsigned>(ids[j]) >= static_cast<unsigned>(V)) {
-                        bad = true;
-                    } else {
-                        atomicOr(&bitmap[ids[j] >> 5], 1u << (ids[j] & 31));
-                    }
-                }
+                visit(v.x);
+                visit(v.y);
+                visit(v.z);
+                visit(v.w);
             }
             const int rest = m.hist_len - nst;   // ids outside the staged span: [0, hs_lo) and [hs_hi, len)
-            for (int q = tid; q < rest; q += kThreads) {
-                const int i = q < m.hs_lo ? q : q - m.hs_lo + m.hs_hi;
-                const int id = gh[i];
-                if (static_cast<unsigned>(id) >= static_cast<unsigned>(V)) {
-                    bad = true;
-                } else {
-                    atomicOr(&bitmap[id >> 5], 1u << (id & 31));
-                }
-            }
+            for (int q = tid; q < rest; q += kThreads) visit(gh[q < m.hs_lo ? q : q - m.hs_lo + m.hs_hi]);
             if (bad) atomicOr(p.err, kErrHistRange);
         }
         if (m.pen_on || m.direct) cbar();
@@ -1602,7 +1653,7 @@ __global__ void __launch_bounds__(kBlockThreads, 5) sampler_kernel(const __grid_
         c.sup_hi = g.sup_hi;
         c.eos = g.eos;
         c.eos_blocked = m.step < g.min_new;
-        c.pen_on = m.pen_on != 0;
+        c.pen_on = m.pen_on != 0 && dtype != 0;   // per element only for bf16 rows
         c.pen = o.rep_penalty;
         c.pen_rcp = __drcp_rn(static_cast<double>(o.rep_penalty));
         c.sample = o.do_sample != 0;
@@ -1664,10 +1715,17 @@ __global__ void __launch_bounds__(kBlockThreads, 5) sampler_kernel(const __grid_
         float tmax = neg_inf(), tmax2 = neg_inf();   // the two largest values of this thread
         float bestv = neg_inf();
         int besti = 0x7fffffff;
-        if (dtype == 0)
-            process_vectors<4>(sl, nvec, mp, c, tid, x, tmax, tmax2, bestv, besti);
-        else
-            process_vectors<8>(sl, nvec, mp, c, tid, x, tmax, tmax2, bestv, besti);
+        if (c.sample) {
+            if (dtype == 0)
+                process_vectors<4, true>(sl, nvec, mp, c, tid, x, tmax, tmax2, bestv, besti);
+            else
+                process_vectors<8, true>(sl, nvec, mp, c, tid, x, tmax, tmax2, bestv, besti);
+        } else {
+            if (dtype == 0)
+                process_vectors<4, false>(sl, nvec, mp, c, tid, x, tmax, tmax2, bestv, besti);
+            else
+                process_vectors<8, false>(sl, nvec, mp, c, tid, x, tmax, tmax2, bestv, besti);
+        }
         cbar();   // the stage has been read
         if (m.pen_on)
             for (int i = tid; i < p.bitmap_words; i += kThreads) bitmap[i] = 0u;
@@ -1697,16 +1755,23 @@ __global__ void __launch_bounds__(kBlockThreads, 5) sampler_kernel(const __grid_
             // tau_w = ceil(K/4)-th largest of the warp's 64 per-thread top-2 values: >= ceil(K/4) distinct
             // elements of this warp are >= tau_w, so >= K elements of the row are >= min over warps
             const int cw = (K + kWarps - 1) / kWarps;
-            uint64_t lk[2] = {static_cast<uint64_t>(~okey(tmax)), static_cast<uint64_t>(~okey(tmax2))};
-            warp_sort<2>(lk, lane);
-            const float tw = okey_inv(~static_cast<uint32_t>(__shfl_sync(kFull, lk[0], cw - 1)));
-            if (lane == 0) misc.tau_w[warp] = tw;
+            uint32_t lk[2] = {~okey(tmax), ~okey(tmax2)};
+            warp_sort32<2>(lk, lane);
+            const float tw = okey_inv(~__shfl_sync(kFull, lk[0], cw - 1));
+            const float wm = okey_inv(~__shfl_sync(kFull, lk[0], 0));   // warp maximum
+            if (lane == 0) {
+                misc.tau_w[warp] = tw;
+                misc.red_f[5][warp] = wm;
+            }
             cbar();
-            float tau = misc.tau_w[0];
+            float tau = misc.tau_w[0], mx = misc.red_f[5][0];
 #pragma unroll
-            for (int w = 1; w < kWarps; ++w) tau = fminf(tau, misc.tau_w[w]);
+            for (int w = 1; w < kWarps; ++w) {
+                tau = fminf(tau, misc.tau_w[w]);
+                mx = fmaxf(mx, misc.red_f[5][w]);
+            }
             if (!is_neg_inf(tau)) {
-                // ---- candidates x >= tau -> shared buffer (warp-scan positions, one atomic per warp)
+                // ---- candidates x >= tau -> shared keys okey(x) << 32 | id (warp-scan positions, one atomic per warp)
                 int cnt = 0;
 #pragma unroll
                 for (int e = 0; e < kRegElems; ++e) cnt += (x[e] >= tau) ? 1 : 0;
@@ -1727,7 +1792,8 @@ __global__ void __launch_bounds__(kBlockThreads, 5) sampler_kernel(const __grid_
                             if (pos < kCandCap) {
                                 const int gg = e / VWe;
                                 const int qv = tid + gg * kThreads;
-                                cand[pos] = Cand{x[e], mp.idx(qv * VWe + (e - gg * VWe))};
+                                ckey[pos] = (static_cast<unsigned long long>(okey(x[e])) << 32) |
+                                            static_cast<uint32_t>(mp.idx(qv * VWe + (e - gg * VWe)));
                             }
                             ++pos;
                         }
@@ -1738,11 +1804,11 @@ __global__ void __launch_bounds__(kBlockThreads, 5) sampler_kernel(const __grid_
                 cbar();   // every thread has read the count
                 if (tid == 0) misc.cand_count = 0;
                 if (C <= kCandCap) {
-                    int res = p.force_exact ? -1 : cand_parallel(cand, C, K, o, m.uniform, out_probs, V, misc.u.cw,
-                                                                tid, lane, warp);
+                    int res = p.force_exact ? -1 : cand_parallel(ckey, C, K, o, m.uniform, mx, out_probs, V,
+                                                                misc.u.cw, tid, lane, warp);
                     if (res < 0) {
                         if (warp == 0) {
-                            const int rr = replay_candidates(cand, C, K, o, m.uniform, V, out_probs, misc.flags, lane);
+                            const int rr = replay_candidates(ckey, C, K, o, m.uniform, V, out_probs, misc.flags, lane);
                             if (lane == 0) misc.bc_i[3] = rr;
                         }
                         cbar();
@@ -1826,7 +1892,7 @@ size_t sampler_smem_bytes(const LaunchParams& p) {
     size_t b = stage * p.n_stages;
     b += sizeof(uint64_t) * (2 * p.n_stages);
     b += sizeof(uint32_t) * ((p.bitmap_words + 3) & ~3);
-    b += sizeof(Cand) * kCandCap;
+    b += sizeof(unsigned long long) * kCandCap;
     b += sizeof(SmemMisc);
     return b;
 }
