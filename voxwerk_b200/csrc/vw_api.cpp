@@ -26,6 +26,8 @@ struct vw_handle {
     char* d_scratch = nullptr;      // general-path scratch, one slice per CTA
     size_t scratch_bytes = 0;
     char* d_stage = nullptr;        // VW_MEM_HOST: device copies of the caller's arrays
+    int32_t* d_defer = nullptr;     // two counters + the rows the candidate kernel defers
+    size_t defer_cap = 0;
     size_t stage_bytes = 0;
     vw::DevOptions* d_opts = nullptr;
     vw::DevOptions* h_opts = nullptr;   // pinned upload buffer for option tables > kInlineOptions
@@ -236,6 +238,7 @@ vw_status read_device_error(vw_handle* h, cudaStream_t st) {
     const unsigned bits = *h->h_err;
     if (bits) {
         cudaMemsetAsync(h->d_err, 0, sizeof(unsigned), st);
+        if (h->d_defer) cudaMemsetAsync(h->d_defer, 0, 2 * sizeof(int32_t), st);
         cudaStreamSynchronize(st);
     }
     if (bits & vw::kErrTimeout) return fail(h, VW_ERR_TIMEOUT, "a bounded wait in the sampler kernel gave up");
@@ -359,23 +362,40 @@ vw_status sample_impl(vw_handle* h, const vw_segment* segs, int32_t n_segs, cons
     p.stats = h->d_stats;
     p.force_exact = h->force_exact;
 
-    int ctas = 0;
+    int ctas = 0, ctas_g = 0;
     size_t smem = 0;
-    for (int stages = vw::kStages; stages >= 2 && ctas == 0; --stages) {
+    for (int stages = vw::kStages; stages >= 2 && (ctas == 0 || ctas_g == 0); --stages) {
         p.n_stages = stages;
         smem = vw::sampler_smem_bytes(p);
-        ctas = vw::sampler_ctas_per_sm(smem);
+        ctas = vw::sampler_ctas_per_sm(smem, false);
+        ctas_g = vw::sampler_ctas_per_sm(smem, true);
     }
-    if (ctas == 0) return fail(h, VW_ERR_INVALID_ARG, "rows too large for shared memory");
+    if (ctas == 0 || ctas_g == 0) return fail(h, VW_ERR_INVALID_ARG, "rows too large for shared memory");
     const int grid = static_cast<int>(std::min<int64_t>(p.total_rows, static_cast<int64_t>(h->sm_count) * ctas));
+    const int grid_g = static_cast<int>(std::min<int64_t>(p.total_rows, static_cast<int64_t>(h->sm_count) * ctas_g));
     p.gscratch_stride = vw::sampler_gscratch_stride(vmax);
-    r = grow(h, &h->d_scratch, &h->scratch_bytes, static_cast<size_t>(grid) * p.gscratch_stride, "scratch");
+    r = grow(h, &h->d_scratch, &h->scratch_bytes, static_cast<size_t>(grid_g) * p.gscratch_stride, "scratch");
     if (r != VW_OK) return r;
     p.gscratch = h->d_scratch;
+    // deferred-row list: total_rows entries plus two counters (zero between calls)
+    if (static_cast<size_t>(p.total_rows) + 2 > h->defer_cap) {
+        cudaError_t e = cudaStreamSynchronize(st);
+        if (e == cudaSuccess && h->d_defer) e = cudaFree(h->d_defer);
+        h->d_defer = nullptr;
+        h->defer_cap = 0;
+        const size_t cap = static_cast<size_t>(p.total_rows) + 2 + 4096;
+        if (e == cudaSuccess) e = cudaMalloc(&h->d_defer, cap * sizeof(int32_t));
+        if (e == cudaSuccess) e = cudaMemset(h->d_defer, 0, 2 * sizeof(int32_t));
+        if (e != cudaSuccess) return cuda_fail(h, e, "deferred-row list");
+        h->defer_cap = cap;
+    }
+    p.deferred_count = reinterpret_cast<uint32_t*>(h->d_defer);
+    p.done_count = reinterpret_cast<uint32_t*>(h->d_defer) + 1;
+    p.deferred_rows = h->d_defer + 2;
 
     cudaError_t e = cudaSuccess;
     if (sync) e = cudaMemsetAsync(h->d_err, 0, sizeof(unsigned), st);
-    if (e == cudaSuccess) e = vw::launch_sampler(p, grid, smem, st);
+    if (e == cudaSuccess) e = vw::launch_sampler(p, grid, smem, grid_g, st);
     if (e != cudaSuccess) return cuda_fail(h, e, "sampler launch");
     if (mem == VW_MEM_HOST) {
         for (int i = 0; i < n_segs && e == cudaSuccess; ++i) {
@@ -451,6 +471,7 @@ VW_EXPORT vw_status vw_destroy(vw_handle* h) {
         if (h->h_opts) cudaFreeHost(h->h_opts);
         if (h->d_err) cudaFree(h->d_err);
         if (h->d_stats) cudaFree(h->d_stats);
+        if (h->d_defer) cudaFree(h->d_defer);
         if (h->h_err) cudaFreeHost(h->h_err);
         if (h->opts_done) cudaEventDestroy(h->opts_done);
         if (h->stream) cudaStreamDestroy(h->stream);

@@ -80,6 +80,9 @@ struct LaunchParams {
     int32_t bitmap_words;         // vmax / 32 rounded up
     int32_t vmax;
     unsigned* err;
+    int32_t* deferred_rows;       // rows the candidate kernel leaves to the whole-row kernel (total_rows entries)
+    uint32_t* deferred_count;     // their number (the whole-row kernel resets it to 0 when it is done)
+    uint32_t* done_count;         // whole-row kernel CTAs finished (reset with deferred_count)
     unsigned long long* stats;    // kNumStats counters (nullable)
     int32_t force_exact;          // replay every sampled row in the reference's order (test hook)
     char* gscratch;               // large-path scratch, gscratch_stride bytes per CTA
@@ -90,9 +93,10 @@ struct LaunchParams {
 size_t sampler_smem_bytes(const LaunchParams& p);
 // Global scratch bytes per CTA for rows of up to `vmax` ids.
 int64_t sampler_gscratch_stride(int vmax);
-// Resident CTAs per SM at that shared-memory size (0 if it does not fit).
-int sampler_ctas_per_sm(size_t smem);
-cudaError_t launch_sampler(const LaunchParams& p, int grid, size_t smem, cudaStream_t stream);
+// Resident CTAs per SM at that shared-memory size (0 if it does not fit).  `general` selects the whole-row kernel.
+int sampler_ctas_per_sm(size_t smem, bool general);
+// The candidate kernel over every row, then the whole-row kernel over the rows it deferred (stream-ordered).
+cudaError_t launch_sampler(const LaunchParams& p, int grid, size_t smem, int grid_general, cudaStream_t stream);
 
 // Sampler.ApplyRepetitionPenalty on one device row, in place.
 cudaError_t launch_apply_penalty(float* logits, int vocab, const int32_t* hist, int64_t hist_len, float penalty,

@@ -59,6 +59,7 @@ struct RowMeta {
     int32_t direct;       // logits were not bulk-copied: the element warps load them
     int32_t pen_on;       // repetition penalty active
     int32_t opt_ok;       // option index valid
+    int32_t deferred;     // candidate kernel: the row goes to the whole-row kernel (nothing staged)
     DevOptions opt;
 };
 static_assert(sizeof(RowMeta) <= kMetaBytes, "RowMeta too large");
@@ -120,14 +121,17 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                  : "memory");
 }
+// Waits for the phase with `parity` to complete; the thread sleeps in the barrier for up to kSuspendNs per try
+// instead of spinning (a spinning warp would take issue slots from the working warps of its SM).
+constexpr uint32_t kSuspendNs = 1000000;   // 1 ms per try; the phase completing wakes the thread at once
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
         : "memory");
     return ok != 0;
 }
@@ -136,8 +140,8 @@ __device__ __forceinline__ uint64_t global_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
-// Waits for the phase with `parity` to complete; gives up after kWaitLimitNs without progress and returns
-// false.  `progress` (nullable) is a counter whose change restarts the clock.
+// Gives up after kWaitLimitNs without progress and returns false.  `progress` (nullable) is a counter whose
+// change restarts the clock.
 __device__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, const volatile uint32_t* progress = nullptr) {
     if (mbar_try_wait(bar, parity)) return true;
     uint64_t t0 = global_ns();
@@ -1404,7 +1408,10 @@ __device__ int block_argmax(float bestv, int besti, SmemMisc& m, int lane, int w
 }
 
 // ---------------------------------------------------------------- the kernel
-__global__ void __launch_bounds__(kBlockThreads, 5) sampler_kernel(const __grid_constant__ LaunchParams p) {
+// kGeneral == false: the candidate kernel (every row; greedy and top-k <= 64 rows finish here, the rest are
+// deferred).  kGeneral == true: the whole-row kernel over the deferred rows.
+template <bool kGeneral>
+__global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kernel(const __grid_constant__ LaunchParams p) {
     extern __shared__ __align__(128) unsigned char smem[];
     const int tid = threadIdx.x;
     const int lane = tid & 31;
@@ -1420,7 +1427,10 @@ __global__ void __launch_bounds__(kBlockThreads, 5) sampler_kernel(const __grid_
 
     const int first = blockIdx.x;
     const int gstride = gridDim.x;
-    const int n_my = first < p.total_rows ? (p.total_rows - 1 - first) / gstride + 1 : 0;
+    const int n_rows = kGeneral ? min(static_cast<int>(*reinterpret_cast<volatile uint32_t*>(p.deferred_count)),
+                                      p.total_rows)
+                                : p.total_rows;
+    const int n_my = first < n_rows ? (n_rows - 1 - first) / gstride + 1 : 0;
 
     if (tid == 0) {
         for (int s = 0; s < S_; ++s) {
@@ -1447,7 +1457,8 @@ __global__ void __launch_bounds__(kBlockThreads, 5) sampler_kernel(const __grid_
             int esize = 4;
             uint32_t bytes = 0;
             if (kj < n_my) {
-                const int r = first + kj * gstride;
+                int r = first + kj * gstride;
+                if (kGeneral) r = min(max(p.deferred_rows[r], 0), p.total_rows - 1);
                 int s = 0;
                 for (int i = 1; i < p.n_segs; ++i)
                     if (r >= p.seg[i].row_begin) s = i;
@@ -1504,8 +1515,20 @@ __global__ void __launch_bounds__(kBlockThreads, 5) sampler_kernel(const __grid_
                 }
                 row_ptr = static_cast<const unsigned char*>(sg->logits) +
                           static_cast<int64_t>(local) * sg->row_stride * esize;
-                if (!m.direct) bytes += static_cast<uint32_t>((m.lo_al + m.kvw + V - m.hi_al) * esize);
-                bytes += static_cast<uint32_t>(m.hs_hi - m.hs_lo) * 4u;
+                m.deferred = 0;
+                if (!kGeneral && m.opt_ok) {
+                    // rows the candidate kernel does not take: more than 3072 staged ids, or sampling without a
+                    // top-k <= 64
+                    const int na = m.lo_al + m.kvw + V - m.hi_al;
+                    const bool big = (na + VWe - 1) / VWe > kThreads * (kRegElems / VWe);
+                    const int K = m.opt.top_k;
+                    const bool cand = !m.opt.do_sample || (K > 0 && K < V && K <= kSmallK);
+                    m.deferred = (big || !cand) ? 1 : 0;
+                }
+                if (!m.deferred) {
+                    if (!m.direct) bytes += static_cast<uint32_t>((m.lo_al + m.kvw + V - m.hi_al) * esize);
+                    bytes += static_cast<uint32_t>(m.hs_hi - m.hs_lo) * 4u;
+                }
             }
             const int nb = (n_my - k0) < 32 ? (n_my - k0) : 32;
             for (int j = 0; j < nb; ++j) {
@@ -1523,7 +1546,7 @@ __global__ void __launch_bounds__(kBlockThreads, 5) sampler_kernel(const __grid_
                         unsigned char* hist_dst = log_dst + p.stage_logit_bytes;
                         fence_proxy_async();
                         mbar_arrive_expect_tx(&full_bar[s], bytes);
-                        if (!m.direct) {
+                        if (!m.direct && !m.deferred) {
                             const int V = sg->vocab;
                             if (m.lo_al > 0)
                                 bulk_g2s(log_dst, row_ptr, static_cast<uint32_t>(m.lo_al * esize), &full_bar[s]);
@@ -1535,7 +1558,7 @@ __global__ void __launch_bounds__(kBlockThreads, 5) sampler_kernel(const __grid_
                                          row_ptr + static_cast<int64_t>(m.hi_al) * esize,
                                          static_cast<uint32_t>((V - m.hi_al) * esize), &full_bar[s]);
                         }
-                        if (m.hs_hi > m.hs_lo)
+                        if (m.hs_hi > m.hs_lo && !m.deferred)
                             bulk_g2s(hist_dst, sg->hist_ids + m.hist_begin + m.hs_lo,
                                      static_cast<uint32_t>(m.hs_hi - m.hs_lo) * 4u, &full_bar[s]);
                         misc.issued = k + 1;
@@ -1596,6 +1619,15 @@ __global__ void __launch_bounds__(kBlockThreads, 5) sampler_kernel(const __grid_
             continue;
         }
         const DevOptions o = m.opt;
+        if (!kGeneral && m.deferred) {
+            cbar();   // every thread has read the row's metadata
+            if (tid == 0) {
+                p.deferred_rows[atomicAdd(p.deferred_count, 1u)] = m.row;
+                mbar_arrive(&empty_bar[s]);
+                ++misc.progress;
+            }
+            continue;
+        }
 
         // ---- unaligned rows: the element warps stage the active ids themselves
         if (m.direct) {
@@ -1668,7 +1700,7 @@ __global__ void __launch_bounds__(kBlockThreads, 5) sampler_kernel(const __grid_
         int sort_n = 1;
         while (sort_n < V) sort_n <<= 1;
 
-        const bool big = nvec > kThreads * (kRegElems / VWe);
+        const bool big = kGeneral && nvec > kThreads * (kRegElems / VWe);
         if (big) {
             // ---- rows with more than 3072 active ids: transform into global scratch, exact path
             float tmax = neg_inf(), bestv = neg_inf();
@@ -1750,7 +1782,7 @@ __global__ void __launch_bounds__(kBlockThreads, 5) sampler_kernel(const __grid_
 
         const int K = o.top_k;
         bool handed = false;
-        if (K > 0 && K < V && K <= kSmallK) {
+        if (!kGeneral && K > 0 && K < V && K <= kSmallK) {
             release();   // the candidate path no longer reads the stage
             // tau_w = ceil(K/4)-th largest of the warp's 64 per-thread top-2 values: >= ceil(K/4) distinct
             // elements of this warp are >= tau_w, so >= K elements of the row are >= min over warps
@@ -1821,9 +1853,13 @@ __global__ void __launch_bounds__(kBlockThreads, 5) sampler_kernel(const __grid_
                     handed = true;
                 }
             }
-            if (!handed) ++st_overflow;
+            if (!handed) {   // no finite tau or too many candidates: the whole-row kernel takes the row
+                ++st_overflow;
+                if (tid == 0) p.deferred_rows[atomicAdd(p.deferred_count, 1u)] = m.row;
+                handed = true;
+            }
         }
-        if (!handed) {
+        if (kGeneral && !handed) {
             const float mx = block_max_f(tmax, misc, 0, lane, warp);
             // numerator cache: the consumed stage when it is large enough, else this CTA's global scratch
             const bool in_stage = !released && (stage_bytes - kMetaBytes) >= kRegElems * kThreads * 8;
@@ -1850,6 +1886,15 @@ __global__ void __launch_bounds__(kBlockThreads, 5) sampler_kernel(const __grid_
             if (tid == 0) g.out_ids[m.local] = res;
         }
         if (tid == 0) ++misc.progress;
+    }
+    if (kGeneral && tid == 0) {
+        // the last whole-row CTA to finish clears the deferred list for the next call
+        __threadfence();
+        if (atomicAdd(p.done_count, 1u) == gridDim.x - 1) {
+            *reinterpret_cast<volatile uint32_t*>(p.deferred_count) = 0u;
+            *reinterpret_cast<volatile uint32_t*>(p.done_count) = 0u;
+            __threadfence();
+        }
     }
     if (tid == 0 && p.stats) {
         const uint32_t v[7] = {st_greedy, st_fast, st_fast_exact, st_general, st_general_exact, st_large, st_overflow};
@@ -1905,22 +1950,25 @@ int64_t sampler_gscratch_stride(int vmax) {
     return (b + 255) & ~static_cast<int64_t>(255);
 }
 
-int sampler_ctas_per_sm(size_t smem) {
-    static size_t configured = 0;
-    if (smem > 48 * 1024 && smem > configured) {
-        if (cudaFuncSetAttribute(sampler_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(smem)) != cudaSuccess)
+int sampler_ctas_per_sm(size_t smem, bool general) {
+    static size_t configured[2] = {0, 0};
+    const void* fn = general ? reinterpret_cast<const void*>(&sampler_kernel<true>)
+                             : reinterpret_cast<const void*>(&sampler_kernel<false>);
+    if (smem > 48 * 1024 && smem > configured[general]) {
+        if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
             return 0;
-        configured = smem;
+        configured[general] = smem;
     }
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, sampler_kernel, kBlockThreads, smem) != cudaSuccess)
-        return 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, kBlockThreads, smem) != cudaSuccess) return 0;
     return n;
 }
 
-cudaError_t launch_sampler(const LaunchParams& p, int grid, size_t smem, cudaStream_t stream) {
-    sampler_kernel<<<grid, kBlockThreads, smem, stream>>>(p);
+cudaError_t launch_sampler(const LaunchParams& p, int grid, size_t smem, int grid_general, cudaStream_t stream) {
+    sampler_kernel<false><<<grid, kBlockThreads, smem, stream>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    sampler_kernel<true><<<grid_general, kBlockThreads, smem, stream>>>(p);
     return cudaGetLastError();
 }
 
