@@ -32,6 +32,7 @@
 // intrinsics) to match the reference's separately rounded fp32 / fp64 operations.
 
 #include <algorithm>
+#include <cstddef>
 #include <cstdint>
 #include <cuda_runtime.h>
 
@@ -69,16 +70,18 @@ struct Cand {
     int32_t idx;
 };
 
-// Candidate-path work area.
-struct CandWork {
-    double ae[kCandCap];   // survivors' softmax numerators in ascending (value, index) order
-    float ax[kCandCap];
-    int32_t ai[kCandCap];
-    double be[kCandCap];   // kept survivors' numerators in index order
-    int32_t bi[kCandCap];
-    float kth, mx;
-    int32_t S, cut, ambiguous, res;
-    double B;
+// Candidate-path work area: the candidates in ascending (value, index) order (position = rank).
+struct __align__(16) CandWork {
+    unsigned long long pk[kCandCap];   // keys okey(x) << 32 | id
+    unsigned long long pf[kCandCap];   // softmax numerators in fixed point, round(e * 2^52)
+    double pe[kCandCap];               // the same numerators in fp64
+    unsigned long long tot;            // mass of every candidate
+    unsigned long long pre_first;      // mass below the first survivor
+    unsigned long long pre_cut;        // mass below the first kept candidate
+    uint32_t kth_key;                  // okey of the K-th largest value
+    int32_t first;                     // position of the first survivor
+    int32_t cut;                       // position of the first kept candidate (-1: undecided)
+    int32_t ambiguous, res, hits;
 };
 
 // Binned-search histograms: counts and the three 20-bit chunks of fixed-point masses per bin.
@@ -87,7 +90,7 @@ struct Bins {
     uint32_t m[3][256];
 };
 
-struct SmemMisc {
+struct __align__(16) SmemMisc {
     float tau_w[kWarps];
     float red_f[8][kWarps];
     int32_t red_i[8][kWarps];
@@ -100,7 +103,7 @@ struct SmemMisc {
     int32_t bc_i[4];
     unsigned long long bc_u[2];
     double bc_d[4];
-    union {
+    union __align__(16) {
         CandWork cw;      // candidate path
         Bins bins;        // general path
     } u;
@@ -1002,16 +1005,27 @@ __device__ int general_parallel(const float (&x)[kRegElems], int nvec, const Row
 
 
 // ---------------------------------------------------------------- candidate path (top-k <= 64)
+constexpr double kFix52 = 4503599627370496.0;   // 2^52: candidate masses in fixed point (e <= 1, <= 128 values)
+
 // key[0, C) (C <= 128) = okey(x) << 32 | id of every value >= tau, so of every survivor; keys are unique.  All 128
-// element threads: thread t counts the keys below key t, its position in (value, index)-ascending order.  `mx` is
-// the row maximum.  Returns the id, or -1 when a decision lies inside the error band (the caller replays the row).
+// element threads; candidate t is owned by thread t.  Sums are exact 64-bit integer sums of round(e * 2^52), each
+// thread adding up the ranks below its own (no shuffles, no fp64 chains); the rounding, at most 2^-53 per value,
+// is inside the error band.  `mx` is the row maximum.  Returns the id, or -1 when a decision lies inside the band
+// (the caller replays the row).
 __device__ int cand_parallel(const unsigned long long* key, int C, int K, const DevOptions& o, double r, float mx,
-                             double* out_probs, int V, CandWork& w, int tid, int lane, int warp) {
+                             double* out_probs, int V, CandWork& w, int tid) {
     const bool mine = tid < C;
+    unsigned long long kt = 0, ft = 0;
+    double et = 0.0;
     int lt = 0;
-    uint32_t it = 0;
+    if (tid == 0) {
+        w.cut = -1;
+        w.ambiguous = 0;
+        w.res = -1;
+        w.hits = 0;
+    }
     if (mine) {
-        const unsigned long long kt = key[tid];
+        kt = key[tid];
         const ulonglong2* k2 = reinterpret_cast<const ulonglong2*>(key);
         const int C2 = C >> 1;
 #pragma unroll 4
@@ -1020,182 +1034,102 @@ __device__ int cand_parallel(const unsigned long long* key, int C, int K, const 
             lt += (v.x < kt ? 1 : 0) + (v.y < kt ? 1 : 0);
         }
         if (C & 1) lt += key[C - 1] < kt ? 1 : 0;
-        const float xt = okey_inv(static_cast<uint32_t>(kt >> 32));
-        it = static_cast<uint32_t>(kt);
-        w.ax[lt] = xt;
-        w.ai[lt] = static_cast<int32_t>(it);
-        w.ae[lt] = softmax_num(xt, mx);
+        et = softmax_num(okey_inv(static_cast<uint32_t>(kt >> 32)), mx);   // Sampler.cs:57
+        ft = __double2ull_rn(__dmul_rn(et, kFix52));
+        w.pk[lt] = kt;
+        w.pf[lt] = ft;
+        w.pe[lt] = et;
+        if (lt == C - K) w.kth_key = static_cast<uint32_t>(kt >> 32);
     }
     if (out_probs)
         for (int i = tid; i < V; i += kThreads) out_probs[i] = 0.0;
     cbar();
-    if (warp == 0) {
-        // survivors: the values >= the K-th largest, i.e. positions [C - S, C)
-        const float kth = w.ax[C - K];
-        int S = 0;
-#pragma unroll
-        for (int s = 0; s < 4; ++s) {
-            const int p = s * 32 + lane;
-            S += __popc(__ballot_sync(kFull, p < C && w.ax[p] >= kth));
+    const uint32_t kth_key = w.kth_key;
+    const uint32_t vt = static_cast<uint32_t>(kt >> 32);
+    const bool surv = mine && vt >= kth_key;
+    unsigned long long pre = 0;   // mass of the candidates ranked below this one
+    if (mine) {
+        const ulonglong2* f2 = reinterpret_cast<const ulonglong2*>(w.pf);
+#pragma unroll 4
+        for (int q = 0; q < (lt >> 1); ++q) {
+            const ulonglong2 v = f2[q];
+            pre += v.x + v.y;
         }
-        const int base0 = C - S;
-        double e[4];
-        float xv[4];
-        bool sv[4];
-#pragma unroll
-        for (int s = 0; s < 4; ++s) {
-            const int p = s * 32 + lane;
-            sv[s] = p < S;
-            e[s] = sv[s] ? w.ae[base0 + p] : 0.0;
-            xv[s] = sv[s] ? w.ax[base0 + p] : 0.0f;
+        if (lt & 1) pre += w.pf[lt - 1];
+        if (lt == C - 1) w.tot = pre + ft;
+        if (surv && (lt == 0 || static_cast<uint32_t>(w.pk[lt - 1] >> 32) < kth_key)) {
+            w.first = lt;
+            w.pre_first = pre;
         }
-        const double total = warp_sum_d(__dadd_rn(__dadd_rn(e[0], e[1]), __dadd_rn(e[2], e[3])));
-        const double eta = (4.0 * S + 128.0) * kU;
-        int pb = 0;   // survivors at positions < pb (counted from the smallest) are removed
-        bool amb = false;
-        if (o.top_p < 1.0f) {   // Sampler.cs:62-72
-            const double thr = static_cast<double>(__fsub_rn(1.0f, o.top_p));
-            const double T = __dmul_rn(thr, total);
-            const double band = __dmul_rn(eta, total);
-            double incl[4], excl[4], base = 0.0;
-#pragma unroll
-            for (int s = 0; s < 4; ++s) {
-                const double in = warp_incl_d(e[s], lane);
-                excl[s] = __dadd_rn(base, warp_excl_from_incl_d(in, lane));
-                incl[s] = __dadd_rn(base, in);
-                base = __dadd_rn(base, shfl_d(in, 31));
-            }
-            // the break element: the first position <= S - 2 (the last is never removed) whose cum exceeds T
-            unsigned bm[4];
-            int nb = 0;
-#pragma unroll
-            for (int s = 0; s < 4; ++s) {
-                const int p = s * 32 + lane;
-                bm[s] = __ballot_sync(kFull, sv[s] && p <= S - 2 && incl[s] > T && !(excl[s] > T));
-                nb += __popc(bm[s]);
-            }
-            if (nb == 1) {
-                int bs = 0;
-#pragma unroll
-                for (int s = 0; s < 4; ++s)
-                    if (bm[s]) bs = s;
-                const int bl = __ffs(bm[bs]) - 1;
-                pb = bs * 32 + bl;
-                double bi = 0.0, be = 0.0;
-                float bx = 0.0f;
-#pragma unroll
-                for (int s = 0; s < 4; ++s) {
-                    const double a = shfl_d(incl[s], bl), b = shfl_d(excl[s], bl);
-                    const float xx = __shfl_sync(kFull, xv[s], bl);
-                    if (s == bs) {
-                        bi = a;
-                        be = b;
-                        bx = xx;
-                    }
-                }
-                if (!(__dsub_rn(bi, T) > band)) amb = true;
-                if (be > 0.0 && !(__dsub_rn(T, be) > band)) amb = true;
-                // the groups next to the break value must be strictly apart in probability
-                float lo_n = neg_inf(), hi_n = pos_inf();
-                bool cut_inside = false;
-#pragma unroll
-                for (int s = 0; s < 4; ++s) {
-                    const int p = s * 32 + lane;
-                    if (sv[s]) {
-                        if (xv[s] < bx) lo_n = fmaxf(lo_n, xv[s]);
-                        if (xv[s] > bx) hi_n = fminf(hi_n, xv[s]);
-                        if (xv[s] == bx && p < pb) cut_inside = true;
-                    }
-                }
-                lo_n = warp_max_f(lo_n);
-                hi_n = warp_min_f(hi_n);
-                cut_inside = __any_sync(kFull, cut_inside);
-                const double eb = softmax_num(bx, mx);
-                if (!is_neg_inf(lo_n) && !(softmax_num(lo_n, mx) < eb * (1.0 - 32.0 * kU))) amb = true;
-                if (cut_inside && hi_n != pos_inf() && !(softmax_num(hi_n, mx) > eb * (1.0 + 32.0 * kU))) amb = true;
-            } else if (nb == 0) {
-                // no crossing before the last survivor: all but the last go, if certainly below T
-                pb = S - 1;
-                if (S > 1) {
-                    const int q = S - 2;
-                    double at = 0.0;
-#pragma unroll
-                    for (int s = 0; s < 4; ++s) {
-                        const double a = shfl_d(incl[s], q & 31);
-                        if (s == (q >> 5)) at = a;
-                    }
-                    if (!(__dsub_rn(T, at) > band)) amb = true;
-                    float lo_n = neg_inf();
-#pragma unroll
-                    for (int s = 0; s < 4; ++s)
-                        if (sv[s] && xv[s] < mx) lo_n = fmaxf(lo_n, xv[s]);
-                    lo_n = warp_max_f(lo_n);
-                    if (!is_neg_inf(lo_n) && !(softmax_num(lo_n, mx) < 1.0 - 32.0 * kU)) amb = true;
-                }
-            } else {
-                amb = true;
-            }
+    }
+    cbar();
+    const int first = w.first;
+    const int S = C - first;
+    const double eta = (6.0 * S + 128.0) * kU;
+    if (o.top_p >= 1.0f) {
+        if (tid == 0) {
+            w.cut = first;
+            w.pre_cut = w.pre_first;
         }
-        if (lane == 0) {
-            w.cut = base0 + pb;   // candidates at positions >= cut are kept
-            w.S = S;
+    } else if (surv) {
+        // ---- top-p cut over the ascending order (Sampler.cs:62-72): the element whose cumulative mass first
+        //      exceeds (1 - TopP) of the total breaks the loop; the last element is never removed
+        const unsigned long long tot_s = w.tot - w.pre_first;
+        const double tot_d = static_cast<double>(tot_s);
+        const double thr = static_cast<double>(__fsub_rn(1.0f, o.top_p));
+        const double T = __dmul_rn(thr, tot_d);
+        const double band = __dmul_rn(eta, tot_d);
+        const double bd = static_cast<double>(pre - w.pre_first);            // cum before this element
+        const double id = static_cast<double>(pre - w.pre_first + ft);       // cum including it
+        const int pos = lt - first;
+        const bool brk = pos <= S - 2 && !(bd > T) && id > T;
+        const bool all_but_last = pos == S - 1 && !(bd > T);
+        if (brk || all_but_last) {
+            bool amb = false;
+            if (brk && !(__dsub_rn(id, T) > band)) amb = true;
+            if (bd > 0.0 && !(__dsub_rn(T, bd) > band)) amb = true;
+            // the value groups next to the cut must be strictly apart in probability (the reference orders by
+            // probability, then index)
+            int qlo = lt - 1;
+            while (qlo >= first && static_cast<uint32_t>(w.pk[qlo] >> 32) == vt) --qlo;
+            if (qlo >= first && !(w.pe[qlo] < et * (1.0 - 32.0 * kU))) amb = true;
+            if (brk && qlo < lt - 1) {   // the cut falls inside this value group: the group above matters too
+                int qhi = lt + 1;
+                while (qhi < C && static_cast<uint32_t>(w.pk[qhi] >> 32) == vt) ++qhi;
+                if (qhi < C && !(w.pe[qhi] > et * (1.0 + 32.0 * kU))) amb = true;
+            }
+            w.cut = lt;
+            w.pre_cut = pre;
             w.ambiguous = amb ? 1 : 0;
         }
     }
     cbar();
-    if (w.ambiguous) return -1;
+    if (w.ambiguous || w.cut < 0) return -1;
     const int cut = w.cut;
     const bool kept = mine && lt >= cut;
-    if (kept) {   // index-order position among the kept survivors
-        int pidx = 0;
-        for (int j = cut; j < C; ++j) pidx += w.ai[j] < static_cast<int32_t>(it) ? 1 : 0;
-        w.be[pidx] = w.ae[lt];
-        w.bi[pidx] = static_cast<int32_t>(it);
-    }
-    cbar();
-    if (warp == 0) {
+    const unsigned long long B = w.tot - w.pre_cut;   // mass of the kept candidates
+    if (kept) {
         // ---- inverse-CDF draw over the kept ids in index order (Sampler.cs:73-87)
-        const int nk = C - cut;
-        double e2[4];
-        double b4 = 0.0;
-#pragma unroll
-        for (int s = 0; s < 4; ++s) {
-            const int p = s * 32 + lane;
-            e2[s] = p < nk ? w.be[p] : 0.0;
-            b4 = __dadd_rn(b4, e2[s]);
+        const uint32_t it = static_cast<uint32_t>(kt);
+        unsigned long long pre2 = 0;
+        for (int q = cut; q < C; ++q) {
+            const unsigned long long kq = w.pk[q];
+            if (static_cast<uint32_t>(kq) < it) pre2 += w.pf[q];
         }
-        const double B = warp_sum_d(b4);
-        const double eta = (4.0 * w.S + 128.0) * kU;
-        const double rB = __dmul_rn(r, B);
-        const double bandB = __dmul_rn(eta, B);
-        double base = 0.0;
-        int hits = 0, hit = -1;
-        bool unsure = false;
-#pragma unroll
-        for (int s = 0; s < 4; ++s) {
-            const double in = warp_incl_d(e2[s], lane);
-            const double inc = __dadd_rn(base, in);
-            const double exc = __dadd_rn(base, warp_excl_from_incl_d(in, lane));
-            const bool h = e2[s] > 0.0 && inc > rB && !(exc > rB);
-            if (h) {
-                hit = w.bi[s * 32 + lane];
-                if (!(__dsub_rn(inc, rB) > bandB)) unsure = true;
-                if (exc > 0.0 && !(__dsub_rn(rB, exc) > bandB)) unsure = true;
-            }
-            hits += __popc(__ballot_sync(kFull, h));
-            base = __dadd_rn(base, shfl_d(in, 31));
-        }
-        const bool bad = hits != 1 || __any_sync(kFull, unsure);
-        hit = warp_max_i(hit);
-        if (lane == 0) {
-            w.res = bad ? -1 : hit;
-            w.B = B;
+        const double Bd = static_cast<double>(B);
+        const double rB = __dmul_rn(r, Bd);
+        const double lo = static_cast<double>(pre2), hi = static_cast<double>(pre2 + ft);
+        if (ft > 0 && !(lo > rB) && hi > rB) {
+            bool amb = !(__dsub_rn(hi, rB) > __dmul_rn(eta, Bd));
+            if (pre2 > 0 && !(__dsub_rn(rB, lo) > __dmul_rn(eta, Bd))) amb = true;
+            atomicAdd(&w.hits, 1);
+            w.res = amb ? -1 : static_cast<int>(it);
         }
     }
     cbar();
-    const int res = w.res;
+    const int res = w.hits == 1 ? w.res : -1;
     if (res >= 0 && out_probs) {
-        if (kept) out_probs[it] = __ddiv_rn(w.ae[lt], w.B);
+        if (kept) out_probs[static_cast<uint32_t>(kt)] = __ddiv_rn(et, __dmul_rn(static_cast<double>(B), 1.0 / kFix52));
         cbar();
     }
     return res;
@@ -1803,21 +1737,12 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
                 mx = fmaxf(mx, misc.red_f[5][w]);
             }
             if (!is_neg_inf(tau)) {
-                // ---- candidates x >= tau -> shared keys okey(x) << 32 | id (warp-scan positions, one atomic per warp)
+                // ---- candidates x >= tau -> shared keys okey(x) << 32 | id (one atomic per thread with candidates)
                 int cnt = 0;
 #pragma unroll
                 for (int e = 0; e < kRegElems; ++e) cnt += (x[e] >= tau) ? 1 : 0;
-                int incl = cnt;
-#pragma unroll
-                for (int off = 1; off < 32; off <<= 1) {
-                    const int y = __shfl_up_sync(kFull, incl, off);
-                    if (lane >= off) incl += y;
-                }
-                uint32_t base = 0;
-                if (lane == 31) base = atomicAdd(&misc.cand_count, static_cast<uint32_t>(incl));
-                base = __shfl_sync(kFull, base, 31);
-                int pos = static_cast<int>(base) + incl - cnt;
                 if (cnt > 0) {
+                    int pos = static_cast<int>(atomicAdd(&misc.cand_count, static_cast<uint32_t>(cnt)));
 #pragma unroll
                     for (int e = 0; e < kRegElems; ++e) {
                         if (x[e] >= tau) {
@@ -1837,7 +1762,7 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
                 if (tid == 0) misc.cand_count = 0;
                 if (C <= kCandCap) {
                     int res = p.force_exact ? -1 : cand_parallel(ckey, C, K, o, m.uniform, mx, out_probs, V,
-                                                                misc.u.cw, tid, lane, warp);
+                                                                misc.u.cw, tid);
                     if (res < 0) {
                         if (warp == 0) {
                             const int rr = replay_candidates(ckey, C, K, o, m.uniform, V, out_probs, misc.flags, lane);
@@ -1984,4 +1909,11 @@ cudaError_t launch_apply_penalty(float* logits, int vocab, const int32_t* hist, 
     return cudaGetLastError();
 }
 
+}  // namespace vw
+
+namespace vw {
+namespace {
+static_assert(offsetof(CandWork, pf) % 16 == 0 && offsetof(CandWork, pk) % 16 == 0, "CandWork alignment");
+static_assert(sizeof(SmemMisc) % 16 == 0, "SmemMisc alignment");
+}  // namespace
 }  // namespace vw
