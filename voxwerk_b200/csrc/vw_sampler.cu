@@ -49,7 +49,7 @@ constexpr double kFix = 2251799813685248.0;         // 2^51: fixed-point scale o
 constexpr int kProducerWarp = kWarps;              // warp 4
 constexpr int kBlockThreads = (kWarps + 1) * 32;   // 160
 
-struct RowMeta {
+struct __align__(16) RowMeta {
     double uniform;
     int64_t hist_begin;   // absolute offset into the segment's hist_ids
     int32_t row;          // global row index
@@ -62,7 +62,9 @@ struct RowMeta {
     int32_t opt_ok;       // option index valid
     int32_t deferred;     // candidate kernel: the row goes to the whole-row kernel (nothing staged)
     DevOptions opt;
+    int32_t pad_[3];
 };
+static_assert(sizeof(RowMeta) % 16 == 0, "RowMeta is copied in 16-byte units");
 static_assert(sizeof(RowMeta) <= kMetaBytes, "RowMeta too large");
 
 struct Cand {
@@ -450,6 +452,8 @@ struct RowCtx {
     bool sample;
     float inv_t;         // fp32(1 / T)
     const uint32_t* bitmap;
+    int slow_vlo, slow_vhi;   // staged vectors that may hold suppressed ids
+    int eos_vec;              // staged vector holding a suppressed EOS, or -1
 };
 
 // Staged position -> vocabulary id: [0, lo_al) | kvw ids from kbase | [hi_al, V)
@@ -1271,8 +1275,8 @@ __device__ __forceinline__ void process_vectors(const unsigned char* sl, int nve
             const int i0 = mp.idx(qv * VW);
             const uint32_t bits = c.pen_on ? c.bitmap[i0 >> 5] : 0u;
             const bool slow = (c.pen_on && ((bits >> (i0 & 31)) & ((1u << VW) - 1u)) != 0u) ||
-                              (c.kind == 0 && ((i0 + VW > c.sup_lo && i0 < c.sup_hi) ||
-                                               (c.eos_blocked && c.eos >= i0 && c.eos < i0 + VW)));
+                              static_cast<unsigned>(qv - c.slow_vlo) < static_cast<unsigned>(c.slow_vhi - c.slow_vlo) ||
+                              qv == c.eos_vec;
 #pragma unroll
             for (int e = 0; e < VW; ++e) {
                 float t;
@@ -1282,12 +1286,8 @@ __device__ __forceinline__ void process_vectors(const unsigned char* sl, int nve
                     t = kSample ? __fmul_rn(v[e], c.inv_t) : v[e];
                 x[g * VW + e] = t;
                 if (kSample) {
-                    if (t > tmax) {
-                        tmax2 = tmax;
-                        tmax = t;
-                    } else if (t > tmax2) {
-                        tmax2 = t;
-                    }
+                    tmax2 = fmaxf(tmax2, fminf(tmax, t));
+                    tmax = fmaxf(tmax, t);
                 } else if (t > bestv) {
                     bestv = t;
                     besti = i0 + e;
@@ -1528,7 +1528,13 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
             cbar();
             break;
         }
-        const RowMeta m = *reinterpret_cast<const RowMeta*>(st);
+        RowMeta m;
+        {
+            const uint4* src = reinterpret_cast<const uint4*>(st);
+            uint4* dst = reinterpret_cast<uint4*>(&m);
+#pragma unroll
+            for (int i = 0; i < static_cast<int>(sizeof(RowMeta) / 16); ++i) dst[i] = src[i];
+        }
         const DevSegment& g = p.seg[m.seg];
         unsigned char* sl = st + kMetaBytes;
         const int32_t* sh = reinterpret_cast<const int32_t*>(sl + p.stage_logit_bytes);
@@ -1601,10 +1607,22 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
             const int nst = m.hs_hi - m.hs_lo;
             for (int c4 = tid; c4 < nst / 4; c4 += kThreads) {
                 const int4 v = reinterpret_cast<const int4*>(sh)[c4];
-                visit(v.x);
-                visit(v.y);
-                visit(v.z);
-                visit(v.w);
+                const int ids[4] = {v.x, v.y, v.z, v.w};
+                uint32_t old[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j)   // the four atomics are issued before any result is used
+                    old[j] = static_cast<unsigned>(ids[j]) < static_cast<unsigned>(V)
+                                 ? atomicOr(&bitmap[ids[j] >> 5], 1u << (ids[j] & 31))
+                                 : ~0u;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    if (static_cast<unsigned>(ids[j]) >= static_cast<unsigned>(V)) {
+                        bad = true;
+                    } else if (inplace && !(old[j] & (1u << (ids[j] & 31)))) {
+                        const int q = mp.pos(ids[j]);
+                        if (q >= 0) sf[q] = penalize(sf[q], pen, pen_rcp);
+                    }
+                }
             }
             const int rest = m.hist_len - nst;   // ids outside the staged span: [0, hs_lo) and [hs_hi, len)
             for (int q = tid; q < rest; q += kThreads) visit(gh[q < m.hs_lo ? q : q - m.hs_lo + m.hs_hi]);
@@ -1625,6 +1643,18 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
         c.sample = o.do_sample != 0;
         c.inv_t = __fdiv_rn(1.0f, o.temperature);
         c.bitmap = bitmap;
+        c.slow_vlo = c.slow_vhi = 0;
+        c.eos_vec = -1;
+        if (g.kind == 0) {
+            if (g.sup_lo < g.sup_hi) {   // staged positions [sup_lo, lo_al + kvw + (sup_hi - hi_al)) may be suppressed
+                c.slow_vlo = g.sup_lo / VWe;
+                c.slow_vhi = (m.lo_al + m.kvw + max(g.sup_hi - m.hi_al, 0) + VWe - 1) / VWe;
+            }
+            if (c.eos_blocked && g.eos >= 0 && g.eos < V) {
+                const int ep = mp.pos(g.eos);
+                if (ep >= 0) c.eos_vec = ep / VWe;
+            }
+        }
 
         char* gbase = p.gscratch + static_cast<int64_t>(blockIdx.x) * p.gscratch_stride;
         const int vpad = (max(p.vmax, kRegElems * kThreads) + 31) & ~31;
@@ -1737,22 +1767,16 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
                 mx = fmaxf(mx, misc.red_f[5][w]);
             }
             if (!is_neg_inf(tau)) {
-                // ---- candidates x >= tau -> shared keys okey(x) << 32 | id (one atomic per thread with candidates)
-                int cnt = 0;
+                // ---- candidates x >= tau -> shared keys okey(x) << 32 | id
 #pragma unroll
-                for (int e = 0; e < kRegElems; ++e) cnt += (x[e] >= tau) ? 1 : 0;
-                if (cnt > 0) {
-                    int pos = static_cast<int>(atomicAdd(&misc.cand_count, static_cast<uint32_t>(cnt)));
-#pragma unroll
-                    for (int e = 0; e < kRegElems; ++e) {
-                        if (x[e] >= tau) {
-                            if (pos < kCandCap) {
-                                const int gg = e / VWe;
-                                const int qv = tid + gg * kThreads;
-                                ckey[pos] = (static_cast<unsigned long long>(okey(x[e])) << 32) |
-                                            static_cast<uint32_t>(mp.idx(qv * VWe + (e - gg * VWe)));
-                            }
-                            ++pos;
+                for (int e = 0; e < kRegElems; ++e) {
+                    if (x[e] >= tau) {
+                        const uint32_t pos = atomicAdd(&misc.cand_count, 1u);
+                        if (pos < static_cast<uint32_t>(kCandCap)) {
+                            const int gg = e / VWe;
+                            const int qv = tid + gg * kThreads;
+                            ckey[pos] = (static_cast<unsigned long long>(okey(x[e])) << 32) |
+                                        static_cast<uint32_t>(mp.idx(qv * VWe + (e - gg * VWe)));
                         }
                     }
                 }
