@@ -42,30 +42,36 @@ namespace vw {
 namespace {
 
 constexpr unsigned kFull = 0xffffffffu;
-constexpr int kMetaBytes = 128;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;   // bounded mbarrier waits: 2 s without progress
 constexpr double kU = 1.1102230246251565e-16;      // 2^-53
 constexpr double kFix = 2251799813685248.0;         // 2^51: fixed-point scale of histogram masses (e <= 1)
 constexpr int kProducerWarp = kWarps;              // warp 4
 constexpr int kBlockThreads = (kWarps + 1) * 32;   // 160
 
+// Everything the element warps need about a row, prepared by the producer warp.  Kept in its own ring of 2 x
+// n_stages entries, so an entry outlives the early release of its row's stage.
 struct __align__(16) RowMeta {
-    double uniform;
-    int64_t hist_begin;   // absolute offset into the segment's hist_ids
-    int32_t row;          // global row index
-    int32_t seg, local, step, hist_len;
-    int32_t hs_lo, hs_hi; // history ids [hs_lo, hs_hi) (relative to hist_begin) are staged in shared memory
-    int32_t lo_al, hi_al; // staged logits: ids [0, lo_al) | kvw ids from kbase (the EOS vector) | [hi_al, V)
+    double uniform;               // the row's NextDouble() draw
+    double pen_rcp;               // RN64(1 / repetition penalty)
+    const unsigned char* row_ptr; // the row in global memory (unaligned rows are staged by the element warps)
+    const int32_t* hist;          // the row's history ids in global memory
+    int32_t* out_id;              // where the row's id goes
+    double* out_probs;            // the row's probability output, or null
+    int32_t row, seg, opt_idx, step;
+    int32_t hist_len, hs_lo, hs_hi;   // history ids [hs_lo, hs_hi) are staged in shared memory
+    int32_t lo_al, hi_al;         // staged logits: ids [0, lo_al) | kvw ids from kbase (the EOS vector) | [hi_al, V)
     int32_t kvw, kbase;
-    int32_t direct;       // logits were not bulk-copied: the element warps load them
-    int32_t pen_on;       // repetition penalty active
-    int32_t opt_ok;       // option index valid
-    int32_t deferred;     // candidate kernel: the row goes to the whole-row kernel (nothing staged)
+    int32_t direct;               // logits were not bulk-copied: the element warps load them
+    int32_t pen_on;               // repetition penalty active
+    int32_t opt_ok;               // option index valid
+    int32_t deferred;             // candidate kernel: the row goes to the whole-row kernel (nothing staged)
+    int32_t V, dtype, kind;
+    int32_t sup_lo, sup_hi, eos, eos_blocked;
+    int32_t slow_vlo, slow_vhi, eos_vec;   // staged vectors that need the per-element mask rules
+    float inv_t;                  // fp32(1 / T)
     DevOptions opt;
-    int32_t pad_[3];
 };
-static_assert(sizeof(RowMeta) % 16 == 0, "RowMeta is copied in 16-byte units");
-static_assert(sizeof(RowMeta) <= kMetaBytes, "RowMeta too large");
+static_assert(sizeof(RowMeta) % 16 == 0, "RowMeta alignment");
 
 struct Cand {
     float x;
@@ -101,7 +107,7 @@ struct __align__(16) SmemMisc {
     double red_v[kWarps][8];
     int32_t issued;       // rows the producer has issued (timeout drain)
     uint32_t progress;    // rows finished by the element warps (extends the producer's wait bound)
-    uint32_t cand_count;
+    uint32_t cand_count[2];   // candidate counters, alternating by row (reset one row after use)
     int32_t bc_i[4];
     unsigned long long bc_u[2];
     double bc_d[4];
@@ -1259,12 +1265,14 @@ __device__ int replay_candidates(const unsigned long long* ck, int C, int K, con
 
 // ---------------------------------------------------------------- element pass
 // One pass over the staged row: transform every element into x[] (registers).  Sampling rows track each thread's
-// two largest values (tau); greedy rows the first maximum.  Vectors that no mask boundary, EOS rule or per-element
-// penalty touches take the short path (temperature only).
-template <int VW, bool kSample>
+// two largest values; greedy rows the first maximum.  Vectors that no mask boundary, EOS rule or per-element
+// penalty touches take the short path (temperature only).  kFuse: every value >= tau_g is also appended to the
+// candidate keys (okey(x) << 32 | id).
+template <int VW, bool kSample, bool kFuse>
 __device__ __forceinline__ void process_vectors(const unsigned char* sl, int nvec, const RowMap& mp,
                                                 const RowCtx& c, int tid, float (&x)[kRegElems],
-                                                float& tmax, float& tmax2, float& bestv, int& besti) {
+                                                float& tmax, float& tmax2, float& bestv, int& besti,
+                                                float tau_g, uint32_t* cand_count, unsigned long long* ckey) {
     constexpr int G = kRegElems / VW;
 #pragma unroll
     for (int g = 0; g < G; ++g) {
@@ -1288,6 +1296,11 @@ __device__ __forceinline__ void process_vectors(const unsigned char* sl, int nve
                 if (kSample) {
                     tmax2 = fmaxf(tmax2, fminf(tmax, t));
                     tmax = fmaxf(tmax, t);
+                    if (kFuse && t >= tau_g) {
+                        const uint32_t pos = atomicAdd(cand_count, 1u);
+                        if (pos < static_cast<uint32_t>(kCandCap))
+                            ckey[pos] = (static_cast<unsigned long long>(okey(t)) << 32) | static_cast<uint32_t>(i0 + e);
+                    }
                 } else if (t > bestv) {
                     bestv = t;
                     besti = i0 + e;
@@ -1351,9 +1364,10 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
     const int lane = tid & 31;
     const int warp = tid >> 5;
     const int S_ = p.n_stages;
-    const int stage_bytes = kMetaBytes + p.stage_logit_bytes + p.stage_hist_cap * 4;
+    const int stage_bytes = p.stage_logit_bytes + p.stage_hist_cap * 4;
     unsigned char* stages = smem;
-    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(S_) * stage_bytes);
+    RowMeta* metas = reinterpret_cast<RowMeta*>(smem + static_cast<size_t>(S_) * stage_bytes);   // 2 * S_ entries
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(metas + 2 * S_);
     uint64_t* empty_bar = full_bar + S_;
     uint32_t* bitmap = reinterpret_cast<uint32_t*>(empty_bar + S_);
     unsigned long long* ckey = reinterpret_cast<unsigned long long*>(bitmap + ((p.bitmap_words + 3) & ~3));
@@ -1365,6 +1379,8 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
                                       p.total_rows)
                                 : p.total_rows;
     const int n_my = first < n_rows ? (n_rows - 1 - first) / gstride + 1 : 0;
+    // nothing deferred: the counters are already zero, so no CTA has anything to do
+    if (kGeneral && n_rows == 0) return;
 
     if (tid == 0) {
         for (int s = 0; s < S_; ++s) {
@@ -1374,7 +1390,8 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
         fence_mbar_init();
         misc.issued = 0;
         misc.progress = 0;
-        misc.cand_count = 0;
+        misc.cand_count[0] = 0;
+        misc.cand_count[1] = 0;
     }
     for (int i = tid; i < p.bitmap_words; i += blockDim.x) bitmap[i] = 0u;
     __syncthreads();
@@ -1383,11 +1400,9 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
         // ================= producer warp: plans rows and issues the bulk copies =================
         bool alive = true;
         for (int k0 = 0; k0 < n_my && alive; k0 += 32) {
-            // lane j prefetches the metadata of the CTA's row k0 + j
+            // lane j prepares the metadata of the CTA's row k0 + j
             const int kj = k0 + lane;
             RowMeta m;
-            const DevSegment* sg = &p.seg[0];
-            const unsigned char* row_ptr = nullptr;
             int esize = 4;
             uint32_t bytes = 0;
             if (kj < n_my) {
@@ -1396,18 +1411,19 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
                 int s = 0;
                 for (int i = 1; i < p.n_segs; ++i)
                     if (r >= p.seg[i].row_begin) s = i;
-                sg = &p.seg[s];
-                const int local = r - sg->row_begin;
-                const int opt_raw = sg->opt_index ? sg->opt_index[local] : 0;
+                const DevSegment& sg = p.seg[s];
+                const int local = r - sg.row_begin;
+                const int opt_raw = sg.opt_index ? sg.opt_index[local] : 0;
+                const int V = sg.vocab;
                 m.row = r;
                 m.seg = s;
-                m.local = local;
-                m.step = sg->steps ? sg->steps[local] : 0x7fffffff;
-                m.uniform = sg->uniforms ? sg->uniforms[local] : 0.0;
+                m.opt_idx = opt_raw;
+                m.step = sg.steps ? sg.steps[local] : 0x7fffffff;
+                m.uniform = sg.uniforms ? sg.uniforms[local] : 0.0;
                 int64_t hb = 0, he = 0;
-                if (sg->kind == 0 && sg->hist_offsets) {
-                    hb = sg->hist_offsets[local];
-                    he = sg->hist_offsets[local + 1];
+                if (sg.kind == 0 && sg.hist_offsets) {
+                    hb = sg.hist_offsets[local];
+                    he = sg.hist_offsets[local + 1];
                 }
                 m.opt_ok = (opt_raw >= 0 && opt_raw < p.n_opts) ? 1 : 0;
                 if (m.opt_ok) {
@@ -1415,30 +1431,39 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
                 } else {
                     m.opt = DevOptions{0, 0, 1.0f, 1.0f, 1.0f};
                 }
-                const int V = sg->vocab;
-                esize = sg->dtype == 0 ? 4 : 2;
+                esize = sg.dtype == 0 ? 4 : 2;
                 const int VWe = 16 / esize;
-                m.pen_on = (m.opt_ok && sg->kind == 0 && m.opt.rep_penalty != 1.0f && he > hb) ? 1 : 0;
-                m.hist_begin = hb;
+                m.V = V;
+                m.dtype = sg.dtype;
+                m.kind = sg.kind;
+                m.sup_lo = sg.sup_lo;
+                m.sup_hi = sg.sup_hi;
+                m.eos = sg.eos;
+                m.eos_blocked = (sg.kind == 0 && m.step < sg.min_new) ? 1 : 0;
+                m.pen_on = (m.opt_ok && sg.kind == 0 && m.opt.rep_penalty != 1.0f && he > hb) ? 1 : 0;
+                m.pen_rcp = __drcp_rn(static_cast<double>(m.opt.rep_penalty));
+                m.inv_t = __fdiv_rn(1.0f, m.opt.temperature);
+                m.hist = sg.hist_ids ? sg.hist_ids + hb : nullptr;
                 m.hist_len = static_cast<int32_t>(he - hb);
+                m.out_id = sg.out_ids + local;
+                m.out_probs = sg.out_probs ? sg.out_probs + static_cast<int64_t>(local) * V : nullptr;
                 m.lo_al = V;
                 m.hi_al = V;
-                if (sg->kind == 0 && sg->sup_lo < sg->sup_hi) {
-                    const int la = (sg->sup_lo + VWe - 1) / VWe * VWe;
-                    const int ha = sg->sup_hi / VWe * VWe;
+                if (sg.kind == 0 && sg.sup_lo < sg.sup_hi) {
+                    const int la = (sg.sup_lo + VWe - 1) / VWe * VWe;
+                    const int ha = sg.sup_hi / VWe * VWe;
                     if (la < ha) {
                         m.lo_al = la;
                         m.hi_al = ha;
                     }
                 }
-                const bool keep =
-                    sg->kind == 0 && sg->eos >= m.lo_al && sg->eos < m.hi_al && m.step >= sg->min_new;
+                const bool keep = sg.kind == 0 && sg.eos >= m.lo_al && sg.eos < m.hi_al && !m.eos_blocked;
                 m.kvw = keep ? VWe : 0;
-                m.kbase = keep ? sg->eos / VWe * VWe : 0;
-                m.direct = sg->bulk_ok ? 0 : 1;
+                m.kbase = keep ? sg.eos / VWe * VWe : 0;
+                m.direct = sg.bulk_ok ? 0 : 1;
                 m.hs_lo = 0;
                 m.hs_hi = 0;
-                if (m.pen_on && sg->hist_aligned && p.stage_hist_cap > 0) {
+                if (m.pen_on && sg.hist_aligned && p.stage_hist_cap > 0) {
                     int64_t a = (hb + 3) / 4 * 4;
                     int64_t b = he / 4 * 4;
                     if (b > a + p.stage_hist_cap) b = a + p.stage_hist_cap;
@@ -1447,8 +1472,22 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
                         m.hs_hi = static_cast<int32_t>(b - hb);
                     }
                 }
-                row_ptr = static_cast<const unsigned char*>(sg->logits) +
-                          static_cast<int64_t>(local) * sg->row_stride * esize;
+                // staged vectors that may hold suppressed ids: positions [sup_lo, lo_al + kvw + (sup_hi - hi_al))
+                m.slow_vlo = m.slow_vhi = 0;
+                m.eos_vec = -1;
+                if (sg.kind == 0) {
+                    if (sg.sup_lo < sg.sup_hi) {
+                        m.slow_vlo = sg.sup_lo / VWe;
+                        m.slow_vhi = (m.lo_al + m.kvw + max(sg.sup_hi - m.hi_al, 0) + VWe - 1) / VWe;
+                    }
+                    if (m.eos_blocked && sg.eos >= 0 && sg.eos < V) {
+                        const RowMap mp{m.lo_al, m.kvw, m.kbase, m.hi_al};
+                        const int ep = mp.pos(sg.eos);
+                        if (ep >= 0) m.eos_vec = ep / VWe;
+                    }
+                }
+                m.row_ptr = static_cast<const unsigned char*>(sg.logits) +
+                            static_cast<int64_t>(local) * sg.row_stride * esize;
                 m.deferred = 0;
                 if (!kGeneral && m.opt_ok) {
                     // rows the candidate kernel does not take: more than 3072 staged ids, or sampling without a
@@ -1459,7 +1498,7 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
                     const bool cand = !m.opt.do_sample || (K > 0 && K < V && K <= kSmallK);
                     m.deferred = (big || !cand) ? 1 : 0;
                 }
-                if (!m.deferred) {
+                if (!m.deferred && m.opt_ok) {
                     if (!m.direct) bytes += static_cast<uint32_t>((m.lo_al + m.kvw + V - m.hi_al) * esize);
                     bytes += static_cast<uint32_t>(m.hs_hi - m.hs_lo) * 4u;
                 }
@@ -1474,27 +1513,26 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
                     if (n > 0)
                         ok = mbar_wait_bounded(&empty_bar[s], static_cast<uint32_t>((n - 1) & 1), &misc.progress);
                     if (ok) {
-                        unsigned char* st = stages + static_cast<size_t>(s) * stage_bytes;
-                        *reinterpret_cast<RowMeta*>(st) = m;
-                        unsigned char* log_dst = st + kMetaBytes;
+                        unsigned char* log_dst = stages + static_cast<size_t>(s) * stage_bytes;
                         unsigned char* hist_dst = log_dst + p.stage_logit_bytes;
+                        metas[k % (2 * S_)] = m;
                         fence_proxy_async();
                         mbar_arrive_expect_tx(&full_bar[s], bytes);
-                        if (!m.direct && !m.deferred) {
-                            const int V = sg->vocab;
+                        if (!m.direct && !m.deferred && m.opt_ok) {
+                            const int V = m.V;
                             if (m.lo_al > 0)
-                                bulk_g2s(log_dst, row_ptr, static_cast<uint32_t>(m.lo_al * esize), &full_bar[s]);
+                                bulk_g2s(log_dst, m.row_ptr, static_cast<uint32_t>(m.lo_al * esize), &full_bar[s]);
                             if (m.kvw > 0)
-                                bulk_g2s(log_dst + m.lo_al * esize, row_ptr + static_cast<int64_t>(m.kbase) * esize,
+                                bulk_g2s(log_dst + m.lo_al * esize, m.row_ptr + static_cast<int64_t>(m.kbase) * esize,
                                          16u, &full_bar[s]);
                             if (V > m.hi_al)
                                 bulk_g2s(log_dst + (m.lo_al + m.kvw) * esize,
-                                         row_ptr + static_cast<int64_t>(m.hi_al) * esize,
+                                         m.row_ptr + static_cast<int64_t>(m.hi_al) * esize,
                                          static_cast<uint32_t>((V - m.hi_al) * esize), &full_bar[s]);
                         }
-                        if (m.hs_hi > m.hs_lo && !m.deferred)
-                            bulk_g2s(hist_dst, sg->hist_ids + m.hist_begin + m.hs_lo,
-                                     static_cast<uint32_t>(m.hs_hi - m.hs_lo) * 4u, &full_bar[s]);
+                        if (m.hs_hi > m.hs_lo && !m.deferred && m.opt_ok)
+                            bulk_g2s(hist_dst, m.hist + m.hs_lo, static_cast<uint32_t>(m.hs_hi - m.hs_lo) * 4u,
+                                     &full_bar[s]);
                         misc.issued = k + 1;
                     } else {
                         atomicOr(p.err, kErrTimeout);
@@ -1513,9 +1551,13 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
     // ================= element warps =================
     uint32_t st_greedy = 0, st_fast = 0, st_fast_exact = 0, st_general = 0, st_general_exact = 0, st_large = 0,
              st_overflow = 0;
+    // candidate threshold carried from the previous candidate row, and the (segment, option) it belongs to (-1:
+    // none); every element thread holds the same copy
+    int guess_id = -1;
+    float guess_tau = 0.0f;
     for (int k = 0; k < n_my; ++k) {
         const int s = k % S_;
-        unsigned char* st = stages + static_cast<size_t>(s) * stage_bytes;
+        unsigned char* sl = stages + static_cast<size_t>(s) * stage_bytes;
         const bool ok = mbar_wait_bounded(&full_bar[s], static_cast<uint32_t>((k / S_) & 1));
         if (cbar_or(!ok)) {
             if (tid == 0) {
@@ -1528,39 +1570,28 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
             cbar();
             break;
         }
-        RowMeta m;
-        {
-            const uint4* src = reinterpret_cast<const uint4*>(st);
-            uint4* dst = reinterpret_cast<uint4*>(&m);
-#pragma unroll
-            for (int i = 0; i < static_cast<int>(sizeof(RowMeta) / 16); ++i) dst[i] = src[i];
-        }
-        const DevSegment& g = p.seg[m.seg];
-        unsigned char* sl = st + kMetaBytes;
+        const RowMeta& m = metas[k % (2 * S_)];
         const int32_t* sh = reinterpret_cast<const int32_t*>(sl + p.stage_logit_bytes);
-        const int V = g.vocab;
-        const int dtype = g.dtype;
+        const int V = m.V;
+        const int dtype = m.dtype;
         const int VWe = dtype == 0 ? 4 : 8;
         const RowMap mp{m.lo_al, m.kvw, m.kbase, m.hi_al};
         const int NA = m.lo_al + m.kvw + (V - m.hi_al);
         const int nvec = (NA + VWe - 1) / VWe;   // bulk-copied rows have NA % VWe == 0
-        double* out_probs = g.out_probs ? g.out_probs + static_cast<int64_t>(m.local) * V : nullptr;
+        double* out_probs = m.out_probs;
 
         if (!m.opt_ok) {
-            if (tid == 0) {
-                atomicOr(p.err, kErrBadOption);
-                g.out_ids[m.local] = -1;
-            }
             cbar();
             if (tid == 0) {
+                atomicOr(p.err, kErrBadOption);
+                *m.out_id = -1;
                 mbar_arrive(&empty_bar[s]);
                 ++misc.progress;
             }
             continue;
         }
-        const DevOptions o = m.opt;
         if (!kGeneral && m.deferred) {
-            cbar();   // every thread has read the row's metadata
+            cbar();   // every thread is past the full-barrier wait of this stage
             if (tid == 0) {
                 p.deferred_rows[atomicAdd(p.deferred_count, 1u)] = m.row;
                 mbar_arrive(&empty_bar[s]);
@@ -1568,17 +1599,17 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
             }
             continue;
         }
+        const DevOptions o = m.opt;
 
         // ---- unaligned rows: the element warps stage the active ids themselves
         if (m.direct) {
-            const unsigned char* row = static_cast<const unsigned char*>(g.logits) +
-                                       static_cast<int64_t>(m.local) * g.row_stride * (dtype == 0 ? 4 : 2);
             for (int q = tid; q < nvec * VWe; q += kThreads) {
                 const int i = mp.idx(q);
                 if (dtype == 0)
-                    reinterpret_cast<float*>(sl)[q] = i < V ? reinterpret_cast<const float*>(row)[i] : neg_inf();
+                    reinterpret_cast<float*>(sl)[q] = i < V ? reinterpret_cast<const float*>(m.row_ptr)[i] : neg_inf();
                 else   // padding past V reads as bf16 -inf
-                    reinterpret_cast<uint16_t*>(sl)[q] = i < V ? reinterpret_cast<const uint16_t*>(row)[i] : 0xff80u;
+                    reinterpret_cast<uint16_t*>(sl)[q] =
+                        i < V ? reinterpret_cast<const uint16_t*>(m.row_ptr)[i] : 0xff80u;
             }
         }
 
@@ -1588,22 +1619,9 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
             if (m.direct) cbar();   // the staged copy is complete before ids update it in place
             const bool inplace = dtype == 0;
             const float pen = o.rep_penalty;
-            const double pen_rcp = __drcp_rn(static_cast<double>(o.rep_penalty));
+            const double pen_rcp = m.pen_rcp;
             float* sf = reinterpret_cast<float*>(sl);
             bool bad = false;
-            auto visit = [&](int id) {
-                if (static_cast<unsigned>(id) >= static_cast<unsigned>(V)) {
-                    bad = true;
-                    return;
-                }
-                const uint32_t bit = 1u << (id & 31);
-                const uint32_t old = atomicOr(&bitmap[id >> 5], bit);
-                if (inplace && !(old & bit)) {
-                    const int q = mp.pos(id);
-                    if (q >= 0) sf[q] = penalize(sf[q], pen, pen_rcp);
-                }
-            };
-            const int32_t* gh = g.hist_ids + m.hist_begin;
             const int nst = m.hs_hi - m.hs_lo;
             for (int c4 = tid; c4 < nst / 4; c4 += kThreads) {
                 const int4 v = reinterpret_cast<const int4*>(sh)[c4];
@@ -1625,36 +1643,39 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
                 }
             }
             const int rest = m.hist_len - nst;   // ids outside the staged span: [0, hs_lo) and [hs_hi, len)
-            for (int q = tid; q < rest; q += kThreads) visit(gh[q < m.hs_lo ? q : q - m.hs_lo + m.hs_hi]);
+            for (int q = tid; q < rest; q += kThreads) {
+                const int id = m.hist[q < m.hs_lo ? q : q - m.hs_lo + m.hs_hi];
+                if (static_cast<unsigned>(id) >= static_cast<unsigned>(V)) {
+                    bad = true;
+                    continue;
+                }
+                const uint32_t bit = 1u << (id & 31);
+                const uint32_t old = atomicOr(&bitmap[id >> 5], bit);
+                if (inplace && !(old & bit)) {
+                    const int q2 = mp.pos(id);
+                    if (q2 >= 0) sf[q2] = penalize(sf[q2], pen, pen_rcp);
+                }
+            }
             if (bad) atomicOr(p.err, kErrHistRange);
         }
         if (m.pen_on || m.direct) cbar();
 
         RowCtx c;
         c.vocab = V;
-        c.kind = g.kind;
-        c.sup_lo = g.sup_lo;
-        c.sup_hi = g.sup_hi;
-        c.eos = g.eos;
-        c.eos_blocked = m.step < g.min_new;
+        c.kind = m.kind;
+        c.sup_lo = m.sup_lo;
+        c.sup_hi = m.sup_hi;
+        c.eos = m.eos;
+        c.eos_blocked = m.eos_blocked != 0;
         c.pen_on = m.pen_on != 0 && dtype != 0;   // per element only for bf16 rows
         c.pen = o.rep_penalty;
-        c.pen_rcp = __drcp_rn(static_cast<double>(o.rep_penalty));
+        c.pen_rcp = m.pen_rcp;
         c.sample = o.do_sample != 0;
-        c.inv_t = __fdiv_rn(1.0f, o.temperature);
+        c.inv_t = m.inv_t;
         c.bitmap = bitmap;
-        c.slow_vlo = c.slow_vhi = 0;
-        c.eos_vec = -1;
-        if (g.kind == 0) {
-            if (g.sup_lo < g.sup_hi) {   // staged positions [sup_lo, lo_al + kvw + (sup_hi - hi_al)) may be suppressed
-                c.slow_vlo = g.sup_lo / VWe;
-                c.slow_vhi = (m.lo_al + m.kvw + max(g.sup_hi - m.hi_al, 0) + VWe - 1) / VWe;
-            }
-            if (c.eos_blocked && g.eos >= 0 && g.eos < V) {
-                const int ep = mp.pos(g.eos);
-                if (ep >= 0) c.eos_vec = ep / VWe;
-            }
-        }
+        c.slow_vlo = m.slow_vlo;
+        c.slow_vhi = m.slow_vhi;
+        c.eos_vec = m.eos_vec;
 
         char* gbase = p.gscratch + static_cast<int64_t>(blockIdx.x) * p.gscratch_stride;
         const int vpad = (max(p.vmax, kRegElems * kThreads) + 31) & ~31;
@@ -1699,7 +1720,7 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
                 res = exact_block_path(c, o, m.uniform, mx, gx, gp, gs, sort_n, out_probs, misc, tid);
             }
             if (tid == 0) {
-                g.out_ids[m.local] = res;
+                *m.out_id = res;
                 ++misc.progress;
             }
             ++st_large;
@@ -1707,20 +1728,46 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
             continue;
         }
 
+        const int K = o.top_k;
+        const bool cand_row = !kGeneral && c.sample && K > 0 && K < V && K <= kSmallK;
+        // A candidate threshold carried from this CTA's previous row of the same segment and option: any tau with
+        // K <= count(x >= tau) <= 128 is exact (the K-th largest is then >= tau), so the candidates can be collected
+        // during the element pass; otherwise the threshold is derived from this row below.
+        const int gid = m.seg * 65536 + m.opt_idx;
+        const bool fuse = cand_row && guess_id == gid;
+        const float tau_g = guess_tau;
+        uint32_t* const ccount = &misc.cand_count[k & 1];
         float x[kRegElems];
         float tmax = neg_inf(), tmax2 = neg_inf();   // the two largest values of this thread
         float bestv = neg_inf();
         int besti = 0x7fffffff;
         if (c.sample) {
-            if (dtype == 0)
-                process_vectors<4, true>(sl, nvec, mp, c, tid, x, tmax, tmax2, bestv, besti);
-            else
-                process_vectors<8, true>(sl, nvec, mp, c, tid, x, tmax, tmax2, bestv, besti);
+            if (fuse) {
+                if (dtype == 0)
+                    process_vectors<4, true, true>(sl, nvec, mp, c, tid, x, tmax, tmax2, bestv, besti, tau_g,
+                                                   ccount, ckey);
+                else
+                    process_vectors<8, true, true>(sl, nvec, mp, c, tid, x, tmax, tmax2, bestv, besti, tau_g,
+                                                   ccount, ckey);
+            } else {
+                if (dtype == 0)
+                    process_vectors<4, true, false>(sl, nvec, mp, c, tid, x, tmax, tmax2, bestv, besti, 0.0f,
+                                                    nullptr, nullptr);
+                else
+                    process_vectors<8, true, false>(sl, nvec, mp, c, tid, x, tmax, tmax2, bestv, besti, 0.0f,
+                                                    nullptr, nullptr);
+            }
         } else {
             if (dtype == 0)
-                process_vectors<4, false>(sl, nvec, mp, c, tid, x, tmax, tmax2, bestv, besti);
+                process_vectors<4, false, false>(sl, nvec, mp, c, tid, x, tmax, tmax2, bestv, besti, 0.0f, nullptr,
+                                                 nullptr);
             else
-                process_vectors<8, false>(sl, nvec, mp, c, tid, x, tmax, tmax2, bestv, besti);
+                process_vectors<8, false, false>(sl, nvec, mp, c, tid, x, tmax, tmax2, bestv, besti, 0.0f, nullptr,
+                                                 nullptr);
+        }
+        if (cand_row) {   // row maximum, published with the pass's barrier
+            const float wm = warp_max_f(tmax);
+            if (lane == 0) misc.red_f[5][warp] = wm;
         }
         cbar();   // the stage has been read
         if (m.pen_on)
@@ -1737,81 +1784,100 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
             if (out_probs)
                 for (int i = tid; i < V; i += kThreads) out_probs[i] = 0.0;
             if (tid == 0) {
-                g.out_ids[m.local] = res;
+                *m.out_id = res;
                 ++misc.progress;
             }
             ++st_greedy;
             continue;
         }
 
-        const int K = o.top_k;
         bool handed = false;
-        if (!kGeneral && K > 0 && K < V && K <= kSmallK) {
+        if (cand_row) {
             release();   // the candidate path no longer reads the stage
-            // tau_w = ceil(K/4)-th largest of the warp's 64 per-thread top-2 values: >= ceil(K/4) distinct
-            // elements of this warp are >= tau_w, so >= K elements of the row are >= min over warps
-            const int cw = (K + kWarps - 1) / kWarps;
-            uint32_t lk[2] = {~okey(tmax), ~okey(tmax2)};
-            warp_sort32<2>(lk, lane);
-            const float tw = okey_inv(~__shfl_sync(kFull, lk[0], cw - 1));
-            const float wm = okey_inv(~__shfl_sync(kFull, lk[0], 0));   // warp maximum
-            if (lane == 0) {
-                misc.tau_w[warp] = tw;
-                misc.red_f[5][warp] = wm;
-            }
-            cbar();
-            float tau = misc.tau_w[0], mx = misc.red_f[5][0];
+            float mx = misc.red_f[5][0];
 #pragma unroll
-            for (int w = 1; w < kWarps; ++w) {
-                tau = fminf(tau, misc.tau_w[w]);
-                mx = fmaxf(mx, misc.red_f[5][w]);
-            }
-            if (!is_neg_inf(tau)) {
-                // ---- candidates x >= tau -> shared keys okey(x) << 32 | id
-#pragma unroll
-                for (int e = 0; e < kRegElems; ++e) {
-                    if (x[e] >= tau) {
-                        const uint32_t pos = atomicAdd(&misc.cand_count, 1u);
-                        if (pos < static_cast<uint32_t>(kCandCap)) {
-                            const int gg = e / VWe;
-                            const int qv = tid + gg * kThreads;
-                            ckey[pos] = (static_cast<unsigned long long>(okey(x[e])) << 32) |
-                                        static_cast<uint32_t>(mp.idx(qv * VWe + (e - gg * VWe)));
-                        }
-                    }
-                }
+            for (int w = 1; w < kWarps; ++w) mx = fmaxf(mx, misc.red_f[5][w]);
+            int C = fuse ? static_cast<int>(*ccount) : 0;
+            if (!fuse || C < K || C > kCandCap) {
+                // no usable carried threshold: tau = min over warps of the ceil(K/4)-th largest of each warp's 64
+                // per-thread top-2 values (>= ceil(K/4) distinct elements of each warp are >= it, so >= K elements
+                // of the row are >= tau)
+                cbar();   // every thread has read the fused count
+                if (tid == 0) *ccount = 0;
+                const int cw = (K + kWarps - 1) / kWarps;
+                uint32_t lk[2] = {~okey(tmax), ~okey(tmax2)};
+                warp_sort32<2>(lk, lane);
+                const float tw = okey_inv(~__shfl_sync(kFull, lk[0], cw - 1));
+                if (lane == 0) misc.tau_w[warp] = tw;
                 cbar();
-                const int C = static_cast<int>(misc.cand_count);
-                cbar();   // every thread has read the count
-                if (tid == 0) misc.cand_count = 0;
-                if (C <= kCandCap) {
-                    int res = p.force_exact ? -1 : cand_parallel(ckey, C, K, o, m.uniform, mx, out_probs, V,
-                                                                misc.u.cw, tid);
-                    if (res < 0) {
-                        if (warp == 0) {
-                            const int rr = replay_candidates(ckey, C, K, o, m.uniform, V, out_probs, misc.flags, lane);
-                            if (lane == 0) misc.bc_i[3] = rr;
+                float tau = misc.tau_w[0];
+#pragma unroll
+                for (int w = 1; w < kWarps; ++w) tau = fminf(tau, misc.tau_w[w]);
+                C = kCandCap + 1;
+                if (!is_neg_inf(tau)) {
+                    // ---- candidates x >= tau -> shared keys okey(x) << 32 | id
+#pragma unroll
+                    for (int e = 0; e < kRegElems; ++e) {
+                        if (x[e] >= tau) {
+                            const uint32_t pos = atomicAdd(ccount, 1u);
+                            if (pos < static_cast<uint32_t>(kCandCap)) {
+                                const int gg = e / VWe;
+                                const int qv = tid + gg * kThreads;
+                                ckey[pos] = (static_cast<unsigned long long>(okey(x[e])) << 32) |
+                                            static_cast<uint32_t>(mp.idx(qv * VWe + (e - gg * VWe)));
+                            }
                         }
-                        cbar();
-                        res = misc.bc_i[3];
-                        ++st_fast_exact;
-                    } else {
-                        ++st_fast;
                     }
-                    if (tid == 0) g.out_ids[m.local] = res;
-                    handed = true;
+                    cbar();
+                    C = static_cast<int>(*ccount);
                 }
             }
-            if (!handed) {   // no finite tau or too many candidates: the whole-row kernel takes the row
+            if (C <= kCandCap) {
+                // every thread read C before the first barrier inside cand_parallel / the replay; the counter is
+                // next used two rows on, and the row between always passes a barrier
+                const bool par = !p.force_exact;
+                int res = par ? cand_parallel(ckey, C, K, o, m.uniform, mx, out_probs, V, misc.u.cw, tid) : -1;
+                if (res < 0) {
+                    if (warp == 0) {
+                        const int rr = replay_candidates(ckey, C, K, o, m.uniform, V, out_probs, misc.flags, lane);
+                        if (lane == 0) misc.bc_i[3] = rr;
+                    }
+                    cbar();
+                    res = misc.bc_i[3];
+                    ++st_fast_exact;
+                } else {
+                    ++st_fast;
+                }
+                if (tid == 0) {
+                    *m.out_id = res;
+                    *ccount = 0;
+                }
+                // carry a threshold to the next row: the candidate ranked ~1.25 K from the top (or the lowest), so
+                // that a similar row collects ~1.25 K candidates (cand_parallel left them in ascending order)
+                guess_id = -1;
+                if (par) {
+                    const int target = K + (K >> 2) + 4;
+                    const float g = okey_inv(static_cast<uint32_t>(misc.u.cw.pk[C >= target ? C - target : 0] >> 32));
+                    if (!is_neg_inf(g)) {
+                        guess_tau = g;
+                        guess_id = gid;
+                    }
+                }
+            } else {   // no finite tau or too many candidates: the whole-row kernel takes the row
+                cbar();   // every thread has read the count
                 ++st_overflow;
-                if (tid == 0) p.deferred_rows[atomicAdd(p.deferred_count, 1u)] = m.row;
-                handed = true;
+                if (tid == 0) {
+                    p.deferred_rows[atomicAdd(p.deferred_count, 1u)] = m.row;
+                    *ccount = 0;
+                }
+                guess_id = -1;
             }
+            handed = true;
         }
         if (kGeneral && !handed) {
             const float mx = block_max_f(tmax, misc, 0, lane, warp);
             // numerator cache: the consumed stage when it is large enough, else this CTA's global scratch
-            const bool in_stage = !released && (stage_bytes - kMetaBytes) >= kRegElems * kThreads * 8;
+            const bool in_stage = !released && stage_bytes >= kRegElems * kThreads * 8;
             double* ecache = in_stage ? reinterpret_cast<double*>(sl) : gp;
             if (!in_stage) release();
             int res = -1;
@@ -1832,7 +1898,7 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
                 cbar();
                 res = exact_block_path(c, o, m.uniform, mx, gx, gp, gs, sort_n, out_probs, misc, tid);
             }
-            if (tid == 0) g.out_ids[m.local] = res;
+            if (tid == 0) *m.out_id = res;
         }
         if (tid == 0) ++misc.progress;
     }
@@ -1882,8 +1948,9 @@ __global__ void __launch_bounds__(256) penalty_kernel(float* logits, int vocab, 
 
 // ---------------------------------------------------------------- host-side launch helpers
 size_t sampler_smem_bytes(const LaunchParams& p) {
-    const size_t stage = kMetaBytes + static_cast<size_t>(p.stage_logit_bytes) + static_cast<size_t>(p.stage_hist_cap) * 4;
+    const size_t stage = static_cast<size_t>(p.stage_logit_bytes) + static_cast<size_t>(p.stage_hist_cap) * 4;
     size_t b = stage * p.n_stages;
+    b += sizeof(RowMeta) * 2 * p.n_stages;
     b += sizeof(uint64_t) * (2 * p.n_stages);
     b += sizeof(uint32_t) * ((p.bitmap_words + 3) & ~3);
     b += sizeof(unsigned long long) * kCandCap;
