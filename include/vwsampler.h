@@ -147,6 +147,31 @@ vw_status vw_synchronize(vw_handle* handle, void* stream);
 vw_status vw_get_stats(vw_handle* handle, vw_stats* out, int32_t reset);
 
 /*
+ * vw_sample for callers that cannot allocate device memory: a process whose memory is all held by its own pool
+ * (a serving engine that reserves the free HBM up front), a host runtime whose binding exposes no device
+ * allocator, or code inside a region where allocation is forbidden.  No counterpart in the reference: voxwerk
+ * samples on the CPU and manages no device memory.  Results are vw_sample's.
+ *
+ * The call takes no handle and allocates nothing.  Its scratch is one fixed device array per device (about
+ * 16.4 MiB, built into the library, loaded on first use); the first call on a device looks up that array's
+ * address, so make that first call before any stream capture.
+ *
+ * Limits (larger requests fail with VW_ERR_INVALID_ARG and a message): at most 65536 rows per call over all
+ * segments, vocab <= 4096, n_options <= 32.  Every array is device memory of `device` (as VW_MEM_DEVICE); there
+ * is no host-memory mode.
+ *
+ * stream: a cudaStream_t of `device`, or NULL for the default stream.  The call returns after the stream has
+ *   finished it, reporting device-side errors in its status.
+ * err_msg / err_msg_len: optional buffer for a NUL-terminated message ("" on success).
+ *
+ * Calls on one device share the array: two calls that overlap in time (from two host threads, say) race and
+ * both results are undefined.  Serialise them per device.
+ */
+vw_status vw_sample_static(int32_t device, const vw_segment* segments, int32_t n_segments,
+                           const vw_options* options, int32_t n_options, void* stream, char* err_msg,
+                           int32_t err_msg_len);
+
+/*
  * Single-row mirrors of the reference's Sampler methods, for callers that keep the reference's call shape.
  * Pointers follow `mem`; the calls are synchronous.
  */

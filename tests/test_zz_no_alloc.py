@@ -1,0 +1,85 @@
+"""vw_sample_static, the entry point that allocates no device memory, against vw_sample on the same inputs.
+
+Kept in its own file, collected last, so that it runs both after every other test (the library's shared static
+scratch has then seen other calls) and alone.  Ids must be identical; probabilities within the 1e-6 relative
+tolerance of the parity tests.  Each workload runs through vw_sample_static twice in a row.
+"""
+
+import numpy as np
+import pytest
+
+from tests.gpu_util import make_segment, options_table, to_device
+from voxwerk_b200 import Segment, VwInvalidArgument, sample_rows, sample_rows_static, workloads
+from voxwerk_b200._lib import VW_ROWS_SUB, VwOptions
+
+PROB_RTOL = 1e-6
+
+
+def _run(w, call, want_probs):
+    import torch
+    segs, outs, probs = [], [], []
+    for seg in w.segments:
+        arr = to_device(seg, torch)
+        pr = torch.zeros((seg.n_rows, seg.vocab), dtype=torch.float64, device="cuda") if want_probs else None
+        segs.append(make_segment(seg, arr, pr))
+        outs.append(arr["out_ids"])
+        probs.append(pr)
+    call(segs, options_table(w))
+    torch.cuda.synchronize()
+    return [o.cpu().numpy() for o in outs], [p.cpu().numpy() if p is not None else None for p in probs]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("cfg,rows,want_probs", [(0, None, True), (1, None, True), (2, 1024, False), (2, 96, True),
+                                                 (3, None, False), (4, 1024, False), (4, 96, True)])
+def test_static_matches_vw_sample_twice(device, cfg, rows, want_probs):
+    w = workloads.make(cfg, rows)
+    ref_ids, ref_probs = _run(w, lambda s, o: sample_rows(device, s, o), want_probs)
+    for call in range(2):
+        ids, probs = _run(w, lambda s, o: sample_rows_static(0, s, o), want_probs)
+        for k, (g, r) in enumerate(zip(ids, ref_ids)):
+            bad = np.flatnonzero(g != r)
+            assert bad.size == 0, f"{w.name} call {call} segment {k}: {bad.size} ids differ, rows {bad[:10]}"
+        if want_probs:
+            for g, r in zip(probs, ref_probs):
+                np.testing.assert_allclose(g, r, rtol=PROB_RTOL, atol=0.0)
+
+
+@pytest.mark.gpu
+def test_static_rejects_sizes_beyond_its_limits(device):
+    import torch
+    opts = [VwOptions(1, 50, 0.8, 0.9, 1.0)]
+    logits = torch.zeros((4, 8192), dtype=torch.float32, device="cuda")
+    out = torch.zeros(4, dtype=torch.int32, device="cuda")
+    uni = torch.zeros(4, dtype=torch.float64, device="cuda")
+    big_vocab = Segment(logits, kind=VW_ROWS_SUB, vocab=8192, out_ids=out, uniforms=uni)
+    with pytest.raises(VwInvalidArgument, match="vocab 8192 exceeds"):
+        sample_rows_static(0, [big_vocab], opts)
+    many = torch.zeros((65537, 16), dtype=torch.float32, device="cuda")
+    seg = Segment(many, kind=VW_ROWS_SUB, vocab=16, out_ids=torch.zeros(65537, dtype=torch.int32, device="cuda"),
+                  uniforms=torch.zeros(65537, dtype=torch.float64, device="cuda"))
+    with pytest.raises(VwInvalidArgument, match="65537 rows exceed"):
+        sample_rows_static(0, [seg], opts)
+    small = torch.zeros((4, 2048), dtype=torch.float32, device="cuda")
+    with pytest.raises(VwInvalidArgument, match="at most 32 options"):
+        sample_rows_static(0, [Segment(small, kind=VW_ROWS_SUB, vocab=2048, out_ids=out, uniforms=uni)], opts * 33)
+
+
+def test_static_limits_checked_before_any_device_work():
+    """The row limit is enforced on the host, before the device is touched (runs without a GPU)."""
+    import ctypes
+    from voxwerk_b200._lib import VwSegment, lib, VW_ERR_INVALID_ARG, VW_F32
+    seg = VwSegment()
+    seg.logits = 1 << 20
+    seg.row_stride = 16
+    seg.n_rows = 70000
+    seg.vocab = 16
+    seg.dtype = VW_F32
+    seg.kind = VW_ROWS_SUB
+    seg.out_ids = 1 << 21
+    seg.uniforms = 1 << 22
+    opts = (VwOptions * 1)(VwOptions(1, 5, 0.8, 0.9, 1.0))
+    msg = ctypes.create_string_buffer(256)
+    st = lib.vw_sample_static(0, (VwSegment * 1)(seg), 1, opts, 1, None, msg, len(msg))
+    assert st == VW_ERR_INVALID_ARG
+    assert b"70000 rows exceed" in msg.value

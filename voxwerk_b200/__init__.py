@@ -9,11 +9,11 @@ from ._lib import (VW_BF16, VW_F32, VW_MEM_DEVICE, VW_MEM_HOST, VW_ROWS_SUB, VW_
                    VwInvalidArgument, VwOutOfRange)
 from .sampler import (CODEC_EOS_ID, CP_VOCAB_SIZE, MIN_NEW_TOKENS, NUM_CODE_GROUPS, VOCAB_SIZE, Device,
                       DotNetRandom, GenerationOptions, Sampler, SamplingOptions, Segment, TalkerBatchSampler,
-                      sample_rows, vw_options)
+                      sample_rows, sample_rows_static, vw_options)
 
 __all__ = [
     "VW_BF16", "VW_F32", "VW_MEM_DEVICE", "VW_MEM_HOST", "VW_ROWS_SUB", "VW_ROWS_TALKER", "VwError",
     "VwInvalidArgument", "VwOutOfRange", "CODEC_EOS_ID", "CP_VOCAB_SIZE", "MIN_NEW_TOKENS", "NUM_CODE_GROUPS",
     "VOCAB_SIZE", "Device", "DotNetRandom", "GenerationOptions", "Sampler", "SamplingOptions", "Segment",
-    "TalkerBatchSampler", "sample_rows", "vw_options",
+    "TalkerBatchSampler", "sample_rows", "sample_rows_static", "vw_options",
 ]

@@ -40,6 +40,7 @@ EXPORTED = (
     "vw_apply_repetition_penalty",
     "vw_select",
     "vw_argmax",
+    "vw_sample_static",
 )
 
 
@@ -145,6 +146,9 @@ def _load() -> ctypes.CDLL:
                               ctypes.POINTER(i32)]
     lib.vw_argmax.restype = ctypes.c_int
     lib.vw_argmax.argtypes = [vp, vp, i32, i32, ctypes.POINTER(i32)]
+    lib.vw_sample_static.restype = ctypes.c_int
+    lib.vw_sample_static.argtypes = [i32, ctypes.POINTER(VwSegment), i32, ctypes.POINTER(VwOptions), i32, vp,
+                                     ctypes.c_char_p, i32]
     return lib
 
 

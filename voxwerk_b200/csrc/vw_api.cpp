@@ -589,3 +589,200 @@ VW_EXPORT vw_status vw_argmax(vw_handle* h, const float* logits, int32_t vocab, 
     o.repetition_penalty = 1.0f;
     return vw_select(h, logits, vocab, &o, 0.0, mem, out_id);
 }
+
+// ------------------------------------------------------------------------------------- vw_sample_static
+// vw_sample for callers that must not allocate device memory: no handle, device pointers only, and the kernels'
+// scratch (error word, deferred-row list, whole-row slices) in the fixed array of vw_static.cu.
+namespace {
+
+constexpr int kStaticMaxDevices = 64;
+
+struct StaticDevice {
+    bool ready = false;
+    char* scratch = nullptr;   // device address of the array on this device
+    int sm_count = 0;
+};
+
+std::mutex g_static_mutex;
+StaticDevice g_static_devices[kStaticMaxDevices];
+
+void copy_message(const vw_handle& h, char* err_msg, int32_t err_msg_len) {
+    if (!err_msg || err_msg_len <= 0) return;
+    const size_t n = std::min(h.last_error.size(), static_cast<size_t>(err_msg_len - 1));
+    std::memcpy(err_msg, h.last_error.data(), n);
+    err_msg[n] = '\0';
+}
+
+// One-time set-up of `device` (current): the array's device address and the SM count.
+vw_status static_setup(vw_handle* h, int device, StaticDevice* out) {
+    std::lock_guard<std::mutex> lock(g_static_mutex);
+    StaticDevice& d = g_static_devices[device];
+    if (!d.ready) {
+        char* ptr = nullptr;
+        cudaError_t e = vw::static_scratch_address(&ptr);
+        if (e != cudaSuccess) return cuda_fail(h, e, "cudaGetSymbolAddress of the static scratch");
+        if (!ptr) return fail(h, VW_ERR_CUDA, "cudaGetSymbolAddress returned NULL");
+        int sms = 0;
+        e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+        if (e != cudaSuccess) return cuda_fail(h, e, "cudaDeviceGetAttribute");
+        d.scratch = ptr;
+        d.sm_count = sms;
+        d.ready = true;
+    }
+    *out = d;
+    return VW_OK;
+}
+
+vw_status sample_static_impl(vw_handle* h, int32_t device, const vw_segment* segs, int32_t n_segs,
+                             const vw_options* opts, int32_t n_opts, void* stream) {
+    if (!segs || n_segs < 1 || n_segs > vw::kMaxSegments)
+        return fail(h, VW_ERR_INVALID_ARG, "n_segments must be in [1, VW_MAX_SEGMENTS]");
+    bool any_sample = false;
+    vw_status r = check_options(h, opts, n_opts, &any_sample);
+    if (r != VW_OK) return r;
+    if (n_opts > vw::kInlineOptions)
+        return fail(h, VW_ERR_INVALID_ARG, "vw_sample_static takes at most " + std::to_string(vw::kInlineOptions) +
+                                               " options (got " + std::to_string(n_opts) + ")");
+    int64_t total = 0;
+    for (int i = 0; i < n_segs; ++i) {
+        r = check_segment(h, segs[i], i, n_opts, any_sample, VW_MEM_DEVICE);
+        if (r != VW_OK) return r;
+        if (segs[i].n_rows > 0 && segs[i].vocab > vw::kStaticMaxVocab)
+            return fail(h, VW_ERR_INVALID_ARG, "segment " + std::to_string(i) + ": vocab " +
+                                                   std::to_string(segs[i].vocab) + " exceeds vw_sample_static's maximum " +
+                                                   std::to_string(vw::kStaticMaxVocab));
+        total += segs[i].n_rows;
+    }
+    if (total > vw::kStaticMaxRows)
+        return fail(h, VW_ERR_INVALID_ARG, std::to_string(total) + " rows exceed vw_sample_static's maximum of " +
+                                               std::to_string(vw::kStaticMaxRows) + " rows per call");
+    if (total == 0) return VW_OK;
+
+    int n_dev = 0;
+    if (cudaGetDeviceCount(&n_dev) != cudaSuccess || device < 0 || device >= n_dev || device >= kStaticMaxDevices)
+        return fail(h, VW_ERR_NO_DEVICE, "no CUDA device " + std::to_string(device));
+    DeviceGuard guard(device);
+    if (!guard.ok()) return fail(h, VW_ERR_CUDA, "cudaSetDevice failed");
+    int major = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device) != cudaSuccess || major != 10)
+        return fail(h, VW_ERR_NO_DEVICE, "device " + std::to_string(device) + " is not an sm_100 device");
+    StaticDevice sd;
+    r = static_setup(h, device, &sd);
+    if (r != VW_OK) return r;
+    // the logits and the ids must be device memory of this device (host memory would need staging buffers)
+    for (int i = 0; i < n_segs; ++i) {
+        if (segs[i].n_rows == 0) continue;
+        const void* ptrs[2] = {segs[i].logits, segs[i].out_ids};
+        for (const void* q : ptrs) {
+            cudaPointerAttributes a;
+            if (cudaPointerGetAttributes(&a, q) != cudaSuccess ||
+                (a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged) || a.device != device) {
+                cudaGetLastError();
+                return fail(h, VW_ERR_INVALID_ARG, "segment " + std::to_string(i) +
+                                                       ": logits and out_ids must be device memory of device " +
+                                                       std::to_string(device));
+            }
+        }
+    }
+
+    vw::LaunchParams p;
+    std::memset(&p, 0, sizeof p);
+    int row_begin = 0, vmax = 1, logit_bytes = 16, hist_cap = 0;
+    bool any_pen = false;
+    for (int i = 0; i < n_opts; ++i) any_pen |= opts[i].repetition_penalty != 1.0f;
+    int nd = 0;
+    for (int i = 0; i < n_segs; ++i) {
+        const vw_segment& s = segs[i];
+        if (s.n_rows == 0) continue;
+        vw::DevSegment& d = p.seg[nd++];
+        const bool talker = s.kind == VW_ROWS_TALKER;
+        d.logits = s.logits;
+        d.hist_offsets = talker ? s.hist_offsets : nullptr;
+        d.hist_ids = talker ? s.hist_ids : nullptr;
+        d.steps = talker ? s.steps : nullptr;
+        d.opt_index = s.opt_index;
+        d.uniforms = s.uniforms;
+        d.out_ids = s.out_ids;
+        d.out_probs = s.out_probs;
+        d.row_stride = s.row_stride;
+        d.row_begin = row_begin;
+        d.n_rows = s.n_rows;
+        d.vocab = s.vocab;
+        d.dtype = s.dtype;
+        d.kind = s.kind;
+        d.sup_lo = talker ? std::clamp(s.suppress_lo, 0, s.vocab) : 0;
+        d.sup_hi = talker ? std::clamp(s.suppress_hi, 0, s.vocab) : 0;
+        if (d.sup_hi < d.sup_lo) d.sup_hi = d.sup_lo;
+        d.eos = talker ? s.eos_id : -1;
+        d.min_new = talker ? s.min_new_tokens : 0;
+        const size_t es = s.dtype == VW_F32 ? 4 : 2;
+        d.bulk_ok = aligned(s.logits, 16) && (s.row_stride * es) % 16 == 0 && (s.vocab * es) % 16 == 0;
+        d.hist_aligned = d.hist_ids ? aligned(d.hist_ids, 16) : 0;
+        row_begin += s.n_rows;
+        vmax = std::max(vmax, s.vocab);
+        const int vwe = s.dtype == VW_F32 ? 4 : 8;
+        logit_bytes = std::max(logit_bytes, (staged_elems(s) + vwe - 1) / vwe * 16);
+        if (talker && s.hist_offsets && any_pen) {
+            const int hint = s.max_hist_len > 0 ? s.max_hist_len : 1024;
+            hist_cap = std::max(hist_cap, static_cast<int>(round_up(std::min(hint, vw::kMaxHistStage), 4)));
+        }
+    }
+    p.n_segs = nd;
+    p.total_rows = row_begin;
+    p.n_opts = n_opts;
+    std::memcpy(p.inl_opts, opts, sizeof(vw_options) * n_opts);
+    p.stage_logit_bytes = logit_bytes;
+    p.stage_hist_cap = hist_cap;
+    p.bitmap_words = (vmax + 31) / 32;
+    p.vmax = vmax;
+    p.stats = nullptr;
+    const char* fe = std::getenv("VW_FORCE_EXACT");
+    p.force_exact = (fe && fe[0] == '1') ? 1 : 0;
+
+    int ctas = 0, ctas_g = 0;
+    size_t smem = 0;
+    for (int stages = vw::kStages; stages >= 2 && (ctas == 0 || ctas_g == 0); --stages) {
+        p.n_stages = stages;
+        smem = vw::sampler_smem_bytes(p);
+        ctas = vw::sampler_ctas_per_sm(smem, false);
+        ctas_g = vw::sampler_ctas_per_sm(smem, true);
+    }
+    if (ctas == 0 || ctas_g == 0) return fail(h, VW_ERR_INVALID_ARG, "rows too large for shared memory");
+    const int grid = static_cast<int>(std::min<int64_t>(p.total_rows, static_cast<int64_t>(sd.sm_count) * ctas));
+    const int grid_g = static_cast<int>(std::min<int64_t>(
+        {static_cast<int64_t>(p.total_rows), static_cast<int64_t>(sd.sm_count) * ctas_g, vw::kStaticGeneralCtas}));
+    p.gscratch_stride = vw::sampler_gscratch_stride(vmax);
+    if (p.gscratch_stride > vw::kStaticCtaStride)
+        return fail(h, VW_ERR_INVALID_ARG, "vocab too large for the static scratch");
+    p.err = reinterpret_cast<unsigned*>(sd.scratch);
+    p.deferred_count = reinterpret_cast<uint32_t*>(sd.scratch) + 1;
+    p.done_count = reinterpret_cast<uint32_t*>(sd.scratch) + 2;
+    p.deferred_rows = reinterpret_cast<int32_t*>(sd.scratch + vw::kStaticRowsOffset);
+    p.gscratch = sd.scratch + vw::kStaticScratchOffset;
+
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // the error word and both counters must start at zero (an earlier call that timed out may have left them set)
+    cudaError_t e = cudaMemsetAsync(sd.scratch, 0, 4 * sizeof(uint32_t), st);
+    if (e == cudaSuccess) e = vw::launch_sampler(p, grid, smem, grid_g, st);
+    if (e != cudaSuccess) return cuda_fail(h, e, "sampler launch");
+    unsigned bits = 0;   // pageable host word: the copy completes before cudaMemcpyAsync returns or at the sync
+    e = cudaMemcpyAsync(&bits, sd.scratch, sizeof(unsigned), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_fail(h, e, "synchronize");
+    if (bits & vw::kErrTimeout) return fail(h, VW_ERR_TIMEOUT, "a bounded wait in the sampler kernel gave up");
+    if (bits & vw::kErrHistRange) return fail(h, VW_ERR_OUT_OF_RANGE, "a history id is outside [0, vocab)");
+    if (bits & vw::kErrBadOption) return fail(h, VW_ERR_INVALID_ARG, "a row's opt_index is outside the options table");
+    return VW_OK;
+}
+
+}  // namespace
+
+VW_EXPORT vw_status vw_sample_static(int32_t device, const vw_segment* segments, int32_t n_segments,
+                                     const vw_options* options, int32_t n_options, void* stream, char* err_msg,
+                                     int32_t err_msg_len) {
+    vw_handle h;   // carries the message only; no device state
+    if (err_msg && err_msg_len > 0) err_msg[0] = '\0';
+    const vw_status r = sample_static_impl(&h, device, segments, n_segments, options, n_options, stream);
+    copy_message(h, err_msg, err_msg_len);
+    return r;
+}

@@ -98,6 +98,20 @@ int sampler_ctas_per_sm(size_t smem, bool general);
 // The candidate kernel over every row, then the whole-row kernel over the rows it deferred (stream-ordered).
 cudaError_t launch_sampler(const LaunchParams& p, int grid, size_t smem, int grid_general, cudaStream_t stream);
 
+// ---- fixed scratch of vw_sample_static: one file-scope device array per device, no allocation.
+// Layout: the error word and the two deferred-list counters at offset 0 (zeroed before every call), the deferred
+// rows at kStaticRowsOffset, then one kStaticCtaStride slice per whole-row CTA at kStaticScratchOffset.
+constexpr int kStaticMaxRows = 65536;       // rows per call (all segments)
+constexpr int kStaticMaxVocab = 4096;       // ids per row (a power of two >= kRegElems * kThreads)
+constexpr int kStaticGeneralCtas = 148;     // whole-row kernel CTAs (one per B200 SM)
+constexpr int64_t kStaticRowsOffset = 256;
+constexpr int64_t kStaticScratchOffset = kStaticRowsOffset + 4 * static_cast<int64_t>(kStaticMaxRows);
+// sampler_gscratch_stride(kStaticMaxVocab): 12 bytes per id plus a 16-byte sort slot per id
+constexpr int64_t kStaticCtaStride = (static_cast<int64_t>(kStaticMaxVocab) * 28 + 255) / 256 * 256;
+constexpr int64_t kStaticBytes = kStaticScratchOffset + kStaticGeneralCtas * kStaticCtaStride;   // ~16.4 MiB
+// Device address of this device's array (the device must be current); cudaGetSymbolAddress's status.
+cudaError_t static_scratch_address(char** ptr);
+
 // Sampler.ApplyRepetitionPenalty on one device row, in place.
 cudaError_t launch_apply_penalty(float* logits, int vocab, const int32_t* hist, int64_t hist_len, float penalty,
                                  unsigned* err, cudaStream_t stream);

@@ -277,6 +277,33 @@ def sample_rows(device: Device, segments: Sequence[Segment], options: Sequence[V
     check(lib.vw_sample(device.handle, segs, len(segments), opts, len(options), mem, st), device.handle)
 
 
+def sample_rows_static(device: int, segments: Sequence[Segment], options: Sequence[VwOptions],
+                       stream: Optional[int] = None) -> None:
+    """One vw_sample_static call: ``sample_rows`` on CUDA tensors of GPU `device`, without a handle and without any
+    device allocation (for processes whose device memory is all held elsewhere, e.g. by a serving engine's pool).
+
+    The library's fixed per-device scratch bounds a call to 65536 rows, vocab <= 4096 and 32 options.  The call
+    returns after `stream` (None: the default stream) has finished it.  Two calls on one device must not overlap
+    in time: they share that scratch.
+    """
+    if not 1 <= len(segments) <= _lib.VW_MAX_SEGMENTS:
+        raise ValueError("1..8 segments per call")
+    if _mem_of(segments) != VW_MEM_DEVICE:
+        raise ValueError("vw_sample_static takes device tensors only")
+    segs = (VwSegment * len(segments))(*[s.to_c(VW_MEM_DEVICE) for s in segments])
+    opts = (VwOptions * len(options))(*options)
+    msg = ctypes.create_string_buffer(512)
+    st = lib.vw_sample_static(device, segs, len(segments), opts, len(options),
+                              ctypes.c_void_p(stream) if stream else None, msg, len(msg))
+    if st != _lib.VW_OK:
+        text = msg.value.decode() or lib.vw_status_string(st).decode()
+        if st == _lib.VW_ERR_INVALID_ARG:
+            raise _lib.VwInvalidArgument(st, text)
+        if st == _lib.VW_ERR_OUT_OF_RANGE:
+            raise _lib.VwOutOfRange(st, text)
+        raise _lib.VwError(st, text)
+
+
 # ----------------------------------------------------------------------------- Sampler mirror
 _default_device: Optional[Device] = None
 
