@@ -108,6 +108,14 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def workload_keys(w) -> dict:
+    """The workload's shape and decoding settings for the JSON line's `config`."""
+    seg = w.segments[0]
+    hist = int(np.max(np.diff(seg.hist_offsets))) if seg.hist_offsets is not None else 0
+    opts = [dict(zip(("do_sample", "top_k", "top_p", "temperature", "repetition_penalty"), o)) for o in w.options]
+    return {"vocab": [s.vocab for s in w.segments], "history": hist, "options": opts}
+
+
 def cpu_reference(workload, seconds: float, threads: int):
     """Times the CPU restatement (oracle port) on repeated passes over the workload's rows."""
     from oracle import oracle
@@ -142,7 +150,7 @@ def run_reference_arm(args):
         "metric": METRIC, "value": value, "unit": "rows/s", "impl": "reference", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": w.name, "rows_per_step": w.n_rows, "vocab": 3072},
+        "config": {"workload": w.name, "rows_per_step": w.n_rows, **workload_keys(w)},
         "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads, "kind": "port", "sample": sample,
                          "what": "C++ restatement of voxwerk Sampler.cs (oracle/vw_oracle.cpp); the C# reference "
                                  "cannot be built or run in this environment"},
@@ -179,6 +187,7 @@ def main():
 
     from tests.gpu_util import make_segment, options_table, to_device
     from voxwerk_b200 import Device, sample_rows, workloads
+    from voxwerk_b200.shard import max_over_ranks
 
     dev = Device(local)
     w = workloads.make(args.config)
@@ -249,10 +258,7 @@ def main():
     elapsed_ms = ev0.elapsed_time(ev1)
     dev.synchronize(sp)   # raises if the kernel latched an error
     paths = dev.stats(reset=True)
-    t = torch.tensor([elapsed_ms], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    elapsed_max = float(t.item())
+    elapsed_max = max_over_ranks(elapsed_ms, device="cuda")
     rows_per_rank = w.n_rows
     total_rows = rows_per_rank * world * args.steps
     value = total_rows / (elapsed_max * 1e-3)
@@ -279,10 +285,7 @@ def main():
     for _ in range(args.e2e_steps):
         sample_rows(dev, hsegs, opts)
     e2e_s = time.perf_counter() - t0
-    te = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_value = rows_per_rank * world * args.e2e_steps / float(te.item())
+    e2e_value = rows_per_rank * world * args.e2e_steps / max_over_ranks(e2e_s, device="cuda")
 
     line = None
     if rank == 0:
@@ -311,8 +314,7 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": w.name, "rows_per_gpu": rows_per_rank, "global_rows": rows_per_rank * world,
-                       "vocab": 3072, "history": 1024, "top_k": 50, "top_p": 0.8, "temperature": 0.9,
-                       "repetition_penalty": 1.05, "parallelism": f"row shards x{world}, no collective",
+                       **workload_keys(w), "parallelism": f"row shards x{world}, no collective",
                        "l2": f"{n_copies} rotating input copies ({n_copies * alg / 1e6:.0f} MB > 126 MB L2)",
                        "timing": "K steps in one CUDA graph, CUDA events on the launching stream, max over ranks"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -324,7 +326,7 @@ def main():
                     "steps": args.e2e_steps, "path": "vw_sample(VW_MEM_HOST) from pinned host buffers"},
             "cpu_baseline": cpu,
             "clocks": clocks.summary(),
-            "gpu_launches": args.steps,
+            "gpu_launches": 2 * args.steps,   # per step: the candidate kernel + the whole-row kernel
             "parity": parity,
             "rows_by_path": paths,
         }

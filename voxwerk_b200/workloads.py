@@ -108,21 +108,9 @@ class Workload:
 
     def shard(self, rank: int, world: int) -> "Workload":
         """Contiguous row shard for `rank` of `world`, cost-weighted across segments by bytes per row."""
-        costs = []
-        for s in self.segments:
-            per = s.algorithmic_bytes() / max(s.n_rows, 1)
-            costs.append((s, per))
-        total = sum(per * s.n_rows for s, per in costs)
-        lo_c, hi_c = total * rank / world, total * (rank + 1) / world
-        out, acc = [], 0.0
-        for s, per in costs:
-            seg_lo, seg_hi = acc, acc + per * s.n_rows
-            a = int(round(max(0.0, lo_c - seg_lo) / per)) if per else 0
-            b = int(round(max(0.0, min(hi_c, seg_hi) - seg_lo) / per)) if per else 0
-            a, b = min(a, s.n_rows), min(b, s.n_rows)
-            if b > a:
-                out.append(s.slice(a, b))
-            acc = seg_hi
+        from .shard import shard_bounds
+        costs = [(s.n_rows, s.algorithmic_bytes() / max(s.n_rows, 1)) for s in self.segments]
+        out = [self.segments[k].slice(a, b) for k, a, b in shard_bounds(costs, rank, world)]
         return Workload(f"{self.name}[{rank}/{world}]", self.config, out, self.options, dict(self.notes))
 
 
