@@ -34,6 +34,7 @@ struct vw_handle {
     size_t opts_cap = 0;
     cudaEvent_t opts_done = nullptr;
     unsigned long long* d_stats = nullptr;   // vw::kNumStats per-path row counters
+    unsigned long long* d_guess = nullptr;   // candidate threshold carried from call to call
     int force_exact = 0;                     // VW_FORCE_EXACT at creation
     std::string last_error;
 };
@@ -360,19 +361,13 @@ vw_status sample_impl(vw_handle* h, const vw_segment* segs, int32_t n_segs, cons
     p.vmax = vmax;
     p.err = h->d_err;
     p.stats = h->d_stats;
+    p.guess_seed = h->d_guess;
     p.force_exact = h->force_exact;
 
-    int ctas = 0, ctas_g = 0;
-    size_t smem = 0;
-    for (int stages = vw::kStages; stages >= 2 && (ctas == 0 || ctas_g == 0); --stages) {
-        p.n_stages = stages;
-        smem = vw::sampler_smem_bytes(p);
-        ctas = vw::sampler_ctas_per_sm(smem, false);
-        ctas_g = vw::sampler_ctas_per_sm(smem, true);
-    }
-    if (ctas == 0 || ctas_g == 0) return fail(h, VW_ERR_INVALID_ARG, "rows too large for shared memory");
-    const int grid = static_cast<int>(std::min<int64_t>(p.total_rows, static_cast<int64_t>(h->sm_count) * ctas));
-    const int grid_g = static_cast<int>(std::min<int64_t>(p.total_rows, static_cast<int64_t>(h->sm_count) * ctas_g));
+    vw::LaunchPlan plan;
+    if (!vw::plan_launch(p, h->sm_count, INT32_MAX, &plan))
+        return fail(h, VW_ERR_INVALID_ARG, "rows too large for shared memory");
+    const int grid_g = plan.grid_general;
     p.gscratch_stride = vw::sampler_gscratch_stride(vmax);
     r = grow(h, &h->d_scratch, &h->scratch_bytes, static_cast<size_t>(grid_g) * p.gscratch_stride, "scratch");
     if (r != VW_OK) return r;
@@ -395,7 +390,7 @@ vw_status sample_impl(vw_handle* h, const vw_segment* segs, int32_t n_segs, cons
 
     cudaError_t e = cudaSuccess;
     if (sync) e = cudaMemsetAsync(h->d_err, 0, sizeof(unsigned), st);
-    if (e == cudaSuccess) e = vw::launch_sampler(p, grid, smem, grid_g, st);
+    if (e == cudaSuccess) e = vw::launch_sampler(p, plan, st);
     if (e != cudaSuccess) return cuda_fail(h, e, "sampler launch");
     if (mem == VW_MEM_HOST) {
         for (int i = 0; i < n_segs && e == cudaSuccess; ++i) {
@@ -449,6 +444,8 @@ VW_EXPORT vw_status vw_create(int32_t device, vw_handle** out) {
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->opts_done, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaMalloc(&h->d_stats, sizeof(unsigned long long) * vw::kNumStats);
     if (e == cudaSuccess) e = cudaMemset(h->d_stats, 0, sizeof(unsigned long long) * vw::kNumStats);
+    if (e == cudaSuccess) e = cudaMalloc(&h->d_guess, sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaMemset(h->d_guess, 0xff, sizeof(unsigned long long));   // (segment, option) -1: none
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     const char* fe = std::getenv("VW_FORCE_EXACT");
     h->force_exact = (fe && fe[0] == '1') ? 1 : 0;
@@ -471,6 +468,7 @@ VW_EXPORT vw_status vw_destroy(vw_handle* h) {
         if (h->h_opts) cudaFreeHost(h->h_opts);
         if (h->d_err) cudaFree(h->d_err);
         if (h->d_stats) cudaFree(h->d_stats);
+        if (h->d_guess) cudaFree(h->d_guess);
         if (h->d_defer) cudaFree(h->d_defer);
         if (h->h_err) cudaFreeHost(h->h_err);
         if (h->opts_done) cudaEventDestroy(h->opts_done);
@@ -739,18 +737,9 @@ vw_status sample_static_impl(vw_handle* h, int32_t device, const vw_segment* seg
     const char* fe = std::getenv("VW_FORCE_EXACT");
     p.force_exact = (fe && fe[0] == '1') ? 1 : 0;
 
-    int ctas = 0, ctas_g = 0;
-    size_t smem = 0;
-    for (int stages = vw::kStages; stages >= 2 && (ctas == 0 || ctas_g == 0); --stages) {
-        p.n_stages = stages;
-        smem = vw::sampler_smem_bytes(p);
-        ctas = vw::sampler_ctas_per_sm(smem, false);
-        ctas_g = vw::sampler_ctas_per_sm(smem, true);
-    }
-    if (ctas == 0 || ctas_g == 0) return fail(h, VW_ERR_INVALID_ARG, "rows too large for shared memory");
-    const int grid = static_cast<int>(std::min<int64_t>(p.total_rows, static_cast<int64_t>(sd.sm_count) * ctas));
-    const int grid_g = static_cast<int>(std::min<int64_t>(
-        {static_cast<int64_t>(p.total_rows), static_cast<int64_t>(sd.sm_count) * ctas_g, vw::kStaticGeneralCtas}));
+    vw::LaunchPlan plan;
+    if (!vw::plan_launch(p, sd.sm_count, vw::kStaticGeneralCtas, &plan))
+        return fail(h, VW_ERR_INVALID_ARG, "rows too large for shared memory");
     p.gscratch_stride = vw::sampler_gscratch_stride(vmax);
     if (p.gscratch_stride > vw::kStaticCtaStride)
         return fail(h, VW_ERR_INVALID_ARG, "vocab too large for the static scratch");
@@ -759,11 +748,12 @@ vw_status sample_static_impl(vw_handle* h, int32_t device, const vw_segment* seg
     p.done_count = reinterpret_cast<uint32_t*>(sd.scratch) + 2;
     p.deferred_rows = reinterpret_cast<int32_t*>(sd.scratch + vw::kStaticRowsOffset);
     p.gscratch = sd.scratch + vw::kStaticScratchOffset;
+    p.guess_seed = reinterpret_cast<unsigned long long*>(sd.scratch + vw::kStaticGuessOffset);
 
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     // the error word and both counters must start at zero (an earlier call that timed out may have left them set)
     cudaError_t e = cudaMemsetAsync(sd.scratch, 0, 4 * sizeof(uint32_t), st);
-    if (e == cudaSuccess) e = vw::launch_sampler(p, grid, smem, grid_g, st);
+    if (e == cudaSuccess) e = vw::launch_sampler(p, plan, st);
     if (e != cudaSuccess) return cuda_fail(h, e, "sampler launch");
     unsigned bits = 0;   // pageable host word: the copy completes before cudaMemcpyAsync returns or at the sync
     e = cudaMemcpyAsync(&bits, sd.scratch, sizeof(unsigned), cudaMemcpyDeviceToHost, st);

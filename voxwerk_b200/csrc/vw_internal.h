@@ -87,23 +87,35 @@ struct LaunchParams {
     int32_t force_exact;          // replay every sampled row in the reference's order (test hook)
     char* gscratch;               // large-path scratch, gscratch_stride bytes per CTA
     int64_t gscratch_stride;
+    unsigned long long* guess_seed;   // candidate threshold carried across calls: float bits << 32 | (segment,
+                                      // option) id; nullable (any value is safe: it only saves work when it fits)
 };
 
-// Dynamic shared memory the sampler kernel needs for `p`.
+// Dynamic shared memory the whole-row kernel needs for `p`.
 size_t sampler_smem_bytes(const LaunchParams& p);
 // Global scratch bytes per CTA for rows of up to `vmax` ids.
 int64_t sampler_gscratch_stride(int vmax);
-// Resident CTAs per SM at that shared-memory size (0 if it does not fit).  `general` selects the whole-row kernel.
-int sampler_ctas_per_sm(size_t smem, bool general);
+
+struct LaunchPlan {
+    int grid;              // candidate kernel CTAs (every row)
+    int grid_general;      // whole-row kernel CTAs (the deferred rows)
+    size_t smem_cand;      // dynamic shared memory of each
+    size_t smem_general;
+};
+// Picks p.n_stages and both grids for `sm_count` SMs on the current device (whole-row grid <= max_grid_general).
+// False when a row does not fit in shared memory.
+bool plan_launch(LaunchParams& p, int sm_count, int max_grid_general, LaunchPlan* plan);
 // The candidate kernel over every row, then the whole-row kernel over the rows it deferred (stream-ordered).
-cudaError_t launch_sampler(const LaunchParams& p, int grid, size_t smem, int grid_general, cudaStream_t stream);
+cudaError_t launch_sampler(const LaunchParams& p, const LaunchPlan& plan, cudaStream_t stream);
 
 // ---- fixed scratch of vw_sample_static: one file-scope device array per device, no allocation.
-// Layout: the error word and the two deferred-list counters at offset 0 (zeroed before every call), the deferred
+// Layout: the error word and the two deferred-list counters at offset 0 (zeroed before every call), the carried
+// candidate threshold at kStaticGuessOffset, the deferred
 // rows at kStaticRowsOffset, then one kStaticCtaStride slice per whole-row CTA at kStaticScratchOffset.
 constexpr int kStaticMaxRows = 65536;       // rows per call (all segments)
 constexpr int kStaticMaxVocab = 4096;       // ids per row (a power of two >= kRegElems * kThreads)
 constexpr int kStaticGeneralCtas = 148;     // whole-row kernel CTAs (one per B200 SM)
+constexpr int64_t kStaticGuessOffset = 32;
 constexpr int64_t kStaticRowsOffset = 256;
 constexpr int64_t kStaticScratchOffset = kStaticRowsOffset + 4 * static_cast<int64_t>(kStaticMaxRows);
 // sampler_gscratch_stride(kStaticMaxVocab): 12 bytes per id plus a 16-byte sort slot per id
