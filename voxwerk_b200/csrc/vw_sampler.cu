@@ -1556,6 +1556,7 @@ struct __align__(16) CandMisc {
     int32_t issued;                    // rows the producer has issued (timeout drain)
     uint32_t progress;                 // rows finished by the element warps
     int32_t flags[kCandCap];           // replay scratch
+    uint32_t desc[kWarps][kCandCap];   // per-warp staged positions of the elements that passed the pass's test
 };
 
 __device__ __forceinline__ unsigned long long warp_incl_u64(unsigned long long v, int lane) {
@@ -1784,10 +1785,110 @@ __device__ __forceinline__ void row_pass(const unsigned char* sl, int nvec, cons
     }
 }
 
+// Fused / Append pass: every value >= tau goes to keys (count = their number), `a` = the largest of them.  The
+// pass itself only marks, per thread, the elements whose short-path value is >= tau (for a lazy penalty that is
+// the unpenalized value, an upper bound); each warp then gathers its marked elements, one per lane, computes their
+// exact values (penalty, mask, temperature) and appends those still >= tau with one counter update per warp.
+template <int VW>
+__device__ __forceinline__ void row_pass_append(const unsigned char* sl, int nvec, const RowMap& mp, const RowCtx& c,
+                                                int tid, float& a, float tau, uint32_t* count,
+                                                unsigned long long* keys, uint32_t* desc) {
+    const int lane = tid & 31;
+    const bool lazy = c.pen_lazy;
+    uint32_t marks = 0u;   // bit (iteration * VW + e); at most 3072 / (128 * VW) iterations
+    int it = 0;
+#pragma unroll 1
+    for (int qv = tid; qv < nvec; qv += kThreads, ++it) {
+        float v[VW];
+        load_vec<VW>(sl, qv, v);
+        bool slow = static_cast<unsigned>(qv - c.slow_vlo) < static_cast<unsigned>(c.slow_vhi - c.slow_vlo) ||
+                    qv == c.eos_vec;
+        int i0 = -1;
+        uint32_t bits = 0u;
+        if (c.pen_on && (slow || !lazy)) {
+            i0 = mp.idx(qv * VW);
+            bits = c.bitmap[i0 >> 5];
+            slow = slow || ((bits >> (i0 & 31)) & ((1u << VW) - 1u)) != 0u;
+        }
+        float t[VW];
+        if (slow) {
+            if (i0 < 0) i0 = mp.idx(qv * VW);
+#pragma unroll
+            for (int e = 0; e < VW; ++e) t[e] = transform(v[e], i0 + e, bits, c);
+        } else {
+#pragma unroll
+            for (int e = 0; e < VW; ++e) t[e] = __fmul_rn(v[e], c.inv_t);
+        }
+        float vm = t[0];
+#pragma unroll
+        for (int e = 1; e < VW; ++e) vm = fmaxf(vm, t[e]);
+        if (vm >= tau) {
+            uint32_t m = 0u;
+#pragma unroll
+            for (int e = 0; e < VW; ++e) m |= (t[e] >= tau ? 1u : 0u) << e;
+            marks |= m << (it * VW);
+        }
+    }
+    // gather this warp's marked elements: lane l writes its positions from the warp prefix of the counts on
+    const int n = __popc(marks);
+    int incl = n;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl += y;
+    }
+    const int total = __shfl_sync(kFull, incl, 31);
+    if (total > kCandCap) {   // more than the candidate buffer holds: the row takes the overflow path
+        if (lane == 0) atomicAdd(count, static_cast<uint32_t>(kCandCap + 1));
+        return;
+    }
+    int w = incl - n;
+    while (marks) {
+        const int bit = __ffs(marks) - 1;
+        marks &= marks - 1u;
+        const int iter = bit / VW, e = bit - iter * VW;
+        desc[w++] = static_cast<uint32_t>((tid + iter * kThreads) * VW + e);
+    }
+    __syncwarp();
+    for (int b0 = 0; b0 < total; b0 += 32) {
+        const int i = b0 + lane;
+        bool pr = false;
+        float x = 0.0f;
+        int id = 0;
+        if (i < total) {
+            const int pos = static_cast<int>(desc[i]);
+            id = mp.idx(pos);
+            x = transform(VW == 4 ? reinterpret_cast<const float*>(sl)[pos]
+                                  : __uint_as_float(static_cast<uint32_t>(reinterpret_cast<const uint16_t*>(sl)[pos]) << 16),
+                          id, c.pen_on ? c.bitmap[id >> 5] : 0u, c);
+            pr = x >= tau;
+        }
+        const unsigned bal = __ballot_sync(kFull, pr);
+        if (bal) {
+            uint32_t base = 0;
+            if (lane == 0) base = atomicAdd(count, static_cast<uint32_t>(__popc(bal)));
+            base = __shfl_sync(kFull, base, 0) + __popc(bal & ((1u << lane) - 1u));
+            if (pr) {
+                a = fmaxf(a, x);
+                if (base < static_cast<uint32_t>(kCandCap))
+                    keys[base] = (static_cast<unsigned long long>(okey(x)) << 32) | static_cast<uint32_t>(id);
+            }
+        }
+    }
+}
+
 template <int kMode>
 __device__ __forceinline__ void row_pass_dt(int dtype, const unsigned char* sl, int nvec, const RowMap& mp,
                                             const RowCtx& c, int tid, float& a, float& b, int& bi, float tau,
-                                            uint32_t* count, unsigned long long* keys) {
+                                            uint32_t* count, unsigned long long* keys, uint32_t* b_desc = nullptr) {
+    if (kMode == kPassFused || kMode == kPassAppend) {
+        uint32_t* desc = reinterpret_cast<uint32_t*>(b_desc);
+        if (dtype == 0)
+            row_pass_append<4>(sl, nvec, mp, c, tid, a, tau, count, keys, desc);
+        else
+            row_pass_append<8>(sl, nvec, mp, c, tid, a, tau, count, keys, desc);
+        return;
+    }
     if (dtype == 0)
         row_pass<4, kMode>(sl, nvec, mp, c, tid, a, b, bi, tau, count, keys);
     else
@@ -1990,7 +2091,7 @@ __global__ void __launch_bounds__(kBlockThreads, 6) cand_kernel(const __grid_con
         const bool fuse = guess_id == gid;
         uint32_t* const count = &cm.count[k & 1];
         if (fuse)
-            row_pass_dt<kPassFused>(dtype, sl, nvec, mp, c, tid, a, b, bi, guess_tau, count, cm.key);
+            row_pass_dt<kPassFused>(dtype, sl, nvec, mp, c, tid, a, b, bi, guess_tau, count, cm.key, cm.desc[warp]);
         else
             row_pass_dt<kPassTop2>(dtype, sl, nvec, mp, c, tid, a, b, bi, 0.0f, nullptr, nullptr);
         {
@@ -2030,7 +2131,7 @@ __global__ void __launch_bounds__(kBlockThreads, 6) cand_kernel(const __grid_con
             }
             C = kCandCap + 1;
             if (!is_neg_inf(tau)) {
-                row_pass_dt<kPassAppend>(dtype, sl, nvec, mp, c, tid, a, b, bi, tau, count, cm.key);
+                row_pass_dt<kPassAppend>(dtype, sl, nvec, mp, c, tid, a, b, bi, tau, count, cm.key, cm.desc[warp]);
                 cbar();
                 C = static_cast<int>(*reinterpret_cast<volatile uint32_t*>(count));
             }
