@@ -26,7 +26,7 @@ struct vw_handle {
     char* d_scratch = nullptr;      // general-path scratch, one slice per CTA
     size_t scratch_bytes = 0;
     char* d_stage = nullptr;        // VW_MEM_HOST: device copies of the caller's arrays
-    int32_t* d_defer = nullptr;     // two counters + the rows the candidate kernel defers
+    int32_t* d_defer = nullptr;     // four counters + the rows the candidate kernel defers
     size_t defer_cap = 0;
     size_t stage_bytes = 0;
     vw::DevOptions* d_opts = nullptr;
@@ -68,6 +68,8 @@ vw_status cuda_fail(vw_handle* h, cudaError_t e, const char* where) {
 }
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+constexpr int kDeferHeader = 4;   // counters ahead of the deferred-row list
 
 size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
@@ -239,7 +241,7 @@ vw_status read_device_error(vw_handle* h, cudaStream_t st) {
     const unsigned bits = *h->h_err;
     if (bits) {
         cudaMemsetAsync(h->d_err, 0, sizeof(unsigned), st);
-        if (h->d_defer) cudaMemsetAsync(h->d_defer, 0, 2 * sizeof(int32_t), st);
+        if (h->d_defer) cudaMemsetAsync(h->d_defer, 0, kDeferHeader * sizeof(int32_t), st);
         cudaStreamSynchronize(st);
     }
     if (bits & vw::kErrTimeout) return fail(h, VW_ERR_TIMEOUT, "a bounded wait in the sampler kernel gave up");
@@ -372,21 +374,24 @@ vw_status sample_impl(vw_handle* h, const vw_segment* segs, int32_t n_segs, cons
     r = grow(h, &h->d_scratch, &h->scratch_bytes, static_cast<size_t>(grid_g) * p.gscratch_stride, "scratch");
     if (r != VW_OK) return r;
     p.gscratch = h->d_scratch;
-    // deferred-row list: total_rows entries plus two counters (zero between calls)
-    if (static_cast<size_t>(p.total_rows) + 2 > h->defer_cap) {
+    // deferred-row list: total_rows entries after four counters (deferred rows, whole-row CTAs done, next row of
+    // the candidate kernel, candidate CTAs done), all zero between calls
+    if (static_cast<size_t>(p.total_rows) + kDeferHeader > h->defer_cap) {
         cudaError_t e = cudaStreamSynchronize(st);
         if (e == cudaSuccess && h->d_defer) e = cudaFree(h->d_defer);
         h->d_defer = nullptr;
         h->defer_cap = 0;
-        const size_t cap = static_cast<size_t>(p.total_rows) + 2 + 4096;
+        const size_t cap = static_cast<size_t>(p.total_rows) + kDeferHeader + 4096;
         if (e == cudaSuccess) e = cudaMalloc(&h->d_defer, cap * sizeof(int32_t));
-        if (e == cudaSuccess) e = cudaMemset(h->d_defer, 0, 2 * sizeof(int32_t));
+        if (e == cudaSuccess) e = cudaMemset(h->d_defer, 0, kDeferHeader * sizeof(int32_t));
         if (e != cudaSuccess) return cuda_fail(h, e, "deferred-row list");
         h->defer_cap = cap;
     }
     p.deferred_count = reinterpret_cast<uint32_t*>(h->d_defer);
     p.done_count = reinterpret_cast<uint32_t*>(h->d_defer) + 1;
-    p.deferred_rows = h->d_defer + 2;
+    p.row_counter = reinterpret_cast<uint32_t*>(h->d_defer) + 2;
+    p.cand_done = reinterpret_cast<uint32_t*>(h->d_defer) + 3;
+    p.deferred_rows = h->d_defer + kDeferHeader;
 
     cudaError_t e = cudaSuccess;
     if (sync) e = cudaMemsetAsync(h->d_err, 0, sizeof(unsigned), st);
@@ -746,13 +751,16 @@ vw_status sample_static_impl(vw_handle* h, int32_t device, const vw_segment* seg
     p.err = reinterpret_cast<unsigned*>(sd.scratch);
     p.deferred_count = reinterpret_cast<uint32_t*>(sd.scratch) + 1;
     p.done_count = reinterpret_cast<uint32_t*>(sd.scratch) + 2;
+    p.row_counter = reinterpret_cast<uint32_t*>(sd.scratch) + 3;
+    p.cand_done = reinterpret_cast<uint32_t*>(sd.scratch) + 4;
     p.deferred_rows = reinterpret_cast<int32_t*>(sd.scratch + vw::kStaticRowsOffset);
     p.gscratch = sd.scratch + vw::kStaticScratchOffset;
     p.guess_seed = reinterpret_cast<unsigned long long*>(sd.scratch + vw::kStaticGuessOffset);
 
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    // the error word and both counters must start at zero (an earlier call that timed out may have left them set)
-    cudaError_t e = cudaMemsetAsync(sd.scratch, 0, 4 * sizeof(uint32_t), st);
+    // the error word and the four counters must start at zero (an earlier call that timed out may have left them
+    // set)
+    cudaError_t e = cudaMemsetAsync(sd.scratch, 0, 8 * sizeof(uint32_t), st);
     if (e == cudaSuccess) e = vw::launch_sampler(p, plan, st);
     if (e != cudaSuccess) return cuda_fail(h, e, "sampler launch");
     unsigned bits = 0;   // pageable host word: the copy completes before cudaMemcpyAsync returns or at the sync

@@ -83,6 +83,8 @@ struct LaunchParams {
     int32_t* deferred_rows;       // rows the candidate kernel leaves to the whole-row kernel (total_rows entries)
     uint32_t* deferred_count;     // their number (the whole-row kernel resets it to 0 when it is done)
     uint32_t* done_count;         // whole-row kernel CTAs finished (reset with deferred_count)
+    uint32_t* row_counter;        // next row for the candidate kernel's CTAs to take (its last CTA resets it)
+    uint32_t* cand_done;          // candidate kernel CTAs finished (reset with row_counter)
     unsigned long long* stats;    // kNumStats counters (nullable)
     int32_t force_exact;          // replay every sampled row in the reference's order (test hook)
     char* gscratch;               // large-path scratch, gscratch_stride bytes per CTA
@@ -109,7 +111,8 @@ bool plan_launch(LaunchParams& p, int sm_count, int max_grid_general, LaunchPlan
 cudaError_t launch_sampler(const LaunchParams& p, const LaunchPlan& plan, cudaStream_t stream);
 
 // ---- fixed scratch of vw_sample_static: one file-scope device array per device, no allocation.
-// Layout: the error word and the two deferred-list counters at offset 0 (zeroed before every call), the carried
+// Layout: the error word, the two deferred-list counters and the two row-scheduling counters at offset 0 (zeroed
+// before every call), the carried
 // candidate threshold at kStaticGuessOffset, the deferred
 // rows at kStaticRowsOffset, then one kStaticCtaStride slice per whole-row CTA at kStaticScratchOffset.
 constexpr int kStaticMaxRows = 65536;       // rows per call (all segments)

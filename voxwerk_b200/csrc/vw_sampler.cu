@@ -1369,6 +1369,127 @@ __device__ int block_argmax(float bestv, int besti, SmemMisc& m, int lane, int w
 // deferred list) and streams each row's staged logits and history into the stage ring with bulk copies that
 // complete on full_bar.  The row's RowMeta goes into metas[k % (2 * S)].  In the candidate kernel, rows that kernel
 // does not take (sampling without a top-k <= 64, or more than 3072 staged ids) are marked deferred and copy nothing.
+// The RowMeta of row r: where its data is, what to stage and how the element warps treat it.  `bytes` = the
+// bytes its bulk copies bring into the stage (0 for a row that copies nothing), `esize` the logit size.
+template <bool kGeneral>
+__device__ RowMeta plan_row(const LaunchParams& p, int r, uint32_t& bytes, int& esize) {
+    RowMeta m;
+    bytes = 0;
+    esize = 4;
+    int s = 0;
+    for (int i = 1; i < p.n_segs; ++i)
+        if (r >= p.seg[i].row_begin) s = i;
+    const DevSegment& sg = p.seg[s];
+    const int local = r - sg.row_begin;
+    const int opt_raw = sg.opt_index ? sg.opt_index[local] : 0;
+    const int V = sg.vocab;
+    m.row = r;
+    m.seg = s;
+    m.opt_idx = opt_raw;
+    m.step = sg.steps ? sg.steps[local] : 0x7fffffff;
+    m.uniform = sg.uniforms ? sg.uniforms[local] : 0.0;
+    int64_t hb = 0, he = 0;
+    if (sg.kind == 0 && sg.hist_offsets) {
+        hb = sg.hist_offsets[local];
+        he = sg.hist_offsets[local + 1];
+    }
+    m.opt_ok = (opt_raw >= 0 && opt_raw < p.n_opts) ? 1 : 0;
+    if (m.opt_ok) {
+        m.opt = p.n_opts <= kInlineOptions ? p.inl_opts[opt_raw] : p.dev_opts[opt_raw];
+    } else {
+        m.opt = DevOptions{0, 0, 1.0f, 1.0f, 1.0f};
+    }
+    esize = sg.dtype == 0 ? 4 : 2;
+    const int VWe = 16 / esize;
+    m.V = V;
+    m.dtype = sg.dtype;
+    m.kind = sg.kind;
+    m.sup_lo = sg.sup_lo;
+    m.sup_hi = sg.sup_hi;
+    m.eos = sg.eos;
+    m.eos_blocked = (sg.kind == 0 && m.step < sg.min_new) ? 1 : 0;
+    m.pen_on = (m.opt_ok && sg.kind == 0 && m.opt.rep_penalty != 1.0f && he > hb) ? 1 : 0;
+    m.pen_rcp = __drcp_rn(static_cast<double>(m.opt.rep_penalty));
+    m.inv_t = __fdiv_rn(1.0f, m.opt.temperature);
+    m.hist = sg.hist_ids ? sg.hist_ids + hb : nullptr;
+    m.hist_len = static_cast<int32_t>(he - hb);
+    m.out_id = sg.out_ids + local;
+    m.out_probs = sg.out_probs ? sg.out_probs + static_cast<int64_t>(local) * V : nullptr;
+    m.lo_al = V;
+    m.hi_al = V;
+    if (sg.kind == 0 && sg.sup_lo < sg.sup_hi) {
+        const int la = (sg.sup_lo + VWe - 1) / VWe * VWe;
+        const int ha = sg.sup_hi / VWe * VWe;
+        if (la < ha) {
+            m.lo_al = la;
+            m.hi_al = ha;
+        }
+    }
+    const bool keep = sg.kind == 0 && sg.eos >= m.lo_al && sg.eos < m.hi_al && !m.eos_blocked;
+    m.kvw = keep ? VWe : 0;
+    m.kbase = keep ? sg.eos / VWe * VWe : 0;
+    m.direct = sg.bulk_ok ? 0 : 1;
+    m.hs_lo = 0;
+    m.hs_hi = 0;
+    if (m.pen_on && sg.hist_aligned && p.stage_hist_cap > 0) {
+        int64_t a = (hb + 3) / 4 * 4;
+        int64_t b = he / 4 * 4;
+        if (b > a + p.stage_hist_cap) b = a + p.stage_hist_cap;
+        if (b > a) {
+            m.hs_lo = static_cast<int32_t>(a - hb);
+            m.hs_hi = static_cast<int32_t>(b - hb);
+        }
+    }
+    // staged vectors that may hold suppressed ids: positions [sup_lo, lo_al + kvw + (sup_hi - hi_al))
+    m.slow_vlo = m.slow_vhi = 0;
+    m.eos_vec = -1;
+    if (sg.kind == 0) {
+        if (sg.sup_lo < sg.sup_hi) {
+            m.slow_vlo = sg.sup_lo / VWe;
+            m.slow_vhi = (m.lo_al + m.kvw + max(sg.sup_hi - m.hi_al, 0) + VWe - 1) / VWe;
+        }
+        if (m.eos_blocked && sg.eos >= 0 && sg.eos < V) {
+            const RowMap mp{m.lo_al, m.kvw, m.kbase, m.hi_al};
+            const int ep = mp.pos(sg.eos);
+            if (ep >= 0) m.eos_vec = ep / VWe;
+        }
+    }
+    m.row_ptr = static_cast<const unsigned char*>(sg.logits) +
+                static_cast<int64_t>(local) * sg.row_stride * esize;
+    m.deferred = 0;
+    if (!kGeneral && m.opt_ok) {
+        // rows the candidate kernel does not take: more than 3072 staged ids, or sampling without a
+        // top-k <= 64
+        const int na = m.lo_al + m.kvw + V - m.hi_al;
+        const bool big = (na + VWe - 1) / VWe > kThreads * (kRegElems / VWe);
+        const int K = m.opt.top_k;
+        const bool cand = !m.opt.do_sample || (K > 0 && K < V && K <= kSmallK);
+        m.deferred = (big || !cand) ? 1 : 0;
+    }
+    if (!m.deferred && m.opt_ok) {
+        if (!m.direct) bytes += static_cast<uint32_t>((m.lo_al + m.kvw + V - m.hi_al) * esize);
+        bytes += static_cast<uint32_t>(m.hs_hi - m.hs_lo) * 4u;
+    }
+    return m;
+}
+
+// Issues row m's bulk copies into stage `s` (the caller has armed full_bar[s] with their byte count).
+__device__ __forceinline__ void issue_row(const LaunchParams& p, const RowMeta& m, int esize, unsigned char* log_dst,
+                                          uint64_t* bar) {
+    unsigned char* hist_dst = log_dst + p.stage_logit_bytes;
+    if (!m.direct && !m.deferred && m.opt_ok) {
+        const int V = m.V;
+        if (m.lo_al > 0) bulk_g2s(log_dst, m.row_ptr, static_cast<uint32_t>(m.lo_al * esize), bar);
+        if (m.kvw > 0)
+            bulk_g2s(log_dst + m.lo_al * esize, m.row_ptr + static_cast<int64_t>(m.kbase) * esize, 16u, bar);
+        if (V > m.hi_al)
+            bulk_g2s(log_dst + (m.lo_al + m.kvw) * esize, m.row_ptr + static_cast<int64_t>(m.hi_al) * esize,
+                     static_cast<uint32_t>((V - m.hi_al) * esize), bar);
+    }
+    if (m.hs_hi > m.hs_lo && !m.deferred && m.opt_ok)
+        bulk_g2s(hist_dst, m.hist + m.hs_lo, static_cast<uint32_t>(m.hs_hi - m.hs_lo) * 4u, bar);
+}
+
 template <bool kGeneral>
 __device__ void produce_rows(const LaunchParams& p, int first, int gstride, int n_my, int lane, unsigned char* stages,
                              int stage_bytes, RowMeta* metas, uint64_t* full_bar, uint64_t* empty_bar,
@@ -1384,100 +1505,7 @@ __device__ void produce_rows(const LaunchParams& p, int first, int gstride, int 
         if (kj < n_my) {
             int r = first + kj * gstride;
             if (kGeneral) r = min(max(p.deferred_rows[r], 0), p.total_rows - 1);
-            int s = 0;
-            for (int i = 1; i < p.n_segs; ++i)
-                if (r >= p.seg[i].row_begin) s = i;
-            const DevSegment& sg = p.seg[s];
-            const int local = r - sg.row_begin;
-            const int opt_raw = sg.opt_index ? sg.opt_index[local] : 0;
-            const int V = sg.vocab;
-            m.row = r;
-            m.seg = s;
-            m.opt_idx = opt_raw;
-            m.step = sg.steps ? sg.steps[local] : 0x7fffffff;
-            m.uniform = sg.uniforms ? sg.uniforms[local] : 0.0;
-            int64_t hb = 0, he = 0;
-            if (sg.kind == 0 && sg.hist_offsets) {
-                hb = sg.hist_offsets[local];
-                he = sg.hist_offsets[local + 1];
-            }
-            m.opt_ok = (opt_raw >= 0 && opt_raw < p.n_opts) ? 1 : 0;
-            if (m.opt_ok) {
-                m.opt = p.n_opts <= kInlineOptions ? p.inl_opts[opt_raw] : p.dev_opts[opt_raw];
-            } else {
-                m.opt = DevOptions{0, 0, 1.0f, 1.0f, 1.0f};
-            }
-            esize = sg.dtype == 0 ? 4 : 2;
-            const int VWe = 16 / esize;
-            m.V = V;
-            m.dtype = sg.dtype;
-            m.kind = sg.kind;
-            m.sup_lo = sg.sup_lo;
-            m.sup_hi = sg.sup_hi;
-            m.eos = sg.eos;
-            m.eos_blocked = (sg.kind == 0 && m.step < sg.min_new) ? 1 : 0;
-            m.pen_on = (m.opt_ok && sg.kind == 0 && m.opt.rep_penalty != 1.0f && he > hb) ? 1 : 0;
-            m.pen_rcp = __drcp_rn(static_cast<double>(m.opt.rep_penalty));
-            m.inv_t = __fdiv_rn(1.0f, m.opt.temperature);
-            m.hist = sg.hist_ids ? sg.hist_ids + hb : nullptr;
-            m.hist_len = static_cast<int32_t>(he - hb);
-            m.out_id = sg.out_ids + local;
-            m.out_probs = sg.out_probs ? sg.out_probs + static_cast<int64_t>(local) * V : nullptr;
-            m.lo_al = V;
-            m.hi_al = V;
-            if (sg.kind == 0 && sg.sup_lo < sg.sup_hi) {
-                const int la = (sg.sup_lo + VWe - 1) / VWe * VWe;
-                const int ha = sg.sup_hi / VWe * VWe;
-                if (la < ha) {
-                    m.lo_al = la;
-                    m.hi_al = ha;
-                }
-            }
-            const bool keep = sg.kind == 0 && sg.eos >= m.lo_al && sg.eos < m.hi_al && !m.eos_blocked;
-            m.kvw = keep ? VWe : 0;
-            m.kbase = keep ? sg.eos / VWe * VWe : 0;
-            m.direct = sg.bulk_ok ? 0 : 1;
-            m.hs_lo = 0;
-            m.hs_hi = 0;
-            if (m.pen_on && sg.hist_aligned && p.stage_hist_cap > 0) {
-                int64_t a = (hb + 3) / 4 * 4;
-                int64_t b = he / 4 * 4;
-                if (b > a + p.stage_hist_cap) b = a + p.stage_hist_cap;
-                if (b > a) {
-                    m.hs_lo = static_cast<int32_t>(a - hb);
-                    m.hs_hi = static_cast<int32_t>(b - hb);
-                }
-            }
-            // staged vectors that may hold suppressed ids: positions [sup_lo, lo_al + kvw + (sup_hi - hi_al))
-            m.slow_vlo = m.slow_vhi = 0;
-            m.eos_vec = -1;
-            if (sg.kind == 0) {
-                if (sg.sup_lo < sg.sup_hi) {
-                    m.slow_vlo = sg.sup_lo / VWe;
-                    m.slow_vhi = (m.lo_al + m.kvw + max(sg.sup_hi - m.hi_al, 0) + VWe - 1) / VWe;
-                }
-                if (m.eos_blocked && sg.eos >= 0 && sg.eos < V) {
-                    const RowMap mp{m.lo_al, m.kvw, m.kbase, m.hi_al};
-                    const int ep = mp.pos(sg.eos);
-                    if (ep >= 0) m.eos_vec = ep / VWe;
-                }
-            }
-            m.row_ptr = static_cast<const unsigned char*>(sg.logits) +
-                        static_cast<int64_t>(local) * sg.row_stride * esize;
-            m.deferred = 0;
-            if (!kGeneral && m.opt_ok) {
-                // rows the candidate kernel does not take: more than 3072 staged ids, or sampling without a
-                // top-k <= 64
-                const int na = m.lo_al + m.kvw + V - m.hi_al;
-                const bool big = (na + VWe - 1) / VWe > kThreads * (kRegElems / VWe);
-                const int K = m.opt.top_k;
-                const bool cand = !m.opt.do_sample || (K > 0 && K < V && K <= kSmallK);
-                m.deferred = (big || !cand) ? 1 : 0;
-            }
-            if (!m.deferred && m.opt_ok) {
-                if (!m.direct) bytes += static_cast<uint32_t>((m.lo_al + m.kvw + V - m.hi_al) * esize);
-                bytes += static_cast<uint32_t>(m.hs_hi - m.hs_lo) * 4u;
-            }
+            m = plan_row<kGeneral>(p, r, bytes, esize);
         }
         const int nb = (n_my - k0) < 32 ? (n_my - k0) : 32;
         for (int j = 0; j < nb; ++j) {
@@ -1489,26 +1517,10 @@ __device__ void produce_rows(const LaunchParams& p, int first, int gstride, int 
                 if (n > 0)
                     ok = mbar_wait_bounded(&empty_bar[s], static_cast<uint32_t>((n - 1) & 1), progress);
                 if (ok) {
-                    unsigned char* log_dst = stages + static_cast<size_t>(s) * stage_bytes;
-                    unsigned char* hist_dst = log_dst + p.stage_logit_bytes;
                     metas[k % (2 * S_)] = m;
                     fence_proxy_async();
                     mbar_arrive_expect_tx(&full_bar[s], bytes);
-                    if (!m.direct && !m.deferred && m.opt_ok) {
-                        const int V = m.V;
-                        if (m.lo_al > 0)
-                            bulk_g2s(log_dst, m.row_ptr, static_cast<uint32_t>(m.lo_al * esize), &full_bar[s]);
-                        if (m.kvw > 0)
-                            bulk_g2s(log_dst + m.lo_al * esize, m.row_ptr + static_cast<int64_t>(m.kbase) * esize,
-                                     16u, &full_bar[s]);
-                        if (V > m.hi_al)
-                            bulk_g2s(log_dst + (m.lo_al + m.kvw) * esize,
-                                     m.row_ptr + static_cast<int64_t>(m.hi_al) * esize,
-                                     static_cast<uint32_t>((V - m.hi_al) * esize), &full_bar[s]);
-                    }
-                    if (m.hs_hi > m.hs_lo && !m.deferred && m.opt_ok)
-                        bulk_g2s(hist_dst, m.hist + m.hs_lo, static_cast<uint32_t>(m.hs_hi - m.hs_lo) * 4u,
-                                 &full_bar[s]);
+                    issue_row(p, m, esize, stages + static_cast<size_t>(s) * stage_bytes, &full_bar[s]);
                     *issued = k + 1;
                 } else {
                     atomicOr(p.err, kErrTimeout);
@@ -1520,6 +1532,38 @@ __device__ void produce_rows(const LaunchParams& p, int first, int gstride, int 
                 break;
             }
         }
+    }
+}
+
+// Candidate-kernel producer: rows are taken one at a time from a global counter as stages free up, so CTAs that
+// finish early take more rows.  After the last row it publishes an entry with row = -1 (no copies).
+__device__ void produce_rows_dynamic(const LaunchParams& p, int lane, unsigned char* stages, int stage_bytes,
+                                     RowMeta* metas, uint64_t* full_bar, uint64_t* empty_bar,
+                                     const volatile uint32_t* progress, int* issued) {
+    if (lane != 0) return;
+    const int S_ = p.n_stages;
+    for (int k = 0;; ++k) {
+        const int s = k % S_;
+        const int n = k / S_;
+        if (n > 0 && !mbar_wait_bounded(&empty_bar[s], static_cast<uint32_t>((n - 1) & 1), progress)) {
+            atomicOr(p.err, kErrTimeout);
+            return;
+        }
+        const int r = static_cast<int>(atomicAdd(p.row_counter, 1u));
+        if (r >= p.total_rows) {
+            metas[k % (2 * S_)].row = -1;
+            mbar_arrive(&full_bar[s]);
+            *issued = k + 1;
+            return;
+        }
+        uint32_t bytes = 0;
+        int esize = 4;
+        const RowMeta m = plan_row<false>(p, r, bytes, esize);
+        metas[k % (2 * S_)] = m;
+        fence_proxy_async();
+        mbar_arrive_expect_tx(&full_bar[s], bytes);
+        issue_row(p, m, esize, stages + static_cast<size_t>(s) * stage_bytes, &full_bar[s]);
+        *issued = k + 1;
     }
 }
 
@@ -1911,10 +1955,6 @@ __global__ void __launch_bounds__(kBlockThreads, 6) cand_kernel(const __grid_con
     uint32_t* bitmaps = reinterpret_cast<uint32_t*>(empty_bar + S_);
     CandMisc& cm = *reinterpret_cast<CandMisc*>(bitmaps + 2 * words4);
 
-    const int first = blockIdx.x;
-    const int gstride = gridDim.x;
-    const int n_my = first < p.total_rows ? (p.total_rows - 1 - first) / gstride + 1 : 0;
-
     if (tid == 0) {
         for (int s = 0; s < S_; ++s) {
             mbar_init(&full_bar[s], 1);
@@ -1931,8 +1971,7 @@ __global__ void __launch_bounds__(kBlockThreads, 6) cand_kernel(const __grid_con
     __syncthreads();
 
     if (warp == kProducerWarp) {
-        produce_rows<false>(p, first, gstride, n_my, lane, stages, stage_bytes, metas, full_bar, empty_bar,
-                            &cm.progress, &cm.issued);
+        produce_rows_dynamic(p, lane, stages, stage_bytes, metas, full_bar, empty_bar, &cm.progress, &cm.issued);
         return;
     }
 
@@ -1944,15 +1983,18 @@ __global__ void __launch_bounds__(kBlockThreads, 6) cand_kernel(const __grid_con
     float guess_tau = __uint_as_float(static_cast<uint32_t>(cm.seed >> 32));
     int k = 0;
     bool failed = false;
-    for (; k < n_my; ++k) {
+    for (;; ++k) {
         const int s = k % S_;
         unsigned char* sl = stages + static_cast<size_t>(s) * stage_bytes;
-        const bool ok = mbar_wait_bounded(&full_bar[s], static_cast<uint32_t>((k / S_) & 1));
+        // the producer's progress counts as progress here too (it may be waiting for rows of other CTAs)
+        const bool ok = mbar_wait_bounded(&full_bar[s], static_cast<uint32_t>((k / S_) & 1),
+                                          reinterpret_cast<volatile uint32_t*>(&cm.issued));
         if (cbar_or(!ok)) {
             failed = true;
             break;
         }
         const RowMeta& m = metas[k % (2 * S_)];
+        if (m.row < 0) break;   // no more rows
         uint32_t* bitmap = bitmaps + (k & 1) * words4;
         if (!m.opt_ok) {
             cbar();
@@ -2161,12 +2203,12 @@ __global__ void __launch_bounds__(kBlockThreads, 6) cand_kernel(const __grid_con
                 *m.out_id = res;
                 *count = 0;
             }
-            // carry a threshold to the next row: the candidate ranked ~1.25 K from the top (or the lowest), so
-            // that a similar row collects ~1.25 K candidates (cand_block left them in ascending order)
+            // carry a threshold to the next row: the candidate ranked ~1.5 K from the top, so that a similar row
+            // collects ~1.5 K candidates (cand_block left them in ascending order)
             if (par) {
                 // the value ranked `target` from the top; with fewer candidates, the lowest one moved down by
                 // the missing count times the mean gap of the lowest candidates
-                const int target = K + (K >> 2) + 4;
+                const int target = K + (K >> 1) + 4;
                 float g;
                 if (C >= target) {
                     g = okey_inv(static_cast<uint32_t>(cm.w.pk[C - target] >> 32));
@@ -2198,6 +2240,13 @@ __global__ void __launch_bounds__(kBlockThreads, 6) cand_kernel(const __grid_con
             const int issued = *reinterpret_cast<volatile int*>(&cm.issued);
             for (int kk = k; kk < issued; ++kk)
                 mbar_wait_bounded(&full_bar[kk % S_], static_cast<uint32_t>((kk / S_) & 1));
+        }
+        // the last CTA to finish resets the row counter for the next call
+        __threadfence();
+        if (atomicAdd(p.cand_done, 1u) == gridDim.x - 1) {
+            *reinterpret_cast<volatile uint32_t*>(p.row_counter) = 0u;
+            *reinterpret_cast<volatile uint32_t*>(p.cand_done) = 0u;
+            __threadfence();
         }
         if (p.guess_seed && guess_id >= 0)   // seeds the next launch's first rows
             *reinterpret_cast<volatile unsigned long long*>(p.guess_seed) =
