@@ -321,7 +321,7 @@ def main():
                          "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
                          "algorithmic_bytes_per_launch": alg, "needed_bytes_per_launch": need,
                          "frac_of_needed_bytes": need / (ms_per_step * 1e-3) / 1e9 / peak,
-                         "kernel": "sampler_kernel"},
+                         "kernel": "cand_kernel (the step: cand_kernel + whole-row kernel launch, CUDA events)"},
             "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "steps": args.e2e_steps, "path": "vw_sample(VW_MEM_HOST) from pinned host buffers"},
             "cpu_baseline": cpu,
