@@ -1574,12 +1574,16 @@ __device__ void produce_rows_dynamic(const LaunchParams& p, int lane, unsigned c
 // collects the top-k candidates; the candidates are then ranked, and the softmax, top-p cut and draw decided, by
 // all 128 element threads.
 
+constexpr int kRankBuckets = 64;   // value buckets of the candidate counting sort
+
 // Candidate work area: the candidates in ascending (value, index) order (position = rank).
 struct __align__(16) CandRank {
     unsigned long long pk[kCandCap];   // keys okey(x) << 32 | id
     unsigned long long pf[kCandCap];   // softmax numerators in fixed point, round(e * 2^52)
     double pe[kCandCap];               // the same numerators in fp64
     unsigned long long wsum[kWarps];   // per-warp totals of the survivor-mass scan
+    int32_t bcount[kRankBuckets];      // candidates per value bucket
+    int32_t bstart[kRankBuckets];      // exclusive prefix of bcount
     unsigned long long pre_cut;        // mass below the first kept candidate
     uint32_t kth_key;                  // okey of the K-th largest value
     int32_t first;                     // position of the first survivor
@@ -1600,8 +1604,12 @@ struct __align__(16) CandMisc {
     int32_t issued;                    // rows the producer has issued (timeout drain)
     uint32_t progress;                 // rows finished by the element warps
     int32_t flags[kCandCap];           // replay scratch
-    uint32_t desc[kWarps][kCandCap];   // per-warp staged positions of the elements that passed the pass's test
+    // per-warp staged positions of the elements that passed the pass's test; cand_block reuses the area as
+    // 256 uint64 keys, so it is 16-byte aligned
+    alignas(16) uint32_t desc[kWarps][kCandCap];
 };
+static_assert(offsetof(CandMisc, desc) % 16 == 0 && sizeof(CandMisc) % 16 == 0, "CandMisc alignment");
+static_assert(offsetof(CandMisc, key) % 16 == 0 && offsetof(CandMisc, w) % 16 == 0, "CandMisc alignment");
 
 __device__ __forceinline__ unsigned long long warp_incl_u64(unsigned long long v, int lane) {
 #pragma unroll
@@ -1618,28 +1626,57 @@ __device__ __forceinline__ unsigned long long warp_incl_u64(unsigned long long v
 // round(e * 2^52) (a block scan); the rounding, at most 2^-53 per value, is inside the error band.  `mx` is the
 // row maximum.  Returns the id, or -1 when a decision lies inside the band (the caller replays the row).
 __device__ int cand_block(const unsigned long long* key, int C, int K, const DevOptions& o, double r, float mx,
-                          double* out_probs, int V, CandRank& w, int tid, int lane, int warp) {
+                          float tau, double* out_probs, int V, CandRank& w, unsigned long long* tmp, int tid, int lane,
+                          int warp) {
     if (tid == 0) {
         w.cut = -1;
         w.ambiguous = 0;
         w.res = -1;
         w.hits = 0;
     }
+    // ---- rank: a counting sort over value buckets, then a count within the bucket.  Every candidate lies in
+    //      [tau, mx]; the bucket of x is trunc((x - tau) * 64 / (mx - tau)) in fp32, non-decreasing in x, so the
+    //      buckets keep the key order and only keys of the same bucket need comparing.
+    if (tid < kRankBuckets) w.bcount[tid] = 0;
+    cbar();
+    const float span = __fsub_rn(mx, tau);
+    const float scale = span > 0.0f ? __fdiv_rn(static_cast<float>(kRankBuckets), span) : 0.0f;
+    unsigned long long ka = 0ull;
+    int bk = 0, arrival = 0;
     if (tid < C) {
-        const unsigned long long kt = key[tid];
-        const ulonglong2* k2 = reinterpret_cast<const ulonglong2*>(key);
-        int lt = 0;
-#pragma unroll 4
-        for (int j = 0; j < (C >> 1); ++j) {
-            const ulonglong2 v = k2[j];
-            lt += (v.x < kt ? 1 : 0) + (v.y < kt ? 1 : 0);
+        ka = key[tid];
+        const float x = okey_inv(static_cast<uint32_t>(ka >> 32));
+        bk = min(max(static_cast<int>(__fmul_rn(__fsub_rn(x, tau), scale)), 0), kRankBuckets - 1);
+        arrival = atomicAdd(&w.bcount[bk], 1);
+    }
+    cbar();
+    if (warp == 0) {   // exclusive prefix of the 64 bucket counts
+        const int c0 = w.bcount[2 * lane], c1 = w.bcount[2 * lane + 1];
+        int incl = c0 + c1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(kFull, incl, o);
+            if (lane >= o) incl += y;
         }
-        if (C & 1) lt += key[C - 1] < kt ? 1 : 0;
-        const double et = softmax_num(okey_inv(static_cast<uint32_t>(kt >> 32)), mx);   // Sampler.cs:57
-        w.pk[lt] = kt;
+        w.bstart[2 * lane] = incl - c0 - c1;
+        w.bstart[2 * lane + 1] = incl - c1;
+    }
+    cbar();
+    int b0 = 0, bn = 0;
+    if (tid < C) {
+        b0 = w.bstart[bk];
+        bn = w.bcount[bk];
+        tmp[b0 + arrival] = ka;
+    }
+    cbar();
+    if (tid < C) {
+        int lt = b0;
+        for (int j = b0; j < b0 + bn; ++j) lt += tmp[j] < ka ? 1 : 0;
+        const double et = softmax_num(okey_inv(static_cast<uint32_t>(ka >> 32)), mx);   // Sampler.cs:57
+        w.pk[lt] = ka;
         w.pf[lt] = __double2ull_rn(__dmul_rn(et, kFix52));
         w.pe[lt] = et;
-        if (lt == C - K) w.kth_key = static_cast<uint32_t>(kt >> 32);   // Sampler.cs:45-46
+        if (lt == C - K) w.kth_key = static_cast<uint32_t>(ka >> 32);   // Sampler.cs:45-46
     }
     if (out_probs)
         for (int i = tid; i < V; i += kThreads) out_probs[i] = 0.0;
@@ -2131,6 +2168,7 @@ __global__ void __launch_bounds__(kBlockThreads, 6) cand_kernel(const __grid_con
         const int K = o.top_k;
         const int gid = m.seg * 65536 + m.opt_idx;
         const bool fuse = guess_id == gid;
+        float tau_used = guess_tau;   // every candidate is >= it
         uint32_t* const count = &cm.count[k & 1];
         if (fuse)
             row_pass_dt<kPassFused>(dtype, sl, nvec, mp, c, tid, a, b, bi, guess_tau, count, cm.key, cm.desc[warp]);
@@ -2172,6 +2210,7 @@ __global__ void __launch_bounds__(kBlockThreads, 6) cand_kernel(const __grid_con
                 mx = fmaxf(mx, cm.red_f[w]);
             }
             C = kCandCap + 1;
+            tau_used = tau;
             if (!is_neg_inf(tau)) {
                 row_pass_dt<kPassAppend>(dtype, sl, nvec, mp, c, tid, a, b, bi, tau, count, cm.key, cm.desc[warp]);
                 cbar();
@@ -2187,7 +2226,9 @@ __global__ void __launch_bounds__(kBlockThreads, 6) cand_kernel(const __grid_con
             // every thread read C before the first barrier inside cand_block / the replay; the counter is next
             // used two rows on, and the row between always passes a barrier
             const bool par = !p.force_exact;
-            int res = par ? cand_block(cm.key, C, K, o, m.uniform, mx, out_probs, V, cm.w, tid, lane, warp) : -1;
+            int res = par ? cand_block(cm.key, C, K, o, m.uniform, mx, tau_used, out_probs, V, cm.w,
+                                       reinterpret_cast<unsigned long long*>(&cm.desc[0][0]), tid, lane, warp)
+                          : -1;
             if (res < 0) {
                 if (warp == 0) {
                     const int rr = replay_candidates(cm.key, C, K, o, m.uniform, V, out_probs, cm.flags, lane);
