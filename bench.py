@@ -274,17 +274,18 @@ def main():
                    out_ids=torch.full((s.n_rows,), -1, dtype=torch.int32).pin_memory())
         host_arrays.append((s, arr))
     hsegs = [make_segment(s, arr) for s, arr in host_arrays]
-    h2d = sum(int(a.numel() * a.element_size()) for _, arr in host_arrays for k, a in arr.items()
-              if a is not None and k != "out_ids")
     d2h = sum(int(arr["out_ids"].numel() * 4) for _, arr in host_arrays)
     for _ in range(2):
         sample_rows(dev, hsegs, opts)
+    dev.stats(reset=True)
     if world > 1:
         dist.barrier()
     t0 = time.perf_counter()
     for _ in range(args.e2e_steps):
         sample_rows(dev, hsegs, opts)
     e2e_s = time.perf_counter() - t0
+    # bytes the library copied host -> device per step (it skips the logit columns no kernel reads)
+    h2d = dev.stats(reset=True)["h2d_bytes"] // max(args.e2e_steps, 1)
     e2e_value = rows_per_rank * world * args.e2e_steps / max_over_ranks(e2e_s, device="cuda")
 
     line = None
@@ -323,7 +324,9 @@ def main():
                          "frac_of_needed_bytes": need / (ms_per_step * 1e-3) / 1e9 / peak,
                          "kernel": "cand_kernel (the step: cand_kernel + whole-row kernel launch, CUDA events)"},
             "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "steps": args.e2e_steps, "path": "vw_sample(VW_MEM_HOST) from pinned host buffers"},
+                    "steps": args.e2e_steps,
+                    "path": "vw_sample(VW_MEM_HOST) from pinned host buffers: logits (without the suppressed "
+                            "span's columns), histories, steps, options, uniforms in; ids out"},
             "cpu_baseline": cpu,
             "clocks": clocks.summary(),
             "gpu_launches": 2 * args.steps,   # per step: the candidate kernel + the whole-row kernel

@@ -57,6 +57,20 @@ def test_host_memory_path_matches_device_path(device, cfg):
     assert_ids_equal(w, b, oracle_ids(w))
 
 
+def test_host_path_copies_only_read_columns(device):
+    """A talker row's suppressed span [2048, 3072) is not copied to the device: only [0, 2152) (through the
+    16-byte vector holding EOS 2150) of each fp32 row travels, and the ids still match the oracle."""
+    w = workloads.make(2, 64)
+    device.stats(reset=True)
+    ids = run_workload(device, w, mem="host")
+    h2d = device.stats(reset=True)["h2d_bytes"]
+    seg = w.segments[0]
+    logits = seg.n_rows * 2152 * 4
+    others = (seg.n_rows + 1) * 8 + seg.hist_ids.nbytes + seg.steps.nbytes + seg.opt_index.nbytes + seg.uniforms.nbytes
+    assert h2d == logits + others
+    assert_ids_equal(w, ids, oracle_ids(w))
+
+
 def test_stream_ordered_call(device):
     import torch
     w = workloads.make(2, 256)

@@ -92,11 +92,11 @@ class VwStats(ctypes.Structure):
         ("rows_general_replayed", ctypes.c_uint64),
         ("rows_large", ctypes.c_uint64),
         ("rows_overflow", ctypes.c_uint64),
-        ("reserved", ctypes.c_uint64),
+        ("h2d_bytes", ctypes.c_uint64),
     ]
 
     def as_dict(self) -> dict:
-        return {name: int(getattr(self, name)) for name, _ in self._fields_ if name != "reserved"}
+        return {name: int(getattr(self, name)) for name, _ in self._fields_}
 
 
 class VwError(RuntimeError):

@@ -36,6 +36,7 @@ struct vw_handle {
     unsigned long long* d_stats = nullptr;   // vw::kNumStats per-path row counters
     unsigned long long* d_guess = nullptr;   // candidate threshold carried from call to call
     int force_exact = 0;                     // VW_FORCE_EXACT at creation
+    unsigned long long h2d_bytes = 0;        // host -> device input bytes of VW_MEM_HOST calls (vw_stats.h2d_bytes)
     std::string last_error;
 };
 
@@ -164,7 +165,18 @@ T* stage_copy(vw_handle* h, const T* src, size_t count, size_t* off, cudaStream_
     T* dst = reinterpret_cast<T*>(h->d_stage + *off);
     *off += count * sizeof(T);
     if (*err == cudaSuccess) *err = cudaMemcpyAsync(dst, src, count * sizeof(T), cudaMemcpyHostToDevice, st);
+    h->h2d_bytes += count * sizeof(T);
     return dst;
+}
+
+// Logit columns [c0, c1) of every row of segment s, copied with one 2D copy into the staging area at dst.
+void stage_columns(vw_handle* h, const vw_segment& s, size_t es, unsigned char* dst, int c0, int c1, cudaStream_t st,
+                   cudaError_t* err) {
+    if (c1 <= c0 || *err != cudaSuccess) return;
+    const size_t pitch = static_cast<size_t>(s.row_stride) * es;
+    *err = cudaMemcpy2DAsync(dst + c0 * es, pitch, static_cast<const unsigned char*>(s.logits) + c0 * es, pitch,
+                             static_cast<size_t>(c1 - c0) * es, s.n_rows, cudaMemcpyHostToDevice, st);
+    h->h2d_bytes += static_cast<size_t>(c1 - c0) * es * s.n_rows;
 }
 
 struct HostStaging {
@@ -202,7 +214,32 @@ vw_status stage_host_inputs(vw_handle* h, const vw_segment* segs, int n, cudaStr
         if (s.n_rows == 0) continue;
         const size_t es = s.dtype == VW_F32 ? 4 : 2;
         const size_t nel = static_cast<size_t>(s.n_rows - 1) * s.row_stride + s.vocab;
-        d.logits = stage_copy(h, static_cast<const unsigned char*>(s.logits), nel * es, &off, st, &e);
+        // The kernels read, of a talker row with a suppress span, only the columns outside the span's 16-byte
+        // aligned interior plus the 16-byte vector holding EOS (the rest become -inf unread).  Those columns are
+        // copied as [0, lo_al) (extended over the EOS vector when it lies in the first half of the span) and
+        // [hi_al, V); every other segment is copied whole.
+        int c_lo = s.vocab, c_hi = s.vocab;
+        if (s.kind == VW_ROWS_TALKER) {
+            const int vw = s.dtype == VW_F32 ? 4 : 8;
+            const int lo = std::clamp(s.suppress_lo, 0, s.vocab), hi = std::clamp(s.suppress_hi, 0, s.vocab);
+            const int la = (lo + vw - 1) / vw * vw, ha = hi / vw * vw;
+            if (lo < hi && la < ha) {
+                c_lo = la;
+                c_hi = ha;
+                if (s.eos_id >= la && s.eos_id < ha) c_lo = (s.eos_id / vw + 1) * vw;   // through the EOS vector
+                if (c_lo - la > (ha - la) / 2) c_lo = c_hi = s.vocab;                    // no saving: copy whole
+            }
+        }
+        if (c_lo < c_hi) {
+            off = round_up(off, 256);
+            unsigned char* dst = reinterpret_cast<unsigned char*>(h->d_stage) + off;
+            off += nel * es;
+            stage_columns(h, s, es, dst, 0, c_lo, st, &e);
+            stage_columns(h, s, es, dst, c_hi, s.vocab, st, &e);
+            d.logits = dst;
+        } else {
+            d.logits = stage_copy(h, static_cast<const unsigned char*>(s.logits), nel * es, &off, st, &e);
+        }
         if (s.kind == VW_ROWS_TALKER && s.hist_offsets) {
             auto& ofs = hs->offsets[i];
             ofs.resize(static_cast<size_t>(s.n_rows) + 1);
@@ -507,6 +544,8 @@ VW_EXPORT vw_status vw_get_stats(vw_handle* h, vw_stats* out, int32_t reset) {
     if (e == cudaSuccess && reset) e = cudaMemset(h->d_stats, 0, sizeof(vw_stats));
     if (e == cudaSuccess && reset) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return cuda_fail(h, e, "vw_get_stats");
+    out->h2d_bytes = h->h2d_bytes;   // host-side counter (the device word in that slot is unused)
+    if (reset) h->h2d_bytes = 0;
     return VW_OK;
 }
 
