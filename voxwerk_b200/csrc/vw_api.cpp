@@ -17,9 +17,13 @@
 
 #define VW_EXPORT extern "C" __attribute__((visibility("default")))
 
+constexpr int kCopyStreams = 3;   // host -> device copies of VW_MEM_HOST calls run on this many copy engines
+
 struct vw_handle {
     int device = -1;
     cudaStream_t stream = nullptr;
+    cudaStream_t copy_streams[kCopyStreams] = {};
+    cudaEvent_t copy_events[kCopyStreams + 1] = {};   // one per copy stream, and the fork point
     int sm_count = 0;
     unsigned* d_err = nullptr;      // device error word (kErr* bits)
     unsigned* h_err = nullptr;      // pinned mirror
@@ -169,14 +173,54 @@ T* stage_copy(vw_handle* h, const T* src, size_t count, size_t* off, cudaStream_
     return dst;
 }
 
-// Logit columns [c0, c1) of every row of segment s, copied with one 2D copy into the staging area at dst.
-void stage_columns(vw_handle* h, const vw_segment& s, size_t es, unsigned char* dst, int c0, int c1, cudaStream_t st,
+// The copy streams start after the work already on st (fork) and st continues after them (join).
+cudaError_t fork_copies(vw_handle* h, cudaStream_t st) {
+    cudaError_t e = cudaEventRecord(h->copy_events[kCopyStreams], st);
+    for (int i = 0; i < kCopyStreams && e == cudaSuccess; ++i)
+        e = cudaStreamWaitEvent(h->copy_streams[i], h->copy_events[kCopyStreams], 0);
+    return e;
+}
+cudaError_t join_copies(vw_handle* h, cudaStream_t st) {
+    cudaError_t e = cudaSuccess;
+    for (int i = 0; i < kCopyStreams && e == cudaSuccess; ++i) {
+        e = cudaEventRecord(h->copy_events[i], h->copy_streams[i]);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(st, h->copy_events[i], 0);
+    }
+    return e;
+}
+
+// Logit columns [c0, c1) of every row of segment s, copied into the staging area at dst by 2D copies, the rows
+// split over the copy streams.
+void stage_columns(vw_handle* h, const vw_segment& s, size_t es, unsigned char* dst, int c0, int c1,
                    cudaError_t* err) {
-    if (c1 <= c0 || *err != cudaSuccess) return;
+    if (c1 <= c0) return;
     const size_t pitch = static_cast<size_t>(s.row_stride) * es;
-    *err = cudaMemcpy2DAsync(dst + c0 * es, pitch, static_cast<const unsigned char*>(s.logits) + c0 * es, pitch,
-                             static_cast<size_t>(c1 - c0) * es, s.n_rows, cudaMemcpyHostToDevice, st);
+    for (int i = 0; i < kCopyStreams && *err == cudaSuccess; ++i) {
+        const int r0 = static_cast<int>(static_cast<int64_t>(s.n_rows) * i / kCopyStreams);
+        const int r1 = static_cast<int>(static_cast<int64_t>(s.n_rows) * (i + 1) / kCopyStreams);
+        if (r1 <= r0) continue;
+        *err = cudaMemcpy2DAsync(dst + r0 * pitch + c0 * es, pitch,
+                                 static_cast<const unsigned char*>(s.logits) + r0 * pitch + c0 * es, pitch,
+                                 static_cast<size_t>(c1 - c0) * es, r1 - r0, cudaMemcpyHostToDevice,
+                                 h->copy_streams[i]);
+    }
     h->h2d_bytes += static_cast<size_t>(c1 - c0) * es * s.n_rows;
+}
+
+// One large host array into the staging area at *off, split over the copy streams; returns the device pointer.
+template <typename T>
+T* stage_copy_split(vw_handle* h, const T* src, size_t count, size_t* off, cudaError_t* err) {
+    if (!src || count == 0) return nullptr;
+    *off = round_up(*off, 256);
+    T* dst = reinterpret_cast<T*>(h->d_stage + *off);
+    *off += count * sizeof(T);
+    for (int i = 0; i < kCopyStreams && *err == cudaSuccess; ++i) {
+        const size_t a = count * i / kCopyStreams, b = count * (i + 1) / kCopyStreams;
+        if (b > a)
+            *err = cudaMemcpyAsync(dst + a, src + a, (b - a) * sizeof(T), cudaMemcpyHostToDevice, h->copy_streams[i]);
+    }
+    h->h2d_bytes += count * sizeof(T);
+    return dst;
 }
 
 struct HostStaging {
@@ -207,7 +251,7 @@ vw_status stage_host_inputs(vw_handle* h, const vw_segment* segs, int n, cudaStr
     vw_status r = grow(h, &h->d_stage, &h->stage_bytes, need, "staging buffer");
     if (r != VW_OK) return r;
     size_t off = 0;
-    cudaError_t e = cudaSuccess;
+    cudaError_t e = fork_copies(h, st);
     for (int i = 0; i < n; ++i) {
         const vw_segment& s = segs[i];
         vw_segment& d = hs->dev[i];
@@ -234,11 +278,11 @@ vw_status stage_host_inputs(vw_handle* h, const vw_segment* segs, int n, cudaStr
             off = round_up(off, 256);
             unsigned char* dst = reinterpret_cast<unsigned char*>(h->d_stage) + off;
             off += nel * es;
-            stage_columns(h, s, es, dst, 0, c_lo, st, &e);
-            stage_columns(h, s, es, dst, c_hi, s.vocab, st, &e);
+            stage_columns(h, s, es, dst, 0, c_lo, &e);
+            stage_columns(h, s, es, dst, c_hi, s.vocab, &e);
             d.logits = dst;
         } else {
-            d.logits = stage_copy(h, static_cast<const unsigned char*>(s.logits), nel * es, &off, st, &e);
+            d.logits = stage_copy_split(h, static_cast<const unsigned char*>(s.logits), nel * es, &off, &e);
         }
         if (s.kind == VW_ROWS_TALKER && s.hist_offsets) {
             auto& ofs = hs->offsets[i];
@@ -246,7 +290,7 @@ vw_status stage_host_inputs(vw_handle* h, const vw_segment* segs, int n, cudaStr
             for (int k = 0; k <= s.n_rows; ++k) ofs[k] = s.hist_offsets[k] - s.hist_offsets[0];
             d.hist_offsets = stage_copy(h, ofs.data(), ofs.size(), &off, st, &e);
             const size_t nh = static_cast<size_t>(s.hist_offsets[s.n_rows] - s.hist_offsets[0]);
-            d.hist_ids = nh ? stage_copy(h, s.hist_ids + s.hist_offsets[0], nh, &off, st, &e) : nullptr;
+            d.hist_ids = nh ? stage_copy_split(h, s.hist_ids + s.hist_offsets[0], nh, &off, &e) : nullptr;
             if (!d.hist_ids) {
                 off = round_up(off, 256);
                 d.hist_ids = reinterpret_cast<int32_t*>(h->d_stage + off);   // never read: every history empty
@@ -267,6 +311,7 @@ vw_status stage_host_inputs(vw_handle* h, const vw_segment* segs, int n, cudaStr
             off += static_cast<size_t>(s.n_rows) * s.vocab * 8;
         }
     }
+    if (e == cudaSuccess) e = join_copies(h, st);
     if (e != cudaSuccess) return cuda_fail(h, e, "host-to-device copy");
     return VW_OK;
 }
@@ -484,6 +529,10 @@ VW_EXPORT vw_status vw_create(int32_t device, vw_handle** out) {
     if (e == cudaSuccess) e = cudaMallocHost(&h->h_err, sizeof(unsigned));
     if (e == cudaSuccess) e = cudaMemset(h->d_err, 0, sizeof(unsigned));
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&h->opts_done, cudaEventDisableTiming);
+    for (int i = 0; i < kCopyStreams && e == cudaSuccess; ++i)
+        e = cudaStreamCreateWithFlags(&h->copy_streams[i], cudaStreamNonBlocking);
+    for (int i = 0; i <= kCopyStreams && e == cudaSuccess; ++i)
+        e = cudaEventCreateWithFlags(&h->copy_events[i], cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaMalloc(&h->d_stats, sizeof(unsigned long long) * vw::kNumStats);
     if (e == cudaSuccess) e = cudaMemset(h->d_stats, 0, sizeof(unsigned long long) * vw::kNumStats);
     if (e == cudaSuccess) e = cudaMalloc(&h->d_guess, sizeof(unsigned long long));
@@ -515,6 +564,10 @@ VW_EXPORT vw_status vw_destroy(vw_handle* h) {
         if (h->h_err) cudaFreeHost(h->h_err);
         if (h->opts_done) cudaEventDestroy(h->opts_done);
         if (h->stream) cudaStreamDestroy(h->stream);
+        for (int i = 0; i < kCopyStreams; ++i)
+            if (h->copy_streams[i]) cudaStreamDestroy(h->copy_streams[i]);
+        for (int i = 0; i <= kCopyStreams; ++i)
+            if (h->copy_events[i]) cudaEventDestroy(h->copy_events[i]);
     }
     delete h;
     return VW_OK;
