@@ -441,7 +441,7 @@ vw_status sample_impl(vw_handle* h, const vw_segment* segs, int32_t n_segs, cons
     }
     p.stage_logit_bytes = logit_bytes;
     p.stage_hist_cap = hist_cap;
-    p.bitmap_words = (vmax + 31) / 32;
+    p.flag_bytes = static_cast<int32_t>(round_up(static_cast<size_t>(vmax), 16));
     p.vmax = vmax;
     p.err = h->d_err;
     p.stats = h->d_stats;
@@ -828,7 +828,7 @@ vw_status sample_static_impl(vw_handle* h, int32_t device, const vw_segment* seg
     std::memcpy(p.inl_opts, opts, sizeof(vw_options) * n_opts);
     p.stage_logit_bytes = logit_bytes;
     p.stage_hist_cap = hist_cap;
-    p.bitmap_words = (vmax + 31) / 32;
+    p.flag_bytes = static_cast<int32_t>(round_up(static_cast<size_t>(vmax), 16));
     p.vmax = vmax;
     p.stats = nullptr;
     const char* fe = std::getenv("VW_FORCE_EXACT");

@@ -77,7 +77,7 @@ struct LaunchParams {
     int32_t n_stages;
     int32_t stage_logit_bytes;    // multiple of 16
     int32_t stage_hist_cap;       // ids per stage, multiple of 4
-    int32_t bitmap_words;         // vmax / 32 rounded up
+    int32_t flag_bytes;           // history flag map: a byte per id, vmax rounded up to 16
     int32_t vmax;
     unsigned* err;
     int32_t* deferred_rows;       // rows the candidate kernel leaves to the whole-row kernel (total_rows entries)

@@ -6,11 +6,11 @@
 //     suppressed span of talker rows is never read.
 //   * four element warps (one warp-group per row) do the rest of the row.
 // cand_kernel takes every row (CTA b: rows b, b + grid, ...).  It finishes greedy rows and sampling rows with
-// top-k <= 64, keeping the row in its stage, and appends every other row to a deferred list.  sampler_kernel<true>
-// (the whole-row kernel) takes the deferred rows, with each row held in registers.
+// top-k <= 64, keeping the row in its stage, and appends every other row to a deferred list.  whole_row_kernel
+// takes the deferred rows, with each row held in registers.
 //
 // Per row, in the order of the reference (src/Voxwerk/Talker/Sampler.cs, TalkerGenerator.cs):
-//   1. repetition penalty (talker rows; Sampler.cs:25-33): history ids -> a V-bit shared bitmap (Distinct());
+//   1. repetition penalty (talker rows; Sampler.cs:25-33): history ids -> a flag byte per id (Distinct());
 //      each element whose bit is set becomes s < 0 ? s * p : s / p in fp32.  The IEEE quotient s / p is formed
 //      as fp32(fp64(s) * RN64(1/p)): the fp64 product is within 2^-52 relative of s/p while no fp32 rounding
 //      midpoint lies closer than 2^-49 relative to a quotient of two fp32 values, so both round the same way.
@@ -87,19 +87,6 @@ struct Cand {
     int32_t idx;
 };
 
-// Candidate-path work area: the candidates in ascending (value, index) order (position = rank).
-struct __align__(16) CandWork {
-    unsigned long long pk[kCandCap];   // keys okey(x) << 32 | id
-    unsigned long long pf[kCandCap];   // softmax numerators in fixed point, round(e * 2^52)
-    double pe[kCandCap];               // the same numerators in fp64
-    unsigned long long tot;            // mass of every candidate
-    unsigned long long pre_first;      // mass below the first survivor
-    unsigned long long pre_cut;        // mass below the first kept candidate
-    uint32_t kth_key;                  // okey of the K-th largest value
-    int32_t first;                     // position of the first survivor
-    int32_t cut;                       // position of the first kept candidate (-1: undecided)
-    int32_t ambiguous, res, hits;
-};
 
 // Binned-search histograms: counts and the three 20-bit chunks of fixed-point masses per bin.
 struct Bins {
@@ -121,8 +108,7 @@ struct __align__(16) SmemMisc {
     unsigned long long bc_u[2];
     double bc_d[4];
     union __align__(16) {
-        CandWork cw;      // candidate path
-        Bins bins;        // general path
+        Bins bins;        // whole-row path histograms
     } u;
     int32_t flags[kCandCap];   // candidate replay scratch
 };
@@ -466,7 +452,7 @@ struct RowCtx {
     double pen_rcp;      // RN64(1 / pen)
     bool sample;
     float inv_t;         // fp32(1 / T)
-    const uint32_t* bitmap;
+    const uint8_t* flags;     // flags[id] = 1: id is in the history (Distinct()); penalised when pen_on
     int slow_vlo, slow_vhi;   // staged vectors that may hold suppressed ids
     int eos_vec;              // staged vector holding a suppressed EOS, or -1
     bool pen_lazy;            // candidate kernel: penalty > 1, applied to the candidates only
@@ -495,16 +481,28 @@ __device__ __forceinline__ float penalize(float s, float pen, double pen_rcp) {
     return s < 0.0f ? __fmul_rn(s, pen) : __double2float_rn(__dmul_rn(static_cast<double>(s), pen_rcp));
 }
 
-// penalty (Sampler.cs:31) -> mask (TalkerGenerator.cs:247-248) -> temperature (Sampler.cs:40)
-// c.pen_on is set only where the penalty is applied per element (bf16 rows; fp32 rows take it in place).
-__device__ __forceinline__ float transform(float v, int idx, uint32_t bits, const RowCtx& c) {
-    if (c.pen_on && ((bits >> (idx & 31)) & 1u)) v = penalize(v, c.pen, c.pen_rcp);
+// penalty (Sampler.cs:31) -> mask (TalkerGenerator.cs:247-248) -> temperature (Sampler.cs:40); `pen`: the id is
+// in the history
+__device__ __forceinline__ float transform(float v, int idx, bool pen, const RowCtx& c) {
+    if (c.pen_on && pen) v = penalize(v, c.pen, c.pen_rcp);
     if (c.kind == 0) {
         const bool masked = (idx >= c.sup_lo && idx < c.sup_hi && idx != c.eos) || (idx == c.eos && c.eos_blocked);
         if (masked) v = neg_inf();
     }
     if (c.sample) v = __fmul_rn(v, c.inv_t);
     return v;
+}
+
+// Bit e set: id i0 + e is in the history (its flag byte is 1).  i0 is a multiple of VW.
+template <int VW>
+__device__ __forceinline__ uint32_t pen_mask(const uint8_t* flags, int i0) {
+    uint32_t m = 0u;
+#pragma unroll
+    for (int w = 0; w < VW / 4; ++w) {
+        const uint32_t f = reinterpret_cast<const uint32_t*>(flags + i0)[w];   // four 0/1 bytes
+        m |= ((f & 1u) | ((f >> 7) & 2u) | ((f >> 14) & 4u) | ((f >> 21) & 8u)) << (4 * w);
+    }
+    return m;
 }
 
 template <int VW>
@@ -1027,134 +1025,6 @@ __device__ int general_parallel(const float (&x)[kRegElems], int nvec, const Row
 // ---------------------------------------------------------------- candidate path (top-k <= 64)
 constexpr double kFix52 = 4503599627370496.0;   // 2^52: candidate masses in fixed point (e <= 1, <= 128 values)
 
-// key[0, C) (C <= 128) = okey(x) << 32 | id of every value >= tau, so of every survivor; keys are unique.  All 128
-// element threads; candidate t is owned by thread t.  Sums are exact 64-bit integer sums of round(e * 2^52), each
-// thread adding up the ranks below its own (no shuffles, no fp64 chains); the rounding, at most 2^-53 per value,
-// is inside the error band.  `mx` is the row maximum.  Returns the id, or -1 when a decision lies inside the band
-// (the caller replays the row).
-__device__ int cand_parallel(const unsigned long long* key, int C, int K, const DevOptions& o, double r, float mx,
-                             double* out_probs, int V, CandWork& w, int tid) {
-    const bool mine = tid < C;
-    unsigned long long kt = 0, ft = 0;
-    double et = 0.0;
-    int lt = 0;
-    if (tid == 0) {
-        w.cut = -1;
-        w.ambiguous = 0;
-        w.res = -1;
-        w.hits = 0;
-    }
-    if (mine) {
-        kt = key[tid];
-        const ulonglong2* k2 = reinterpret_cast<const ulonglong2*>(key);
-        const int C2 = C >> 1;
-#pragma unroll 4
-        for (int j = 0; j < C2; ++j) {
-            const ulonglong2 v = k2[j];
-            lt += (v.x < kt ? 1 : 0) + (v.y < kt ? 1 : 0);
-        }
-        if (C & 1) lt += key[C - 1] < kt ? 1 : 0;
-        et = softmax_num(okey_inv(static_cast<uint32_t>(kt >> 32)), mx);   // Sampler.cs:57
-        ft = __double2ull_rn(__dmul_rn(et, kFix52));
-        w.pk[lt] = kt;
-        w.pf[lt] = ft;
-        w.pe[lt] = et;
-        if (lt == C - K) w.kth_key = static_cast<uint32_t>(kt >> 32);
-    }
-    if (out_probs)
-        for (int i = tid; i < V; i += kThreads) out_probs[i] = 0.0;
-    cbar();
-    const uint32_t kth_key = w.kth_key;
-    const uint32_t vt = static_cast<uint32_t>(kt >> 32);
-    const bool surv = mine && vt >= kth_key;
-    unsigned long long pre = 0;   // mass of the candidates ranked below this one
-    if (mine) {
-        const ulonglong2* f2 = reinterpret_cast<const ulonglong2*>(w.pf);
-#pragma unroll 4
-        for (int q = 0; q < (lt >> 1); ++q) {
-            const ulonglong2 v = f2[q];
-            pre += v.x + v.y;
-        }
-        if (lt & 1) pre += w.pf[lt - 1];
-        if (lt == C - 1) w.tot = pre + ft;
-        if (surv && (lt == 0 || static_cast<uint32_t>(w.pk[lt - 1] >> 32) < kth_key)) {
-            w.first = lt;
-            w.pre_first = pre;
-        }
-    }
-    cbar();
-    const int first = w.first;
-    const int S = C - first;
-    const double eta = (6.0 * S + 128.0) * kU;
-    if (o.top_p >= 1.0f) {
-        if (tid == 0) {
-            w.cut = first;
-            w.pre_cut = w.pre_first;
-        }
-    } else if (surv) {
-        // ---- top-p cut over the ascending order (Sampler.cs:62-72): the element whose cumulative mass first
-        //      exceeds (1 - TopP) of the total breaks the loop; the last element is never removed
-        const unsigned long long tot_s = w.tot - w.pre_first;
-        const double tot_d = static_cast<double>(tot_s);
-        const double thr = static_cast<double>(__fsub_rn(1.0f, o.top_p));
-        const double T = __dmul_rn(thr, tot_d);
-        const double band = __dmul_rn(eta, tot_d);
-        const double bd = static_cast<double>(pre - w.pre_first);            // cum before this element
-        const double id = static_cast<double>(pre - w.pre_first + ft);       // cum including it
-        const int pos = lt - first;
-        const bool brk = pos <= S - 2 && !(bd > T) && id > T;
-        const bool all_but_last = pos == S - 1 && !(bd > T);
-        if (brk || all_but_last) {
-            bool amb = false;
-            if (brk && !(__dsub_rn(id, T) > band)) amb = true;
-            if (bd > 0.0 && !(__dsub_rn(T, bd) > band)) amb = true;
-            // the value groups next to the cut must be strictly apart in probability (the reference orders by
-            // probability, then index)
-            int qlo = lt - 1;
-            while (qlo >= first && static_cast<uint32_t>(w.pk[qlo] >> 32) == vt) --qlo;
-            if (qlo >= first && !(w.pe[qlo] < et * (1.0 - 32.0 * kU))) amb = true;
-            if (brk && qlo < lt - 1) {   // the cut falls inside this value group: the group above matters too
-                int qhi = lt + 1;
-                while (qhi < C && static_cast<uint32_t>(w.pk[qhi] >> 32) == vt) ++qhi;
-                if (qhi < C && !(w.pe[qhi] > et * (1.0 + 32.0 * kU))) amb = true;
-            }
-            w.cut = lt;
-            w.pre_cut = pre;
-            w.ambiguous = amb ? 1 : 0;
-        }
-    }
-    cbar();
-    if (w.ambiguous || w.cut < 0) return -1;
-    const int cut = w.cut;
-    const bool kept = mine && lt >= cut;
-    const unsigned long long B = w.tot - w.pre_cut;   // mass of the kept candidates
-    if (kept) {
-        // ---- inverse-CDF draw over the kept ids in index order (Sampler.cs:73-87)
-        const uint32_t it = static_cast<uint32_t>(kt);
-        unsigned long long pre2 = 0;
-        for (int q = cut; q < C; ++q) {
-            const unsigned long long kq = w.pk[q];
-            if (static_cast<uint32_t>(kq) < it) pre2 += w.pf[q];
-        }
-        const double Bd = static_cast<double>(B);
-        const double rB = __dmul_rn(r, Bd);
-        const double lo = static_cast<double>(pre2), hi = static_cast<double>(pre2 + ft);
-        if (ft > 0 && !(lo > rB) && hi > rB) {
-            bool amb = !(__dsub_rn(hi, rB) > __dmul_rn(eta, Bd));
-            if (pre2 > 0 && !(__dsub_rn(rB, lo) > __dmul_rn(eta, Bd))) amb = true;
-            atomicAdd(&w.hits, 1);
-            w.res = amb ? -1 : static_cast<int>(it);
-        }
-    }
-    cbar();
-    const int res = w.hits == 1 ? w.res : -1;
-    if (res >= 0 && out_probs) {
-        if (kept) out_probs[static_cast<uint32_t>(kt)] = __ddiv_rn(et, __dmul_rn(static_cast<double>(B), 1.0 / kFix52));
-        cbar();
-    }
-    return res;
-}
-
 // ---------------------------------------------------------------- candidate replay (warp 0)
 // The reference's sequential operations on the candidates (<= 128 survivors), every lane of one warp running the
 // same chain on shuffled values.
@@ -1276,13 +1146,11 @@ __device__ int replay_candidates(const unsigned long long* ck, int C, int K, con
 // ---------------------------------------------------------------- element pass
 // One pass over the staged row: transform every element into x[] (registers).  Sampling rows track each thread's
 // two largest values; greedy rows the first maximum.  Vectors that no mask boundary, EOS rule or per-element
-// penalty touches take the short path (temperature only).  kFuse: every value >= tau_g is also appended to the
-// candidate keys (okey(x) << 32 | id).
-template <int VW, bool kSample, bool kFuse>
+// penalty touches take the short path (temperature only).
+template <int VW, bool kSample>
 __device__ __forceinline__ void process_vectors(const unsigned char* sl, int nvec, const RowMap& mp,
                                                 const RowCtx& c, int tid, float (&x)[kRegElems],
-                                                float& tmax, float& tmax2, float& bestv, int& besti,
-                                                float tau_g, uint32_t* cand_count, unsigned long long* ckey) {
+                                                float& tmax, float& tmax2, float& bestv, int& besti) {
     constexpr int G = kRegElems / VW;
 #pragma unroll
     for (int g = 0; g < G; ++g) {
@@ -1291,26 +1159,21 @@ __device__ __forceinline__ void process_vectors(const unsigned char* sl, int nve
             float v[VW];
             load_vec<VW>(sl, qv, v);
             const int i0 = mp.idx(qv * VW);
-            const uint32_t bits = c.pen_on ? c.bitmap[i0 >> 5] : 0u;
-            const bool slow = (c.pen_on && ((bits >> (i0 & 31)) & ((1u << VW) - 1u)) != 0u) ||
+            const uint32_t bits = c.pen_on ? pen_mask<VW>(c.flags, i0) : 0u;
+            const bool slow = bits != 0u ||
                               static_cast<unsigned>(qv - c.slow_vlo) < static_cast<unsigned>(c.slow_vhi - c.slow_vlo) ||
                               qv == c.eos_vec;
 #pragma unroll
             for (int e = 0; e < VW; ++e) {
                 float t;
                 if (slow)
-                    t = transform(v[e], i0 + e, bits, c);
+                    t = transform(v[e], i0 + e, (bits >> e) & 1u, c);
                 else
                     t = kSample ? __fmul_rn(v[e], c.inv_t) : v[e];
                 x[g * VW + e] = t;
                 if (kSample) {
                     tmax2 = fmaxf(tmax2, fminf(tmax, t));
                     tmax = fmaxf(tmax, t);
-                    if (kFuse && t >= tau_g) {
-                        const uint32_t pos = atomicAdd(cand_count, 1u);
-                        if (pos < static_cast<uint32_t>(kCandCap))
-                            ckey[pos] = (static_cast<unsigned long long>(okey(t)) << 32) | static_cast<uint32_t>(i0 + e);
-                    }
                 } else if (t > bestv) {
                     bestv = t;
                     besti = i0 + e;
@@ -1800,14 +1663,14 @@ __device__ __forceinline__ void row_pass(const unsigned char* sl, int nvec, cons
                     qv == c.eos_vec;
         if (c.pen_on && (slow || !lazy)) {
             i0 = mp.idx(qv * VW);
-            bits = c.bitmap[i0 >> 5];
-            slow = slow || ((bits >> (i0 & 31)) & ((1u << VW) - 1u)) != 0u;
+            bits = pen_mask<VW>(c.flags, i0);
+            slow = slow || bits != 0u;
         }
         float t[VW];
         if (slow) {
             if (i0 < 0) i0 = mp.idx(qv * VW);
 #pragma unroll
-            for (int e = 0; e < VW; ++e) t[e] = transform(v[e], i0 + e, bits, c);
+            for (int e = 0; e < VW; ++e) t[e] = transform(v[e], i0 + e, (bits >> e) & 1u, c);
         } else {
 #pragma unroll
             for (int e = 0; e < VW; ++e) t[e] = kMode == kPassGreedy ? v[e] : __fmul_rn(v[e], c.inv_t);
@@ -1838,7 +1701,7 @@ __device__ __forceinline__ void row_pass(const unsigned char* sl, int nvec, cons
         if (kAppend && vm >= tau) {
             if (i0 < 0) {
                 i0 = mp.idx(qv * VW);
-                if (c.pen_on) bits = c.bitmap[i0 >> 5];
+                if (c.pen_on) bits = pen_mask<VW>(c.flags, i0);
             }
             unsigned m4 = 0u;
 #pragma unroll
@@ -1854,7 +1717,7 @@ __device__ __forceinline__ void row_pass(const unsigned char* sl, int nvec, cons
                         raw = v[j];
                     }
                 // a vector on the short path got no penalty yet (lazy): apply it where the id's bit is set
-                if (!slow && ((bits >> ((i0 + e) & 31)) & 1u)) x = __fmul_rn(penalize(raw, c.pen, c.pen_rcp), c.inv_t);
+                if (!slow && ((bits >> e) & 1u)) x = __fmul_rn(penalize(raw, c.pen, c.pen_rcp), c.inv_t);
                 if (x >= tau) {
                     a = fmaxf(a, x);
                     const uint32_t pos = atomicAdd(count, 1u);
@@ -1888,14 +1751,14 @@ __device__ __forceinline__ void row_pass_append(const unsigned char* sl, int nve
         uint32_t bits = 0u;
         if (c.pen_on && (slow || !lazy)) {
             i0 = mp.idx(qv * VW);
-            bits = c.bitmap[i0 >> 5];
-            slow = slow || ((bits >> (i0 & 31)) & ((1u << VW) - 1u)) != 0u;
+            bits = pen_mask<VW>(c.flags, i0);
+            slow = slow || bits != 0u;
         }
         float t[VW];
         if (slow) {
             if (i0 < 0) i0 = mp.idx(qv * VW);
 #pragma unroll
-            for (int e = 0; e < VW; ++e) t[e] = transform(v[e], i0 + e, bits, c);
+            for (int e = 0; e < VW; ++e) t[e] = transform(v[e], i0 + e, (bits >> e) & 1u, c);
         } else {
 #pragma unroll
             for (int e = 0; e < VW; ++e) t[e] = __fmul_rn(v[e], c.inv_t);
@@ -1941,7 +1804,7 @@ __device__ __forceinline__ void row_pass_append(const unsigned char* sl, int nve
             id = mp.idx(pos);
             x = transform(VW == 4 ? reinterpret_cast<const float*>(sl)[pos]
                                   : __uint_as_float(static_cast<uint32_t>(reinterpret_cast<const uint16_t*>(sl)[pos]) << 16),
-                          id, c.pen_on ? c.bitmap[id >> 5] : 0u, c);
+                          id, c.pen_on && c.flags[id] != 0, c);
             pr = x >= tau;
         }
         const unsigned bal = __ballot_sync(kFull, pr);
@@ -1987,10 +1850,11 @@ __global__ void __launch_bounds__(kBlockThreads, 6) cand_kernel(const __grid_con
     RowMeta* metas = reinterpret_cast<RowMeta*>(smem + static_cast<size_t>(S_) * stage_bytes);   // 2 * S_ entries
     uint64_t* full_bar = reinterpret_cast<uint64_t*>(metas + 2 * S_);
     uint64_t* empty_bar = full_bar + S_;
-    // two bitmaps, alternating by row: a row clears its own after use while the next row fills the other
-    const int words4 = (p.bitmap_words + 3) & ~3;
-    uint32_t* bitmaps = reinterpret_cast<uint32_t*>(empty_bar + S_);
-    CandMisc& cm = *reinterpret_cast<CandMisc*>(bitmaps + 2 * words4);
+    // history flag map (a byte per id).  A row clears it after its last read; every path then passes a barrier
+    // before the next row sets flags (cand_block, the replay, the argmax or the overflow barrier).
+    const int fbytes = p.flag_bytes;
+    uint8_t* flags = reinterpret_cast<uint8_t*>(empty_bar + S_);
+    CandMisc& cm = *reinterpret_cast<CandMisc*>(flags + fbytes);
 
     if (tid == 0) {
         for (int s = 0; s < S_; ++s) {
@@ -2004,7 +1868,7 @@ __global__ void __launch_bounds__(kBlockThreads, 6) cand_kernel(const __grid_con
         cm.count[1] = 0;
         cm.seed = p.guess_seed ? *reinterpret_cast<volatile unsigned long long*>(p.guess_seed) : 0xffffffffull;
     }
-    for (int i = tid; i < 2 * words4; i += blockDim.x) bitmaps[i] = 0u;
+    for (int i = tid; i < fbytes / 16; i += blockDim.x) reinterpret_cast<uint4*>(flags)[i] = make_uint4(0, 0, 0, 0);
     __syncthreads();
 
     if (warp == kProducerWarp) {
@@ -2032,7 +1896,6 @@ __global__ void __launch_bounds__(kBlockThreads, 6) cand_kernel(const __grid_con
         }
         const RowMeta& m = metas[k % (2 * S_)];
         if (m.row < 0) break;   // no more rows
-        uint32_t* bitmap = bitmaps + (k & 1) * words4;
         if (!m.opt_ok) {
             cbar();
             if (tid == 0) {
@@ -2074,8 +1937,9 @@ __global__ void __launch_bounds__(kBlockThreads, 6) cand_kernel(const __grid_con
             }
         }
 
-        // ---- repetition penalty (Sampler.cs:25-33).  Distinct(): the history ids go into a V-bit bitmap; the pass
-        //      applies the penalty where a bit is set (to the candidates only, when the penalty is > 1).
+        // ---- repetition penalty (Sampler.cs:25-33).  Distinct(): every history id sets its flag byte (plain
+        //      stores: no read-modify-write); the pass applies the penalty where a flag is set (to the candidates
+        //      only, when the penalty is > 1).
         if (m.pen_on) {
             const int32_t* sh = reinterpret_cast<const int32_t*>(sl + p.stage_logit_bytes);
             bool bad = false;
@@ -2086,18 +1950,29 @@ __global__ void __launch_bounds__(kBlockThreads, 6) cand_kernel(const __grid_con
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     if (static_cast<unsigned>(ids[j]) < static_cast<unsigned>(V))
-                        atomicOr(&bitmap[ids[j] >> 5], 1u << (ids[j] & 31));
+                        flags[ids[j]] = 1;
                     else
                         bad = true;
                 }
             }
-            const int rest = m.hist_len - nst;   // ids outside the staged span: [0, hs_lo) and [hs_hi, len)
-            for (int q = tid; q < rest; q += kThreads) {
-                const int id = m.hist[q < m.hs_lo ? q : q - m.hs_lo + m.hs_hi];
-                if (static_cast<unsigned>(id) < static_cast<unsigned>(V))
-                    atomicOr(&bitmap[id >> 5], 1u << (id & 31));
-                else
-                    bad = true;
+            // ids outside the staged span, [0, hs_lo) and [hs_hi, len), from global memory: four independent
+            // loads per thread in flight
+            const int rest = m.hist_len - nst;
+            for (int q0 = tid; q0 < rest; q0 += 4 * kThreads) {
+                int ids[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int q = q0 + j * kThreads;
+                    ids[j] = q < rest ? m.hist[q < m.hs_lo ? q : q - m.hs_lo + m.hs_hi] : 0;
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    if (q0 + j * kThreads >= rest) continue;
+                    if (static_cast<unsigned>(ids[j]) < static_cast<unsigned>(V))
+                        flags[ids[j]] = 1;
+                    else
+                        bad = true;
+                }
             }
             if (bad) atomicOr(p.err, kErrHistRange);
         }
@@ -2115,7 +1990,7 @@ __global__ void __launch_bounds__(kBlockThreads, 6) cand_kernel(const __grid_con
         c.pen_rcp = m.pen_rcp;
         c.sample = sample;
         c.inv_t = m.inv_t;
-        c.bitmap = bitmap;
+        c.flags = flags;
         c.slow_vlo = m.slow_vlo;
         c.slow_vhi = m.slow_vhi;
         c.eos_vec = m.eos_vec;
@@ -2127,7 +2002,7 @@ __global__ void __launch_bounds__(kBlockThreads, 6) cand_kernel(const __grid_con
             row_pass_dt<kPassGreedy>(dtype, sl, nvec, mp, c, tid, a, b, bi, 0.0f, nullptr, nullptr);
             cbar();   // the stage has been read
             if (m.pen_on)
-                for (int i = tid; i < p.bitmap_words; i += kThreads) bitmap[i] = 0u;
+                for (int i = tid; i < p.flag_bytes / 16; i += kThreads) reinterpret_cast<uint4*>(flags)[i] = make_uint4(0, 0, 0, 0);
             if (tid == 0) mbar_arrive(&empty_bar[s]);
             // first index of the maximum (Sampler.cs:90-95)
 #pragma unroll
@@ -2217,9 +2092,9 @@ __global__ void __launch_bounds__(kBlockThreads, 6) cand_kernel(const __grid_con
                 C = static_cast<int>(*reinterpret_cast<volatile uint32_t*>(count));
             }
         }
-        // every thread is past its last read of the stage and of the bitmap (the barrier above)
+        // every thread is past its last read of the stage and of the flags (the barrier above)
         if (m.pen_on)
-            for (int i = tid; i < p.bitmap_words; i += kThreads) bitmap[i] = 0u;
+            for (int i = tid; i < p.flag_bytes / 16; i += kThreads) reinterpret_cast<uint4*>(flags)[i] = make_uint4(0, 0, 0, 0);
         if (tid == 0) mbar_arrive(&empty_bar[s]);
         guess_id = -1;
         if (C <= kCandCap) {
@@ -2306,16 +2181,17 @@ size_t cand_smem_bytes(const LaunchParams& p) {
     size_t b = stage * p.n_stages;
     b += sizeof(RowMeta) * 2 * p.n_stages;
     b += sizeof(uint64_t) * (2 * p.n_stages);
-    b += sizeof(uint32_t) * 2 * ((p.bitmap_words + 3) & ~3);
+    b += static_cast<size_t>(p.flag_bytes);
     b += sizeof(CandMisc);
     return b;
 }
 
-// ---------------------------------------------------------------- the kernel
-// kGeneral == false: the candidate kernel (every row; greedy and top-k <= 64 rows finish here, the rest are
-// deferred).  kGeneral == true: the whole-row kernel over the deferred rows.
-template <bool kGeneral>
-__global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kernel(const __grid_constant__ LaunchParams p) {
+// ---------------------------------------------------------------- whole-row kernel
+// The rows the candidate kernel deferred (the first deferred_count entries of deferred_rows): sampling rows with
+// top-k off or K > 64, rows whose candidates overflowed, and rows of more than 3072 staged ids.  CTA b takes list
+// entries b, b + grid, ...; each row is held in registers (24 values per thread) for the binned top-k / top-p
+// searches, and rows whose decisions fall inside the error band are replayed in the reference's order.
+__global__ void __launch_bounds__(kBlockThreads, 3) whole_row_kernel(const __grid_constant__ LaunchParams p) {
     extern __shared__ __align__(128) unsigned char smem[];
     const int tid = threadIdx.x;
     const int lane = tid & 31;
@@ -2326,18 +2202,16 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
     RowMeta* metas = reinterpret_cast<RowMeta*>(smem + static_cast<size_t>(S_) * stage_bytes);   // 2 * S_ entries
     uint64_t* full_bar = reinterpret_cast<uint64_t*>(metas + 2 * S_);
     uint64_t* empty_bar = full_bar + S_;
-    uint32_t* bitmap = reinterpret_cast<uint32_t*>(empty_bar + S_);
-    unsigned long long* ckey = reinterpret_cast<unsigned long long*>(bitmap + ((p.bitmap_words + 3) & ~3));
+    uint8_t* flags = reinterpret_cast<uint8_t*>(empty_bar + S_);   // history flag map, a byte per id
+    unsigned long long* ckey = reinterpret_cast<unsigned long long*>(flags + p.flag_bytes);
     SmemMisc& misc = *reinterpret_cast<SmemMisc*>(ckey + kCandCap);
 
     const int first = blockIdx.x;
     const int gstride = gridDim.x;
-    const int n_rows = kGeneral ? min(static_cast<int>(*reinterpret_cast<volatile uint32_t*>(p.deferred_count)),
-                                      p.total_rows)
-                                : p.total_rows;
+    const int n_rows = min(static_cast<int>(*reinterpret_cast<volatile uint32_t*>(p.deferred_count)), p.total_rows);
     const int n_my = first < n_rows ? (n_rows - 1 - first) / gstride + 1 : 0;
     // nothing deferred: the counters are already zero, so no CTA has anything to do
-    if (kGeneral && n_rows == 0) return;
+    if (n_rows == 0) return;
 
     if (tid == 0) {
         for (int s = 0; s < S_; ++s) {
@@ -2347,26 +2221,19 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
         fence_mbar_init();
         misc.issued = 0;
         misc.progress = 0;
-        misc.cand_count[0] = 0;
-        misc.cand_count[1] = 0;
     }
-    for (int i = tid; i < p.bitmap_words; i += blockDim.x) bitmap[i] = 0u;
+    for (int i = tid; i < p.flag_bytes / 16; i += blockDim.x) reinterpret_cast<uint4*>(flags)[i] = make_uint4(0, 0, 0, 0);
     __syncthreads();
 
     if (warp == kProducerWarp) {
         // ================= producer warp: plans rows and issues the bulk copies =================
-        produce_rows<kGeneral>(p, first, gstride, n_my, lane, stages, stage_bytes, metas, full_bar, empty_bar,
+        produce_rows<true>(p, first, gstride, n_my, lane, stages, stage_bytes, metas, full_bar, empty_bar,
                                &misc.progress, &misc.issued);
         return;
     }
 
     // ================= element warps =================
-    uint32_t st_greedy = 0, st_fast = 0, st_fast_exact = 0, st_general = 0, st_general_exact = 0, st_large = 0,
-             st_overflow = 0;
-    // candidate threshold carried from the previous candidate row, and the (segment, option) it belongs to (-1:
-    // none); every element thread holds the same copy
-    int guess_id = -1;
-    float guess_tau = 0.0f;
+    uint32_t st_greedy = 0, st_general = 0, st_general_exact = 0, st_large = 0;
     for (int k = 0; k < n_my; ++k) {
         const int s = k % S_;
         unsigned char* sl = stages + static_cast<size_t>(s) * stage_bytes;
@@ -2402,15 +2269,6 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
             }
             continue;
         }
-        if (!kGeneral && m.deferred) {
-            cbar();   // every thread is past the full-barrier wait of this stage
-            if (tid == 0) {
-                p.deferred_rows[atomicAdd(p.deferred_count, 1u)] = m.row;
-                mbar_arrive(&empty_bar[s]);
-                ++misc.progress;
-            }
-            continue;
-        }
         const DevOptions o = m.opt;
 
         // ---- unaligned rows: the element warps stage the active ids themselves
@@ -2425,47 +2283,39 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
             }
         }
 
-        // ---- repetition penalty (Sampler.cs:25-33): Distinct() through a V-bit bitmap.  fp32 rows take the penalty
-        //      in place in the stage, applied by the thread that first sets an id's bit; bf16 rows per element.
+        // ---- repetition penalty (Sampler.cs:25-33): Distinct() through a flag byte per id (plain stores); the
+        //      element pass applies the penalty to every element whose flag is set
         if (m.pen_on) {
-            if (m.direct) cbar();   // the staged copy is complete before ids update it in place
-            const bool inplace = dtype == 0;
-            const float pen = o.rep_penalty;
-            const double pen_rcp = m.pen_rcp;
-            float* sf = reinterpret_cast<float*>(sl);
             bool bad = false;
             const int nst = m.hs_hi - m.hs_lo;
             for (int c4 = tid; c4 < nst / 4; c4 += kThreads) {
-                const int4 v = reinterpret_cast<const int4*>(sh)[c4];
-                const int ids[4] = {v.x, v.y, v.z, v.w};
-                uint32_t old[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j)   // the four atomics are issued before any result is used
-                    old[j] = static_cast<unsigned>(ids[j]) < static_cast<unsigned>(V)
-                                 ? atomicOr(&bitmap[ids[j] >> 5], 1u << (ids[j] & 31))
-                                 : ~0u;
+                const int4 hv = reinterpret_cast<const int4*>(sh)[c4];
+                const int ids[4] = {hv.x, hv.y, hv.z, hv.w};
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    if (static_cast<unsigned>(ids[j]) >= static_cast<unsigned>(V)) {
+                    if (static_cast<unsigned>(ids[j]) < static_cast<unsigned>(V))
+                        flags[ids[j]] = 1;
+                    else
                         bad = true;
-                    } else if (inplace && !(old[j] & (1u << (ids[j] & 31)))) {
-                        const int q = mp.pos(ids[j]);
-                        if (q >= 0) sf[q] = penalize(sf[q], pen, pen_rcp);
-                    }
                 }
             }
-            const int rest = m.hist_len - nst;   // ids outside the staged span: [0, hs_lo) and [hs_hi, len)
-            for (int q = tid; q < rest; q += kThreads) {
-                const int id = m.hist[q < m.hs_lo ? q : q - m.hs_lo + m.hs_hi];
-                if (static_cast<unsigned>(id) >= static_cast<unsigned>(V)) {
-                    bad = true;
-                    continue;
+            // ids outside the staged span, [0, hs_lo) and [hs_hi, len), from global memory: four independent
+            // loads per thread in flight
+            const int rest = m.hist_len - nst;
+            for (int q0 = tid; q0 < rest; q0 += 4 * kThreads) {
+                int ids[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int q = q0 + j * kThreads;
+                    ids[j] = q < rest ? m.hist[q < m.hs_lo ? q : q - m.hs_lo + m.hs_hi] : 0;
                 }
-                const uint32_t bit = 1u << (id & 31);
-                const uint32_t old = atomicOr(&bitmap[id >> 5], bit);
-                if (inplace && !(old & bit)) {
-                    const int q2 = mp.pos(id);
-                    if (q2 >= 0) sf[q2] = penalize(sf[q2], pen, pen_rcp);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    if (q0 + j * kThreads >= rest) continue;
+                    if (static_cast<unsigned>(ids[j]) < static_cast<unsigned>(V))
+                        flags[ids[j]] = 1;
+                    else
+                        bad = true;
                 }
             }
             if (bad) atomicOr(p.err, kErrHistRange);
@@ -2479,12 +2329,12 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
         c.sup_hi = m.sup_hi;
         c.eos = m.eos;
         c.eos_blocked = m.eos_blocked != 0;
-        c.pen_on = m.pen_on != 0 && dtype != 0;   // per element only for bf16 rows
+        c.pen_on = m.pen_on != 0;
         c.pen = o.rep_penalty;
         c.pen_rcp = m.pen_rcp;
         c.sample = o.do_sample != 0;
         c.inv_t = m.inv_t;
-        c.bitmap = bitmap;
+        c.flags = flags;
         c.slow_vlo = m.slow_vlo;
         c.slow_vhi = m.slow_vhi;
         c.eos_vec = m.eos_vec;
@@ -2497,7 +2347,7 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
         int sort_n = 1;
         while (sort_n < V) sort_n <<= 1;
 
-        const bool big = kGeneral && nvec > kThreads * (kRegElems / VWe);
+        const bool big = nvec > kThreads * (kRegElems / VWe);
         if (big) {
             // ---- rows with more than 3072 active ids: transform into global scratch, exact path
             float tmax = neg_inf(), bestv = neg_inf();
@@ -2507,9 +2357,8 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
             for (int qv = tid; qv < nvec; qv += kThreads) {
                 const int q0 = qv * VWe;
                 const int i0 = mp.idx(q0);
-                const uint32_t bits = c.pen_on ? bitmap[i0 >> 5] : 0u;
                 for (int e = 0; e < VWe && i0 + e < V; ++e) {
-                    const float t = transform(load_elem(sl, q0 + e, dtype), i0 + e, bits, c);
+                    const float t = transform(load_elem(sl, q0 + e, dtype), i0 + e, flags[i0 + e] != 0, c);
                     gx[i0 + e] = t;
                     tmax = fmaxf(tmax, t);
                     if (t > bestv) {
@@ -2521,7 +2370,7 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
             cbar();
             if (tid == 0) mbar_arrive(&empty_bar[s]);
             if (m.pen_on)
-                for (int i = tid; i < p.bitmap_words; i += kThreads) bitmap[i] = 0u;
+                for (int i = tid; i < p.flag_bytes / 16; i += kThreads) reinterpret_cast<uint4*>(flags)[i] = make_uint4(0, 0, 0, 0);
             int res;
             if (!c.sample) {
                 res = block_argmax(bestv, besti, misc, lane, warp);
@@ -2540,50 +2389,24 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
             continue;
         }
 
-        const int K = o.top_k;
-        const bool cand_row = !kGeneral && c.sample && K > 0 && K < V && K <= kSmallK;
-        // A candidate threshold carried from this CTA's previous row of the same segment and option: any tau with
-        // K <= count(x >= tau) <= 128 is exact (the K-th largest is then >= tau), so the candidates can be collected
-        // during the element pass; otherwise the threshold is derived from this row below.
-        const int gid = m.seg * 65536 + m.opt_idx;
-        const bool fuse = cand_row && guess_id == gid;
-        const float tau_g = guess_tau;
-        uint32_t* const ccount = &misc.cand_count[k & 1];
         float x[kRegElems];
         float tmax = neg_inf(), tmax2 = neg_inf();   // the two largest values of this thread
         float bestv = neg_inf();
         int besti = 0x7fffffff;
         if (c.sample) {
-            if (fuse) {
-                if (dtype == 0)
-                    process_vectors<4, true, true>(sl, nvec, mp, c, tid, x, tmax, tmax2, bestv, besti, tau_g,
-                                                   ccount, ckey);
-                else
-                    process_vectors<8, true, true>(sl, nvec, mp, c, tid, x, tmax, tmax2, bestv, besti, tau_g,
-                                                   ccount, ckey);
-            } else {
-                if (dtype == 0)
-                    process_vectors<4, true, false>(sl, nvec, mp, c, tid, x, tmax, tmax2, bestv, besti, 0.0f,
-                                                    nullptr, nullptr);
-                else
-                    process_vectors<8, true, false>(sl, nvec, mp, c, tid, x, tmax, tmax2, bestv, besti, 0.0f,
-                                                    nullptr, nullptr);
-            }
+            if (dtype == 0)
+                process_vectors<4, true>(sl, nvec, mp, c, tid, x, tmax, tmax2, bestv, besti);
+            else
+                process_vectors<8, true>(sl, nvec, mp, c, tid, x, tmax, tmax2, bestv, besti);
         } else {
             if (dtype == 0)
-                process_vectors<4, false, false>(sl, nvec, mp, c, tid, x, tmax, tmax2, bestv, besti, 0.0f, nullptr,
-                                                 nullptr);
+                process_vectors<4, false>(sl, nvec, mp, c, tid, x, tmax, tmax2, bestv, besti);
             else
-                process_vectors<8, false, false>(sl, nvec, mp, c, tid, x, tmax, tmax2, bestv, besti, 0.0f, nullptr,
-                                                 nullptr);
-        }
-        if (cand_row) {   // row maximum, published with the pass's barrier
-            const float wm = warp_max_f(tmax);
-            if (lane == 0) misc.red_f[5][warp] = wm;
+                process_vectors<8, false>(sl, nvec, mp, c, tid, x, tmax, tmax2, bestv, besti);
         }
         cbar();   // the stage has been read
         if (m.pen_on)
-            for (int i = tid; i < p.bitmap_words; i += kThreads) bitmap[i] = 0u;
+            for (int i = tid; i < p.flag_bytes / 16; i += kThreads) reinterpret_cast<uint4*>(flags)[i] = make_uint4(0, 0, 0, 0);
         bool released = false;
         auto release = [&]() {   // hand the stage back to the producer (after a cbar)
             if (!released && tid == 0) mbar_arrive(&empty_bar[s]);
@@ -2603,90 +2426,7 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
             continue;
         }
 
-        bool handed = false;
-        if (cand_row) {
-            release();   // the candidate path no longer reads the stage
-            float mx = misc.red_f[5][0];
-#pragma unroll
-            for (int w = 1; w < kWarps; ++w) mx = fmaxf(mx, misc.red_f[5][w]);
-            int C = fuse ? static_cast<int>(*ccount) : 0;
-            if (!fuse || C < K || C > kCandCap) {
-                // no usable carried threshold: tau = min over warps of the ceil(K/4)-th largest of each warp's 64
-                // per-thread top-2 values (>= ceil(K/4) distinct elements of each warp are >= it, so >= K elements
-                // of the row are >= tau)
-                cbar();   // every thread has read the fused count
-                if (tid == 0) *ccount = 0;
-                const int cw = (K + kWarps - 1) / kWarps;
-                uint32_t lk[2] = {~okey(tmax), ~okey(tmax2)};
-                warp_sort32<2>(lk, lane);
-                const float tw = okey_inv(~__shfl_sync(kFull, lk[0], cw - 1));
-                if (lane == 0) misc.tau_w[warp] = tw;
-                cbar();
-                float tau = misc.tau_w[0];
-#pragma unroll
-                for (int w = 1; w < kWarps; ++w) tau = fminf(tau, misc.tau_w[w]);
-                C = kCandCap + 1;
-                if (!is_neg_inf(tau)) {
-                    // ---- candidates x >= tau -> shared keys okey(x) << 32 | id
-#pragma unroll
-                    for (int e = 0; e < kRegElems; ++e) {
-                        if (x[e] >= tau) {
-                            const uint32_t pos = atomicAdd(ccount, 1u);
-                            if (pos < static_cast<uint32_t>(kCandCap)) {
-                                const int gg = e / VWe;
-                                const int qv = tid + gg * kThreads;
-                                ckey[pos] = (static_cast<unsigned long long>(okey(x[e])) << 32) |
-                                            static_cast<uint32_t>(mp.idx(qv * VWe + (e - gg * VWe)));
-                            }
-                        }
-                    }
-                    cbar();
-                    C = static_cast<int>(*ccount);
-                }
-            }
-            if (C <= kCandCap) {
-                // every thread read C before the first barrier inside cand_parallel / the replay; the counter is
-                // next used two rows on, and the row between always passes a barrier
-                const bool par = !p.force_exact;
-                int res = par ? cand_parallel(ckey, C, K, o, m.uniform, mx, out_probs, V, misc.u.cw, tid) : -1;
-                if (res < 0) {
-                    if (warp == 0) {
-                        const int rr = replay_candidates(ckey, C, K, o, m.uniform, V, out_probs, misc.flags, lane);
-                        if (lane == 0) misc.bc_i[3] = rr;
-                    }
-                    cbar();
-                    res = misc.bc_i[3];
-                    ++st_fast_exact;
-                } else {
-                    ++st_fast;
-                }
-                if (tid == 0) {
-                    *m.out_id = res;
-                    *ccount = 0;
-                }
-                // carry a threshold to the next row: the candidate ranked ~1.25 K from the top (or the lowest), so
-                // that a similar row collects ~1.25 K candidates (cand_parallel left them in ascending order)
-                guess_id = -1;
-                if (par) {
-                    const int target = K + (K >> 2) + 4;
-                    const float g = okey_inv(static_cast<uint32_t>(misc.u.cw.pk[C >= target ? C - target : 0] >> 32));
-                    if (!is_neg_inf(g)) {
-                        guess_tau = g;
-                        guess_id = gid;
-                    }
-                }
-            } else {   // no finite tau or too many candidates: the whole-row kernel takes the row
-                cbar();   // every thread has read the count
-                ++st_overflow;
-                if (tid == 0) {
-                    p.deferred_rows[atomicAdd(p.deferred_count, 1u)] = m.row;
-                    *ccount = 0;
-                }
-                guess_id = -1;
-            }
-            handed = true;
-        }
-        if (kGeneral && !handed) {
+        {
             const float mx = block_max_f(tmax, misc, 0, lane, warp);
             // numerator cache: the consumed stage when it is large enough, else this CTA's global scratch
             const bool in_stage = !released && stage_bytes >= kRegElems * kThreads * 8;
@@ -2714,7 +2454,7 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
         }
         if (tid == 0) ++misc.progress;
     }
-    if (kGeneral && tid == 0) {
+    if (tid == 0) {
         // the last whole-row CTA to finish clears the deferred list for the next call
         __threadfence();
         if (atomicAdd(p.done_count, 1u) == gridDim.x - 1) {
@@ -2724,10 +2464,9 @@ __global__ void __launch_bounds__(kBlockThreads, kGeneral ? 3 : 5) sampler_kerne
         }
     }
     if (tid == 0 && p.stats) {
-        const uint32_t v[7] = {st_greedy, st_fast, st_fast_exact, st_general, st_general_exact, st_large, st_overflow};
-        const int idx[7] = {kStatGreedy, kStatFast, kStatFastReplayed, kStatGeneral, kStatGeneralReplayed,
-                            kStatLarge, kStatOverflow};
-        for (int i = 0; i < 7; ++i)
+        const uint32_t v[4] = {st_greedy, st_general, st_general_exact, st_large};
+        const int idx[4] = {kStatGreedy, kStatGeneral, kStatGeneralReplayed, kStatLarge};
+        for (int i = 0; i < 4; ++i)
             if (v[i]) atomicAdd(&p.stats[idx[i]], static_cast<unsigned long long>(v[i]));
     }
 }
@@ -2764,7 +2503,7 @@ size_t sampler_smem_bytes(const LaunchParams& p) {
     size_t b = stage * p.n_stages;
     b += sizeof(RowMeta) * 2 * p.n_stages;
     b += sizeof(uint64_t) * (2 * p.n_stages);
-    b += sizeof(uint32_t) * ((p.bitmap_words + 3) & ~3);
+    b += static_cast<size_t>(p.flag_bytes);
     b += sizeof(unsigned long long) * kCandCap;
     b += sizeof(SmemMisc);
     return b;
@@ -2804,7 +2543,7 @@ int ctas_per_sm(const void* fn, int which, int threads, size_t smem) {
 
 bool plan_launch(LaunchParams& p, int sm_count, int max_grid_general, LaunchPlan* plan) {
     const void* fc = reinterpret_cast<const void*>(&cand_kernel);
-    const void* fg = reinterpret_cast<const void*>(&sampler_kernel<true>);
+    const void* fg = reinterpret_cast<const void*>(&whole_row_kernel);
     // the stage count that keeps the most candidate-kernel CTAs resident (ties: the deeper ring)
     int best_stages = 0, best_cc = 0, best_cg = 0;
     for (int stages = kStages; stages >= 2; --stages) {
@@ -2832,7 +2571,7 @@ cudaError_t launch_sampler(const LaunchParams& p, const LaunchPlan& plan, cudaSt
     cand_kernel<<<plan.grid, kBlockThreads, plan.smem_cand, stream>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    sampler_kernel<true><<<plan.grid_general, kBlockThreads, plan.smem_general, stream>>>(p);
+    whole_row_kernel<<<plan.grid_general, kBlockThreads, plan.smem_general, stream>>>(p);
     return cudaGetLastError();
 }
 
@@ -2852,7 +2591,6 @@ cudaError_t launch_apply_penalty(float* logits, int vocab, const int32_t* hist, 
 
 namespace vw {
 namespace {
-static_assert(offsetof(CandWork, pf) % 16 == 0 && offsetof(CandWork, pk) % 16 == 0, "CandWork alignment");
 static_assert(sizeof(SmemMisc) % 16 == 0, "SmemMisc alignment");
 }  // namespace
 }  // namespace vw
