@@ -158,6 +158,29 @@ def test_random_edge_cases(device, seed):
     assert_ids_equal(w, got, ref)
 
 
+def test_carried_threshold_misses_and_overflow(device):
+    """Rows alternate between very different logit scales (and some rows are all ties), so the threshold the
+    candidate kernel carries from row to row keeps missing: the fallback (row top-2 threshold, second append
+    pass) and the overflow hand-off to the whole-row kernel both run.  Ids stay bit-exact."""
+    rng = np.random.default_rng(77)
+    n, V = 1024, 3072
+    scales = np.where(np.arange(n) % 3 == 0, 8.0, np.where(np.arange(n) % 3 == 1, 0.05, 1.0)).astype(np.float32)
+    x = (rng.normal(0.0, 1.0, size=(n, V)).astype(np.float32) * scales[:, None]).astype(np.float32)
+    x[::17] = np.float32(0.25)                       # all ties: more than 128 candidates at any threshold
+    ho = np.arange(0, (n + 1) * 64, 64, dtype=np.int64)
+    hi = rng.integers(0, 2048, size=n * 64).astype(np.int32)
+    greedy = np.zeros(n, bool)
+    seg = SegData(x, 0, 0, V, workloads._uniforms(5, n, greedy), np.zeros(n, np.int32), ho, hi,
+                  np.full(n, 2, np.int32), suppress_lo=V - 1024, suppress_hi=V)
+    w = Workload("mixed_scales", 2, [seg], [(1, 40, 0.9, 0.8, 1.1)])
+    device.stats(reset=True)
+    got = run_workload(device, w)
+    st = device.stats(reset=True)
+    assert_ids_equal(w, got, oracle_ids(w))
+    assert st["rows_fast"] + st["rows_fast_replayed"] + st["rows_general"] + st["rows_general_replayed"] == n
+    assert st["rows_overflow"] > 0 and st["rows_fast"] > 0
+
+
 def test_history_out_of_range_raises(device):
     from voxwerk_b200 import VwOutOfRange
     w = workloads.make(0)
