@@ -1871,6 +1871,8 @@ __global__ void __launch_bounds__(kBlockThreads, 6) cand_kernel(const __grid_con
     for (int i = tid; i < fbytes / 16; i += blockDim.x) reinterpret_cast<uint4*>(flags)[i] = make_uint4(0, 0, 0, 0);
     __syncthreads();
 
+    // the whole-row kernel may be scheduled now; it waits (griddepcontrol.wait) until this grid has finished
+    if (tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (warp == kProducerWarp) {
         produce_rows_dynamic(p, lane, stages, stage_bytes, metas, full_bar, empty_bar, &cm.progress, &cm.issued);
         return;
@@ -2208,6 +2210,9 @@ __global__ void __launch_bounds__(kBlockThreads, 3) whole_row_kernel(const __gri
 
     const int first = blockIdx.x;
     const int gstride = gridDim.x;
+    // launched as a programmatic dependent of the candidate kernel: wait until that grid has finished and its
+    // deferred-row list is visible
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int n_rows = min(static_cast<int>(*reinterpret_cast<volatile uint32_t*>(p.deferred_count)), p.total_rows);
     const int n_my = first < n_rows ? (n_rows - 1 - first) / gstride + 1 : 0;
     // nothing deferred: the counters are already zero, so no CTA has anything to do
@@ -2571,7 +2576,20 @@ cudaError_t launch_sampler(const LaunchParams& p, const LaunchPlan& plan, cudaSt
     cand_kernel<<<plan.grid, kBlockThreads, plan.smem_cand, stream>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    whole_row_kernel<<<plan.grid_general, kBlockThreads, plan.smem_general, stream>>>(p);
+    // programmatic dependent launch: the whole-row grid is scheduled while the candidate grid drains, instead of
+    // after it (its kernel waits for the candidate grid's completion before reading the deferred list)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(plan.grid_general);
+    cfg.blockDim = dim3(kBlockThreads);
+    cfg.dynamicSmemBytes = plan.smem_general;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, whole_row_kernel, p);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 
