@@ -1641,18 +1641,13 @@ __device__ int cand_block(const unsigned long long* key, int C, int K, const Dev
 // ---- element pass of the candidate kernel (the row stays in shared memory; nothing is kept in registers)
 enum PassMode { kPassGreedy = 0, kPassFused = 1, kPassTop2 = 2, kPassAppend = 3 };
 
-// Greedy: first maximum (a, bi) over the thread's ids.  Top2: the thread's two largest values (a >= b).  Fused and
-// Append: every value >= tau appended to keys, `a` the largest appended value (Fused and Append differ only in
-// where tau comes from).  Vectors that no mask boundary, EOS rule or per-element penalty touches take the short
-// path (temperature only).  With c.pen_lazy the appending passes test a vector's unpenalized values first: a
-// penalty > 1 only lowers a value (s / p <= s for s >= 0, s * p <= s for s < 0, and fp32 rounding and the
-// positive temperature keep the order), so only values that pass get the penalty, and are tested again.
+// Greedy: first maximum (a, bi) over the thread's ids, on the values after penalty and mask (no temperature).
+// Top2: the thread's two largest values (a >= b) after penalty, mask and temperature.  Vectors that no mask
+// boundary, EOS rule or history flag touches take the short path (temperature only).
 template <int VW, int kMode>
 __device__ __forceinline__ void row_pass(const unsigned char* sl, int nvec, const RowMap& mp, const RowCtx& c,
-                                         int tid, float& a, float& b, int& bi, float tau, uint32_t* count,
-                                         unsigned long long* keys) {
-    constexpr bool kAppend = kMode == kPassFused || kMode == kPassAppend;
-    const bool lazy = kAppend && c.pen_lazy;   // penalty bits are looked up for vectors that pass tau only
+                                         int tid, float& a, float& b, int& bi) {
+    static_assert(kMode == kPassGreedy || kMode == kPassTop2, "the appending passes are row_pass_append");
 #pragma unroll 1
     for (int qv = tid; qv < nvec; qv += kThreads) {
         float v[VW];
@@ -1661,7 +1656,7 @@ __device__ __forceinline__ void row_pass(const unsigned char* sl, int nvec, cons
         uint32_t bits = 0u;
         bool slow = static_cast<unsigned>(qv - c.slow_vlo) < static_cast<unsigned>(c.slow_vhi - c.slow_vlo) ||
                     qv == c.eos_vec;
-        if (c.pen_on && (slow || !lazy)) {
+        if (c.pen_on) {
             i0 = mp.idx(qv * VW);
             bits = pen_mask<VW>(c.flags, i0);
             slow = slow || bits != 0u;
@@ -1686,45 +1681,14 @@ __device__ __forceinline__ void row_pass(const unsigned char* sl, int nvec, cons
         float vm = t[0];
 #pragma unroll
         for (int e = 1; e < VW; ++e) vm = fmaxf(vm, t[e]);
-        if (kMode == kPassGreedy) {
-            if (vm > a) {
-                if (i0 < 0) i0 = mp.idx(qv * VW);
+        if (vm > a) {
+            if (i0 < 0) i0 = mp.idx(qv * VW);
 #pragma unroll
-                for (int e = 0; e < VW; ++e)
-                    if (t[e] > a) {
-                        a = t[e];
-                        bi = i0 + e;
-                    }
-            }
-            continue;
-        }
-        if (kAppend && vm >= tau) {
-            if (i0 < 0) {
-                i0 = mp.idx(qv * VW);
-                if (c.pen_on) bits = pen_mask<VW>(c.flags, i0);
-            }
-            unsigned m4 = 0u;
-#pragma unroll
-            for (int e = 0; e < VW; ++e) m4 |= (t[e] >= tau ? 1u : 0u) << e;
-            do {
-                const int e = __ffs(m4) - 1;
-                m4 &= m4 - 1u;
-                float x = t[0], raw = v[0];
-#pragma unroll
-                for (int j = 1; j < VW; ++j)
-                    if (e == j) {
-                        x = t[j];
-                        raw = v[j];
-                    }
-                // a vector on the short path got no penalty yet (lazy): apply it where the id's bit is set
-                if (!slow && ((bits >> e) & 1u)) x = __fmul_rn(penalize(raw, c.pen, c.pen_rcp), c.inv_t);
-                if (x >= tau) {
-                    a = fmaxf(a, x);
-                    const uint32_t pos = atomicAdd(count, 1u);
-                    if (pos < static_cast<uint32_t>(kCandCap))
-                        keys[pos] = (static_cast<unsigned long long>(okey(x)) << 32) | static_cast<uint32_t>(i0 + e);
+            for (int e = 0; e < VW; ++e)
+                if (t[e] > a) {
+                    a = t[e];
+                    bi = i0 + e;
                 }
-            } while (m4);
         }
     }
 }
@@ -1825,18 +1789,18 @@ template <int kMode>
 __device__ __forceinline__ void row_pass_dt(int dtype, const unsigned char* sl, int nvec, const RowMap& mp,
                                             const RowCtx& c, int tid, float& a, float& b, int& bi, float tau,
                                             uint32_t* count, unsigned long long* keys, uint32_t* b_desc = nullptr) {
-    if (kMode == kPassFused || kMode == kPassAppend) {
+    if constexpr (kMode == kPassFused || kMode == kPassAppend) {
         uint32_t* desc = reinterpret_cast<uint32_t*>(b_desc);
         if (dtype == 0)
             row_pass_append<4>(sl, nvec, mp, c, tid, a, tau, count, keys, desc);
         else
             row_pass_append<8>(sl, nvec, mp, c, tid, a, tau, count, keys, desc);
-        return;
+    } else {
+        if (dtype == 0)
+            row_pass<4, kMode>(sl, nvec, mp, c, tid, a, b, bi);
+        else
+            row_pass<8, kMode>(sl, nvec, mp, c, tid, a, b, bi);
     }
-    if (dtype == 0)
-        row_pass<4, kMode>(sl, nvec, mp, c, tid, a, b, bi, tau, count, keys);
-    else
-        row_pass<8, kMode>(sl, nvec, mp, c, tid, a, b, bi, tau, count, keys);
 }
 
 __global__ void __launch_bounds__(kBlockThreads, 6) cand_kernel(const __grid_constant__ LaunchParams p) {
