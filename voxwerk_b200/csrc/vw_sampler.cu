@@ -194,6 +194,19 @@ __device__ __forceinline__ bool cbar_or(bool v) {
 }
 
 // ---------------------------------------------------------------- value helpers
+// Position k of the stage ring, kept incrementally (no integer division per row): stage s = k % S, round
+// n = k / S; the meta slot k % (2 S) is s + S (n & 1).
+struct RingPos {
+    int s, n;
+    __device__ __forceinline__ void next(int S) {
+        if (++s == S) {
+            s = 0;
+            ++n;
+        }
+    }
+    __device__ __forceinline__ int meta(int S) const { return s + (n & 1) * S; }
+};
+
 __device__ __forceinline__ float neg_inf() { return __int_as_float(0xff800000); }
 __device__ __forceinline__ float pos_inf() { return __int_as_float(0x7f800000); }
 __device__ __forceinline__ bool is_neg_inf(float x) { return __float_as_uint(x) == 0xff800000u; }
@@ -1263,7 +1276,8 @@ __device__ RowMeta plan_row(const LaunchParams& p, int r, uint32_t& bytes, int& 
         m.opt = DevOptions{0, 0, 1.0f, 1.0f, 1.0f};
     }
     esize = sg.dtype == 0 ? 4 : 2;
-    const int VWe = 16 / esize;
+    const int vsh = sg.dtype == 0 ? 2 : 3;   // log2 of the ids per 16-byte vector (no integer division per row)
+    const int VWe = 1 << vsh;
     m.V = V;
     m.dtype = sg.dtype;
     m.kind = sg.kind;
@@ -1281,8 +1295,8 @@ __device__ RowMeta plan_row(const LaunchParams& p, int r, uint32_t& bytes, int& 
     m.lo_al = V;
     m.hi_al = V;
     if (sg.kind == 0 && sg.sup_lo < sg.sup_hi) {
-        const int la = (sg.sup_lo + VWe - 1) / VWe * VWe;
-        const int ha = sg.sup_hi / VWe * VWe;
+        const int la = ((sg.sup_lo + VWe - 1) >> vsh) << vsh;   // sup_lo, sup_hi are clamped to [0, V]
+        const int ha = (sg.sup_hi >> vsh) << vsh;
         if (la < ha) {
             m.lo_al = la;
             m.hi_al = ha;
@@ -1290,7 +1304,7 @@ __device__ RowMeta plan_row(const LaunchParams& p, int r, uint32_t& bytes, int& 
     }
     const bool keep = sg.kind == 0 && sg.eos >= m.lo_al && sg.eos < m.hi_al && !m.eos_blocked;
     m.kvw = keep ? VWe : 0;
-    m.kbase = keep ? sg.eos / VWe * VWe : 0;
+    m.kbase = keep ? (sg.eos >> vsh) << vsh : 0;   // keep: eos >= lo_al >= 0
     m.direct = sg.bulk_ok ? 0 : 1;
     m.hs_lo = 0;
     m.hs_hi = 0;
@@ -1308,13 +1322,13 @@ __device__ RowMeta plan_row(const LaunchParams& p, int r, uint32_t& bytes, int& 
     m.eos_vec = -1;
     if (sg.kind == 0) {
         if (sg.sup_lo < sg.sup_hi) {
-            m.slow_vlo = sg.sup_lo / VWe;
-            m.slow_vhi = (m.lo_al + m.kvw + max(sg.sup_hi - m.hi_al, 0) + VWe - 1) / VWe;
+            m.slow_vlo = sg.sup_lo >> vsh;
+            m.slow_vhi = (m.lo_al + m.kvw + max(sg.sup_hi - m.hi_al, 0) + VWe - 1) >> vsh;
         }
         if (m.eos_blocked && sg.eos >= 0 && sg.eos < V) {
             const RowMap mp{m.lo_al, m.kvw, m.kbase, m.hi_al};
             const int ep = mp.pos(sg.eos);
-            if (ep >= 0) m.eos_vec = ep / VWe;
+            if (ep >= 0) m.eos_vec = ep >> vsh;
         }
     }
     m.row_ptr = static_cast<const unsigned char*>(sg.logits) +
@@ -1324,7 +1338,7 @@ __device__ RowMeta plan_row(const LaunchParams& p, int r, uint32_t& bytes, int& 
         // rows the candidate kernel does not take: more than 3072 staged ids, or sampling without a
         // top-k <= 64
         const int na = m.lo_al + m.kvw + V - m.hi_al;
-        const bool big = (na + VWe - 1) / VWe > kThreads * (kRegElems / VWe);
+        const bool big = na > kThreads * kRegElems;   // kThreads * kRegElems is a multiple of every VWe
         const int K = m.opt.top_k;
         const bool cand = !m.opt.do_sample || (K > 0 && K < V && K <= kSmallK);
         m.deferred = (big || !cand) ? 1 : 0;
@@ -1359,6 +1373,7 @@ __device__ void produce_rows(const LaunchParams& p, int first, int gstride, int 
                              const volatile uint32_t* progress, int* issued) {
     const int S_ = p.n_stages;
     bool alive = true;
+    RingPos rp{0, 0};   // every lane advances it for every row
     for (int k0 = 0; k0 < n_my && alive; k0 += 32) {
         // lane j prepares the metadata of the CTA's row k0 + j
         const int kj = k0 + lane;
@@ -1375,12 +1390,11 @@ __device__ void produce_rows(const LaunchParams& p, int first, int gstride, int 
             bool ok = true;
             if (lane == j) {
                 const int k = k0 + j;
-                const int s = k % S_;
-                const int n = k / S_;
-                if (n > 0)
-                    ok = mbar_wait_bounded(&empty_bar[s], static_cast<uint32_t>((n - 1) & 1), progress);
+                const int s = rp.s;
+                if (rp.n > 0)
+                    ok = mbar_wait_bounded(&empty_bar[s], static_cast<uint32_t>((rp.n - 1) & 1), progress);
                 if (ok) {
-                    metas[k % (2 * S_)] = m;
+                    metas[rp.meta(S_)] = m;
                     fence_proxy_async();
                     mbar_arrive_expect_tx(&full_bar[s], bytes);
                     issue_row(p, m, esize, stages + static_cast<size_t>(s) * stage_bytes, &full_bar[s]);
@@ -1394,6 +1408,7 @@ __device__ void produce_rows(const LaunchParams& p, int first, int gstride, int 
                 alive = false;
                 break;
             }
+            rp.next(S_);
         }
     }
 }
@@ -1405,16 +1420,16 @@ __device__ void produce_rows_dynamic(const LaunchParams& p, int lane, unsigned c
                                      const volatile uint32_t* progress, int* issued) {
     if (lane != 0) return;
     const int S_ = p.n_stages;
-    for (int k = 0;; ++k) {
-        const int s = k % S_;
-        const int n = k / S_;
-        if (n > 0 && !mbar_wait_bounded(&empty_bar[s], static_cast<uint32_t>((n - 1) & 1), progress)) {
+    RingPos rp{0, 0};
+    for (int k = 0;; ++k, rp.next(S_)) {
+        const int s = rp.s;
+        if (rp.n > 0 && !mbar_wait_bounded(&empty_bar[s], static_cast<uint32_t>((rp.n - 1) & 1), progress)) {
             atomicOr(p.err, kErrTimeout);
             return;
         }
         const int r = static_cast<int>(atomicAdd(p.row_counter, 1u));
         if (r >= p.total_rows) {
-            metas[k % (2 * S_)].row = -1;
+            metas[rp.meta(S_)].row = -1;
             mbar_arrive(&full_bar[s]);
             *issued = k + 1;
             return;
@@ -1422,7 +1437,7 @@ __device__ void produce_rows_dynamic(const LaunchParams& p, int lane, unsigned c
         uint32_t bytes = 0;
         int esize = 4;
         const RowMeta m = plan_row<false>(p, r, bytes, esize);
-        metas[k % (2 * S_)] = m;
+        metas[rp.meta(S_)] = m;
         fence_proxy_async();
         mbar_arrive_expect_tx(&full_bar[s], bytes);
         issue_row(p, m, esize, stages + static_cast<size_t>(s) * stage_bytes, &full_bar[s]);
@@ -1850,17 +1865,18 @@ __global__ void __launch_bounds__(kBlockThreads, 6) cand_kernel(const __grid_con
     float guess_tau = __uint_as_float(static_cast<uint32_t>(cm.seed >> 32));
     int k = 0;
     bool failed = false;
-    for (;; ++k) {
-        const int s = k % S_;
+    RingPos rp{0, 0};
+    for (;; ++k, rp.next(S_)) {
+        const int s = rp.s;
         unsigned char* sl = stages + static_cast<size_t>(s) * stage_bytes;
         // the producer's progress counts as progress here too (it may be waiting for rows of other CTAs)
-        const bool ok = mbar_wait_bounded(&full_bar[s], static_cast<uint32_t>((k / S_) & 1),
+        const bool ok = mbar_wait_bounded(&full_bar[s], static_cast<uint32_t>(rp.n & 1),
                                           reinterpret_cast<volatile uint32_t*>(&cm.issued));
         if (cbar_or(!ok)) {
             failed = true;
             break;
         }
-        const RowMeta& m = metas[k % (2 * S_)];
+        const RowMeta& m = metas[rp.meta(S_)];
         if (m.row < 0) break;   // no more rows
         if (!m.opt_ok) {
             cbar();
@@ -1887,7 +1903,7 @@ __global__ void __launch_bounds__(kBlockThreads, 6) cand_kernel(const __grid_con
         const int VWe = dtype == 0 ? 4 : 8;
         const RowMap mp{m.lo_al, m.kvw, m.kbase, m.hi_al};
         const int NA = m.lo_al + m.kvw + (V - m.hi_al);
-        const int nvec = (NA + VWe - 1) / VWe;   // bulk-copied rows have NA % VWe == 0
+        const int nvec = (NA + VWe - 1) >> (dtype == 0 ? 2 : 3);   // bulk-copied rows have NA % VWe == 0
         double* out_probs = m.out_probs;
         const bool sample = o.do_sample != 0;   // sampling rows here have 0 < K <= 64
 
@@ -2203,10 +2219,11 @@ __global__ void __launch_bounds__(kBlockThreads, 3) whole_row_kernel(const __gri
 
     // ================= element warps =================
     uint32_t st_greedy = 0, st_general = 0, st_general_exact = 0, st_large = 0;
-    for (int k = 0; k < n_my; ++k) {
-        const int s = k % S_;
+    RingPos rp{0, 0};
+    for (int k = 0; k < n_my; ++k, rp.next(S_)) {
+        const int s = rp.s;
         unsigned char* sl = stages + static_cast<size_t>(s) * stage_bytes;
-        const bool ok = mbar_wait_bounded(&full_bar[s], static_cast<uint32_t>((k / S_) & 1));
+        const bool ok = mbar_wait_bounded(&full_bar[s], static_cast<uint32_t>(rp.n & 1));
         if (cbar_or(!ok)) {
             if (tid == 0) {
                 atomicOr(p.err, kErrTimeout);
@@ -2218,14 +2235,14 @@ __global__ void __launch_bounds__(kBlockThreads, 3) whole_row_kernel(const __gri
             cbar();
             break;
         }
-        const RowMeta& m = metas[k % (2 * S_)];
+        const RowMeta& m = metas[rp.meta(S_)];
         const int32_t* sh = reinterpret_cast<const int32_t*>(sl + p.stage_logit_bytes);
         const int V = m.V;
         const int dtype = m.dtype;
         const int VWe = dtype == 0 ? 4 : 8;
         const RowMap mp{m.lo_al, m.kvw, m.kbase, m.hi_al};
         const int NA = m.lo_al + m.kvw + (V - m.hi_al);
-        const int nvec = (NA + VWe - 1) / VWe;   // bulk-copied rows have NA % VWe == 0
+        const int nvec = (NA + VWe - 1) >> (dtype == 0 ? 2 : 3);   // bulk-copied rows have NA % VWe == 0
         double* out_probs = m.out_probs;
 
         if (!m.opt_ok) {
