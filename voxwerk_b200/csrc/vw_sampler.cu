@@ -1863,10 +1863,9 @@ __global__ void __launch_bounds__(kBlockThreads, 6) cand_kernel(const __grid_con
     // element thread holds the same copy
     int guess_id = static_cast<int32_t>(static_cast<uint32_t>(cm.seed));
     float guess_tau = __uint_as_float(static_cast<uint32_t>(cm.seed >> 32));
-    int k = 0;
     bool failed = false;
-    RingPos rp{0, 0};
-    for (;; ++k, rp.next(S_)) {
+    RingPos rp{0, 0};   // the CTA's row k = n * S_ + s
+    for (;; rp.next(S_)) {
         const int s = rp.s;
         unsigned char* sl = stages + static_cast<size_t>(s) * stage_bytes;
         // the producer's progress counts as progress here too (it may be waiting for rows of other CTAs)
@@ -2026,7 +2025,7 @@ __global__ void __launch_bounds__(kBlockThreads, 6) cand_kernel(const __grid_con
         const int gid = m.seg * 65536 + m.opt_idx;
         const bool fuse = guess_id == gid;
         float tau_used = guess_tau;   // every candidate is >= it
-        uint32_t* const count = &cm.count[k & 1];
+        uint32_t* const count = &cm.count[(rp.n * S_ + rp.s) & 1];
         if (fuse)
             row_pass_dt<kPassFused>(dtype, sl, nvec, mp, c, tid, a, b, bi, guess_tau, count, cm.key, cm.desc[warp]);
         else
@@ -2136,7 +2135,7 @@ __global__ void __launch_bounds__(kBlockThreads, 6) cand_kernel(const __grid_con
             atomicOr(p.err, kErrTimeout);
             // drain: wait (bounded) for every copy the producer issued from this row on
             const int issued = *reinterpret_cast<volatile int*>(&cm.issued);
-            for (int kk = k; kk < issued; ++kk)
+            for (int kk = rp.n * S_ + rp.s; kk < issued; ++kk)
                 mbar_wait_bounded(&full_bar[kk % S_], static_cast<uint32_t>((kk / S_) & 1));
         }
         // the last CTA to finish resets the row counter for the next call
