@@ -5,14 +5,18 @@
 One step = one vw_sample call over one batch of 4096 talker rows (V = 3072 fp32 logits, 1024-id histories,
 T 0.9, top-k 50, top-p 0.8, repetition penalty 1.05, suppress mask).  Under torchrun each rank samples its own
 4096-row batch (rows are independent; weak scaling; no collective on the data path -- NCCL only carries the
-barrier and the max-over-ranks of the timings).
+barrier and the max-over-ranks of the timings).  At N > 1 the line also carries `strong` (the one 4096-row batch
+of config 2 split into N row shards) and `cfg3_sharded` (config 3's heterogeneous frame split by cost).
 
-value: rows/s of the whole job with inputs resident in HBM (3 rotating input copies, 201 MB > the 126 MB L2, so
+value: rows/s of the whole job with inputs resident in HBM (3 rotating input copies, larger than the 126 MB L2, so
 no step reads another step's data from L2); K steps captured in one CUDA graph and timed with CUDA events on the
 launching stream.  e2e: the same metric through the public C-ABI call with host buffers (pinned host -> device
 copies of logits, histories and uniforms, and the ids back) inside the timed region.  cpu_baseline: the CPU
 restatement of voxwerk's Sampler (oracle/, "port": the C# reference cannot run here) on a bounded sample.
-`--impl reference` times only that CPU implementation, with every host thread, and prints its own line.
+`parity`: every row of the timed batch against that restatement, with flips counted and attributed.
+At N = 1 `configs` holds the other four configurations (µs per call, rows/s, roofline fraction, parity).
+`--impl reference` times only the CPU implementation, with every host thread, and prints its own line; that
+process loads no GPU library of this repository.
 """
 
 from __future__ import annotations
@@ -32,7 +36,10 @@ sys.path.insert(0, ROOT)
 
 METRIC = "sampled rows/s & HBM GB/s (B=4096,V=3072 talker step) at 1/2/4/8 B200"
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
+TRAFFIC_PATH = os.path.join(ROOT, "profiles", "traffic.json")
 FALLBACK_HBM_GBS = 6650.0
+N_COPIES = 3
+LAUNCHES_PER_CALL = 2   # the candidate kernel and the whole-row kernel
 
 
 def host_threads() -> int:
@@ -116,15 +123,24 @@ def workload_keys(w) -> dict:
     return {"vocab": [s.vocab for s in w.segments], "history": hist, "options": opts}
 
 
+def bench_config(w, world: int) -> dict:
+    """`config` of the JSON line; both arms print the same dict for the same workload and N."""
+    alg = w.algorithmic_bytes()
+    return {"workload": w.name, "rows_per_gpu": w.n_rows, "global_rows": w.n_rows * world, **workload_keys(w),
+            "parallelism": f"row shards x{world}, no collective",
+            "l2": f"{N_COPIES} rotating input copies ({N_COPIES * alg / 1e6:.0f} MB > 126 MB L2)",
+            "timing": "K steps in one CUDA graph, CUDA events on the launching stream, max over ranks"}
+
+
 def cpu_reference(workload, seconds: float, threads: int):
     """Times the CPU restatement (oracle port) on repeated passes over the workload's rows."""
     from oracle import oracle
-    seg = workload.segments[0]
     t0 = time.perf_counter()
     rows = 0
     while True:
-        oracle.sample_segment(seg, workload.options, threads=threads)
-        rows += seg.n_rows
+        for seg in workload.segments:
+            oracle.sample_segment(seg, workload.options, threads=threads)
+            rows += seg.n_rows
         el = time.perf_counter() - t0
         if el >= seconds:
             break
@@ -132,25 +148,28 @@ def cpu_reference(workload, seconds: float, threads: int):
 
 
 def run_reference_arm(args):
+    """The reference's own CPU implementation of the path: voxwerk is C# and cannot run here, so the CPU
+    restatement (oracle/) stands in for it.  Rank 0 alone works under torchrun; the other ranks exit at once."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    from voxwerk_b200 import workloads
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    from voxwerk_b200 import workloads   # pure Python: maps no library of this repository
     w = workloads.make(args.config)
     threads = host_threads()
     per_step = []
     for i in range(args.warmup + args.steps):
-        v, rows, el = cpu_reference(w, 0.0, threads)
+        _, _, el = cpu_reference(w, 0.0, threads)
         if i >= args.warmup:
             per_step.append(el)
     t = float(np.sum(per_step))
     value = args.steps * w.n_rows / t
-    sample = f"{w.n_rows} rows of {w.name} per step, {threads} threads (std::thread over rows)"
+    sample = f"{w.n_rows} rows of {w.name} per step (one rank's batch), {threads} threads (std::thread over rows)"
     line = {
-        "metric": METRIC, "value": value, "unit": "rows/s", "impl": "reference", "n_gpus": args.gpus,
+        "metric": METRIC, "value": value, "unit": "rows/s", "impl": "reference", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": w.name, "rows_per_step": w.n_rows, **workload_keys(w)},
+        "config": bench_config(w, world),
         "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads, "kind": "port", "sample": sample,
                          "what": "C++ restatement of voxwerk Sampler.cs (oracle/vw_oracle.cpp); the C# reference "
                                  "cannot be built or run in this environment"},
@@ -158,6 +177,91 @@ def run_reference_arm(args):
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+# ---------------------------------------------------------------------------------------------- GPU arm helpers
+def device_copies(w, torch, n_copies=N_COPIES):
+    """n_copies distinct device copies of the workload: (segments, arrays) per copy."""
+    from tests.gpu_util import make_segment, to_device
+    copies = []
+    for c in range(n_copies):
+        segs, keep = [], []
+        for s in w.segments:
+            arr = to_device(s, torch)
+            keep.append(arr)
+            hist_max = int(np.max(np.diff(s.hist_offsets))) if s.hist_offsets is not None else 0
+            segs.append(make_segment(s, arr, max_hist_len=hist_max))
+        copies.append((segs, keep))
+    return copies
+
+
+def timed_graph(dev, copies, opts, steps, warmup, stream, torch, barrier=None, clocks_gpu=None):
+    """Warm-up, then `steps` calls (rotating copies) captured in one CUDA graph and timed with CUDA events on the
+    launching stream.  Returns (ms, clocks summary or None, path counters)."""
+    from voxwerk_b200 import sample_rows
+    sp = stream.cuda_stream
+    with torch.cuda.stream(stream):
+        for i in range(max(warmup, 3)):
+            sample_rows(dev, copies[i % len(copies)][0], opts, stream=sp)
+    dev.synchronize(sp)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(steps):
+            sample_rows(dev, copies[i % len(copies)][0], opts, stream=torch.cuda.current_stream().cuda_stream)
+    for _ in range(2):
+        graph.replay()
+    torch.cuda.synchronize()
+    dev.stats(reset=True)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if barrier:
+        barrier()
+    torch.cuda.synchronize()
+    clocks = None
+    if clocks_gpu is not None:
+        with ClockSampler(clocks_gpu) as cs:
+            with torch.cuda.stream(stream):
+                ev0.record(stream)
+                graph.replay()
+                ev1.record(stream)
+            ev1.synchronize()
+        clocks = cs.summary()
+    else:
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            graph.replay()
+            ev1.record(stream)
+        ev1.synchronize()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    dev.synchronize(sp)   # raises if the kernel latched an error
+    paths = dev.stats(reset=True)
+    del graph
+    return ms, clocks, paths
+
+
+def gpu_ids(dev, w, torch, stream):
+    """One device call over the whole workload; ids per segment (numpy)."""
+    from tests.gpu_util import make_segment, options_table, to_device
+    from voxwerk_b200 import sample_rows
+    arrs = [to_device(s, torch) for s in w.segments]
+    sample_rows(dev, [make_segment(s, a) for s, a in zip(w.segments, arrs)], options_table(w),
+                stream=stream.cuda_stream)
+    dev.synchronize(stream.cuda_stream)
+    return [a["out_ids"].cpu().numpy() for a in arrs]
+
+
+def parity_summary(w, ids) -> dict:
+    from tests.parity import compare
+    c = compare(w, ids, threads=host_threads())
+    c.pop("first_flips", None)
+    return c
+
+
+def roofline(w, ms_per_step, peak, peak_kind):
+    alg = w.algorithmic_bytes()
+    achieved = alg / (ms_per_step * 1e-3) / 1e9
+    return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+            "peak_kind": peak_kind, "algorithmic_bytes_per_launch": alg}
 
 
 def main():
@@ -170,6 +274,7 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="skip the other configurations and the shard keys")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference_arm(args)
@@ -184,12 +289,15 @@ def main():
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    barrier = dist.barrier if world > 1 else None
 
-    from tests.gpu_util import make_segment, options_table, to_device
+    from tests.gpu_util import make_segment, options_table
     from voxwerk_b200 import Device, sample_rows, workloads
-    from voxwerk_b200.shard import max_over_ranks
+    from voxwerk_b200.shard import max_over_ranks, sum_over_ranks
 
     dev = Device(local)
+    stream = torch.cuda.Stream()
+    peak, peak_kind = hbm_peak()
     w = workloads.make(args.config)
     if rank > 0:   # weak scaling: each rank its own batch of the same shape
         import copy
@@ -199,70 +307,20 @@ def main():
             perm = rng.permutation(s.n_rows)
             s.logits = np.ascontiguousarray(s.logits[perm])
     opts = options_table(w)
-    n_copies = 3
-    copies = []
-    for c in range(n_copies):
-        segs, keep = [], []
-        for s in w.segments:
-            arr = to_device(s, torch)
-            if c > 0:   # distinct buffers with the same contents
-                arr = {k: (v.clone() if v is not None else None) for k, v in arr.items()}
-            keep.append(arr)
-            hist_max = 0
-            if s.hist_offsets is not None:
-                hist_max = int(np.max(np.diff(s.hist_offsets)))
-            segs.append(make_segment(s, arr, max_hist_len=hist_max))
-        copies.append((segs, keep))
-    stream = torch.cuda.Stream()
-    sp = stream.cuda_stream
 
-    # ---- warm-up (also sizes the library's scratch before capture)
-    with torch.cuda.stream(stream):
-        for i in range(max(args.warmup, 3)):
-            sample_rows(dev, copies[i % n_copies][0], opts, stream=sp)
-    dev.synchronize(sp)
+    # ---- parity: every row of this rank's batch against the CPU restatement, flips counted and attributed
+    par = parity_summary(w, gpu_ids(dev, w, torch, stream))
+    flips_all = int(sum_over_ranks(par["flips"], device="cuda"))
+    rows_all = int(sum_over_ranks(par["rows"], device="cuda"))
 
-    # ---- parity spot check on this rank's first copy (rank 0, first 256 rows)
-    parity = None
-    if rank == 0:
-        from oracle import oracle
-        ids = copies[0][1][0]["out_ids"].cpu().numpy()
-        sub = w.segments[0].slice(0, min(256, w.segments[0].n_rows))
-        sample_rows(dev, copies[0][0], opts, stream=sp)
-        dev.synchronize(sp)
-        ids = copies[0][1][0]["out_ids"].cpu().numpy()[:sub.n_rows]
-        ref = oracle.sample_segment(sub, w.options, threads=host_threads())
-        parity = f"{int((ids == ref).sum())}/{sub.n_rows} rows bit-exact vs oracle"
-
-    # ---- capture K steps in one graph (rotating input copies)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        for i in range(args.steps):
-            sample_rows(dev, copies[i % n_copies][0], opts, stream=torch.cuda.current_stream().cuda_stream)
-    for _ in range(2):
-        graph.replay()
-    torch.cuda.synchronize()
-    dev.stats(reset=True)
-
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(local) as clocks:
-        with torch.cuda.stream(stream):
-            ev0.record(stream)
-            graph.replay()
-            ev1.record(stream)
-        ev1.synchronize()
-    torch.cuda.synchronize()
-    elapsed_ms = ev0.elapsed_time(ev1)
-    dev.synchronize(sp)   # raises if the kernel latched an error
-    paths = dev.stats(reset=True)
+    # ---- headline: K steps of this rank's batch in one CUDA graph
+    copies = device_copies(w, torch)
+    elapsed_ms, clocks, paths = timed_graph(dev, copies, opts, args.steps, args.warmup, stream, torch, barrier,
+                                            clocks_gpu=local)
     elapsed_max = max_over_ranks(elapsed_ms, device="cuda")
-    rows_per_rank = w.n_rows
-    total_rows = rows_per_rank * world * args.steps
-    value = total_rows / (elapsed_max * 1e-3)
+    value = w.n_rows * world * args.steps / (elapsed_max * 1e-3)
     ms_per_step = elapsed_max / args.steps
+    del copies
 
     # ---- e2e through the public API with host buffers (pinned), copies inside the timed region
     host_arrays = []
@@ -278,63 +336,108 @@ def main():
     for _ in range(2):
         sample_rows(dev, hsegs, opts)
     dev.stats(reset=True)
-    if world > 1:
-        dist.barrier()
+    if barrier:
+        barrier()
     t0 = time.perf_counter()
     for _ in range(args.e2e_steps):
         sample_rows(dev, hsegs, opts)
     e2e_s = time.perf_counter() - t0
     # bytes the library copied host -> device per step (it skips the logit columns no kernel reads)
     h2d = dev.stats(reset=True)["h2d_bytes"] // max(args.e2e_steps, 1)
-    e2e_value = rows_per_rank * world * args.e2e_steps / max_over_ranks(e2e_s, device="cuda")
+    e2e_value = w.n_rows * world * args.e2e_steps / max_over_ranks(e2e_s, device="cuda")
+    del host_arrays, hsegs
+
+    # ---- N > 1: config 2's one batch split over the ranks (strong scaling), and config 3 sharded by cost
+    strong = cfg3 = None
+    if world > 1 and not args.no_extra:
+        for name in ("strong", "cfg3_sharded"):
+            full = workloads.make(args.config if name == "strong" else 3)
+            part = full.shard(rank, world)
+            pp = parity_summary(part, gpu_ids(dev, part, torch, stream))
+            cps = device_copies(part, torch)
+            ms, _, _ = timed_graph(dev, cps, options_table(part), args.steps, args.warmup, stream, torch, barrier)
+            del cps
+            t_max = max_over_ranks(ms, device="cuda") / args.steps
+            t_min = -max_over_ranks(-ms, device="cuda") / args.steps
+            entry = {"workload": full.name, "global_rows": full.n_rows, "rows_per_gpu_max":
+                     int(max_over_ranks(part.n_rows, device="cuda")),
+                     "value": full.n_rows / (t_max * 1e-3), "unit": "rows/s", "ms_per_step": t_max,
+                     "ms_per_step_fastest_rank": t_min, "scaling": "strong",
+                     "roofline": roofline(full, t_max, peak, peak_kind),
+                     "parity": {"rows": int(sum_over_ranks(pp["rows"], device="cuda")),
+                                "flips": int(sum_over_ranks(pp["flips"], device="cuda"))}}
+            if name == "strong":
+                strong = entry
+            else:
+                cfg3 = entry
+
+    # ---- N = 1: the other four configurations
+    configs = None
+    if world == 1 and not args.no_extra:
+        configs = {}
+        for cfg in (0, 1, 3, 4):
+            if cfg == args.config:
+                continue
+            wc = workloads.make(cfg)
+            pc = parity_summary(wc, gpu_ids(dev, wc, torch, stream))
+            cps = device_copies(wc, torch)
+            k = max(20, min(args.steps, 100))
+            ms, ck, pth = timed_graph(dev, cps, options_table(wc), k, args.warmup, stream, torch, clocks_gpu=local)
+            del cps
+            per = ms / k
+            configs[wc.name] = {"us_per_call": 1e3 * per, "rows_per_s": wc.n_rows / (per * 1e-3), "steps": k,
+                                "roofline": roofline(wc, per, peak, peak_kind), "parity": pc, "clocks": ck,
+                                "rows_by_path": pth}
 
     line = None
     if rank == 0:
-        alg = w.algorithmic_bytes()
         need = w.needed_bytes()
-        peak, peak_kind = hbm_peak()
-        achieved = alg / (ms_per_step * 1e-3) / 1e9
         traffic = None
-        tpath = os.path.join(ROOT, "profiles", "traffic.json")
-        if os.path.exists(tpath):
+        if os.path.exists(TRAFFIC_PATH):
             try:
-                traffic = json.load(open(tpath)).get(w.name)
+                traffic = json.load(open(TRAFFIC_PATH)).get(w.name)
             except Exception:
                 traffic = None
         cpu = None
         if world == 1 and not args.no_cpu:
             thr = host_threads()
-            v_all, rows_all, el_all = cpu_reference(w, args.cpu_seconds, thr)
-            v_one, rows_one, el_one = cpu_reference(w.shard(0, 16), min(3.0, args.cpu_seconds), 1)
+            v_all, rows_all_cpu, el_all = cpu_reference(w, args.cpu_seconds, thr)
+            v_one, _, _ = cpu_reference(w.shard(0, 16), min(3.0, args.cpu_seconds), 1)
             cpu = {"value": v_all, "unit": "rows/s", "cores": thr, "kind": "port",
-                   "sample": f"{rows_all} rows ({rows_all // w.n_rows} passes over {w.name}) in {el_all:.1f} s "
-                             f"on {thr} threads; 1 thread: {v_one:.0f} rows/s",
+                   "sample": f"{rows_all_cpu} rows ({rows_all_cpu // w.n_rows} passes over {w.name}) in "
+                             f"{el_all:.1f} s on {thr} threads; 1 thread: {v_one:.0f} rows/s",
                    "what": "C++ restatement of voxwerk Sampler.cs (oracle/), the C# reference cannot run here"}
+        rl = roofline(w, ms_per_step, peak, peak_kind)
+        rl.update({"traffic": traffic,
+                   "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one full-size "
+                                     "candidate-kernel launch, read from profiles/traffic.json (not measured in "
+                                     "this run)",
+                   "needed_bytes_per_launch": need,
+                   "frac_of_needed_bytes": need / (ms_per_step * 1e-3) / 1e9 / peak,
+                   "kernel": "cand_kernel (the step: candidate kernel + whole-row kernel launch, CUDA events)"})
         line = {
             "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": w.name, "rows_per_gpu": rows_per_rank, "global_rows": rows_per_rank * world,
-                       **workload_keys(w), "parallelism": f"row shards x{world}, no collective",
-                       "l2": f"{n_copies} rotating input copies ({n_copies * alg / 1e6:.0f} MB > 126 MB L2)",
-                       "timing": "K steps in one CUDA graph, CUDA events on the launching stream, max over ranks"},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
-                         "algorithmic_bytes_per_launch": alg, "needed_bytes_per_launch": need,
-                         "frac_of_needed_bytes": need / (ms_per_step * 1e-3) / 1e9 / peak,
-                         "kernel": "cand_kernel (the step: cand_kernel + whole-row kernel launch, CUDA events)"},
+            "config": bench_config(w, world),
+            "roofline": rl,
             "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "steps": args.e2e_steps,
                     "path": "vw_sample(VW_MEM_HOST) from pinned host buffers: logits (without the suppressed "
                             "span's columns), histories, steps, options, uniforms in; ids out"},
             "cpu_baseline": cpu,
-            "clocks": clocks.summary(),
-            "gpu_launches": 2 * args.steps,   # per step: the candidate kernel + the whole-row kernel
-            "parity": parity,
+            "clocks": clocks,
+            "gpu_launches": LAUNCHES_PER_CALL * args.steps,
+            "parity": {"rows": rows_all, "flips": flips_all, "rank0": par},
             "rows_by_path": paths,
         }
+        if strong is not None:
+            line["strong"] = strong
+        if cfg3 is not None:
+            line["cfg3_sharded"] = cfg3
+        if configs is not None:
+            line["configs"] = configs
         print(json.dumps(line), flush=True)
-    del graph
     dev.close()
     if world > 1:
         dist.barrier()

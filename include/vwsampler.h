@@ -144,7 +144,9 @@ vw_status vw_synchronize(vw_handle* handle, void* stream);
 
 /* Copies the per-path row counters into *out (after any vw_synchronize the caller needs); `reset` != 0 clears
  * them.  Setting the environment variable VW_FORCE_EXACT=1 before vw_create makes every sampled row take the
- * sequential replay (a test hook; results are identical, only slower). */
+ * sequential replay (a test hook; results are identical, only slower).  VW_TEST_STALL_ROW=r before vw_create makes
+ * the handle's first vw_sample call withhold row r's input stage inside the kernel, with the kernel's bounded waits
+ * cut to 1 ms: that call returns VW_ERR_TIMEOUT (a test hook for the timeout path; later calls are unaffected). */
 vw_status vw_get_stats(vw_handle* handle, vw_stats* out, int32_t reset);
 
 /*
@@ -154,12 +156,14 @@ vw_status vw_get_stats(vw_handle* handle, vw_stats* out, int32_t reset);
  * samples on the CPU and manages no device memory.  Results are vw_sample's.
  *
  * The call takes no handle and allocates nothing.  Its scratch is one fixed device array per device (about
- * 16.4 MiB, built into the library, loaded on first use); the first call on a device looks up that array's
- * address, so make that first call before any stream capture.
+ * 16.4 MiB, built into the library, loaded on first use, held until the process exits); every call looks up that
+ * array's address on the device.  The call is synchronous: it ends by synchronizing its stream and reading the
+ * error word back, so it cannot be captured into a CUDA graph.
  *
  * Limits (larger requests fail with VW_ERR_INVALID_ARG and a message): at most 65536 rows per call over all
- * segments, vocab <= 4096, n_options <= 32.  Every array is device memory of `device` (as VW_MEM_DEVICE); there
- * is no host-memory mode.
+ * segments, vocab <= 4096, n_options <= 32.  Every array is device memory of `device` (as VW_MEM_DEVICE; each
+ * non-NULL pointer is checked, and a host or foreign pointer fails with VW_ERR_INVALID_ARG); there is no
+ * host-memory mode.
  *
  * stream: a cudaStream_t of `device`, or NULL for the default stream.  The call returns after the stream has
  *   finished it, reporting device-side errors in its status.
@@ -189,6 +193,14 @@ vw_status vw_select(vw_handle* handle, const float* logits, int32_t vocab, const
 
 /* Sampler.ArgMax (Sampler.cs:90-95): first index of the maximum. */
 vw_status vw_argmax(vw_handle* handle, const float* logits, int32_t vocab, int32_t mem, int32_t* out_id);
+
+/*
+ * Diagnostic: evaluates on the handle's device, for n device doubles x[0..n), the exp the sampler uses for every
+ * softmax numerator (exp_libm[i]: glibc's exp restated, so the device reproduces the reference's Math.Exp values,
+ * Sampler.cs:57) and CUDA's own exp (exp_cuda[i], for comparison).  Either output may be NULL.  Device memory;
+ * synchronous.  No counterpart in the reference: it lets a caller check the device exp against its host libm.
+ */
+vw_status vw_exp_diagnostic(vw_handle* handle, const double* x, int64_t n, double* exp_libm, double* exp_cuda);
 
 #ifdef __cplusplus
 }

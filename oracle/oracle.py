@@ -40,6 +40,9 @@ def _load():
     lib.oracle_dotnet_random.argtypes = [i32, vp, i32]
     lib.oracle_dotnet_random_next.restype = None
     lib.oracle_dotnet_random_next.argtypes = [i32, vp, i32]
+    lib.oracle_exp_args.restype = i64
+    lib.oracle_exp_args.argtypes = [vp, i32, i64, i32, i32, i32, vp, vp, vp, vp, ctypes.POINTER(OracleOptions),
+                                    i32, i32, i32, i32, vp, i64]
     lib.oracle_exp.restype = None
     lib.oracle_exp.argtypes = [vp, vp, i64]
     return lib
@@ -72,6 +75,22 @@ def sample_segment(seg, opts: Sequence, threads: int = 1, want_probs: bool = Fal
     if st != 0:
         raise IndexError("history id out of range")
     return (out, probs) if want_probs else out
+
+
+def exp_args(seg, opts: Sequence) -> np.ndarray:
+    """Every argument the oracle's softmax passes to exp (the fp32 x - max of each survivor), row by row."""
+    table = (OracleOptions * len(opts))(*[options(o) for o in opts])
+    logits = np.ascontiguousarray(seg.logits)
+    call = lambda out, cap: lib.oracle_exp_args(
+        logits.ctypes.data, int(seg.dtype), int(logits.shape[1]), seg.n_rows, int(seg.vocab), int(seg.kind),
+        _p(seg.hist_offsets), _p(seg.hist_ids), _p(seg.steps), _p(seg.opt_index), table, int(seg.suppress_lo),
+        int(seg.suppress_hi), int(seg.eos_id), int(seg.min_new_tokens), out, cap)
+    n = call(None, 0)
+    if n < 0:
+        raise IndexError("history id out of range")
+    out = np.empty(n, dtype=np.float32)
+    call(out.ctypes.data, n)
+    return out
 
 
 def select(logits: np.ndarray, opt: Sequence, r: float, want_probs: bool = False):

@@ -87,8 +87,10 @@ int argmax(const float* x, int n) {
 }
 
 // Sampler.Select (Sampler.cs:35-88).  `r` is the NextDouble() draw the reference takes at :77; greedy rows
-// take no draw.  `probs_out` (nullable, n doubles) receives the final probabilities the draw scans.
-int select(float* logits, int n, const OracleOptions& o, double r, double* probs_out) {
+// take no draw.  `probs_out` (nullable, n doubles) receives the final probabilities the draw scans; `exp_args`
+// (nullable) collects every argument the softmax passes to Math.Exp (the fp32 difference x - max, :57).
+int select(float* logits, int n, const OracleOptions& o, double r, double* probs_out,
+           std::vector<float>* exp_args = nullptr) {
     if (!o.do_sample) {                                              // :37
         if (probs_out) std::fill(probs_out, probs_out + n, 0.0);
         return argmax(logits, n);
@@ -110,7 +112,9 @@ int select(float* logits, int n, const OracleOptions& o, double r, double* probs
     double sum = 0;
     for (int i = 0; i < n; ++i) {                                    // :55-59
         const float d = logits[i] - mx;                              // fp32 subtraction, then widened
-        probs[i] = std::isinf(logits[i]) && logits[i] < 0 ? 0.0 : std::exp(static_cast<double>(d));
+        const bool dropped = std::isinf(logits[i]) && logits[i] < 0;
+        probs[i] = dropped ? 0.0 : std::exp(static_cast<double>(d));
+        if (exp_args && !dropped) exp_args->push_back(d);
         sum += probs[i];
     }
     for (int i = 0; i < n; ++i) probs[i] /= sum;                     // :60
@@ -192,15 +196,9 @@ int32_t dotnet_random_sample(DotNetRandom* g) {
 
 double dotnet_random_next_double(DotNetRandom* g) { return dotnet_random_sample(g) * (1.0 / kMBig); }
 
-}  // namespace
-
-extern "C" {
-
-// One row of the batched call.  Mirrors one iteration of TalkerGenerator.GenerateBatch's talker loop
-// (kind 0: penalty + mask + Select, :369-373) or sub-talker loop (kind 1: Select only, :420).
-int oracle_sample_row(const void* row, int dtype, int n, int kind, const int32_t* hist, int64_t hlen,
-                      int step, const OracleOptions* o, double r, int mask_lo, int mask_hi, int eos,
-                      int min_new, int32_t* out_id, double* probs_out) {
+int sample_row_impl(const void* row, int dtype, int n, int kind, const int32_t* hist, int64_t hlen, int step,
+                    const OracleOptions* o, double r, int mask_lo, int mask_hi, int eos, int min_new,
+                    int32_t* out_id, double* probs_out, std::vector<float>* exp_args) {
     std::vector<float> lg(static_cast<size_t>(n));
     if (dtype == 0) {
         std::memcpy(lg.data(), row, sizeof(float) * n);
@@ -212,8 +210,21 @@ int oracle_sample_row(const void* row, int dtype, int n, int kind, const int32_t
         if (apply_repetition_penalty(lg.data(), n, hist, hlen, o->repetition_penalty) != 0) return -1;
         apply_suppress_mask(lg.data(), n, mask_lo, mask_hi, eos, step, min_new);
     }
-    *out_id = select(lg.data(), n, *o, r, probs_out);
+    *out_id = select(lg.data(), n, *o, r, probs_out, exp_args);
     return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+// One row of the batched call.  Mirrors one iteration of TalkerGenerator.GenerateBatch's talker loop
+// (kind 0: penalty + mask + Select, :369-373) or sub-talker loop (kind 1: Select only, :420).
+int oracle_sample_row(const void* row, int dtype, int n, int kind, const int32_t* hist, int64_t hlen,
+                      int step, const OracleOptions* o, double r, int mask_lo, int mask_hi, int eos,
+                      int min_new, int32_t* out_id, double* probs_out) {
+    return sample_row_impl(row, dtype, n, kind, hist, hlen, step, o, r, mask_lo, mask_hi, eos, min_new, out_id,
+                           probs_out, nullptr);
 }
 
 // Batched form over n_rows rows of one segment, split across `n_threads` std::threads.
@@ -277,6 +288,33 @@ void oracle_dotnet_random_next(int32_t seed, int32_t* out, int count) {
     DotNetRandom g;
     dotnet_random_init(&g, seed);
     for (int i = 0; i < count; ++i) out[i] = dotnet_random_sample(&g);
+}
+
+// Every argument the rows' softmax passes to Math.Exp (Sampler.cs:57), in row order, as the exact fp32 values
+// x - max.  Writes at most `cap` values and returns how many there are in total (-1: a history id out of range).
+int64_t oracle_exp_args(const void* logits, int dtype, int64_t row_stride, int n_rows, int n, int kind,
+                        const int64_t* hist_offsets, const int32_t* hist_ids, const int32_t* steps,
+                        const int32_t* opt_index, const OracleOptions* opts, int mask_lo, int mask_hi, int eos,
+                        int min_new, float* out, int64_t cap) {
+    const size_t esize = dtype == 0 ? 4 : 2;
+    std::vector<float> args;
+    int64_t total = 0;
+    for (int r = 0; r < n_rows; ++r) {
+        const void* row = static_cast<const char*>(logits) + esize * static_cast<size_t>(row_stride) * r;
+        const int32_t* h = hist_offsets ? hist_ids + hist_offsets[r] : nullptr;
+        const int64_t hl = hist_offsets ? hist_offsets[r + 1] - hist_offsets[r] : 0;
+        int32_t id = 0;
+        args.clear();
+        if (sample_row_impl(row, dtype, n, kind, h, hl, steps ? steps[r] : min_new,
+                            opts + (opt_index ? opt_index[r] : 0), 0.0, mask_lo, mask_hi, eos, min_new, &id, nullptr,
+                            &args) != 0)
+            return -1;
+        for (float a : args) {
+            if (total < cap) out[total] = a;
+            ++total;
+        }
+    }
+    return total;
 }
 
 // glibc exp over an array (used to measure the device exp against the host libm).

@@ -7,9 +7,19 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
+# measured figures the tests report (exp mismatch counts, parity and flip counts), printed after the run
+REPORT = []
+
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) CUDA device")
+
+
+def pytest_terminal_summary(terminalreporter, exitstatus, config):
+    if REPORT:
+        terminalreporter.section("measured")
+        for line in REPORT:
+            terminalreporter.write_line(line)
 
 
 @pytest.fixture(scope="session")

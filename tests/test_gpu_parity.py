@@ -10,7 +10,9 @@ import numpy as np
 import pytest
 
 from oracle import oracle
+from tests.conftest import REPORT
 from tests.gpu_util import run_workload
+from tests.parity import compare
 from voxwerk_b200 import workloads
 from voxwerk_b200.workloads import SegData, Workload
 
@@ -32,8 +34,16 @@ def assert_ids_equal(w, got, ref):
 
 @pytest.mark.parametrize("cfg", [0, 1, 2, 3, 4])
 def test_config_ids_bit_exact(device, cfg):
+    """Every row of the configuration; a differing id is a flip, counted with its distance to the oracle's nearest
+    CDF boundary (the specification would accept a flip only within 1e-6 of one; none is accepted here)."""
     w = workloads.make(cfg)
-    assert_ids_equal(w, run_workload(device, w), oracle_ids(w))
+    device.stats(reset=True)
+    c = compare(w, run_workload(device, w), threads=THREADS)
+    st = device.stats(reset=True)
+    REPORT.append(f"parity {w.name}: {c['rows']} rows, {c['flips']} flips (attributable to a CDF boundary: "
+                  f"{c['attributable']}, max distance {c['max_boundary_dist']}); replayed rows: "
+                  f"{st['rows_fast_replayed'] + st['rows_general_replayed'] + st['rows_large']}")
+    assert c["flips"] == 0, c["first_flips"]
 
 
 @pytest.mark.parametrize("cfg,rows", [(2, 96), (3, 8), (4, 96), (0, None), (1, None)])
@@ -245,7 +255,7 @@ def test_talker_batch_sampler_matches_reference_loop(device):
     jobs.append(GenerationOptions.greedy())
     tb = TalkerBatchSampler(jobs, device)
     rng = np.random.default_rng(9)
-    from voxwerk_b200.sampler import DotNetRandom
+    from voxwerk_b200.dotnet_random import DotNetRandom
     ref_rng = [DotNetRandom(j.seed) for j in jobs]
     ref_sub = [DotNetRandom(None if j.seed is None else j.seed + 1) for j in jobs]
     hist = [[] for _ in jobs]

@@ -47,6 +47,39 @@ def test_forced_replay_matches_oracle():
     assert st["rows_fast_replayed"] > 0 and st["rows_general_replayed"] > 0, st
 
 
+STALL_CHILD = r"""
+import json, os, sys
+sys.path.insert(0, sys.argv[1])
+import numpy as np
+from oracle import oracle
+from tests.gpu_util import run_workload
+from voxwerk_b200 import Device, VwError, workloads
+out = {}
+with Device(0) as dev:
+    w = workloads.make(2, 512)
+    try:
+        run_workload(dev, w)
+        out["first"] = "ok"
+    except VwError as e:
+        out["first"] = e.status
+    got = run_workload(dev, w)
+    out["second_exact"] = bool(np.array_equal(got[0], oracle.sample_segment(w.segments[0], w.options, threads=8)))
+print(json.dumps(out))
+"""
+
+
+def test_timeout_is_reported_and_the_handle_recovers():
+    """VW_TEST_STALL_ROW: the kernel's producer withholds one row's stage, so an element warp's bounded mbarrier
+    wait (cut to 1 ms by the hook) runs out.  The call returns VW_ERR_TIMEOUT; the next call on the same handle is
+    bit-exact against the oracle.  No wait is unbounded, so nothing hangs."""
+    env = dict(os.environ, VW_TEST_STALL_ROW="100")
+    res = subprocess.run([sys.executable, "-c", STALL_CHILD, ROOT], env=env, capture_output=True, text=True,
+                         timeout=600)
+    assert res.returncode == 0, res.stderr[-3000:]
+    out = json.loads(res.stdout.strip().splitlines()[-1])
+    assert out == {"first": 4, "second_exact": True}, out
+
+
 def test_parallel_paths_are_taken(device):
     from tests.gpu_util import run_workload
     from voxwerk_b200 import workloads

@@ -32,7 +32,7 @@ def test_dotnet_random_published_values():
 
 
 def test_dotnet_random_python_mirror_matches_oracle():
-    from voxwerk_b200.sampler import DotNetRandom
+    from voxwerk_b200.dotnet_random import DotNetRandom
     for seed in (0, 1, 42, 43, 1234, -7, 2**31 - 1, -2**31):
         g = DotNetRandom(seed)
         got = [g.next_double() for _ in range(200)]
@@ -41,7 +41,7 @@ def test_dotnet_random_python_mirror_matches_oracle():
 
 def test_dotnet_random_seed_plus_one_wraps():
     # Sampler(Seed + 1) with Seed = int.MaxValue wraps to int.MinValue in C# (TalkerGenerator.cs:218).
-    from voxwerk_b200.sampler import DotNetRandom
+    from voxwerk_b200.dotnet_random import DotNetRandom
     g = DotNetRandom(2**31)   # == int.MinValue after the wrap
     assert g.next_double() == oracle.dotnet_random(-2**31, 1)[0]
 

@@ -8,6 +8,7 @@ tolerance of the parity tests.  Each workload runs through vw_sample_static twic
 import numpy as np
 import pytest
 
+from oracle import oracle
 from tests.gpu_util import make_segment, options_table, to_device
 from voxwerk_b200 import Segment, VwInvalidArgument, sample_rows, sample_rows_static, workloads
 from voxwerk_b200._lib import VW_ROWS_SUB, VwOptions
@@ -43,6 +44,51 @@ def test_static_matches_vw_sample_twice(device, cfg, rows, want_probs):
         if want_probs:
             for g, r in zip(probs, ref_probs):
                 np.testing.assert_allclose(g, r, rtol=PROB_RTOL, atol=0.0)
+    # and against the CPU oracle directly, so a regression shared by both entry points shows too
+    for seg, got in zip(w.segments, ids):
+        np.testing.assert_array_equal(got, oracle.sample_segment(seg, w.options, threads=8))
+
+
+@pytest.mark.gpu
+def test_static_allocates_nothing_and_recovers_after_an_error(device):
+    """Repeated calls leave the device's free memory unchanged; a call that ends in an error (a history id out of
+    range, which the kernel checks and reports) leaves the shared array usable for the next call."""
+    import torch
+    from voxwerk_b200 import VwOutOfRange
+    w = workloads.make(2, 512)
+    run = lambda: _run(w, lambda s, o: sample_rows_static(0, s, o), False)[0]
+    run()
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    for _ in range(3):
+        ids = run()
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free0
+    bad = workloads.make(2, 512)
+    bad.segments[0].hist_ids[100] = 5000
+    with pytest.raises(VwOutOfRange):
+        _run(bad, lambda s, o: sample_rows_static(0, s, o), False)
+    again = run()
+    for g, r in zip(again, ids):
+        np.testing.assert_array_equal(g, r)
+    np.testing.assert_array_equal(again[0], oracle.sample_segment(w.segments[0], w.options, threads=8))
+
+
+@pytest.mark.gpu
+def test_static_rejects_host_pointers(device):
+    """Every array of a segment must be device memory: a host array fails with a status, not a fault."""
+    import ctypes
+    import torch
+    from voxwerk_b200._lib import VW_ERR_INVALID_ARG, VwSegment, lib
+    w = workloads.make(1)
+    seg = w.segments[0]
+    c = make_segment(seg, to_device(seg, torch)).to_c(0)
+    host_uniforms = torch.from_numpy(seg.uniforms).pin_memory()
+    c.uniforms = host_uniforms.data_ptr()
+    msg = ctypes.create_string_buffer(256)
+    opts = (VwOptions * 1)(*options_table(w))
+    st = lib.vw_sample_static(0, (VwSegment * 1)(c), 1, opts, 1, None, msg, len(msg))
+    assert st == VW_ERR_INVALID_ARG and b"uniforms must be device memory" in msg.value, (st, msg.value)
 
 
 @pytest.mark.gpu

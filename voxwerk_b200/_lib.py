@@ -41,6 +41,7 @@ EXPORTED = (
     "vw_select",
     "vw_argmax",
     "vw_sample_static",
+    "vw_exp_diagnostic",
 )
 
 
@@ -149,6 +150,8 @@ def _load() -> ctypes.CDLL:
     lib.vw_sample_static.restype = ctypes.c_int
     lib.vw_sample_static.argtypes = [i32, ctypes.POINTER(VwSegment), i32, ctypes.POINTER(VwOptions), i32, vp,
                                      ctypes.c_char_p, i32]
+    lib.vw_exp_diagnostic.restype = ctypes.c_int
+    lib.vw_exp_diagnostic.argtypes = [vp, vp, i64, vp, vp]
     return lib
 
 

@@ -40,6 +40,7 @@ struct vw_handle {
     unsigned long long* d_stats = nullptr;   // vw::kNumStats per-path row counters
     unsigned long long* d_guess = nullptr;   // candidate threshold carried from call to call
     int force_exact = 0;                     // VW_FORCE_EXACT at creation
+    int test_stall_row = -1;                 // VW_TEST_STALL_ROW at creation (first vw_sample call only)
     unsigned long long h2d_bytes = 0;        // host -> device input bytes of VW_MEM_HOST calls (vw_stats.h2d_bytes)
     std::string last_error;
 };
@@ -329,6 +330,7 @@ vw_status read_device_error(vw_handle* h, cudaStream_t st) {
     if (bits & vw::kErrTimeout) return fail(h, VW_ERR_TIMEOUT, "a bounded wait in the sampler kernel gave up");
     if (bits & vw::kErrHistRange) return fail(h, VW_ERR_OUT_OF_RANGE, "a history id is outside [0, vocab)");
     if (bits & vw::kErrBadOption) return fail(h, VW_ERR_INVALID_ARG, "a row's opt_index is outside the options table");
+    if (bits & vw::kErrHistOffsets) return fail(h, VW_ERR_INVALID_ARG, "hist_offsets are negative or decrease");
     return VW_OK;
 }
 
@@ -447,6 +449,9 @@ vw_status sample_impl(vw_handle* h, const vw_segment* segs, int32_t n_segs, cons
     p.stats = h->d_stats;
     p.guess_seed = h->d_guess;
     p.force_exact = h->force_exact;
+    p.wait_ns = h->test_stall_row >= 0 ? vw::kTestWaitLimitNs : vw::kWaitLimitNs;
+    p.test_stall_row = h->test_stall_row;
+    h->test_stall_row = -1;   // one call only
 
     vw::LaunchPlan plan;
     if (!vw::plan_launch(p, h->sm_count, INT32_MAX, &plan))
@@ -540,6 +545,8 @@ VW_EXPORT vw_status vw_create(int32_t device, vw_handle** out) {
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     const char* fe = std::getenv("VW_FORCE_EXACT");
     h->force_exact = (fe && fe[0] == '1') ? 1 : 0;
+    const char* ts = std::getenv("VW_TEST_STALL_ROW");
+    if (ts && ts[0]) h->test_stall_row = std::atoi(ts);
     if (e != cudaSuccess) {
         vw_destroy(h);
         return VW_ERR_CUDA;
@@ -685,6 +692,20 @@ VW_EXPORT vw_status vw_argmax(vw_handle* h, const float* logits, int32_t vocab, 
     return vw_select(h, logits, vocab, &o, 0.0, mem, out_id);
 }
 
+VW_EXPORT vw_status vw_exp_diagnostic(vw_handle* h, const double* x, int64_t n, double* exp_libm,
+                                      double* exp_cuda) {
+    if (!h) return VW_ERR_INVALID_ARG;
+    h->last_error.clear();
+    if (n < 0 || (n > 0 && !x)) return fail(h, VW_ERR_INVALID_ARG, "bad argument array");
+    if (n == 0) return VW_OK;
+    DeviceGuard guard(h->device);
+    if (!guard.ok()) return fail(h, VW_ERR_CUDA, "cudaSetDevice failed");
+    cudaError_t e = vw::launch_exp_diagnostic(x, n, exp_libm, exp_cuda, h->sm_count, h->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(h->stream);
+    if (e != cudaSuccess) return cuda_fail(h, e, "exp diagnostic");
+    return VW_OK;
+}
+
 // ------------------------------------------------------------------------------------- vw_sample_static
 // vw_sample for callers that must not allocate device memory: no handle, device pointers only, and the kernels'
 // scratch (error word, deferred-row list, whole-row slices) in the fixed array of vw_static.cu.
@@ -694,7 +715,7 @@ constexpr int kStaticMaxDevices = 64;
 
 struct StaticDevice {
     bool ready = false;
-    char* scratch = nullptr;   // device address of the array on this device
+    char* scratch = nullptr;   // device address of the array on this device (looked up on every call)
     int sm_count = 0;
 };
 
@@ -708,22 +729,23 @@ void copy_message(const vw_handle& h, char* err_msg, int32_t err_msg_len) {
     err_msg[n] = '\0';
 }
 
-// One-time set-up of `device` (current): the array's device address and the SM count.
+// Set-up of `device` (current): the array's device address, looked up on every call (cheap, allocates nothing, and
+// stays right if the context was reset and the module reloaded), and the SM count, cached.
 vw_status static_setup(vw_handle* h, int device, StaticDevice* out) {
     std::lock_guard<std::mutex> lock(g_static_mutex);
     StaticDevice& d = g_static_devices[device];
     if (!d.ready) {
-        char* ptr = nullptr;
-        cudaError_t e = vw::static_scratch_address(&ptr);
-        if (e != cudaSuccess) return cuda_fail(h, e, "cudaGetSymbolAddress of the static scratch");
-        if (!ptr) return fail(h, VW_ERR_CUDA, "cudaGetSymbolAddress returned NULL");
         int sms = 0;
-        e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+        cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
         if (e != cudaSuccess) return cuda_fail(h, e, "cudaDeviceGetAttribute");
-        d.scratch = ptr;
         d.sm_count = sms;
         d.ready = true;
     }
+    char* ptr = nullptr;
+    cudaError_t e = vw::static_scratch_address(&ptr);
+    if (e != cudaSuccess) return cuda_fail(h, e, "cudaGetSymbolAddress of the static scratch");
+    if (!ptr) return fail(h, VW_ERR_CUDA, "cudaGetSymbolAddress returned NULL");
+    d.scratch = ptr;
     *out = d;
     return VW_OK;
 }
@@ -764,18 +786,25 @@ vw_status sample_static_impl(vw_handle* h, int32_t device, const vw_segment* seg
     StaticDevice sd;
     r = static_setup(h, device, &sd);
     if (r != VW_OK) return r;
-    // the logits and the ids must be device memory of this device (host memory would need staging buffers)
+    // every array must be device memory of this device (host memory would need staging buffers, and a kernel
+    // given a host or foreign pointer would fault instead of returning a status)
     for (int i = 0; i < n_segs; ++i) {
-        if (segs[i].n_rows == 0) continue;
-        const void* ptrs[2] = {segs[i].logits, segs[i].out_ids};
-        for (const void* q : ptrs) {
+        const vw_segment& sg = segs[i];
+        if (sg.n_rows == 0) continue;
+        const bool talker = sg.kind == VW_ROWS_TALKER;
+        const void* ptrs[8] = {sg.logits, sg.out_ids, sg.out_probs, sg.uniforms, sg.opt_index,
+                               talker ? sg.steps : nullptr, talker ? sg.hist_offsets : nullptr,
+                               talker && sg.hist_offsets ? sg.hist_ids : nullptr};
+        static const char* names[8] = {"logits", "out_ids", "out_probs", "uniforms", "opt_index", "steps",
+                                       "hist_offsets", "hist_ids"};
+        for (int k = 0; k < 8; ++k) {
+            if (!ptrs[k]) continue;
             cudaPointerAttributes a;
-            if (cudaPointerGetAttributes(&a, q) != cudaSuccess ||
+            if (cudaPointerGetAttributes(&a, ptrs[k]) != cudaSuccess ||
                 (a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged) || a.device != device) {
                 cudaGetLastError();
-                return fail(h, VW_ERR_INVALID_ARG, "segment " + std::to_string(i) +
-                                                       ": logits and out_ids must be device memory of device " +
-                                                       std::to_string(device));
+                return fail(h, VW_ERR_INVALID_ARG, "segment " + std::to_string(i) + ": " + names[k] +
+                                                       " must be device memory of device " + std::to_string(device));
             }
         }
     }
@@ -831,6 +860,8 @@ vw_status sample_static_impl(vw_handle* h, int32_t device, const vw_segment* seg
     p.flag_bytes = static_cast<int32_t>(round_up(static_cast<size_t>(vmax), 16));
     p.vmax = vmax;
     p.stats = nullptr;
+    p.wait_ns = vw::kWaitLimitNs;
+    p.test_stall_row = -1;
     const char* fe = std::getenv("VW_FORCE_EXACT");
     p.force_exact = (fe && fe[0] == '1') ? 1 : 0;
 
@@ -862,6 +893,7 @@ vw_status sample_static_impl(vw_handle* h, int32_t device, const vw_segment* seg
     if (bits & vw::kErrTimeout) return fail(h, VW_ERR_TIMEOUT, "a bounded wait in the sampler kernel gave up");
     if (bits & vw::kErrHistRange) return fail(h, VW_ERR_OUT_OF_RANGE, "a history id is outside [0, vocab)");
     if (bits & vw::kErrBadOption) return fail(h, VW_ERR_INVALID_ARG, "a row's opt_index is outside the options table");
+    if (bits & vw::kErrHistOffsets) return fail(h, VW_ERR_INVALID_ARG, "hist_offsets are negative or decrease");
     return VW_OK;
 }
 

@@ -29,7 +29,7 @@ enum : int {
     kStatGeneralReplayed = 4,  // whole-row rows replayed in the reference's order
     kStatLarge = 5,            // rows of more than 3072 active ids (always replayed)
     kStatOverflow = 6,         // candidate-eligible rows that took the whole-row path
-    kNumStats = 8,
+    kNumStats = 8,             // slot 7 is vw_stats.h2d_bytes, kept on the host
 };
 
 // Error bits latched in the device error word.
@@ -37,6 +37,7 @@ enum : unsigned {
     kErrHistRange = 1u,   // a history id outside [0, V)
     kErrTimeout = 2u,     // an mbarrier wait gave up
     kErrBadOption = 4u,   // a row's option index outside the table
+    kErrHistOffsets = 8u, // a row's history offsets negative or decreasing (the row is sampled without history)
 };
 
 struct DevOptions {       // same layout as vw_options
@@ -91,7 +92,12 @@ struct LaunchParams {
     int64_t gscratch_stride;
     unsigned long long* guess_seed;   // candidate threshold carried across calls: float bits << 32 | (segment,
                                       // option) id; nullable (any value is safe: it only saves work when it fits)
+    uint64_t wait_ns;             // bound of every mbarrier wait without progress
+    int32_t test_stall_row;       // test hook: the candidate kernel's producer withholds this row's stage (-1: none)
 };
+
+constexpr uint64_t kWaitLimitNs = 2000000000ull;   // default wait bound: 2 s without progress
+constexpr uint64_t kTestWaitLimitNs = 1000000ull;  // with the stall test hook: 1 ms
 
 // Dynamic shared memory the whole-row kernel needs for `p`.
 size_t sampler_smem_bytes(const LaunchParams& p);
@@ -126,6 +132,10 @@ constexpr int64_t kStaticCtaStride = (static_cast<int64_t>(kStaticMaxVocab) * 28
 constexpr int64_t kStaticBytes = kStaticScratchOffset + kStaticGeneralCtas * kStaticCtaStride;   // ~16.4 MiB
 // Device address of this device's array (the device must be current); cudaGetSymbolAddress's status.
 cudaError_t static_scratch_address(char** ptr);
+
+// The sampler's exp and CUDA's exp over n device doubles (see vw_exp_diagnostic).
+cudaError_t launch_exp_diagnostic(const double* x, int64_t n, double* y_libm, double* y_cuda, int sm_count,
+                                  cudaStream_t stream);
 
 // Sampler.ApplyRepetitionPenalty on one device row, in place.
 cudaError_t launch_apply_penalty(float* logits, int vocab, const int32_t* hist, int64_t hist_len, float penalty,

@@ -45,13 +45,13 @@
 #include <mutex>
 #include <cuda_runtime.h>
 
+#include "vw_libm_exp.h"
 #include "vw_internal.h"
 
 namespace vw {
 namespace {
 
 constexpr unsigned kFull = 0xffffffffu;
-constexpr uint64_t kWaitLimitNs = 2000000000ull;   // bounded mbarrier waits: 2 s without progress
 constexpr double kU = 1.1102230246251565e-16;      // 2^-53
 constexpr double kFix = 2251799813685248.0;         // 2^51: fixed-point scale of histogram masses (e <= 1)
 constexpr int kProducerWarp = kWarps;              // warp 4
@@ -146,9 +146,10 @@ __device__ __forceinline__ uint64_t global_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
-// Gives up after kWaitLimitNs without progress and returns false.  `progress` (nullable) is a counter whose
-// change restarts the clock.
-__device__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, const volatile uint32_t* progress = nullptr) {
+// Gives up after `limit_ns` without progress and returns false.  `progress` (nullable) is a counter whose change
+// restarts the clock.
+__device__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns,
+                                  const volatile uint32_t* progress = nullptr) {
     if (mbar_try_wait(bar, parity)) return true;
     uint64_t t0 = global_ns();
     uint32_t last = progress ? *progress : 0u;
@@ -161,7 +162,7 @@ __device__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, const volatile
                 t0 = global_ns();
             }
         }
-        if (global_ns() - t0 > kWaitLimitNs) return false;
+        if (global_ns() - t0 > limit_ns) return false;
     }
 }
 __device__ __forceinline__ void fence_proxy_async() {
@@ -220,9 +221,10 @@ __device__ __forceinline__ uint32_t okey(float x) {
 __device__ __forceinline__ float okey_inv(uint32_t k) {
     return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
-// exp(fp64(fp32(x - mx))), Sampler.cs:57
+// exp(fp64(fp32(x - mx))), Sampler.cs:57, with the host libm's exact exp (vw_libm_exp.h): the replays then
+// reproduce the reference's sums bit for bit, and the parallel paths' bands need no allowance for exp.
 __device__ __forceinline__ double softmax_num(float x, float mx) {
-    return exp(static_cast<double>(__fsub_rn(x, mx)));
+    return libm_exp(static_cast<double>(__fsub_rn(x, mx)));
 }
 
 __device__ __forceinline__ uint64_t shfl_xor_u64(uint64_t v, int m) { return __shfl_xor_sync(kFull, v, m); }
@@ -1268,6 +1270,10 @@ __device__ RowMeta plan_row(const LaunchParams& p, int r, uint32_t& bytes, int& 
     if (sg.kind == 0 && sg.hist_offsets) {
         hb = sg.hist_offsets[local];
         he = sg.hist_offsets[local + 1];
+        if (hb < 0 || he < hb) {   // device-memory offsets are checked here: report, and read no history
+            atomicOr(p.err, kErrHistOffsets);
+            hb = he = 0;
+        }
     }
     m.opt_ok = (opt_raw >= 0 && opt_raw < p.n_opts) ? 1 : 0;
     if (m.opt_ok) {
@@ -1392,7 +1398,7 @@ __device__ void produce_rows(const LaunchParams& p, int first, int gstride, int 
                 const int k = k0 + j;
                 const int s = rp.s;
                 if (rp.n > 0)
-                    ok = mbar_wait_bounded(&empty_bar[s], static_cast<uint32_t>((rp.n - 1) & 1), progress);
+                    ok = mbar_wait_bounded(&empty_bar[s], static_cast<uint32_t>((rp.n - 1) & 1), p.wait_ns, progress);
                 if (ok) {
                     metas[rp.meta(S_)] = m;
                     fence_proxy_async();
@@ -1423,11 +1429,12 @@ __device__ void produce_rows_dynamic(const LaunchParams& p, int lane, unsigned c
     RingPos rp{0, 0};
     for (int k = 0;; ++k, rp.next(S_)) {
         const int s = rp.s;
-        if (rp.n > 0 && !mbar_wait_bounded(&empty_bar[s], static_cast<uint32_t>((rp.n - 1) & 1), progress)) {
+        if (rp.n > 0 && !mbar_wait_bounded(&empty_bar[s], static_cast<uint32_t>((rp.n - 1) & 1), p.wait_ns, progress)) {
             atomicOr(p.err, kErrTimeout);
             return;
         }
         const int r = static_cast<int>(atomicAdd(p.row_counter, 1u));
+        if (r == p.test_stall_row) return;   // test hook: this row's stage never completes (its wait runs out)
         if (r >= p.total_rows) {
             metas[rp.meta(S_)].row = -1;
             mbar_arrive(&full_bar[s]);
@@ -1869,7 +1876,7 @@ __global__ void __launch_bounds__(kBlockThreads, 6) cand_kernel(const __grid_con
         const int s = rp.s;
         unsigned char* sl = stages + static_cast<size_t>(s) * stage_bytes;
         // the producer's progress counts as progress here too (it may be waiting for rows of other CTAs)
-        const bool ok = mbar_wait_bounded(&full_bar[s], static_cast<uint32_t>(rp.n & 1),
+        const bool ok = mbar_wait_bounded(&full_bar[s], static_cast<uint32_t>(rp.n & 1), p.wait_ns,
                                           reinterpret_cast<volatile uint32_t*>(&cm.issued));
         if (cbar_or(!ok)) {
             failed = true;
@@ -2136,7 +2143,7 @@ __global__ void __launch_bounds__(kBlockThreads, 6) cand_kernel(const __grid_con
             // drain: wait (bounded) for every copy the producer issued from this row on
             const int issued = *reinterpret_cast<volatile int*>(&cm.issued);
             for (int kk = rp.n * S_ + rp.s; kk < issued; ++kk)
-                mbar_wait_bounded(&full_bar[kk % S_], static_cast<uint32_t>((kk / S_) & 1));
+                mbar_wait_bounded(&full_bar[kk % S_], static_cast<uint32_t>((kk / S_) & 1), p.wait_ns);
         }
         // the last CTA to finish resets the row counter for the next call
         __threadfence();
@@ -2222,14 +2229,14 @@ __global__ void __launch_bounds__(kBlockThreads, 3) whole_row_kernel(const __gri
     for (int k = 0; k < n_my; ++k, rp.next(S_)) {
         const int s = rp.s;
         unsigned char* sl = stages + static_cast<size_t>(s) * stage_bytes;
-        const bool ok = mbar_wait_bounded(&full_bar[s], static_cast<uint32_t>(rp.n & 1));
+        const bool ok = mbar_wait_bounded(&full_bar[s], static_cast<uint32_t>(rp.n & 1), p.wait_ns);
         if (cbar_or(!ok)) {
             if (tid == 0) {
                 atomicOr(p.err, kErrTimeout);
                 // drain: wait (bounded) for every copy the producer issued after this row
                 const int issued = *reinterpret_cast<volatile int*>(&misc.issued);
                 for (int kk = k; kk < issued; ++kk)
-                    mbar_wait_bounded(&full_bar[kk % S_], static_cast<uint32_t>((kk / S_) & 1));
+                    mbar_wait_bounded(&full_bar[kk % S_], static_cast<uint32_t>((kk / S_) & 1), p.wait_ns);
             }
             cbar();
             break;
@@ -2480,7 +2487,25 @@ __global__ void __launch_bounds__(256) penalty_kernel(float* logits, int vocab, 
     if (bad) atomicOr(err, kErrHistRange);
 }
 
+// ---------------------------------------------------------------- exp diagnostic
+// The sampler's exp (libm_exp) and CUDA's exp over an array.
+__global__ void __launch_bounds__(256) exp_diag_kernel(const double* x, int64_t n, double* y_libm, double* y_cuda) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const double v = x[i];
+        if (y_libm) y_libm[i] = libm_exp(v);
+        if (y_cuda) y_cuda[i] = exp(v);
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_exp_diagnostic(const double* x, int64_t n, double* y_libm, double* y_cuda, int sm_count,
+                                  cudaStream_t stream) {
+    const int64_t blocks = std::min<int64_t>((n + 255) / 256, static_cast<int64_t>(sm_count) * 8);
+    if (blocks > 0) exp_diag_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(x, n, y_libm, y_cuda);
+    return cudaGetLastError();
+}
 
 // ---------------------------------------------------------------- host-side launch helpers
 size_t sampler_smem_bytes(const LaunchParams& p) {

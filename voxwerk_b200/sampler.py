@@ -26,15 +26,9 @@ import numpy as np
 from . import _lib
 from ._lib import (VW_BF16, VW_F32, VW_MEM_DEVICE, VW_MEM_HOST, VW_ROWS_SUB, VW_ROWS_TALKER, VwOptions,
                    VwSegment, check, lib)
-
-# Qwen3-TTS configuration constants used on this path (src/Voxwerk/Talker/Qwen3TtsConfig.cs).
-VOCAB_SIZE = 3072          # :28 talker codec vocabulary
-NUM_CODE_GROUPS = 16       # :31
-CODEC_EOS_ID = 2150        # :34
-CP_VOCAB_SIZE = 2048       # :49 code-predictor vocabulary
-SUPPRESS_SPAN = 1024       # TalkerGenerator.cs:247: ids [V - 1024, V) except EOS
-MIN_NEW_TOKENS = 2         # TalkerGenerator.cs:248: EOS suppressed while t < 2
-
+from .dotnet_random import DotNetRandom
+from .qwen3_tts import (CODEC_EOS_ID, CP_VOCAB_SIZE, MIN_NEW_TOKENS, NUM_CODE_GROUPS, SUPPRESS_SPAN,  # noqa: F401
+                        VOCAB_SIZE)
 
 @dataclass(frozen=True)
 class SamplingOptions:
@@ -72,64 +66,6 @@ def vw_options(opts: SamplingOptions, repetition_penalty: float = 1.0) -> VwOpti
     """The C struct for one stage (talker rows carry the job's RepetitionPenalty, sub rows 1.0)."""
     return VwOptions(int(bool(opts.do_sample)), int(opts.top_k), float(opts.top_p), float(opts.temperature),
                      float(repetition_penalty))
-
-
-class DotNetRandom:
-    """System.Random(int seed): Knuth's subtractive generator with .NET's parameters.
-
-    ``next_double()`` is Random.NextDouble(), the one draw Sampler.Select takes per sampled row (Sampler.cs:77).
-    ``seed=None`` seeds from the OS, like ``new Random()``.
-    """
-
-    _MBIG = 2147483647
-    _MSEED = 161803398
-
-    @staticmethod
-    def _sub(a: int, b: int) -> int:
-        """a - b with C# unchecked int32 wrap-around."""
-        return ((a - b + 2**31) % 2**32) - 2**31
-
-    def __init__(self, seed: Optional[int] = None):
-        if seed is None:
-            seed = int.from_bytes(np.random.default_rng().bytes(4), "little", signed=True)
-        seed = int(np.int32(np.int64(seed)))   # C# int arithmetic wraps (Seed + 1 at int.MaxValue)
-        sub = self._MBIG if seed == -2**31 else abs(seed)
-        a = [0] * 56
-        mj = self._sub(self._MSEED, sub)
-        a[55] = mj
-        mk = 1
-        for i in range(1, 55):
-            ii = (21 * i) % 55
-            a[ii] = mk
-            mk = self._sub(mj, mk)
-            if mk < 0:
-                mk += self._MBIG
-            mj = a[ii]
-        for _ in range(4):
-            for i in range(1, 56):
-                v = self._sub(a[i], a[1 + (i + 30) % 55])
-                if v < 0:
-                    v += self._MBIG
-                a[i] = v
-        self._a = a
-        self._inext = 0
-        self._inextp = 21
-
-    def next(self) -> int:
-        """Random.Next(): a value in [0, 2^31 - 1)."""
-        self._inext = 1 if self._inext + 1 >= 56 else self._inext + 1
-        self._inextp = 1 if self._inextp + 1 >= 56 else self._inextp + 1
-        v = self._sub(self._a[self._inext], self._a[self._inextp])
-        if v == self._MBIG:
-            v -= 1
-        if v < 0:
-            v += self._MBIG
-        self._a[self._inext] = v
-        return v
-
-    def next_double(self) -> float:
-        """Random.NextDouble()."""
-        return self.next() * (1.0 / self._MBIG)
 
 
 class Device:

@@ -43,6 +43,17 @@ def max_over_ranks(value: float, device=None) -> float:
     return float(t.item())
 
 
+def sum_over_ranks(value: float, device=None) -> float:
+    """The sum of `value` over every rank of the default process group (itself when not distributed)."""
+    import torch
+    import torch.distributed as dist
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return float(value)
+    t = torch.tensor([float(value)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
 def gather_ids(local_ids: np.ndarray, device=None) -> np.ndarray:
     """Every rank's ids concatenated in rank order (ranks may hold different row counts)."""
     import torch

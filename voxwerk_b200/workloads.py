@@ -22,7 +22,8 @@ from typing import List, Optional
 
 import numpy as np
 
-from .sampler import CODEC_EOS_ID, CP_VOCAB_SIZE, MIN_NEW_TOKENS, VOCAB_SIZE, DotNetRandom
+from .dotnet_random import DotNetRandom
+from .qwen3_tts import CODEC_EOS_ID, CP_VOCAB_SIZE, MIN_NEW_TOKENS, VOCAB_SIZE
 
 F32, BF16 = 0, 1
 TALKER, SUB = 0, 1
@@ -71,6 +72,21 @@ class SegData:
         if self.hist_ids is not None and self.hist_offsets is not None:
             b += int(self.hist_offsets[-1] - self.hist_offsets[0]) * 4
         return b
+
+    def take(self, rows) -> "SegData":
+        """The listed rows (any order) with their histories gathered into a fresh CSR."""
+        rows = np.asarray(rows, dtype=np.int64)
+        ho = hid = None
+        if self.hist_offsets is not None:
+            lens = self.hist_offsets[rows + 1] - self.hist_offsets[rows]
+            ho = np.zeros(rows.size + 1, dtype=np.int64)
+            ho[1:] = np.cumsum(lens)
+            parts = [self.hist_ids[self.hist_offsets[r]:self.hist_offsets[r + 1]] for r in rows]
+            hid = np.concatenate(parts).astype(np.int32) if parts and ho[-1] > 0 else np.zeros(4, np.int32)
+        pick = lambda a: None if a is None else np.ascontiguousarray(a[rows])
+        return SegData(np.ascontiguousarray(self.logits[rows]), self.dtype, self.kind, self.vocab,
+                       pick(self.uniforms), pick(self.opt_index), ho, hid, pick(self.steps), self.suppress_lo,
+                       self.suppress_hi, self.eos_id, self.min_new_tokens)
 
     def slice(self, lo: int, hi: int) -> "SegData":
         """Rows [lo, hi) with histories re-based (a contiguous row shard)."""
