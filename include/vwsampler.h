@@ -101,6 +101,8 @@ typedef struct vw_stats {
     uint64_t rows_general_replayed;  /* whole-row rows replayed in the reference's order */
     uint64_t rows_large;             /* rows of more than 3072 active ids (always replayed) */
     uint64_t rows_overflow;          /* top-k <= 64 rows whose candidates overflowed (counted in rows_general*) */
+    uint64_t rows_threshold_miss;    /* top-k <= 64 rows whose carried candidate threshold missed and was rebuilt
+                                        from the row (extra work, same result) */
     uint64_t h2d_bytes;              /* bytes VW_MEM_HOST calls copied host -> device (inputs only: the logit
                                         columns of a suppressed span are not copied, no kernel reads them) */
 } vw_stats;
@@ -145,8 +147,9 @@ vw_status vw_synchronize(vw_handle* handle, void* stream);
 /* Copies the per-path row counters into *out (after any vw_synchronize the caller needs); `reset` != 0 clears
  * them.  Setting the environment variable VW_FORCE_EXACT=1 before vw_create makes every sampled row take the
  * sequential replay (a test hook; results are identical, only slower).  VW_TEST_STALL_ROW=r before vw_create makes
- * the handle's first vw_sample call withhold row r's input stage inside the kernel, with the kernel's bounded waits
- * cut to 1 ms: that call returns VW_ERR_TIMEOUT (a test hook for the timeout path; later calls are unaffected). */
+ * the handle's first vw_sample call withhold row r's input stage inside the whole-row kernel (row r must be one that
+ * kernel takes, e.g. a row with top-k off), with the kernel's bounded waits cut to 1 ms: that call returns
+ * VW_ERR_TIMEOUT (a test hook for the timeout path; later calls are unaffected). */
 vw_status vw_get_stats(vw_handle* handle, vw_stats* out, int32_t reset);
 
 /*

@@ -56,7 +56,7 @@ from tests.gpu_util import run_workload
 from voxwerk_b200 import Device, VwError, workloads
 out = {}
 with Device(0) as dev:
-    w = workloads.make(2, 512)
+    w = workloads.make(4, 512)   # top-k off: every sampling row goes through the whole-row kernel
     try:
         run_workload(dev, w)
         out["first"] = "ok"
@@ -69,10 +69,10 @@ print(json.dumps(out))
 
 
 def test_timeout_is_reported_and_the_handle_recovers():
-    """VW_TEST_STALL_ROW: the kernel's producer withholds one row's stage, so an element warp's bounded mbarrier
+    """VW_TEST_STALL_ROW: the whole-row kernel's producer withholds one row's stage, so an element warp's bounded mbarrier
     wait (cut to 1 ms by the hook) runs out.  The call returns VW_ERR_TIMEOUT; the next call on the same handle is
     bit-exact against the oracle.  No wait is unbounded, so nothing hangs."""
-    env = dict(os.environ, VW_TEST_STALL_ROW="100")
+    env = dict(os.environ, VW_TEST_STALL_ROW="101")   # a sampling row (every 10th row is greedy)
     res = subprocess.run([sys.executable, "-c", STALL_CHILD, ROOT], env=env, capture_output=True, text=True,
                          timeout=600)
     assert res.returncode == 0, res.stderr[-3000:]

@@ -93,6 +93,7 @@ class VwStats(ctypes.Structure):
         ("rows_general_replayed", ctypes.c_uint64),
         ("rows_large", ctypes.c_uint64),
         ("rows_overflow", ctypes.c_uint64),
+        ("rows_threshold_miss", ctypes.c_uint64),
         ("h2d_bytes", ctypes.c_uint64),
     ]
 

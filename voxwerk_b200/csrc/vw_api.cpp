@@ -30,7 +30,7 @@ struct vw_handle {
     char* d_scratch = nullptr;      // general-path scratch, one slice per CTA
     size_t scratch_bytes = 0;
     char* d_stage = nullptr;        // VW_MEM_HOST: device copies of the caller's arrays
-    int32_t* d_defer = nullptr;     // four counters + the rows the candidate kernel defers
+    int32_t* d_defer = nullptr;     // four counters + the rows the warp-per-row kernel defers
     size_t defer_cap = 0;
     size_t stage_bytes = 0;
     vw::DevOptions* d_opts = nullptr;
@@ -44,6 +44,37 @@ struct vw_handle {
     unsigned long long h2d_bytes = 0;        // host -> device input bytes of VW_MEM_HOST calls (vw_stats.h2d_bytes)
     std::string last_error;
 };
+
+namespace vw {
+
+void fill_row_layout(DevSegment& d) {
+    const int vsh = d.dtype == 0 ? 2 : 3, vwe = 1 << vsh;
+    const int V = d.vocab;
+    d.vsh = vsh;
+    d.va = V >> vsh;   // everything is part A unless a suppress span is skipped
+    d.c0 = d.va;
+    d.vc = 0;
+    d.eosv = -1;
+    d.spec_a = 1;
+    d.spec_b = 0;
+    if (d.kind == 0 && d.sup_lo < d.sup_hi) {
+        const int la = (d.sup_lo + vwe - 1) >> vsh << vsh;   // the span's aligned interior [la, ha) is never read
+        const int ha = d.sup_hi >> vsh << vsh;
+        if (la < ha) {
+            d.va = la >> vsh;
+            d.c0 = ha >> vsh;
+            d.vc = (V >> vsh) - d.c0;
+            if (d.eos >= la && d.eos < ha) d.eosv = d.eos >> vsh;
+        }
+        d.spec_a = d.sup_lo >> vsh;           // vectors holding suppressed ids outside the skipped interior
+        d.spec_b = (d.sup_hi - 1) >> vsh;
+    }
+    d.cpl_a = (d.va + 31) / 32;
+    d.cpl_c = (d.vc + 31) / 32;
+    d.rw_ok = d.bulk_ok && (V & (vwe - 1)) == 0 && d.cpl_a <= 32 && d.cpl_c <= 32;
+}
+
+}  // namespace vw
 
 namespace {
 
@@ -399,6 +430,7 @@ vw_status sample_impl(vw_handle* h, const vw_segment* segs, int32_t n_segs, cons
         const size_t es = s.dtype == VW_F32 ? 4 : 2;
         d.bulk_ok = aligned(s.logits, 16) && (s.row_stride * es) % 16 == 0 && (s.vocab * es) % 16 == 0;
         d.hist_aligned = d.hist_ids ? aligned(d.hist_ids, 16) : 0;
+        vw::fill_row_layout(d);
         row_begin += s.n_rows;
         vmax = std::max(vmax, s.vocab);
         const int vwe = s.dtype == VW_F32 ? 4 : 8;
@@ -461,8 +493,8 @@ vw_status sample_impl(vw_handle* h, const vw_segment* segs, int32_t n_segs, cons
     r = grow(h, &h->d_scratch, &h->scratch_bytes, static_cast<size_t>(grid_g) * p.gscratch_stride, "scratch");
     if (r != VW_OK) return r;
     p.gscratch = h->d_scratch;
-    // deferred-row list: total_rows entries after four counters (deferred rows, whole-row CTAs done, next row of
-    // the candidate kernel, candidate CTAs done), all zero between calls
+    // deferred-row list: total_rows entries after four counters (deferred rows, whole-row CTAs done, two spare),
+    // all zero between calls
     if (static_cast<size_t>(p.total_rows) + kDeferHeader > h->defer_cap) {
         cudaError_t e = cudaStreamSynchronize(st);
         if (e == cudaSuccess && h->d_defer) e = cudaFree(h->d_defer);
@@ -476,8 +508,6 @@ vw_status sample_impl(vw_handle* h, const vw_segment* segs, int32_t n_segs, cons
     }
     p.deferred_count = reinterpret_cast<uint32_t*>(h->d_defer);
     p.done_count = reinterpret_cast<uint32_t*>(h->d_defer) + 1;
-    p.row_counter = reinterpret_cast<uint32_t*>(h->d_defer) + 2;
-    p.cand_done = reinterpret_cast<uint32_t*>(h->d_defer) + 3;
     p.deferred_rows = h->d_defer + kDeferHeader;
 
     cudaError_t e = cudaSuccess;
@@ -540,8 +570,9 @@ VW_EXPORT vw_status vw_create(int32_t device, vw_handle** out) {
         e = cudaEventCreateWithFlags(&h->copy_events[i], cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaMalloc(&h->d_stats, sizeof(unsigned long long) * vw::kNumStats);
     if (e == cudaSuccess) e = cudaMemset(h->d_stats, 0, sizeof(unsigned long long) * vw::kNumStats);
-    if (e == cudaSuccess) e = cudaMalloc(&h->d_guess, sizeof(unsigned long long));
-    if (e == cudaSuccess) e = cudaMemset(h->d_guess, 0xff, sizeof(unsigned long long));   // (segment, option) -1: none
+    if (e == cudaSuccess) e = cudaMalloc(&h->d_guess, sizeof(unsigned long long) * vw::kMaxSegments);
+    if (e == cudaSuccess)   // option -1 in every slot: no carried threshold yet
+        e = cudaMemset(h->d_guess, 0xff, sizeof(unsigned long long) * vw::kMaxSegments);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     const char* fe = std::getenv("VW_FORCE_EXACT");
     h->force_exact = (fe && fe[0] == '1') ? 1 : 0;
@@ -842,6 +873,7 @@ vw_status sample_static_impl(vw_handle* h, int32_t device, const vw_segment* seg
         const size_t es = s.dtype == VW_F32 ? 4 : 2;
         d.bulk_ok = aligned(s.logits, 16) && (s.row_stride * es) % 16 == 0 && (s.vocab * es) % 16 == 0;
         d.hist_aligned = d.hist_ids ? aligned(d.hist_ids, 16) : 0;
+        vw::fill_row_layout(d);
         row_begin += s.n_rows;
         vmax = std::max(vmax, s.vocab);
         const int vwe = s.dtype == VW_F32 ? 4 : 8;
@@ -874,14 +906,12 @@ vw_status sample_static_impl(vw_handle* h, int32_t device, const vw_segment* seg
     p.err = reinterpret_cast<unsigned*>(sd.scratch);
     p.deferred_count = reinterpret_cast<uint32_t*>(sd.scratch) + 1;
     p.done_count = reinterpret_cast<uint32_t*>(sd.scratch) + 2;
-    p.row_counter = reinterpret_cast<uint32_t*>(sd.scratch) + 3;
-    p.cand_done = reinterpret_cast<uint32_t*>(sd.scratch) + 4;
     p.deferred_rows = reinterpret_cast<int32_t*>(sd.scratch + vw::kStaticRowsOffset);
     p.gscratch = sd.scratch + vw::kStaticScratchOffset;
     p.guess_seed = reinterpret_cast<unsigned long long*>(sd.scratch + vw::kStaticGuessOffset);
 
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    // the error word and the four counters must start at zero (an earlier call that timed out may have left them
+    // the error word and the counters must start at zero (an earlier call that timed out may have left them
     // set)
     cudaError_t e = cudaMemsetAsync(sd.scratch, 0, 8 * sizeof(uint32_t), st);
     if (e == cudaSuccess) e = vw::launch_sampler(p, plan, st);

@@ -29,7 +29,8 @@ enum : int {
     kStatGeneralReplayed = 4,  // whole-row rows replayed in the reference's order
     kStatLarge = 5,            // rows of more than 3072 active ids (always replayed)
     kStatOverflow = 6,         // candidate-eligible rows that took the whole-row path
-    kNumStats = 8,             // slot 7 is vw_stats.h2d_bytes, kept on the host
+    kStatThresholdMiss = 7,    // candidate rows whose carried threshold missed (rebuilt from the row)
+    kNumStats = 9,             // slot 8 is vw_stats.h2d_bytes, kept on the host
 };
 
 // Error bits latched in the device error word.
@@ -66,7 +67,18 @@ struct DevSegment {
     int32_t sup_lo, sup_hi, eos, min_new;   // talker suppress mask (clamped to [0, vocab]); lo == hi: none
     int32_t bulk_ok;      // rows are 16-byte aligned with 16-byte multiple sizes: bulk copies allowed
     int32_t hist_aligned; // hist_ids is 16-byte aligned
+    // ---- the row's active vectors (16 bytes each) for the warp-per-row kernel, in global vector indices:
+    //      part A [0, va), the EOS vector eosv (or -1) when EOS lies inside the skipped suppress span, part C
+    //      [c0, c0 + vc).  Vectors [spec_a, spec_b] of parts A and C hold suppressed ids (partial vectors at the
+    //      span's edges, or a span too short to skip); they are always examined element by element.
+    int32_t vsh;          // log2 of the ids per vector (2 fp32, 3 bf16)
+    int32_t va, c0, vc, eosv, spec_a, spec_b;
+    int32_t cpl_a, cpl_c; // vectors per lane of parts A and C (lane l takes the contiguous vectors l * cpl ...)
+    int32_t rw_ok;        // rows of this segment fit the warp-per-row kernel (aligned, <= 32 vectors per lane)
 };
+
+// Fills the warp-per-row layout fields of a segment whose other fields are set.
+void fill_row_layout(DevSegment& d);
 
 struct LaunchParams {
     DevSegment seg[kMaxSegments];
@@ -81,19 +93,18 @@ struct LaunchParams {
     int32_t flag_bytes;           // history flag map: a byte per id, vmax rounded up to 16
     int32_t vmax;
     unsigned* err;
-    int32_t* deferred_rows;       // rows the candidate kernel leaves to the whole-row kernel (total_rows entries)
+    int32_t* deferred_rows;       // rows the warp-per-row kernel leaves to the whole-row kernel (total_rows entries)
     uint32_t* deferred_count;     // their number (the whole-row kernel resets it to 0 when it is done)
     uint32_t* done_count;         // whole-row kernel CTAs finished (reset with deferred_count)
-    uint32_t* row_counter;        // next row for the candidate kernel's CTAs to take (its last CTA resets it)
-    uint32_t* cand_done;          // candidate kernel CTAs finished (reset with row_counter)
     unsigned long long* stats;    // kNumStats counters (nullable)
     int32_t force_exact;          // replay every sampled row in the reference's order (test hook)
     char* gscratch;               // large-path scratch, gscratch_stride bytes per CTA
     int64_t gscratch_stride;
-    unsigned long long* guess_seed;   // candidate threshold carried across calls: float bits << 32 | (segment,
-                                      // option) id; nullable (any value is safe: it only saves work when it fits)
+    unsigned long long* guess_seed;   // kMaxSegments candidate thresholds carried across calls, one per segment:
+                                      // float bits << 32 | option; nullable (any value is safe: it only saves work
+                                      // when it fits)
     uint64_t wait_ns;             // bound of every mbarrier wait without progress
-    int32_t test_stall_row;       // test hook: the candidate kernel's producer withholds this row's stage (-1: none)
+    int32_t test_stall_row;       // test hook: the whole-row kernel's producer withholds this row's stage (-1: none)
 };
 
 constexpr uint64_t kWaitLimitNs = 2000000000ull;   // default wait bound: 2 s without progress
@@ -105,7 +116,7 @@ size_t sampler_smem_bytes(const LaunchParams& p);
 int64_t sampler_gscratch_stride(int vmax);
 
 struct LaunchPlan {
-    int grid;              // candidate kernel CTAs (every row)
+    int grid;              // warp-per-row kernel CTAs (every row)
     int grid_general;      // whole-row kernel CTAs (the deferred rows)
     size_t smem_cand;      // dynamic shared memory of each
     size_t smem_general;
@@ -113,19 +124,20 @@ struct LaunchPlan {
 // Picks p.n_stages and both grids for `sm_count` SMs on the current device (whole-row grid <= max_grid_general).
 // False when a row does not fit in shared memory.
 bool plan_launch(LaunchParams& p, int sm_count, int max_grid_general, LaunchPlan* plan);
-// The candidate kernel over every row, then the whole-row kernel over the rows it deferred (stream-ordered).
+// The warp-per-row kernel over every row, then the whole-row kernel over the rows it deferred (stream-ordered).
 cudaError_t launch_sampler(const LaunchParams& p, const LaunchPlan& plan, cudaStream_t stream);
 
 // ---- fixed scratch of vw_sample_static: one file-scope device array per device, no allocation.
 // Layout: the error word, the two deferred-list counters and the two row-scheduling counters at offset 0 (zeroed
 // before every call), the carried
-// candidate threshold at kStaticGuessOffset, the deferred
+// candidate thresholds (one per segment) at kStaticGuessOffset, the deferred
 // rows at kStaticRowsOffset, then one kStaticCtaStride slice per whole-row CTA at kStaticScratchOffset.
 constexpr int kStaticMaxRows = 65536;       // rows per call (all segments)
 constexpr int kStaticMaxVocab = 4096;       // ids per row (a power of two >= kRegElems * kThreads)
 constexpr int kStaticGeneralCtas = 148;     // whole-row kernel CTAs (one per B200 SM)
-constexpr int64_t kStaticGuessOffset = 32;
+constexpr int64_t kStaticGuessOffset = 32;   // kMaxSegments carried thresholds
 constexpr int64_t kStaticRowsOffset = 256;
+static_assert(kStaticGuessOffset + 8 * kMaxSegments <= kStaticRowsOffset, "static scratch layout");
 constexpr int64_t kStaticScratchOffset = kStaticRowsOffset + 4 * static_cast<int64_t>(kStaticMaxRows);
 // sampler_gscratch_stride(kStaticMaxVocab): 12 bytes per id plus a 16-byte sort slot per id
 constexpr int64_t kStaticCtaStride = (static_cast<int64_t>(kStaticMaxVocab) * 28 + 255) / 256 * 256;

@@ -1,0 +1,715 @@
+// vw_rowwarp.cuh -- the warp-per-row candidate kernel.  Included by vw_sampler.cu inside its namespace; uses that
+// file's helpers (okey, softmax_num, penalize, transform, replay_candidates, ...).
+//
+// One warp per row and no block barrier: warp g of the grid takes rows g, g + G, g + 2G, ... (G = warps launched),
+// so the warps of a CTA never wait for one another.  A row is read with 16-byte vector loads straight from
+// global memory (the skipped suppress span is never read); lane l owns the contiguous vectors [l * cpl, (l+1) *
+// cpl) of each part, so lane order is index order everywhere below.  Per sampling row with 0 < K <= 64:
+//   1. history ids -> a bitmap of the ids (Distinct(), Sampler.cs:28);
+//   2. mark pass: a vector is marked when its largest raw value is >= x0, the smallest raw value whose
+//      temperature-scaled value reaches the carried threshold tau (a penalty > 1 only lowers values, so raw >= x0 is
+//      necessary for a candidate); vectors holding suppressed ids or EOS are always marked;
+//   3. the marked vectors are listed in index order and re-read (L1 / L2); each element with raw >= x0 becomes a
+//      raw candidate, and each raw candidate's exact value (penalty, mask, temperature: Sampler.cs:31,
+//      TalkerGenerator.cs:247-248, Sampler.cs:40) is kept when >= tau: the candidates, in index order;
+//   4. with K <= C <= 128 candidates the K-th largest value is >= tau, so the candidates hold every survivor of the
+//      top-k cut (Sampler.cs:42-49); a counting sort over value buckets ranks them;
+//   5. softmax numerators (libm exp, Sampler.cs:57) in 64-bit fixed point, the top-p cut over the ascending order
+//      (Sampler.cs:62-72) and the inverse-CDF draw over index order (Sampler.cs:77-87), each decision certified
+//      against the error band of the parallel sums, else the warp replays the row in the reference's order.
+// A threshold that misses (C outside [K, 128]) is rebuilt from the row's own values; rows the kernel does not take
+// (top-k off or > 64, a penalty < 1, unaligned rows, too many candidates) go to the whole-row kernel.
+
+constexpr int kRwWarps = 4;       // warps per CTA, each on its own rows
+constexpr int kRwBatch = 8;       // 16-byte vectors per lane in flight per load batch
+constexpr int kRwRawCap = 256;    // raw candidates (raw value >= x0) per row
+
+// Per-warp shared memory.
+struct __align__(16) RwArea {
+    unsigned long long key[kCandCap];   // candidates in index order: okey(t) << 32 | id
+    unsigned long long srt[kCandCap];   // the same keys in ascending (value, id) order: position = rank
+    unsigned long long fx[kCandCap];    // softmax numerators by rank, fixed point round(e * 2^52)
+    union __align__(16) {
+        struct {
+            float v[kRwRawCap];          // raw candidates (raw value, id), index order
+            int32_t id[kRwRawCap];
+        } raw;
+        struct {
+            unsigned long long tmp[kCandCap];   // bucket-sort scratch
+            double e[kCandCap];                 // softmax numerators by rank (fp64)
+        } s;
+        int32_t rflags[kCandCap];        // replay scratch
+    } u;
+    uint16_t vlist[kRwRawCap];          // marked vectors (global vector index), index order
+    int32_t bcount[kRankBuckets];
+    int32_t bstart[kRankBuckets];
+    int32_t rank[kCandCap];             // rank of the candidate at index-order position c
+};
+static_assert(sizeof(RwArea) % 16 == 0, "RwArea alignment");
+
+__device__ __forceinline__ float prev_float(float x) {   // the next float toward -inf (x finite)
+    const uint32_t u = __float_as_uint(x);
+    if ((u & 0x7fffffffu) == 0) return -__uint_as_float(1u);
+    return __uint_as_float((u & 0x80000000u) ? u + 1u : u - 1u);
+}
+
+// The smallest raw value whose scaled value fl(x * c) can reach tau, minus a margin: fl(x * c) is monotone in x, and
+// fl(tau / c) is within two ulps of the true boundary, so three steps down is a lower bound.
+__device__ __forceinline__ float raw_threshold(float tau, float c) {
+    float y = __fdiv_rn(tau, c);
+    if (!(fabsf(y) < pos_inf())) return y;   // +-inf / nan: handled by the caller (no candidates)
+    y = prev_float(prev_float(prev_float(y)));
+    return y;
+}
+
+template <int VW>
+__device__ __forceinline__ float vec_max(const uint4& u);
+template <>
+__device__ __forceinline__ float vec_max<4>(const uint4& u) {
+    return fmaxf(fmaxf(__uint_as_float(u.x), __uint_as_float(u.y)), fmaxf(__uint_as_float(u.z), __uint_as_float(u.w)));
+}
+template <>
+__device__ __forceinline__ float vec_max<8>(const uint4& u) {   // bf16 pairs: the larger of each pair, widened
+    auto mx2 = [](uint32_t a) { return fmaxf(__uint_as_float(a << 16), __uint_as_float(a & 0xffff0000u)); };
+    return fmaxf(fmaxf(mx2(u.x), mx2(u.y)), fmaxf(mx2(u.z), mx2(u.w)));
+}
+template <int VW>
+__device__ __forceinline__ float vec_elem(const uint4& u, int e) {   // element e (compile-time after unrolling)
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    if (VW == 4) return __uint_as_float(w[e]);
+    return __uint_as_float((e & 1) ? (w[e >> 1] & 0xffff0000u) : (w[e >> 1] << 16));   // Bf16.ToFloat
+}
+__device__ __forceinline__ uint4 neg_inf_vec(int VW) {
+    const uint32_t n = VW == 4 ? 0xff800000u : 0xff80ff80u;
+    return make_uint4(n, n, n, n);
+}
+
+// Mark pass over one part (global vectors [v0, v0 + nv), lane l taking [l * cpl, (l + 1) * cpl)): bit i of the
+// result is set when vector l * cpl + i holds a raw value >= x0.
+template <int VW>
+__device__ __forceinline__ uint32_t mark_part(const uint4* row, int v0, int nv, int cpl, float x0, int lane) {
+    uint32_t marks = 0u;
+    const int q0 = lane * cpl;
+    for (int b0 = 0; b0 < cpl; b0 += kRwBatch) {
+        uint4 v[kRwBatch];
+#pragma unroll
+        for (int i = 0; i < kRwBatch; ++i) {
+            const int it = b0 + i, q = q0 + it;
+            v[i] = (it < cpl && q < nv) ? __ldg(row + v0 + q) : neg_inf_vec(VW);
+        }
+        uint32_t m = 0u;
+#pragma unroll
+        for (int i = 0; i < kRwBatch; ++i)
+            if (vec_max<VW>(v[i]) >= x0) m |= 1u << i;
+        marks |= m << b0;
+    }
+    return marks;
+}
+
+// Bits of lane l's chunk [l * cpl, ...) of a part starting at global vector v0 that fall in [a, b] (global).
+__device__ __forceinline__ uint32_t chunk_bits(int v0, int nv, int cpl, int a, int b, int lane) {
+    const int lo = v0 + lane * cpl;
+    const int hi = min(lo + cpl, v0 + nv) - 1;   // inclusive
+    const int x = max(a, lo), y = min(b, hi);
+    if (x > y) return 0u;
+    const int n = y - x + 1;
+    const uint32_t ones = n >= 32 ? 0xffffffffu : ((1u << n) - 1u);
+    return ones << (x - lo);
+}
+
+// Exclusive prefix of v over the lanes; `total` = the sum over all lanes.
+__device__ __forceinline__ int warp_excl_i(int v, int lane, int& total) {
+    int incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl += y;
+    }
+    total = __shfl_sync(kFull, incl, 31);
+    return incl - v;
+}
+__device__ __forceinline__ unsigned long long warp_incl_ull(unsigned long long v, int lane) {
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long y = __shfl_up_sync(kFull, v, o);
+        if (lane >= o) v += y;
+    }
+    return v;
+}
+
+// What the warp kernel needs about one row.
+struct RwRow {
+    const uint4* row;        // the row's vectors
+    double uniform, pen_rcp;
+    float inv_t, pen;
+    int row_id, seg, opt, local;
+    int V, kind, sup_lo, sup_hi, eos;
+    bool eos_blocked, pen_on;
+};
+
+__device__ __forceinline__ bool bm_test(const uint32_t* bm, int id) { return (bm[id >> 5] >> (id & 31)) & 1u; }
+
+// The exact value of one element: repetition penalty (Sampler.cs:31) -> suppress mask (TalkerGenerator.cs:247-248)
+// -> temperature (Sampler.cs:40).
+__device__ __forceinline__ float rw_exact(float raw, int id, const uint32_t* bm, const RwRow& r) {
+    float v = raw;
+    if (r.pen_on && bm_test(bm, id)) v = penalize(v, r.pen, r.pen_rcp);
+    if (r.kind == 0 && ((id >= r.sup_lo && id < r.sup_hi && id != r.eos) || (id == r.eos && r.eos_blocked)))
+        v = neg_inf();
+    return __fmul_rn(v, r.inv_t);
+}
+// The same without temperature (greedy rows: Sampler.cs:37 takes the argmax of the penalised, masked row).
+__device__ __forceinline__ float rw_exact_greedy(float raw, int id, const uint32_t* bm, const RwRow& r) {
+    float v = raw;
+    if (r.pen_on && bm_test(bm, id)) v = penalize(v, r.pen, r.pen_rcp);
+    if (r.kind == 0 && ((id >= r.sup_lo && id < r.sup_hi && id != r.eos) || (id == r.eos && r.eos_blocked)))
+        v = neg_inf();
+    return v;
+}
+
+// History ids -> bitmap bm (cleared first; id V is the sink of out-of-range ids).  Returns true when an id was
+// outside [0, V) (the reference throws there, Sampler.cs:30).
+__device__ bool rw_history(const int32_t* hist, int len, int V, uint32_t* bm, int lane) {
+    const int words = (V >> 5) + 1;
+    for (int w = lane; w < words; w += 32) bm[w] = 0u;
+    __syncwarp();
+    bool bad = false;
+    auto put = [&](int id) {
+        const unsigned u = static_cast<unsigned>(id);
+        bad |= u >= static_cast<unsigned>(V);
+        const int k = u < static_cast<unsigned>(V) ? id : V;
+        atomicOr(&bm[k >> 5], 1u << (k & 31));
+    };
+    // ragged head up to a 16-byte boundary, then four ids per 16-byte load, then the tail
+    const int head = min(len, static_cast<int>((16u - (reinterpret_cast<uintptr_t>(hist) & 15u)) & 15u) >> 2);
+    if (lane < head) put(hist[lane]);
+    const int4* h4 = reinterpret_cast<const int4*>(hist + head);
+    const int n4 = (len - head) >> 2;
+    for (int j0 = 0; j0 < n4; j0 += 4 * 32) {
+        int4 w[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int j = j0 + k * 32 + lane;
+            w[k] = j < n4 ? __ldg(h4 + j) : make_int4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            if (j0 + k * 32 + lane >= n4) continue;
+            put(w[k].x);
+            put(w[k].y);
+            put(w[k].z);
+            put(w[k].w);
+        }
+    }
+    const int t0 = head + 4 * n4;
+    if (lane < len - t0) put(hist[t0 + lane]);
+    __syncwarp();
+    return __any_sync(kFull, bad);
+}
+
+// Steps 2-3 for one threshold: candidates (index order) into a.key, their number in C, the largest value in mx.
+// Returns false when the list overflows (too many marked vectors or raw candidates: the threshold is too low).
+template <int VW>
+__device__ bool rw_collect(const RwRow& r, const DevSegment& sg, float tau, float x0, const uint32_t* bm,
+                           RwArea& a, int lane, int& C, float& mx) {
+    constexpr int vsh = VW == 4 ? 2 : 3;
+    // marks, with the vectors holding suppressed ids (and EOS while it is blocked) always marked
+    uint32_t mA = mark_part<VW>(r.row, 0, sg.va, sg.cpl_a, x0, lane);
+    uint32_t mC = sg.vc > 0 ? mark_part<VW>(r.row, sg.c0, sg.vc, sg.cpl_c, x0, lane) : 0u;
+    mA |= chunk_bits(0, sg.va, sg.cpl_a, sg.spec_a, sg.spec_b, lane);
+    if (sg.vc > 0) mC |= chunk_bits(sg.c0, sg.vc, sg.cpl_c, sg.spec_a, sg.spec_b, lane);
+    const int ev = (r.kind == 0 && r.eos_blocked && r.eos >= 0 && r.eos < r.V) ? (r.eos >> vsh) : -1;
+    if (ev >= 0) {
+        mA |= chunk_bits(0, sg.va, sg.cpl_a, ev, ev, lane);
+        if (sg.vc > 0) mC |= chunk_bits(sg.c0, sg.vc, sg.cpl_c, ev, ev, lane);
+    }
+    // list in index order: part A, the EOS vector, part C
+    int tA, tC;
+    const int oA = warp_excl_i(__popc(mA), lane, tA);
+    const int oC = warp_excl_i(__popc(mC), lane, tC);
+    const int ne = sg.eosv >= 0 ? 1 : 0;
+    const int M = tA + ne + tC;
+    if (M > kRwRawCap) return false;
+    {
+        int o = oA;
+        for (uint32_t m = mA; m; m &= m - 1u) a.vlist[o++] = static_cast<uint16_t>(lane * sg.cpl_a + __ffs(m) - 1);
+        if (ne && lane == 0) a.vlist[tA] = static_cast<uint16_t>(sg.eosv);
+        o = tA + ne + oC;
+        for (uint32_t m = mC; m; m &= m - 1u)
+            a.vlist[o++] = static_cast<uint16_t>(sg.c0 + lane * sg.cpl_c + __ffs(m) - 1);
+    }
+    __syncwarp();
+    // raw candidates: elements >= x0 of the listed vectors (every element of a vector with suppressed ids)
+    int R = 0;
+    for (int e0 = 0; e0 < M; e0 += 32) {
+        const int e = e0 + lane;
+        uint32_t bits = 0u;
+        uint4 u = neg_inf_vec(VW);
+        int gv = 0;
+        if (e < M) {
+            gv = a.vlist[e];
+            u = __ldg(r.row + gv);
+            const bool spec = (gv >= sg.spec_a && gv <= sg.spec_b) || gv == ev;
+#pragma unroll
+            for (int k = 0; k < VW; ++k)
+                if (spec || vec_elem<VW>(u, k) >= x0) bits |= 1u << k;
+        }
+        int tot;
+        int o = R + warp_excl_i(__popc(bits), lane, tot);
+        if (R + tot > kRwRawCap) return false;
+#pragma unroll
+        for (int k = 0; k < VW; ++k) {
+            if ((bits >> k) & 1u) {
+                a.u.raw.v[o] = vec_elem<VW>(u, k);
+                a.u.raw.id[o] = (gv << vsh) + k;
+                ++o;
+            }
+        }
+        R += tot;
+    }
+    __syncwarp();
+    // exact values; the candidates are those >= tau
+    int c = 0;
+    float m = neg_inf();
+    for (int e0 = 0; e0 < R; e0 += 32) {
+        const int e = e0 + lane;
+        float t = neg_inf();
+        int id = 0;
+        if (e < R) {
+            id = a.u.raw.id[e];
+            t = rw_exact(a.u.raw.v[e], id, bm, r);
+        }
+        const bool keep = e < R && t >= tau;
+        const unsigned bal = __ballot_sync(kFull, keep);
+        const int pos = c + __popc(bal & ((1u << lane) - 1u));
+        if (keep) {
+            m = fmaxf(m, t);
+            if (pos < kCandCap) a.key[pos] = (static_cast<unsigned long long>(okey(t)) << 32) | static_cast<uint32_t>(id);
+        }
+        c += __popc(bal);
+    }
+    __syncwarp();
+    C = c;
+    mx = warp_max_f(m);
+    return true;
+}
+
+// Step 4: ranks of the C candidates (a.key, index order): a.srt[rank] = key, a.rank[c] = rank.  Counting sort over
+// 64 value buckets linear in [tau, mx] (non-decreasing in the value, so the buckets keep the key order), then a
+// count within the bucket.  Slot s of lane l holds position c = 32 s + l.
+__device__ void rw_rank(RwArea& a, int C, float tau, float mx, int lane) {
+    for (int b = lane; b < kRankBuckets; b += 32) a.bcount[b] = 0;
+    __syncwarp();
+    const float span = __fsub_rn(mx, tau);
+    const float scale = span > 0.0f ? __fdiv_rn(static_cast<float>(kRankBuckets), span) : 0.0f;
+    unsigned long long kk[4];
+    int bk[4], arr[4];
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+        const int c = 32 * s + lane;
+        kk[s] = 0;
+        bk[s] = 0;
+        arr[s] = 0;
+        if (c < C) {
+            kk[s] = a.key[c];
+            const float x = okey_inv(static_cast<uint32_t>(kk[s] >> 32));
+            bk[s] = min(max(static_cast<int>(__fmul_rn(__fsub_rn(x, tau), scale)), 0), kRankBuckets - 1);
+            arr[s] = atomicAdd(&a.bcount[bk[s]], 1);
+        }
+    }
+    __syncwarp();
+    {   // exclusive prefix of the 64 bucket counts (lane l: buckets 2l, 2l + 1)
+        const int c0 = a.bcount[2 * lane], c1 = a.bcount[2 * lane + 1];
+        int tot;
+        const int ex = warp_excl_i(c0 + c1, lane, tot);
+        a.bstart[2 * lane] = ex;
+        a.bstart[2 * lane + 1] = ex + c0;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int s = 0; s < 4; ++s)
+        if (32 * s + lane < C) a.u.s.tmp[a.bstart[bk[s]] + arr[s]] = kk[s];
+    __syncwarp();
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+        const int c = 32 * s + lane;
+        if (c < C) {
+            const int b0 = a.bstart[bk[s]], bn = a.bcount[bk[s]];
+            int lt = b0;
+            for (int j = b0; j < b0 + bn; ++j) lt += a.u.s.tmp[j] < kk[s] ? 1 : 0;
+            a.srt[lt] = kk[s];
+            a.rank[c] = lt;
+        }
+    }
+    __syncwarp();
+}
+
+// Step 5 on the ranked candidates: the id, or -1 when a decision lies inside the error band (the caller replays).
+// Follows the candidate logic of Sampler.cs:42-87: kth = the K-th largest value (ties kept), softmax numerators of
+// the survivors, the top-p cut over the ascending (probability, index) order with the last element never removed,
+// and the draw over the kept ids in index order.  Sums are exact 64-bit sums of round(e * 2^52); eta bounds their
+// difference from the reference's sequential fp64 sums.
+__device__ int rw_decide(RwArea& a, int C, int K, float top_p, double r, float mx, int V, double* out_probs,
+                         int lane) {
+    const uint32_t kth = static_cast<uint32_t>(a.srt[C - K] >> 32);   // Sampler.cs:45-47
+    // survivors are the ranks [first, C): the ranks whose value is >= kth (Sampler.cs:48)
+    int first = C;
+#pragma unroll
+    for (int s = 3; s >= 0; --s) {
+        const int q = 32 * s + lane;
+        const bool sv = q < C && static_cast<uint32_t>(a.srt[q] >> 32) >= kth;
+        const unsigned b = __ballot_sync(kFull, sv);
+        if (b) first = 32 * s + __ffs(b) - 1;
+    }
+    const int S = C - first;
+    // numerators by rank, and the inclusive prefix of the survivor masses in rank order
+    unsigned long long f[4], inc[4];
+    unsigned long long carry = 0;
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+        const int q = 32 * s + lane;
+        f[s] = 0;
+        if (q >= first && q < C) {
+            const double e = softmax_num(okey_inv(static_cast<uint32_t>(a.srt[q] >> 32)), mx);   // Sampler.cs:57
+            f[s] = __double2ull_rn(__dmul_rn(e, kFix52));
+            a.u.s.e[q] = e;
+        }
+        if (32 * s < C) {
+            const unsigned long long x = warp_incl_ull(f[s], lane);
+            inc[s] = carry + x;
+            carry += __shfl_sync(kFull, x, 31);
+        } else {
+            inc[s] = carry;
+        }
+        if (q < C) a.fx[q] = f[s];
+    }
+    const unsigned long long tot = carry;
+    const double eta = (6.0 * S + 128.0) * kU;
+    __syncwarp();
+    int cut = first;
+    unsigned long long pre_cut = 0;
+    if (top_p < 1.0f) {
+        // the element whose cumulative mass first exceeds (1 - TopP) of the total breaks the loop (Sampler.cs:67-72)
+        const double tot_d = static_cast<double>(tot);
+        const double thr = static_cast<double>(__fsub_rn(1.0f, top_p));
+        const double T = __dmul_rn(thr, tot_d);
+        const double band = __dmul_rn(eta, tot_d);
+        int found = -1;
+        bool amb = false;
+        unsigned long long pc = 0;
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+            const int q = 32 * s + lane;
+            if (q < first || q >= C) continue;
+            const double bd = static_cast<double>(inc[s] - f[s]);   // cum before this element
+            const double id = static_cast<double>(inc[s]);          // cum including it
+            const int pos = q - first;
+            const bool brk = pos <= S - 2 && !(bd > T) && id > T;
+            const bool last = pos == S - 1 && !(bd > T);
+            if (brk || last) {
+                found = q;
+                pc = inc[s] - f[s];
+                if (brk && !(__dsub_rn(id, T) > band)) amb = true;
+                if (bd > 0.0 && !(__dsub_rn(T, bd) > band)) amb = true;
+                // the value groups next to the cut must be strictly apart in probability (the reference orders by
+                // probability, then index)
+                const uint32_t vt = static_cast<uint32_t>(a.srt[q] >> 32);
+                const double et = a.u.s.e[q];
+                int qlo = q - 1;
+                while (qlo >= first && static_cast<uint32_t>(a.srt[qlo] >> 32) == vt) --qlo;
+                if (qlo >= first && !(a.u.s.e[qlo] < et * (1.0 - 32.0 * kU))) amb = true;
+                if (brk && qlo < q - 1) {   // the cut falls inside this value group: the group above matters too
+                    int qhi = q + 1;
+                    while (qhi < C && static_cast<uint32_t>(a.srt[qhi] >> 32) == vt) ++qhi;
+                    if (qhi < C && !(a.u.s.e[qhi] > et * (1.0 + 32.0 * kU))) amb = true;
+                }
+            }
+        }
+        const unsigned who = __ballot_sync(kFull, found >= 0);
+        if (__popc(who) != 1 || __any_sync(kFull, amb)) return -1;
+        const int src = __ffs(who) - 1;
+        cut = __shfl_sync(kFull, found, src);
+        pre_cut = __shfl_sync(kFull, pc, src);
+    }
+    const unsigned long long B = tot - pre_cut;   // mass of the kept candidates (Sampler.cs:73)
+    // inverse-CDF draw over the kept ids in index order (Sampler.cs:77-87): position c of a.key is index order
+    const double Bd = static_cast<double>(B);
+    const double rB = __dmul_rn(r, Bd);
+    const double bandB = __dmul_rn(eta, Bd);
+    int hit = -1, hits = 0;
+    bool amb = false;
+    unsigned long long run = 0;
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+        if (32 * s >= C) break;
+        const int c = 32 * s + lane;
+        unsigned long long fc = 0;
+        int rk = -1;
+        if (c < C) {
+            rk = a.rank[c];
+            if (rk >= cut) fc = a.fx[rk];
+        }
+        const unsigned long long x = warp_incl_ull(fc, lane);
+        const unsigned long long hi = run + x, lo = hi - fc;
+        const double lod = static_cast<double>(lo), hid = static_cast<double>(hi);
+        if (fc > 0 && !(lod > rB) && hid > rB) {
+            ++hits;
+            hit = static_cast<int>(static_cast<uint32_t>(a.srt[rk]));
+            if (!(__dsub_rn(hid, rB) > bandB)) amb = true;
+            if (lo > 0 && !(__dsub_rn(rB, lod) > bandB)) amb = true;
+        }
+        run += __shfl_sync(kFull, x, 31);
+    }
+    hits = warp_sum_i(hits);
+    if (hits != 1 || __any_sync(kFull, amb)) return -1;
+    const int res = warp_max_i(hit);
+    if (out_probs) {
+        for (int i = lane; i < V; i += 32) out_probs[i] = 0.0;
+        __syncwarp();
+        const double scale = __dmul_rn(Bd, 1.0 / kFix52);
+        for (int q = cut + lane; q < C; q += 32)
+            out_probs[static_cast<uint32_t>(a.srt[q])] = __ddiv_rn(a.u.s.e[q], scale);
+    }
+    return res;
+}
+
+// Calls f(raw, id) for every active element of the row: parts A and C (lane l: its contiguous vectors) and the EOS
+// vector (lane 0).  Used by greedy rows and by the threshold rebuild, which need every element's exact value.
+template <int VW, class F>
+__device__ __forceinline__ void rw_for_each(const RwRow& r, const DevSegment& sg, int lane, F f) {
+    constexpr int vsh = VW == 4 ? 2 : 3;
+#pragma unroll 1
+    for (int part = 0; part < 2; ++part) {
+        const int v0 = part == 0 ? 0 : sg.c0, nv = part == 0 ? sg.va : sg.vc, cpl = part == 0 ? sg.cpl_a : sg.cpl_c;
+        const int q0 = lane * cpl;
+        for (int b0 = 0; b0 < cpl; b0 += kRwBatch) {
+            uint4 v[kRwBatch];
+#pragma unroll
+            for (int i = 0; i < kRwBatch; ++i) {
+                const int it = b0 + i, q = q0 + it;
+                v[i] = (it < cpl && q < nv) ? __ldg(r.row + v0 + q) : neg_inf_vec(VW);
+            }
+#pragma unroll
+            for (int i = 0; i < kRwBatch; ++i) {
+                const int q = q0 + b0 + i;
+                if (b0 + i < cpl && q < nv) {
+#pragma unroll
+                    for (int k = 0; k < VW; ++k) f(vec_elem<VW>(v[i], k), ((v0 + q) << vsh) + k);
+                }
+            }
+        }
+    }
+    if (sg.eosv >= 0 && lane == 0) {
+        const uint4 u = __ldg(r.row + sg.eosv);
+#pragma unroll
+        for (int k = 0; k < VW; ++k) f(vec_elem<VW>(u, k), (sg.eosv << vsh) + k);
+    }
+}
+
+// A threshold tau with at least K exact values >= tau: the K-th largest of the 64 values formed by each lane's two
+// largest (a subset of the row, so its K-th largest is <= the row's).  -inf when the row has fewer than K finite
+// values among them.
+template <int VW>
+__device__ float rw_row_threshold(const RwRow& r, const DevSegment& sg, const uint32_t* bm, int K, int lane) {
+    float t1 = neg_inf(), t2 = neg_inf();
+    rw_for_each<VW>(r, sg, lane, [&](float raw, int id) {
+        const float t = rw_exact(raw, id, bm, r);
+        t2 = fmaxf(t2, fminf(t1, t));
+        t1 = fmaxf(t1, t);
+    });
+    uint32_t lk[2] = {~okey(t1), ~okey(t2)};   // ascending ~key = descending value
+    warp_sort32<2>(lk, lane);
+    const uint32_t kk = __shfl_sync(kFull, (K - 1) < 32 ? lk[0] : lk[1], (K - 1) & 31);
+    return okey_inv(~kk);
+}
+
+// Greedy rows: first index of the maximum of the penalised, masked values (Sampler.cs:90-95); 0 when all are -inf.
+template <int VW>
+__device__ int rw_argmax(const RwRow& r, const DevSegment& sg, const uint32_t* bm, int lane) {
+    float bv = neg_inf();
+    int bi = 0x7fffffff;
+    rw_for_each<VW>(r, sg, lane, [&](float raw, int id) {
+        const float t = rw_exact_greedy(raw, id, bm, r);
+        if (t > bv || (t == bv && id < bi)) {
+            bv = t;
+            bi = id;
+        }
+    });
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const float ov = __shfl_xor_sync(kFull, bv, off);
+        const int oi = __shfl_xor_sync(kFull, bi, off);
+        if (ov > bv || (ov == bv && oi < bi)) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    return is_neg_inf(bv) ? 0 : bi;
+}
+
+// One sampling row with 0 < K <= 64 on candidates: the id, or -2 when the row goes to the whole-row kernel.
+// `carry` (per lane: segment `lane`'s threshold bits << 32 | option) is read and updated.
+template <int VW>
+__device__ int rw_sample_row(const LaunchParams& p, const RwRow& r, const DevSegment& sg, const DevOptions& o,
+                             RwArea& a, const uint32_t* bm, unsigned long long& carry, double* out_probs, int lane,
+                             uint32_t& st_fast, uint32_t& st_exact, uint32_t& st_miss) {
+    const int K = o.top_k;
+    const unsigned long long cs = __shfl_sync(kFull, carry, r.seg);
+    int C = 0;
+    float mx = neg_inf(), tau = neg_inf();
+    bool ok = false;
+    if (static_cast<uint32_t>(cs) == static_cast<uint32_t>(r.opt)) {
+        tau = __uint_as_float(static_cast<uint32_t>(cs >> 32));
+        const float x0 = raw_threshold(tau, r.inv_t);
+        if (fabsf(x0) < pos_inf())
+            ok = rw_collect<VW>(r, sg, tau, x0, bm, a, lane, C, mx) && C >= K && C <= kCandCap;
+    }
+    if (!ok) {   // no usable carried threshold: rebuild it from this row
+        ++st_miss;
+        tau = rw_row_threshold<VW>(r, sg, bm, K, lane);
+        if (is_neg_inf(tau)) return -2;   // fewer than K finite values in reach: the whole-row kernel decides
+        const float x0 = raw_threshold(tau, r.inv_t);
+        if (!(fabsf(x0) < pos_inf())) return -2;
+        ok = rw_collect<VW>(r, sg, tau, x0, bm, a, lane, C, mx) && C >= K && C <= kCandCap;
+        if (!ok) return -2;   // more than 128 candidates (flat rows, ties): the whole-row kernel decides
+    }
+    rw_rank(a, C, tau, mx, lane);
+    int res = p.force_exact ? -1 : rw_decide(a, C, K, o.top_p, r.uniform, mx, r.V, out_probs, lane);
+    if (res >= 0) {
+        ++st_fast;
+    } else {   // a decision inside the error band: the reference's sequential order on the candidates
+        res = replay_candidates(a.key, C, K, o, r.uniform, r.V, out_probs, a.u.rflags, lane);
+        ++st_exact;
+    }
+    // carry to the next row of this segment: the candidate ranked 1.5 K + 4 from the top, so that a similar row
+    // collects about that many; with fewer candidates, the lowest one moved down by the missing count times the
+    // mean gap of the lowest candidates
+    if (!p.force_exact) {
+        const int target = K + (K >> 1) + 4;
+        float gt;
+        if (C >= target) {
+            gt = okey_inv(static_cast<uint32_t>(a.srt[C - target] >> 32));
+        } else {
+            const int j = min(C - 1, 16);
+            const float lo = okey_inv(static_cast<uint32_t>(a.srt[0] >> 32));
+            const float hi = okey_inv(static_cast<uint32_t>(a.srt[j] >> 32));
+            gt = j > 0 ? lo - (hi - lo) * (static_cast<float>(target - C) / static_cast<float>(j)) : lo;
+        }
+        if (lane == r.seg && !is_neg_inf(gt) && !isnan(gt))
+            carry = (static_cast<unsigned long long>(__float_as_uint(gt)) << 32) | static_cast<uint32_t>(r.opt);
+    }
+    return res;
+}
+
+// Shared memory of one warp: its RwArea, then its history bitmap ((vmax >> 5) + 1 words, padded to 16 bytes).
+__host__ __device__ __forceinline__ int rw_bitmap_words(int vmax) { return (((vmax >> 5) + 1) + 3) & ~3; }
+__host__ __device__ __forceinline__ size_t rw_warp_bytes(int vmax) {
+    return sizeof(RwArea) + static_cast<size_t>(rw_bitmap_words(vmax)) * 4;
+}
+
+__global__ void __launch_bounds__(kRwWarps * 32, 6) row_warp_kernel(const __grid_constant__ LaunchParams p) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int lane = threadIdx.x & 31;
+    const int wib = threadIdx.x >> 5;
+    unsigned char* mine = smem + static_cast<size_t>(wib) * rw_warp_bytes(p.vmax);
+    RwArea& a = *reinterpret_cast<RwArea*>(mine);
+    uint32_t* bm = reinterpret_cast<uint32_t*>(mine + sizeof(RwArea));
+    // the whole-row kernel may be scheduled now; it waits (griddepcontrol.wait) until this grid has finished
+    if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+    const int G = gridDim.x * kRwWarps;
+    // carried thresholds: lane s holds segment s's (threshold bits << 32 | option); ~0: none
+    unsigned long long carry = ~0ull;
+    if (p.guess_seed && lane < p.n_segs) carry = *reinterpret_cast<volatile unsigned long long*>(p.guess_seed + lane);
+    const unsigned long long carry0 = carry;
+    uint32_t st_greedy = 0, st_fast = 0, st_exact = 0, st_overflow = 0, st_miss = 0;
+
+    for (int row = blockIdx.x * kRwWarps + wib; row < p.total_rows; row += G) {
+        int s = 0;
+        for (int i = 1; i < p.n_segs; ++i)
+            if (row >= p.seg[i].row_begin) s = i;
+        const DevSegment& sg = p.seg[s];
+        const int local = row - sg.row_begin;
+        const bool talker_hist = sg.kind == 0 && sg.hist_offsets;
+        // the row's own words, one lane each
+        long long w = 0;
+        if (lane == 0) w = sg.opt_index ? sg.opt_index[local] : 0;
+        if (lane == 1) w = (sg.kind == 0 && sg.steps) ? sg.steps[local] : 0x7fffffff;
+        if (lane == 2) w = sg.uniforms ? __double_as_longlong(sg.uniforms[local]) : 0;
+        if (lane == 3 && talker_hist) w = sg.hist_offsets[local];
+        if (lane == 4 && talker_hist) w = sg.hist_offsets[local + 1];
+        const int opt = static_cast<int>(__shfl_sync(kFull, w, 0));
+        const int step = static_cast<int>(__shfl_sync(kFull, w, 1));
+        const double uniform = __longlong_as_double(__shfl_sync(kFull, w, 2));
+        long long hb = __shfl_sync(kFull, w, 3), he = __shfl_sync(kFull, w, 4);
+        if (hb < 0 || he < hb) {   // device-memory offsets are checked here: report, and read no history
+            if (lane == 0) atomicOr(p.err, kErrHistOffsets);
+            hb = he = 0;
+        }
+        int32_t* out_id = sg.out_ids + local;
+        if (opt < 0 || opt >= p.n_opts) {
+            if (lane == 0) {
+                atomicOr(p.err, kErrBadOption);
+                *out_id = -1;
+            }
+            continue;
+        }
+        const DevOptions o = p.n_opts <= kInlineOptions ? p.inl_opts[opt] : p.dev_opts[opt];
+        const int V = sg.vocab;
+        const bool pen_on = sg.kind == 0 && o.rep_penalty != 1.0f && he > hb;
+        const bool sample = o.do_sample != 0;
+        const bool defer = !sg.rw_ok || (sample && !(o.top_k > 0 && o.top_k < V && o.top_k <= kSmallK)) ||
+                           (pen_on && !(o.rep_penalty >= 1.0f));
+        if (defer) {
+            if (lane == 0) p.deferred_rows[atomicAdd(p.deferred_count, 1u)] = row;
+            continue;
+        }
+        RwRow r;
+        r.row = reinterpret_cast<const uint4*>(static_cast<const unsigned char*>(sg.logits) +
+                                              static_cast<int64_t>(local) * sg.row_stride * (sg.dtype == 0 ? 4 : 2));
+        r.uniform = uniform;
+        r.pen = o.rep_penalty;
+        r.pen_rcp = pen_on ? __drcp_rn(static_cast<double>(o.rep_penalty)) : 1.0;
+        r.inv_t = sample ? __fdiv_rn(1.0f, o.temperature) : 1.0f;
+        r.row_id = row;
+        r.seg = s;
+        r.opt = opt;
+        r.local = local;
+        r.V = V;
+        r.kind = sg.kind;
+        r.sup_lo = sg.sup_lo;
+        r.sup_hi = sg.sup_hi;
+        r.eos = sg.eos;
+        r.eos_blocked = sg.kind == 0 && step < sg.min_new;
+        r.pen_on = pen_on;
+        double* out_probs = sg.out_probs ? sg.out_probs + static_cast<int64_t>(local) * V : nullptr;
+        if (pen_on && rw_history(sg.hist_ids + hb, static_cast<int>(he - hb), V, bm, lane) && lane == 0)
+            atomicOr(p.err, kErrHistRange);
+
+        int res;
+        if (!sample) {
+            res = sg.dtype == 0 ? rw_argmax<4>(r, sg, bm, lane) : rw_argmax<8>(r, sg, bm, lane);
+            if (out_probs)
+                for (int i = lane; i < V; i += 32) out_probs[i] = 0.0;
+            ++st_greedy;
+        } else {
+            res = sg.dtype == 0 ? rw_sample_row<4>(p, r, sg, o, a, bm, carry, out_probs, lane, st_fast, st_exact, st_miss)
+                                : rw_sample_row<8>(p, r, sg, o, a, bm, carry, out_probs, lane, st_fast, st_exact, st_miss);
+        }
+        if (res == -2) {   // the whole-row kernel takes the row
+            ++st_overflow;
+            if (lane == 0) p.deferred_rows[atomicAdd(p.deferred_count, 1u)] = row;
+        } else if (lane == 0) {
+            *out_id = res;
+        }
+        __syncwarp();   // the warp's shared area is reused by its next row
+    }
+    if (p.guess_seed && lane < p.n_segs && carry != carry0) p.guess_seed[lane] = carry;   // seeds the next launch
+    if (p.stats && lane == 0) {
+        const uint32_t v[4] = {st_greedy, st_fast, st_exact, st_overflow};
+        const int idx[4] = {kStatGreedy, kStatFast, kStatFastReplayed, kStatOverflow};
+        for (int i = 0; i < 4; ++i)
+            if (v[i]) atomicAdd(&p.stats[idx[i]], static_cast<unsigned long long>(v[i]));
+        if (st_miss) atomicAdd(&p.stats[kStatThresholdMiss], static_cast<unsigned long long>(st_miss));
+    }
+}

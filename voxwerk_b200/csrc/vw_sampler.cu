@@ -1,38 +1,37 @@
 // vw_sampler.cu -- fused token-sampling kernels for sm_100a (B200).
 //
-// Two persistent kernels per call, stream-ordered, both CTAs of five warps:
-//   * a producer warp plans each of the CTA's rows and streams their logits and histories into a shared-memory
-//     ring with cp.async.bulk (TMA bulk copies) completing on mbarriers, so HBM reads run ahead of the work.  The
-//     suppressed span of talker rows is never read.
-//   * four element warps (one warp-group per row) do the rest of the row.
-// cand_kernel takes every row (CTA b: rows b, b + grid, ...).  It finishes greedy rows and sampling rows with
-// top-k <= 64, keeping the row in its stage, and appends every other row to a deferred list.  whole_row_kernel
-// takes the deferred rows, with each row held in registers.
+// Two kernels per call, stream-ordered:
+//   * row_warp_kernel (vw_rowwarp.cuh): one warp per row, every row of the call.  It finishes greedy rows and
+//     sampling rows with 0 < top-k <= 64 from a candidate set, reading each row once with 16-byte loads, and
+//     appends every other row to a deferred list.
+//   * whole_row_kernel: the deferred rows (top-k off or > 64, a penalty < 1, unaligned rows, candidate overflow),
+//     CTAs of five warps: a producer warp streams each row's logits and history into a shared-memory ring with
+//     cp.async.bulk (TMA bulk copies) completing on mbarriers, and four element warps hold the row in registers.
+//     The suppressed span of talker rows is never read by either kernel.
 //
 // Per row, in the order of the reference (src/Voxwerk/Talker/Sampler.cs, TalkerGenerator.cs):
 //   1. repetition penalty (talker rows; Sampler.cs:25-33): history ids -> a flag byte per id (Distinct());
 //      each element whose bit is set becomes s < 0 ? s * p : s / p in fp32.  The IEEE quotient s / p is formed
 //      as fp32(fp64(s) * RN64(1/p)): the fp64 product is within 2^-52 relative of s/p while no fp32 rounding
 //      midpoint lies closer than 2^-49 relative to a quotient of two fp32 values, so both round the same way.
-//      The candidate kernel applies a penalty > 1 to the candidates only (it only lowers values, so the
-//      unpenalized value decides first whether an element can be a candidate at all).
+//      The warp kernel applies a penalty > 1 to the candidates only (it only lowers values, so the unpenalized
+//      value decides first whether an element can be a candidate at all).
 //   2. suppress mask (talker rows; TalkerGenerator.cs:247-248): ids [lo, hi) except EOS, and EOS while
 //      t < min_new_tokens, become -inf.
 //   3. greedy rows: first index of the maximum (Sampler.cs:90-95).
 //   4. temperature: x * fp32(1/T) (Sampler.cs:39-40).
 //   5. top-k (Sampler.cs:42-49): every value >= the K-th largest survives (ties kept).  For K <= 64 the
 //      candidates are the values >= tau for a threshold tau with K <= count <= 128, so the K-th largest is
-//      >= tau: tau is carried from the CTA's previous row of the same options (and from call to call), or else
-//      the min over the 4 warps of the ceil(K/4)-th largest of each warp's per-thread top-2 values.  Each
-//      candidate's exact rank is counted by its own thread.  Otherwise a binned select over the row finds the
-//      K-th largest.
+//      >= tau: tau is carried from the warp's previous row of the same segment and options (and from call to
+//      call), or else rebuilt from the row (the K-th largest of the lanes' top-2 values).  Otherwise a binned
+//      select over the row finds the K-th largest.
 //   6. softmax in fp64, top-p cut over the (prob, index)-ascending order and the inverse-CDF draw
 //      (Sampler.cs:51-88).  The reference's sums are sequential fp64 roundings.  Here they are formed in
 //      parallel; every decision they feed (which ids top-p removes, where the draw lands) is taken only when the
 //      parallel value is farther from the threshold than a proven bound on the difference between the two
 //      (eta = (6n + 128) 2^-53 of the total for n survivors on the candidate path, (8n + 128) 2^-53 where
-//      fixed-point histograms are involved, covering both exp implementations' 1-ulp error, the reference's
-//      n-term sequential roundings and this code's own roundings).  A row with any decision inside that band is
+//      fixed-point histograms are involved, covering the reference's n-term sequential roundings and this
+//      code's own roundings, with room for a 1-ulp exp difference although the device exp is the host libm's).  A row with any decision inside that band is
 //      replayed in the reference's exact sequential order (replay paths below), so the ids equal the
 //      reference's in every case.
 //
@@ -73,7 +72,6 @@ struct __align__(16) RowMeta {
     int32_t direct;               // logits were not bulk-copied: the element warps load them
     int32_t pen_on;               // repetition penalty active
     int32_t opt_ok;               // option index valid
-    int32_t deferred;             // candidate kernel: the row goes to the whole-row kernel (nothing staged)
     int32_t V, dtype, kind;
     int32_t sup_lo, sup_hi, eos, eos_blocked;
     int32_t slow_vlo, slow_vhi, eos_vec;   // staged vectors that need the per-element mask rules
@@ -470,7 +468,6 @@ struct RowCtx {
     const uint8_t* flags;     // flags[id] = 1: id is in the history (Distinct()); penalised when pen_on
     int slow_vlo, slow_vhi;   // staged vectors that may hold suppressed ids
     int eos_vec;              // staged vector holding a suppressed EOS, or -1
-    bool pen_lazy;            // candidate kernel: penalty > 1, applied to the candidates only
 };
 
 // Staged position -> vocabulary id: [0, lo_al) | kvw ids from kbase | [hi_al, V)
@@ -1043,7 +1040,7 @@ constexpr double kFix52 = 4503599627370496.0;   // 2^52: candidate masses in fix
 // ---------------------------------------------------------------- candidate replay (warp 0)
 // The reference's sequential operations on the candidates (<= 128 survivors), every lane of one warp running the
 // same chain on shuffled values.
-__device__ int replay_candidates(const unsigned long long* ck, int C, int K, const DevOptions& o, double uniform,
+__device__ __noinline__ int replay_candidates(const unsigned long long* ck, int C, int K, const DevOptions& o, double uniform,
                                  int V, double* out_probs, int* flags, int lane) {
     uint64_t key[4];   // descending value, ascending index
 #pragma unroll
@@ -1242,14 +1239,12 @@ __device__ int block_argmax(float bestv, int besti, SmemMisc& m, int lane, int w
     return is_neg_inf(bv) ? 0 : bi;   // all -inf: the reference's scan never moves off index 0
 }
 
-// ---------------------------------------------------------------- producer warp
-// Plans the CTA's rows (CTA b takes rows first, first + gstride, ...; in the whole-row kernel, entries of the
-// deferred list) and streams each row's staged logits and history into the stage ring with bulk copies that
-// complete on full_bar.  The row's RowMeta goes into metas[k % (2 * S)].  In the candidate kernel, rows that kernel
-// does not take (sampling without a top-k <= 64, or more than 3072 staged ids) are marked deferred and copy nothing.
+// ---------------------------------------------------------------- producer warp (whole-row kernel)
+// Plans the CTA's rows (CTA b takes entries b, b + gstride, ... of the deferred list) and streams each row's staged
+// logits and history into the stage ring with bulk copies that complete on full_bar.  The row's RowMeta goes into
+// metas[k % (2 * S)].
 // The RowMeta of row r: where its data is, what to stage and how the element warps treat it.  `bytes` = the
 // bytes its bulk copies bring into the stage (0 for a row that copies nothing), `esize` the logit size.
-template <bool kGeneral>
 __device__ RowMeta plan_row(const LaunchParams& p, int r, uint32_t& bytes, int& esize) {
     RowMeta m;
     bytes = 0;
@@ -1339,17 +1334,7 @@ __device__ RowMeta plan_row(const LaunchParams& p, int r, uint32_t& bytes, int& 
     }
     m.row_ptr = static_cast<const unsigned char*>(sg.logits) +
                 static_cast<int64_t>(local) * sg.row_stride * esize;
-    m.deferred = 0;
-    if (!kGeneral && m.opt_ok) {
-        // rows the candidate kernel does not take: more than 3072 staged ids, or sampling without a
-        // top-k <= 64
-        const int na = m.lo_al + m.kvw + V - m.hi_al;
-        const bool big = na > kThreads * kRegElems;   // kThreads * kRegElems is a multiple of every VWe
-        const int K = m.opt.top_k;
-        const bool cand = !m.opt.do_sample || (K > 0 && K < V && K <= kSmallK);
-        m.deferred = (big || !cand) ? 1 : 0;
-    }
-    if (!m.deferred && m.opt_ok) {
+    if (m.opt_ok) {
         if (!m.direct) bytes += static_cast<uint32_t>((m.lo_al + m.kvw + V - m.hi_al) * esize);
         bytes += static_cast<uint32_t>(m.hs_hi - m.hs_lo) * 4u;
     }
@@ -1360,7 +1345,7 @@ __device__ RowMeta plan_row(const LaunchParams& p, int r, uint32_t& bytes, int& 
 __device__ __forceinline__ void issue_row(const LaunchParams& p, const RowMeta& m, int esize, unsigned char* log_dst,
                                           uint64_t* bar) {
     unsigned char* hist_dst = log_dst + p.stage_logit_bytes;
-    if (!m.direct && !m.deferred && m.opt_ok) {
+    if (!m.direct && m.opt_ok) {
         const int V = m.V;
         if (m.lo_al > 0) bulk_g2s(log_dst, m.row_ptr, static_cast<uint32_t>(m.lo_al * esize), bar);
         if (m.kvw > 0)
@@ -1369,11 +1354,10 @@ __device__ __forceinline__ void issue_row(const LaunchParams& p, const RowMeta& 
             bulk_g2s(log_dst + (m.lo_al + m.kvw) * esize, m.row_ptr + static_cast<int64_t>(m.hi_al) * esize,
                      static_cast<uint32_t>((V - m.hi_al) * esize), bar);
     }
-    if (m.hs_hi > m.hs_lo && !m.deferred && m.opt_ok)
+    if (m.hs_hi > m.hs_lo && m.opt_ok)
         bulk_g2s(hist_dst, m.hist + m.hs_lo, static_cast<uint32_t>(m.hs_hi - m.hs_lo) * 4u, bar);
 }
 
-template <bool kGeneral>
 __device__ void produce_rows(const LaunchParams& p, int first, int gstride, int n_my, int lane, unsigned char* stages,
                              int stage_bytes, RowMeta* metas, uint64_t* full_bar, uint64_t* empty_bar,
                              const volatile uint32_t* progress, int* issued) {
@@ -1388,8 +1372,8 @@ __device__ void produce_rows(const LaunchParams& p, int first, int gstride, int 
         uint32_t bytes = 0;
         if (kj < n_my) {
             int r = first + kj * gstride;
-            if (kGeneral) r = min(max(p.deferred_rows[r], 0), p.total_rows - 1);
-            m = plan_row<kGeneral>(p, r, bytes, esize);
+            r = min(max(p.deferred_rows[r], 0), p.total_rows - 1);
+            m = plan_row(p, r, bytes, esize);
         }
         const int nb = (n_my - k0) < 32 ? (n_my - k0) : 32;
         for (int j = 0; j < nb; ++j) {
@@ -1399,7 +1383,9 @@ __device__ void produce_rows(const LaunchParams& p, int first, int gstride, int 
                 const int s = rp.s;
                 if (rp.n > 0)
                     ok = mbar_wait_bounded(&empty_bar[s], static_cast<uint32_t>((rp.n - 1) & 1), p.wait_ns, progress);
-                if (ok) {
+                if (ok && m.row == p.test_stall_row) {
+                    ok = false;   // test hook: this row's stage never completes, so the element warps' wait runs out
+                } else if (ok) {
                     metas[rp.meta(S_)] = m;
                     fence_proxy_async();
                     mbar_arrive_expect_tx(&full_bar[s], bytes);
@@ -1419,763 +1405,12 @@ __device__ void produce_rows(const LaunchParams& p, int first, int gstride, int 
     }
 }
 
-// Candidate-kernel producer: rows are taken one at a time from a global counter as stages free up, so CTAs that
-// finish early take more rows.  After the last row it publishes an entry with row = -1 (no copies).
-__device__ void produce_rows_dynamic(const LaunchParams& p, int lane, unsigned char* stages, int stage_bytes,
-                                     RowMeta* metas, uint64_t* full_bar, uint64_t* empty_bar,
-                                     const volatile uint32_t* progress, int* issued) {
-    if (lane != 0) return;
-    const int S_ = p.n_stages;
-    RingPos rp{0, 0};
-    for (int k = 0;; ++k, rp.next(S_)) {
-        const int s = rp.s;
-        if (rp.n > 0 && !mbar_wait_bounded(&empty_bar[s], static_cast<uint32_t>((rp.n - 1) & 1), p.wait_ns, progress)) {
-            atomicOr(p.err, kErrTimeout);
-            return;
-        }
-        const int r = static_cast<int>(atomicAdd(p.row_counter, 1u));
-        if (r == p.test_stall_row) return;   // test hook: this row's stage never completes (its wait runs out)
-        if (r >= p.total_rows) {
-            metas[rp.meta(S_)].row = -1;
-            mbar_arrive(&full_bar[s]);
-            *issued = k + 1;
-            return;
-        }
-        uint32_t bytes = 0;
-        int esize = 4;
-        const RowMeta m = plan_row<false>(p, r, bytes, esize);
-        metas[rp.meta(S_)] = m;
-        fence_proxy_async();
-        mbar_arrive_expect_tx(&full_bar[s], bytes);
-        issue_row(p, m, esize, stages + static_cast<size_t>(s) * stage_bytes, &full_bar[s]);
-        *issued = k + 1;
-    }
-}
-
-// ================================================================ candidate kernel
-// Every row of a call.  Greedy rows and sampling rows with top-k <= 64 finish here; the producer marks the rest
-// deferred for the whole-row kernel.  Warps 0-3 are the element warps (one warp-group per row), warp 4 the
-// producer.  The row stays in its shared-memory stage: one pass applies penalty, mask and temperature and
-// collects the top-k candidates; the candidates are then ranked, and the softmax, top-p cut and draw decided, by
-// all 128 element threads.
-
 constexpr int kRankBuckets = 64;   // value buckets of the candidate counting sort
 
-// Candidate work area: the candidates in ascending (value, index) order (position = rank).
-struct __align__(16) CandRank {
-    unsigned long long pk[kCandCap];   // keys okey(x) << 32 | id
-    unsigned long long pf[kCandCap];   // softmax numerators in fixed point, round(e * 2^52)
-    double pe[kCandCap];               // the same numerators in fp64
-    unsigned long long wsum[kWarps];   // per-warp totals of the survivor-mass scan
-    int32_t bcount[kRankBuckets];      // candidates per value bucket
-    int32_t bstart[kRankBuckets];      // exclusive prefix of bcount
-    unsigned long long pre_cut;        // mass below the first kept candidate
-    uint32_t kth_key;                  // okey of the K-th largest value
-    int32_t first;                     // position of the first survivor
-    int32_t cut;                       // position of the first kept candidate (-1: undecided)
-    int32_t ambiguous, res, hits;
-};
-
-struct __align__(16) CandMisc {
-    unsigned long long key[kCandCap];  // candidate keys okey(x) << 32 | id, in arrival order
-    CandRank w;
-    float red_f[kWarps];
-    float tau_w[kWarps];
-    float am_v[kWarps];
-    int32_t am_i[kWarps];
-    uint32_t count[2];                 // keys appended, by row parity (reset one row after use)
-    unsigned long long seed;           // the launch's carried threshold (from p.guess_seed)
-    int32_t rr;                        // replay result
-    int32_t issued;                    // rows the producer has issued (timeout drain)
-    uint32_t progress;                 // rows finished by the element warps
-    int32_t flags[kCandCap];           // replay scratch
-    // per-warp staged positions of the elements that passed the pass's test; cand_block reuses the area as
-    // 256 uint64 keys, so it is 16-byte aligned
-    alignas(16) uint32_t desc[kWarps][kCandCap];
-};
-static_assert(offsetof(CandMisc, desc) % 16 == 0 && sizeof(CandMisc) % 16 == 0, "CandMisc alignment");
-static_assert(offsetof(CandMisc, key) % 16 == 0 && offsetof(CandMisc, w) % 16 == 0, "CandMisc alignment");
-
-__device__ __forceinline__ unsigned long long warp_incl_u64(unsigned long long v, int lane) {
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const unsigned long long y = __shfl_up_sync(kFull, v, o);
-        if (lane >= o) v += y;
-    }
-    return v;
-}
-
-// key[0, C) (C <= 128) = okey(x) << 32 | id of every value >= some threshold <= the K-th largest, so of every
-// survivor; keys are unique.  All 128 element threads.  Candidate t is ranked by thread t (it counts the keys
-// below its own) and placed at its rank; thread t then holds rank t.  Sums are exact 64-bit integer sums of
-// round(e * 2^52) (a block scan); the rounding, at most 2^-53 per value, is inside the error band.  `mx` is the
-// row maximum.  Returns the id, or -1 when a decision lies inside the band (the caller replays the row).
-__device__ int cand_block(const unsigned long long* key, int C, int K, const DevOptions& o, double r, float mx,
-                          float tau, double* out_probs, int V, CandRank& w, unsigned long long* tmp, int tid, int lane,
-                          int warp) {
-    if (tid == 0) {
-        w.cut = -1;
-        w.ambiguous = 0;
-        w.res = -1;
-        w.hits = 0;
-    }
-    // ---- rank: a counting sort over value buckets, then a count within the bucket.  Every candidate lies in
-    //      [tau, mx]; the bucket of x is trunc((x - tau) * 64 / (mx - tau)) in fp32, non-decreasing in x, so the
-    //      buckets keep the key order and only keys of the same bucket need comparing.
-    if (tid < kRankBuckets) w.bcount[tid] = 0;
-    cbar();
-    const float span = __fsub_rn(mx, tau);
-    const float scale = span > 0.0f ? __fdiv_rn(static_cast<float>(kRankBuckets), span) : 0.0f;
-    unsigned long long ka = 0ull;
-    int bk = 0, arrival = 0;
-    if (tid < C) {
-        ka = key[tid];
-        const float x = okey_inv(static_cast<uint32_t>(ka >> 32));
-        bk = min(max(static_cast<int>(__fmul_rn(__fsub_rn(x, tau), scale)), 0), kRankBuckets - 1);
-        arrival = atomicAdd(&w.bcount[bk], 1);
-    }
-    cbar();
-    if (warp == 0) {   // exclusive prefix of the 64 bucket counts
-        const int c0 = w.bcount[2 * lane], c1 = w.bcount[2 * lane + 1];
-        int incl = c0 + c1;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int y = __shfl_up_sync(kFull, incl, o);
-            if (lane >= o) incl += y;
-        }
-        w.bstart[2 * lane] = incl - c0 - c1;
-        w.bstart[2 * lane + 1] = incl - c1;
-    }
-    cbar();
-    int b0 = 0, bn = 0;
-    if (tid < C) {
-        b0 = w.bstart[bk];
-        bn = w.bcount[bk];
-        tmp[b0 + arrival] = ka;
-    }
-    cbar();
-    if (tid < C) {
-        int lt = b0;
-        for (int j = b0; j < b0 + bn; ++j) lt += tmp[j] < ka ? 1 : 0;
-        const double et = softmax_num(okey_inv(static_cast<uint32_t>(ka >> 32)), mx);   // Sampler.cs:57
-        w.pk[lt] = ka;
-        w.pf[lt] = __double2ull_rn(__dmul_rn(et, kFix52));
-        w.pe[lt] = et;
-        if (lt == C - K) w.kth_key = static_cast<uint32_t>(ka >> 32);   // Sampler.cs:45-46
-    }
-    if (out_probs)
-        for (int i = tid; i < V; i += kThreads) out_probs[i] = 0.0;
-    cbar();
-    // ---- thread t holds rank t
-    const uint32_t kth = w.kth_key;
-    const bool mine = tid < C;
-    const unsigned long long kt = mine ? w.pk[tid] : 0ull;
-    const unsigned long long ft = mine ? w.pf[tid] : 0ull;
-    const uint32_t vt = static_cast<uint32_t>(kt >> 32);
-    const bool surv = mine && vt >= kth;   // Sampler.cs:47-48
-    if (surv && (tid == 0 || static_cast<uint32_t>(w.pk[tid - 1] >> 32) < kth)) w.first = tid;
-    const unsigned long long fs = surv ? ft : 0ull;
-    const unsigned long long x = warp_incl_u64(fs, lane);
-    if (lane == 31) w.wsum[warp] = x;
-    cbar();
-    unsigned long long off = 0, tot = 0;
-#pragma unroll
-    for (int i = 0; i < kWarps; ++i) {
-        const unsigned long long s = w.wsum[i];
-        off += i < warp ? s : 0ull;
-        tot += s;
-    }
-    const unsigned long long inc = off + x;   // survivor mass up to and including rank tid
-    const unsigned long long exc = inc - fs;
-    const int first = w.first;
-    const int S = C - first;
-    const double eta = (6.0 * S + 128.0) * kU;
-    if (o.top_p >= 1.0f) {
-        if (tid == 0) {
-            w.cut = first;
-            w.pre_cut = 0ull;
-        }
-    } else if (surv) {
-        // ---- top-p cut over the ascending order (Sampler.cs:62-72): the element whose cumulative mass first
-        //      exceeds (1 - TopP) of the total breaks the loop; the last element is never removed
-        const double tot_d = static_cast<double>(tot);
-        const double thr = static_cast<double>(__fsub_rn(1.0f, o.top_p));
-        const double T = __dmul_rn(thr, tot_d);
-        const double band = __dmul_rn(eta, tot_d);
-        const double bd = static_cast<double>(exc);   // cum before this element
-        const double id = static_cast<double>(inc);   // cum including it
-        const int pos = tid - first;
-        const bool brk = pos <= S - 2 && !(bd > T) && id > T;
-        const bool all_but_last = pos == S - 1 && !(bd > T);
-        if (brk || all_but_last) {
-            bool amb = false;
-            if (brk && !(__dsub_rn(id, T) > band)) amb = true;
-            if (bd > 0.0 && !(__dsub_rn(T, bd) > band)) amb = true;
-            // the value groups next to the cut must be strictly apart in probability (the reference orders by
-            // probability, then index)
-            const double et = w.pe[tid];
-            int qlo = tid - 1;
-            while (qlo >= first && static_cast<uint32_t>(w.pk[qlo] >> 32) == vt) --qlo;
-            if (qlo >= first && !(w.pe[qlo] < et * (1.0 - 32.0 * kU))) amb = true;
-            if (brk && qlo < tid - 1) {   // the cut falls inside this value group: the group above matters too
-                int qhi = tid + 1;
-                while (qhi < C && static_cast<uint32_t>(w.pk[qhi] >> 32) == vt) ++qhi;
-                if (qhi < C && !(w.pe[qhi] > et * (1.0 + 32.0 * kU))) amb = true;
-            }
-            w.cut = tid;
-            w.pre_cut = exc;
-            w.ambiguous = amb ? 1 : 0;
-        }
-    }
-    cbar();
-    if (w.ambiguous || w.cut < 0) return -1;
-    const int cut = w.cut;
-    const bool kept = mine && tid >= cut;
-    const unsigned long long B = tot - w.pre_cut;   // mass of the kept candidates
-    if (kept) {
-        // ---- inverse-CDF draw over the kept ids in index order (Sampler.cs:73-87)
-        const uint32_t it = static_cast<uint32_t>(kt);
-        unsigned long long pre2 = 0;
-        for (int q = cut; q < C; ++q) {
-            const unsigned long long kq = w.pk[q];
-            if (static_cast<uint32_t>(kq) < it) pre2 += w.pf[q];
-        }
-        const double Bd = static_cast<double>(B);
-        const double rB = __dmul_rn(r, Bd);
-        const double lo = static_cast<double>(pre2), hi = static_cast<double>(pre2 + ft);
-        if (ft > 0 && !(lo > rB) && hi > rB) {
-            bool amb = !(__dsub_rn(hi, rB) > __dmul_rn(eta, Bd));
-            if (pre2 > 0 && !(__dsub_rn(rB, lo) > __dmul_rn(eta, Bd))) amb = true;
-            atomicAdd(&w.hits, 1);
-            w.res = amb ? -1 : static_cast<int>(it);
-        }
-    }
-    cbar();
-    const int res = w.hits == 1 ? w.res : -1;
-    if (res >= 0 && out_probs) {
-        if (kept)
-            out_probs[static_cast<uint32_t>(kt)] = __ddiv_rn(w.pe[tid], __dmul_rn(static_cast<double>(B), 1.0 / kFix52));
-        cbar();
-    }
-    return res;
-}
-
-// ---- element pass of the candidate kernel (the row stays in shared memory; nothing is kept in registers)
-enum PassMode { kPassGreedy = 0, kPassFused = 1, kPassTop2 = 2, kPassAppend = 3 };
-
-// Greedy: first maximum (a, bi) over the thread's ids, on the values after penalty and mask (no temperature).
-// Top2: the thread's two largest values (a >= b) after penalty, mask and temperature.  Vectors that no mask
-// boundary, EOS rule or history flag touches take the short path (temperature only).
-template <int VW, int kMode>
-__device__ __forceinline__ void row_pass(const unsigned char* sl, int nvec, const RowMap& mp, const RowCtx& c,
-                                         int tid, float& a, float& b, int& bi) {
-    static_assert(kMode == kPassGreedy || kMode == kPassTop2, "the appending passes are row_pass_append");
-#pragma unroll 1
-    for (int qv = tid; qv < nvec; qv += kThreads) {
-        float v[VW];
-        load_vec<VW>(sl, qv, v);
-        int i0 = -1;
-        uint32_t bits = 0u;
-        bool slow = static_cast<unsigned>(qv - c.slow_vlo) < static_cast<unsigned>(c.slow_vhi - c.slow_vlo) ||
-                    qv == c.eos_vec;
-        if (c.pen_on) {
-            i0 = mp.idx(qv * VW);
-            bits = pen_mask<VW>(c.flags, i0);
-            slow = slow || bits != 0u;
-        }
-        float t[VW];
-        if (slow) {
-            if (i0 < 0) i0 = mp.idx(qv * VW);
-#pragma unroll
-            for (int e = 0; e < VW; ++e) t[e] = transform(v[e], i0 + e, (bits >> e) & 1u, c);
-        } else {
-#pragma unroll
-            for (int e = 0; e < VW; ++e) t[e] = kMode == kPassGreedy ? v[e] : __fmul_rn(v[e], c.inv_t);
-        }
-        if (kMode == kPassTop2) {
-#pragma unroll
-            for (int e = 0; e < VW; ++e) {
-                b = fmaxf(b, fminf(a, t[e]));
-                a = fmaxf(a, t[e]);
-            }
-            continue;
-        }
-        float vm = t[0];
-#pragma unroll
-        for (int e = 1; e < VW; ++e) vm = fmaxf(vm, t[e]);
-        if (vm > a) {
-            if (i0 < 0) i0 = mp.idx(qv * VW);
-#pragma unroll
-            for (int e = 0; e < VW; ++e)
-                if (t[e] > a) {
-                    a = t[e];
-                    bi = i0 + e;
-                }
-        }
-    }
-}
-
-// Fused / Append pass: every value >= tau goes to keys (count = their number), `a` = the largest of them.  The
-// pass itself only marks, per thread, the elements whose short-path value is >= tau (for a lazy penalty that is
-// the unpenalized value, an upper bound); each warp then gathers its marked elements, one per lane, computes their
-// exact values (penalty, mask, temperature) and appends those still >= tau with one counter update per warp.
-template <int VW>
-__device__ __forceinline__ void row_pass_append(const unsigned char* sl, int nvec, const RowMap& mp, const RowCtx& c,
-                                                int tid, float& a, float tau, uint32_t* count,
-                                                unsigned long long* keys, uint32_t* desc) {
-    const int lane = tid & 31;
-    const bool lazy = c.pen_lazy;
-    uint32_t marks = 0u;   // bit (iteration * VW + e); at most 3072 / (128 * VW) iterations
-    int it = 0;
-#pragma unroll 1
-    for (int qv = tid; qv < nvec; qv += kThreads, ++it) {
-        float v[VW];
-        load_vec<VW>(sl, qv, v);
-        bool slow = static_cast<unsigned>(qv - c.slow_vlo) < static_cast<unsigned>(c.slow_vhi - c.slow_vlo) ||
-                    qv == c.eos_vec;
-        int i0 = -1;
-        uint32_t bits = 0u;
-        if (c.pen_on && (slow || !lazy)) {
-            i0 = mp.idx(qv * VW);
-            bits = pen_mask<VW>(c.flags, i0);
-            slow = slow || bits != 0u;
-        }
-        float t[VW];
-        if (slow) {
-            if (i0 < 0) i0 = mp.idx(qv * VW);
-#pragma unroll
-            for (int e = 0; e < VW; ++e) t[e] = transform(v[e], i0 + e, (bits >> e) & 1u, c);
-        } else {
-#pragma unroll
-            for (int e = 0; e < VW; ++e) t[e] = __fmul_rn(v[e], c.inv_t);
-        }
-        float vm = t[0];
-#pragma unroll
-        for (int e = 1; e < VW; ++e) vm = fmaxf(vm, t[e]);
-        if (vm >= tau) {
-            uint32_t m = 0u;
-#pragma unroll
-            for (int e = 0; e < VW; ++e) m |= (t[e] >= tau ? 1u : 0u) << e;
-            marks |= m << (it * VW);
-        }
-    }
-    // gather this warp's marked elements: lane l writes its positions from the warp prefix of the counts on
-    const int n = __popc(marks);
-    int incl = n;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(kFull, incl, o);
-        if (lane >= o) incl += y;
-    }
-    const int total = __shfl_sync(kFull, incl, 31);
-    if (total > kCandCap) {   // more than the candidate buffer holds: the row takes the overflow path
-        if (lane == 0) atomicAdd(count, static_cast<uint32_t>(kCandCap + 1));
-        return;
-    }
-    int w = incl - n;
-    while (marks) {
-        const int bit = __ffs(marks) - 1;
-        marks &= marks - 1u;
-        const int iter = bit / VW, e = bit - iter * VW;
-        desc[w++] = static_cast<uint32_t>((tid + iter * kThreads) * VW + e);
-    }
-    __syncwarp();
-    for (int b0 = 0; b0 < total; b0 += 32) {
-        const int i = b0 + lane;
-        bool pr = false;
-        float x = 0.0f;
-        int id = 0;
-        if (i < total) {
-            const int pos = static_cast<int>(desc[i]);
-            id = mp.idx(pos);
-            x = transform(VW == 4 ? reinterpret_cast<const float*>(sl)[pos]
-                                  : __uint_as_float(static_cast<uint32_t>(reinterpret_cast<const uint16_t*>(sl)[pos]) << 16),
-                          id, c.pen_on && c.flags[id] != 0, c);
-            pr = x >= tau;
-        }
-        const unsigned bal = __ballot_sync(kFull, pr);
-        if (bal) {
-            uint32_t base = 0;
-            if (lane == 0) base = atomicAdd(count, static_cast<uint32_t>(__popc(bal)));
-            base = __shfl_sync(kFull, base, 0) + __popc(bal & ((1u << lane) - 1u));
-            if (pr) {
-                a = fmaxf(a, x);
-                if (base < static_cast<uint32_t>(kCandCap))
-                    keys[base] = (static_cast<unsigned long long>(okey(x)) << 32) | static_cast<uint32_t>(id);
-            }
-        }
-    }
-}
-
-template <int kMode>
-__device__ __forceinline__ void row_pass_dt(int dtype, const unsigned char* sl, int nvec, const RowMap& mp,
-                                            const RowCtx& c, int tid, float& a, float& b, int& bi, float tau,
-                                            uint32_t* count, unsigned long long* keys, uint32_t* b_desc = nullptr) {
-    if constexpr (kMode == kPassFused || kMode == kPassAppend) {
-        uint32_t* desc = reinterpret_cast<uint32_t*>(b_desc);
-        if (dtype == 0)
-            row_pass_append<4>(sl, nvec, mp, c, tid, a, tau, count, keys, desc);
-        else
-            row_pass_append<8>(sl, nvec, mp, c, tid, a, tau, count, keys, desc);
-    } else {
-        if (dtype == 0)
-            row_pass<4, kMode>(sl, nvec, mp, c, tid, a, b, bi);
-        else
-            row_pass<8, kMode>(sl, nvec, mp, c, tid, a, b, bi);
-    }
-}
-
-__global__ void __launch_bounds__(kBlockThreads, 6) cand_kernel(const __grid_constant__ LaunchParams p) {
-    extern __shared__ __align__(128) unsigned char smem[];
-    const int tid = threadIdx.x;
-    const int lane = tid & 31;
-    const int warp = tid >> 5;
-    const int S_ = p.n_stages;
-    const int stage_bytes = p.stage_logit_bytes + p.stage_hist_cap * 4;
-    unsigned char* stages = smem;
-    RowMeta* metas = reinterpret_cast<RowMeta*>(smem + static_cast<size_t>(S_) * stage_bytes);   // 2 * S_ entries
-    uint64_t* full_bar = reinterpret_cast<uint64_t*>(metas + 2 * S_);
-    uint64_t* empty_bar = full_bar + S_;
-    // history flag map (a byte per id).  A row clears it after its last read; every path then passes a barrier
-    // before the next row sets flags (cand_block, the replay, the argmax or the overflow barrier).
-    const int fbytes = p.flag_bytes;
-    uint8_t* flags = reinterpret_cast<uint8_t*>(empty_bar + S_);
-    CandMisc& cm = *reinterpret_cast<CandMisc*>(flags + fbytes);
-
-    if (tid == 0) {
-        for (int s = 0; s < S_; ++s) {
-            mbar_init(&full_bar[s], 1);
-            mbar_init(&empty_bar[s], 1);
-        }
-        fence_mbar_init();
-        cm.issued = 0;
-        cm.progress = 0;
-        cm.count[0] = 0;
-        cm.count[1] = 0;
-        cm.seed = p.guess_seed ? *reinterpret_cast<volatile unsigned long long*>(p.guess_seed) : 0xffffffffull;
-    }
-    for (int i = tid; i < fbytes / 16; i += blockDim.x) reinterpret_cast<uint4*>(flags)[i] = make_uint4(0, 0, 0, 0);
-    __syncthreads();
-
-    // the whole-row kernel may be scheduled now; it waits (griddepcontrol.wait) until this grid has finished
-    if (tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    if (warp == kProducerWarp) {
-        produce_rows_dynamic(p, lane, stages, stage_bytes, metas, full_bar, empty_bar, &cm.progress, &cm.issued);
-        return;
-    }
-
-    // ================= element warps =================
-    uint32_t st_greedy = 0, st_fast = 0, st_exact = 0, st_overflow = 0;
-    // threshold carried from the previous candidate row and the (segment, option) it belongs to (-1: none); every
-    // element thread holds the same copy
-    int guess_id = static_cast<int32_t>(static_cast<uint32_t>(cm.seed));
-    float guess_tau = __uint_as_float(static_cast<uint32_t>(cm.seed >> 32));
-    bool failed = false;
-    RingPos rp{0, 0};   // the CTA's row k = n * S_ + s
-    for (;; rp.next(S_)) {
-        const int s = rp.s;
-        unsigned char* sl = stages + static_cast<size_t>(s) * stage_bytes;
-        // the producer's progress counts as progress here too (it may be waiting for rows of other CTAs)
-        const bool ok = mbar_wait_bounded(&full_bar[s], static_cast<uint32_t>(rp.n & 1), p.wait_ns,
-                                          reinterpret_cast<volatile uint32_t*>(&cm.issued));
-        if (cbar_or(!ok)) {
-            failed = true;
-            break;
-        }
-        const RowMeta& m = metas[rp.meta(S_)];
-        if (m.row < 0) break;   // no more rows
-        if (!m.opt_ok) {
-            cbar();
-            if (tid == 0) {
-                atomicOr(p.err, kErrBadOption);
-                *m.out_id = -1;
-                mbar_arrive(&empty_bar[s]);
-                ++cm.progress;
-            }
-            continue;
-        }
-        if (m.deferred) {
-            cbar();   // every thread is past the full-barrier wait of this stage
-            if (tid == 0) {
-                p.deferred_rows[atomicAdd(p.deferred_count, 1u)] = m.row;
-                mbar_arrive(&empty_bar[s]);
-                ++cm.progress;
-            }
-            continue;
-        }
-        const DevOptions o = m.opt;
-        const int V = m.V;
-        const int dtype = m.dtype;
-        const int VWe = dtype == 0 ? 4 : 8;
-        const RowMap mp{m.lo_al, m.kvw, m.kbase, m.hi_al};
-        const int NA = m.lo_al + m.kvw + (V - m.hi_al);
-        const int nvec = (NA + VWe - 1) >> (dtype == 0 ? 2 : 3);   // bulk-copied rows have NA % VWe == 0
-        double* out_probs = m.out_probs;
-        const bool sample = o.do_sample != 0;   // sampling rows here have 0 < K <= 64
-
-        // ---- unaligned rows: the element warps stage the active ids themselves
-        if (m.direct) {
-            for (int q = tid; q < nvec * VWe; q += kThreads) {
-                const int i = mp.idx(q);
-                if (dtype == 0)
-                    reinterpret_cast<float*>(sl)[q] = i < V ? reinterpret_cast<const float*>(m.row_ptr)[i] : neg_inf();
-                else   // padding past V reads as bf16 -inf
-                    reinterpret_cast<uint16_t*>(sl)[q] =
-                        i < V ? reinterpret_cast<const uint16_t*>(m.row_ptr)[i] : 0xff80u;
-            }
-        }
-
-        // ---- repetition penalty (Sampler.cs:25-33).  Distinct(): every history id sets its flag byte (plain
-        //      stores: no read-modify-write); the pass applies the penalty where a flag is set (to the candidates
-        //      only, when the penalty is > 1).
-        if (m.pen_on) {
-            const int32_t* sh = reinterpret_cast<const int32_t*>(sl + p.stage_logit_bytes);
-            bool bad = false;
-            const int nst = m.hs_hi - m.hs_lo;
-            for (int c4 = tid; c4 < nst / 4; c4 += kThreads) {
-                const int4 hv = reinterpret_cast<const int4*>(sh)[c4];
-                const int ids[4] = {hv.x, hv.y, hv.z, hv.w};
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    if (static_cast<unsigned>(ids[j]) < static_cast<unsigned>(V))
-                        flags[ids[j]] = 1;
-                    else
-                        bad = true;
-                }
-            }
-            // ids outside the staged span, [0, hs_lo) and [hs_hi, len), from global memory: four independent
-            // loads per thread in flight
-            const int rest = m.hist_len - nst;
-            for (int q0 = tid; q0 < rest; q0 += 4 * kThreads) {
-                int ids[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int q = q0 + j * kThreads;
-                    ids[j] = q < rest ? m.hist[q < m.hs_lo ? q : q - m.hs_lo + m.hs_hi] : 0;
-                }
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    if (q0 + j * kThreads >= rest) continue;
-                    if (static_cast<unsigned>(ids[j]) < static_cast<unsigned>(V))
-                        flags[ids[j]] = 1;
-                    else
-                        bad = true;
-                }
-            }
-            if (bad) atomicOr(p.err, kErrHistRange);
-        }
-        if (m.pen_on || m.direct) cbar();
-
-        RowCtx c;
-        c.vocab = V;
-        c.kind = m.kind;
-        c.sup_lo = m.sup_lo;
-        c.sup_hi = m.sup_hi;
-        c.eos = m.eos;
-        c.eos_blocked = m.eos_blocked != 0;
-        c.pen_on = m.pen_on != 0;
-        c.pen = o.rep_penalty;
-        c.pen_rcp = m.pen_rcp;
-        c.sample = sample;
-        c.inv_t = m.inv_t;
-        c.flags = flags;
-        c.slow_vlo = m.slow_vlo;
-        c.slow_vhi = m.slow_vhi;
-        c.eos_vec = m.eos_vec;
-        c.pen_lazy = o.rep_penalty > 1.0f;
-
-        float a = neg_inf(), b = neg_inf();
-        int bi = 0x7fffffff;
-        if (!sample) {
-            row_pass_dt<kPassGreedy>(dtype, sl, nvec, mp, c, tid, a, b, bi, 0.0f, nullptr, nullptr);
-            cbar();   // the stage has been read
-            if (m.pen_on)
-                for (int i = tid; i < p.flag_bytes / 16; i += kThreads) reinterpret_cast<uint4*>(flags)[i] = make_uint4(0, 0, 0, 0);
-            if (tid == 0) mbar_arrive(&empty_bar[s]);
-            // first index of the maximum (Sampler.cs:90-95)
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) {
-                const float ov = __shfl_xor_sync(kFull, a, off);
-                const int oi = __shfl_xor_sync(kFull, bi, off);
-                if (ov > a || (ov == a && oi < bi)) {
-                    a = ov;
-                    bi = oi;
-                }
-            }
-            if (lane == 0) {
-                cm.am_v[warp] = a;
-                cm.am_i[warp] = bi;
-            }
-            cbar();
-            float bv = cm.am_v[0];
-            int bx = cm.am_i[0];
-#pragma unroll
-            for (int w = 1; w < kWarps; ++w)
-                if (cm.am_v[w] > bv || (cm.am_v[w] == bv && cm.am_i[w] < bx)) {
-                    bv = cm.am_v[w];
-                    bx = cm.am_i[w];
-                }
-            if (out_probs)
-                for (int i = tid; i < V; i += kThreads) out_probs[i] = 0.0;
-            if (tid == 0) {
-                *m.out_id = is_neg_inf(bv) ? 0 : bx;   // all -inf: the reference's scan never leaves index 0
-                ++cm.progress;
-            }
-            ++st_greedy;
-            continue;
-        }
-
-        // ---- sampling row with 0 < K <= 64.  A threshold carried from the previous row of the same segment and
-        //      option: any tau with K <= count(x >= tau) <= 128 is exact (the K-th largest is then >= tau), so the
-        //      candidates are collected during the element pass; otherwise the threshold is derived from this row.
-        const int K = o.top_k;
-        const int gid = m.seg * 65536 + m.opt_idx;
-        const bool fuse = guess_id == gid;
-        float tau_used = guess_tau;   // every candidate is >= it
-        uint32_t* const count = &cm.count[(rp.n * S_ + rp.s) & 1];
-        if (fuse)
-            row_pass_dt<kPassFused>(dtype, sl, nvec, mp, c, tid, a, b, bi, guess_tau, count, cm.key, cm.desc[warp]);
-        else
-            row_pass_dt<kPassTop2>(dtype, sl, nvec, mp, c, tid, a, b, bi, 0.0f, nullptr, nullptr);
-        {
-            const float wm = warp_max_f(a);
-            if (lane == 0) cm.red_f[warp] = wm;
-        }
-        cbar();   // pass done: the count and the warp maxima are complete
-        float mx = cm.red_f[0];
-#pragma unroll
-        for (int w = 1; w < kWarps; ++w) mx = fmaxf(mx, cm.red_f[w]);
-        int C = fuse ? static_cast<int>(*reinterpret_cast<volatile uint32_t*>(count)) : 0;
-        if (!fuse || C < K || C > kCandCap) {
-            if (fuse) {   // the carried threshold missed: start over from this row's own top-2 values
-                cbar();   // every thread has read the count
-                if (tid == 0) *count = 0;
-                a = neg_inf();
-                row_pass_dt<kPassTop2>(dtype, sl, nvec, mp, c, tid, a, b, bi, 0.0f, nullptr, nullptr);
-            }
-            // tau = min over warps of the ceil(K/4)-th largest of each warp's 64 per-thread top-2 values (>= ceil(K/4)
-            // elements of each warp are >= it, so >= K elements of the row are >= tau)
-            const int cw = (K + kWarps - 1) / kWarps;
-            uint32_t lk[2] = {~okey(a), ~okey(b)};
-            warp_sort32<2>(lk, lane);
-            const float tw = okey_inv(~__shfl_sync(kFull, lk[0], cw - 1));
-            const float wm = okey_inv(~__shfl_sync(kFull, lk[0], 0));   // the warp's maximum
-            if (lane == 0) {
-                cm.tau_w[warp] = tw;
-                cm.red_f[warp] = wm;
-            }
-            cbar();
-            float tau = cm.tau_w[0];
-            mx = cm.red_f[0];
-#pragma unroll
-            for (int w = 1; w < kWarps; ++w) {
-                tau = fminf(tau, cm.tau_w[w]);
-                mx = fmaxf(mx, cm.red_f[w]);
-            }
-            C = kCandCap + 1;
-            tau_used = tau;
-            if (!is_neg_inf(tau)) {
-                row_pass_dt<kPassAppend>(dtype, sl, nvec, mp, c, tid, a, b, bi, tau, count, cm.key, cm.desc[warp]);
-                cbar();
-                C = static_cast<int>(*reinterpret_cast<volatile uint32_t*>(count));
-            }
-        }
-        // every thread is past its last read of the stage and of the flags (the barrier above)
-        if (m.pen_on)
-            for (int i = tid; i < p.flag_bytes / 16; i += kThreads) reinterpret_cast<uint4*>(flags)[i] = make_uint4(0, 0, 0, 0);
-        if (tid == 0) mbar_arrive(&empty_bar[s]);
-        guess_id = -1;
-        if (C <= kCandCap) {
-            // every thread read C before the first barrier inside cand_block / the replay; the counter is next
-            // used two rows on, and the row between always passes a barrier
-            const bool par = !p.force_exact;
-            int res = par ? cand_block(cm.key, C, K, o, m.uniform, mx, tau_used, out_probs, V, cm.w,
-                                       reinterpret_cast<unsigned long long*>(&cm.desc[0][0]), tid, lane, warp)
-                          : -1;
-            if (res < 0) {
-                if (warp == 0) {
-                    const int rr = replay_candidates(cm.key, C, K, o, m.uniform, V, out_probs, cm.flags, lane);
-                    if (lane == 0) cm.rr = rr;
-                }
-                cbar();
-                res = cm.rr;
-                ++st_exact;
-            } else {
-                ++st_fast;
-            }
-            if (tid == 0) {
-                *m.out_id = res;
-                *count = 0;
-            }
-            // carry a threshold to the next row: the candidate ranked ~1.5 K from the top, so that a similar row
-            // collects ~1.5 K candidates (cand_block left them in ascending order)
-            if (par) {
-                // the value ranked `target` from the top; with fewer candidates, the lowest one moved down by
-                // the missing count times the mean gap of the lowest candidates
-                const int target = K + (K >> 1) + 4;
-                float g;
-                if (C >= target) {
-                    g = okey_inv(static_cast<uint32_t>(cm.w.pk[C - target] >> 32));
-                } else {
-                    const int j = min(C - 1, 16);
-                    const float lo = okey_inv(static_cast<uint32_t>(cm.w.pk[0] >> 32));
-                    const float hi = okey_inv(static_cast<uint32_t>(cm.w.pk[j] >> 32));
-                    g = j > 0 ? lo - (hi - lo) * (static_cast<float>(target - C) / static_cast<float>(j)) : lo;
-                }
-                if (!is_neg_inf(g) && !isnan(g)) {
-                    guess_tau = g;
-                    guess_id = gid;
-                }
-            }
-        } else {   // no finite tau or too many candidates: the whole-row kernel takes the row
-            ++st_overflow;
-            cbar();   // every thread has read the count
-            if (tid == 0) {
-                p.deferred_rows[atomicAdd(p.deferred_count, 1u)] = m.row;
-                *count = 0;
-            }
-        }
-        if (tid == 0) ++cm.progress;
-    }
-    if (tid == 0) {
-        if (failed) {
-            atomicOr(p.err, kErrTimeout);
-            // drain: wait (bounded) for every copy the producer issued from this row on
-            const int issued = *reinterpret_cast<volatile int*>(&cm.issued);
-            for (int kk = rp.n * S_ + rp.s; kk < issued; ++kk)
-                mbar_wait_bounded(&full_bar[kk % S_], static_cast<uint32_t>((kk / S_) & 1), p.wait_ns);
-        }
-        // the last CTA to finish resets the row counter for the next call
-        __threadfence();
-        if (atomicAdd(p.cand_done, 1u) == gridDim.x - 1) {
-            *reinterpret_cast<volatile uint32_t*>(p.row_counter) = 0u;
-            *reinterpret_cast<volatile uint32_t*>(p.cand_done) = 0u;
-            __threadfence();
-        }
-        if (p.guess_seed && guess_id >= 0)   // seeds the next launch's first rows
-            *reinterpret_cast<volatile unsigned long long*>(p.guess_seed) =
-                (static_cast<unsigned long long>(__float_as_uint(guess_tau)) << 32) | static_cast<uint32_t>(guess_id);
-        if (p.stats) {
-            const uint32_t v[4] = {st_greedy, st_fast, st_exact, st_overflow};
-            const int idx[4] = {kStatGreedy, kStatFast, kStatFastReplayed, kStatOverflow};
-            for (int i = 0; i < 4; ++i)
-                if (v[i]) atomicAdd(&p.stats[idx[i]], static_cast<unsigned long long>(v[i]));
-        }
-    }
-}
-
-size_t cand_smem_bytes(const LaunchParams& p) {
-    const size_t stage = static_cast<size_t>(p.stage_logit_bytes) + static_cast<size_t>(p.stage_hist_cap) * 4;
-    size_t b = stage * p.n_stages;
-    b += sizeof(RowMeta) * 2 * p.n_stages;
-    b += sizeof(uint64_t) * (2 * p.n_stages);
-    b += static_cast<size_t>(p.flag_bytes);
-    b += sizeof(CandMisc);
-    return b;
-}
+#include "vw_rowwarp.cuh"
 
 // ---------------------------------------------------------------- whole-row kernel
-// The rows the candidate kernel deferred (the first deferred_count entries of deferred_rows): sampling rows with
+// The rows the warp-per-row kernel deferred (the first deferred_count entries of deferred_rows): sampling rows with
 // top-k off or K > 64, rows whose candidates overflowed, and rows of more than 3072 staged ids.  CTA b takes list
 // entries b, b + grid, ...; each row is held in registers (24 values per thread) for the binned top-k / top-p
 // searches, and rows whose decisions fall inside the error band are replayed in the reference's order.
@@ -2196,7 +1431,7 @@ __global__ void __launch_bounds__(kBlockThreads, 3) whole_row_kernel(const __gri
 
     const int first = blockIdx.x;
     const int gstride = gridDim.x;
-    // launched as a programmatic dependent of the candidate kernel: wait until that grid has finished and its
+    // launched as a programmatic dependent of the warp-per-row kernel: wait until that grid has finished and its
     // deferred-row list is visible
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const int n_rows = min(static_cast<int>(*reinterpret_cast<volatile uint32_t*>(p.deferred_count)), p.total_rows);
@@ -2218,7 +1453,7 @@ __global__ void __launch_bounds__(kBlockThreads, 3) whole_row_kernel(const __gri
 
     if (warp == kProducerWarp) {
         // ================= producer warp: plans rows and issues the bulk copies =================
-        produce_rows<true>(p, first, gstride, n_my, lane, stages, stage_bytes, metas, full_bar, empty_bar,
+        produce_rows(p, first, gstride, n_my, lane, stages, stage_bytes, metas, full_bar, empty_bar,
                                &misc.progress, &misc.issued);
         return;
     }
@@ -2552,25 +1787,26 @@ int ctas_per_sm(const void* fn, int which, int threads, size_t smem) {
 }  // namespace
 
 bool plan_launch(LaunchParams& p, int sm_count, int max_grid_general, LaunchPlan* plan) {
-    const void* fc = reinterpret_cast<const void*>(&cand_kernel);
+    const void* fw = reinterpret_cast<const void*>(&row_warp_kernel);
     const void* fg = reinterpret_cast<const void*>(&whole_row_kernel);
-    // the stage count that keeps the most candidate-kernel CTAs resident (ties: the deeper ring)
-    int best_stages = 0, best_cc = 0, best_cg = 0;
+    // the whole-row kernel's stage count: the one that keeps the most of its CTAs resident (ties: the deeper ring)
+    int best_stages = 0, best_cg = 0;
     for (int stages = kStages; stages >= 2; --stages) {
         p.n_stages = stages;
-        const int cc = ctas_per_sm(fc, 0, kBlockThreads, cand_smem_bytes(p));
         const int cg = ctas_per_sm(fg, 1, kBlockThreads, sampler_smem_bytes(p));
-        if (cc > best_cc && cg > 0) {
+        if (cg > best_cg) {
             best_stages = stages;
-            best_cc = cc;
             best_cg = cg;
         }
     }
     if (best_stages == 0) return false;
     p.n_stages = best_stages;
-    plan->smem_cand = cand_smem_bytes(p);
+    plan->smem_cand = static_cast<size_t>(kRwWarps) * rw_warp_bytes(p.vmax);
+    const int cw = ctas_per_sm(fw, 0, kRwWarps * 32, plan->smem_cand);
+    if (cw == 0) return false;
     plan->smem_general = sampler_smem_bytes(p);
-    plan->grid = static_cast<int>(std::min<int64_t>(p.total_rows, static_cast<int64_t>(sm_count) * best_cc));
+    const int64_t warps_needed = (static_cast<int64_t>(p.total_rows) + kRwWarps - 1) / kRwWarps;
+    plan->grid = static_cast<int>(std::min<int64_t>(warps_needed, static_cast<int64_t>(sm_count) * cw));
     plan->grid_general = static_cast<int>(std::min<int64_t>(
         {static_cast<int64_t>(p.total_rows), static_cast<int64_t>(sm_count) * best_cg,
          static_cast<int64_t>(max_grid_general)}));
@@ -2578,11 +1814,11 @@ bool plan_launch(LaunchParams& p, int sm_count, int max_grid_general, LaunchPlan
 }
 
 cudaError_t launch_sampler(const LaunchParams& p, const LaunchPlan& plan, cudaStream_t stream) {
-    cand_kernel<<<plan.grid, kBlockThreads, plan.smem_cand, stream>>>(p);
+    row_warp_kernel<<<plan.grid, kRwWarps * 32, plan.smem_cand, stream>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     // programmatic dependent launch: the whole-row grid is scheduled while the candidate grid drains, instead of
-    // after it (its kernel waits for the candidate grid's completion before reading the deferred list)
+    // after it (its kernel waits for the first grid's completion before reading the deferred list)
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(plan.grid_general);
     cfg.blockDim = dim3(kBlockThreads);
