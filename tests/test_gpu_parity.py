@@ -168,6 +168,31 @@ def test_random_edge_cases(device, seed):
     assert_ids_equal(w, got, ref)
 
 
+@pytest.mark.parametrize("seed", range(4))
+def test_candidate_path_topk_probabilities(device, seed):
+    """Rows decided from candidates (0 < K <= 64) with top-p off or mild, so every survivor of the top-k cut keeps
+    probability: the probabilities must match the oracle within 1e-6 relative and carry mass on the same ids, which
+    pins the K-th largest value (ties included) and the survivor set, not only the drawn id.  A third of the rows are
+    quantised so the K-th value is often tied."""
+    rng = np.random.default_rng(100 + seed)
+    n, V = 512, 2048
+    x = rng.normal(0.0, 1.0, (n, V)).astype(np.float32)
+    q = rng.random(n) < 0.3
+    x[q] = (np.round(x[q] * 4.0) / 4.0).astype(np.float32)
+    table = [(1, k, p, 1.0, 1.0) for k in (1, 2, 8, 33, 50, 63, 64) for p in (1.0, 0.95)]
+    opt = rng.integers(0, len(table), n).astype(np.int32)
+    seg = SegData(x, 0, 1, V, rng.random(n), opt)
+    w = Workload(f"cand_topk{seed}", -1, [seg], table)
+    device.stats(reset=True)
+    got_ids, got_p = run_workload(device, w, want_probs=True)
+    st = device.stats(reset=True)
+    ref_ids, ref_p = oracle.sample_segment(seg, table, threads=THREADS, want_probs=True)
+    np.testing.assert_array_equal(got_ids[0], ref_ids)
+    assert ((got_p[0] == 0) == (ref_p == 0)).all(), "different sets of ids carry probability"
+    np.testing.assert_allclose(got_p[0], ref_p, rtol=PROB_RTOL, atol=0)
+    assert st["rows_fast"] > n // 2, st
+
+
 def test_carried_threshold_misses_and_overflow(device):
     """Rows alternate between very different logit scales (and some rows are all ties), so the threshold the
     candidate kernel carries from row to row keeps missing: the fallback (row top-2 threshold, second append

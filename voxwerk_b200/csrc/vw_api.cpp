@@ -38,7 +38,7 @@ struct vw_handle {
     size_t opts_cap = 0;
     cudaEvent_t opts_done = nullptr;
     unsigned long long* d_stats = nullptr;   // vw::kNumStats per-path row counters
-    unsigned long long* d_guess = nullptr;   // candidate threshold carried from call to call
+    unsigned long long* d_guess = nullptr;   // candidate thresholds carried from call to call
     int force_exact = 0;                     // VW_FORCE_EXACT at creation
     int test_stall_row = -1;                 // VW_TEST_STALL_ROW at creation (first vw_sample call only)
     unsigned long long h2d_bytes = 0;        // host -> device input bytes of VW_MEM_HOST calls (vw_stats.h2d_bytes)
@@ -140,6 +140,15 @@ vw_status grow(vw_handle* h, char** buf, size_t* cap, size_t need, const char* w
     if (e != cudaSuccess) return cuda_fail(h, e, what);
     *cap = n;
     return VW_OK;
+}
+
+// Per-option constants the kernels would otherwise form on every row: both are single IEEE operations, correctly
+// rounded on the host as on the device (Sampler.cs:39: invT = 1f / Temperature).
+void fill_inline_constants(vw::LaunchParams& p) {
+    for (int i = 0; i < p.n_opts && i < vw::kInlineOptions; ++i) {
+        p.inl_inv_t[i] = 1.0f / p.inl_opts[i].temperature;
+        p.inl_pen_rcp[i] = 1.0 / static_cast<double>(p.inl_opts[i].rep_penalty);
+    }
 }
 
 vw_status check_options(vw_handle* h, const vw_options* opts, int32_t n_opts, bool* any_sample) {
@@ -451,6 +460,7 @@ vw_status sample_impl(vw_handle* h, const vw_segment* segs, int32_t n_segs, cons
     p.n_opts = n_opts;
     if (n_opts <= vw::kInlineOptions) {
         std::memcpy(p.inl_opts, opts, sizeof(vw_options) * n_opts);
+        fill_inline_constants(p);
     } else {
         if (static_cast<size_t>(n_opts) > h->opts_cap) {
             cudaStreamSynchronize(st);
@@ -570,9 +580,10 @@ VW_EXPORT vw_status vw_create(int32_t device, vw_handle** out) {
         e = cudaEventCreateWithFlags(&h->copy_events[i], cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaMalloc(&h->d_stats, sizeof(unsigned long long) * vw::kNumStats);
     if (e == cudaSuccess) e = cudaMemset(h->d_stats, 0, sizeof(unsigned long long) * vw::kNumStats);
-    if (e == cudaSuccess) e = cudaMalloc(&h->d_guess, sizeof(unsigned long long) * vw::kMaxSegments);
+    constexpr size_t kSeedBytes = sizeof(unsigned long long) * vw::kMaxSegments * vw::kSeedSlots;
+    if (e == cudaSuccess) e = cudaMalloc(&h->d_guess, kSeedBytes);
     if (e == cudaSuccess)   // option -1 in every slot: no carried threshold yet
-        e = cudaMemset(h->d_guess, 0xff, sizeof(unsigned long long) * vw::kMaxSegments);
+        e = cudaMemset(h->d_guess, 0xff, kSeedBytes);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     const char* fe = std::getenv("VW_FORCE_EXACT");
     h->force_exact = (fe && fe[0] == '1') ? 1 : 0;
@@ -887,6 +898,7 @@ vw_status sample_static_impl(vw_handle* h, int32_t device, const vw_segment* seg
     p.total_rows = row_begin;
     p.n_opts = n_opts;
     std::memcpy(p.inl_opts, opts, sizeof(vw_options) * n_opts);
+    fill_inline_constants(p);
     p.stage_logit_bytes = logit_bytes;
     p.stage_hist_cap = hist_cap;
     p.flag_bytes = static_cast<int32_t>(round_up(static_cast<size_t>(vmax), 16));

@@ -83,6 +83,8 @@ void fill_row_layout(DevSegment& d);
 struct LaunchParams {
     DevSegment seg[kMaxSegments];
     DevOptions inl_opts[kInlineOptions];
+    float inl_inv_t[kInlineOptions];      // fp32(1 / temperature) of each inline option (Sampler.cs:39)
+    double inl_pen_rcp[kInlineOptions];   // RN64(1 / repetition_penalty) of each inline option
     const DevOptions* dev_opts;   // used when n_opts > kInlineOptions
     int32_t n_opts;
     int32_t n_segs;
@@ -100,7 +102,7 @@ struct LaunchParams {
     int32_t force_exact;          // replay every sampled row in the reference's order (test hook)
     char* gscratch;               // large-path scratch, gscratch_stride bytes per CTA
     int64_t gscratch_stride;
-    unsigned long long* guess_seed;   // kMaxSegments candidate thresholds carried across calls, one per segment:
+    unsigned long long* guess_seed;   // kSeedSlots candidate thresholds per segment carried across calls, each
                                       // float bits << 32 | option; nullable (any value is safe: it only saves work
                                       // when it fits)
     uint64_t wait_ns;             // bound of every mbarrier wait without progress
@@ -135,9 +137,10 @@ cudaError_t launch_sampler(const LaunchParams& p, const LaunchPlan& plan, cudaSt
 constexpr int kStaticMaxRows = 65536;       // rows per call (all segments)
 constexpr int kStaticMaxVocab = 4096;       // ids per row (a power of two >= kRegElems * kThreads)
 constexpr int kStaticGeneralCtas = 148;     // whole-row kernel CTAs (one per B200 SM)
-constexpr int64_t kStaticGuessOffset = 32;   // kMaxSegments carried thresholds
-constexpr int64_t kStaticRowsOffset = 256;
-static_assert(kStaticGuessOffset + 8 * kMaxSegments <= kStaticRowsOffset, "static scratch layout");
+constexpr int kSeedSlots = 32;                // carried thresholds per segment (one per warp lane)
+constexpr int64_t kStaticGuessOffset = 256;   // kMaxSegments * kSeedSlots carried thresholds
+constexpr int64_t kStaticRowsOffset = 4096;
+static_assert(kStaticGuessOffset + 8 * kMaxSegments * kSeedSlots <= kStaticRowsOffset, "static scratch layout");
 constexpr int64_t kStaticScratchOffset = kStaticRowsOffset + 4 * static_cast<int64_t>(kStaticMaxRows);
 // sampler_gscratch_stride(kStaticMaxVocab): 12 bytes per id plus a 16-byte sort slot per id
 constexpr int64_t kStaticCtaStride = (static_cast<int64_t>(kStaticMaxVocab) * 28 + 255) / 256 * 256;

@@ -12,38 +12,40 @@
 //   3. the marked vectors are listed in index order and re-read (L1 / L2); each element with raw >= x0 becomes a
 //      raw candidate, and each raw candidate's exact value (penalty, mask, temperature: Sampler.cs:31,
 //      TalkerGenerator.cs:247-248, Sampler.cs:40) is kept when >= tau: the candidates, in index order;
-//   4. with K <= C <= 128 candidates the K-th largest value is >= tau, so the candidates hold every survivor of the
-//      top-k cut (Sampler.cs:42-49); a counting sort over value buckets ranks them;
+//   4. with K <= C <= 256 candidates the K-th largest value is >= tau, so the candidates hold every survivor of the
+//      top-k cut (Sampler.cs:42-49); a count over value buckets finds the K-th largest;
 //   5. softmax numerators (libm exp, Sampler.cs:57) in 64-bit fixed point, the top-p cut over the ascending order
 //      (Sampler.cs:62-72) and the inverse-CDF draw over index order (Sampler.cs:77-87), each decision certified
 //      against the error band of the parallel sums, else the warp replays the row in the reference's order.
-// A threshold that misses (C outside [K, 128]) is rebuilt from the row's own values; rows the kernel does not take
+// A threshold that misses (C outside [K, 256]) is rebuilt from the row's own values; rows the kernel does not take
 // (top-k off or > 64, a penalty < 1, unaligned rows, too many candidates) go to the whole-row kernel.
 
 constexpr int kRwWarps = 4;       // warps per CTA, each on its own rows
 constexpr int kRwBatch = 8;       // 16-byte vectors per lane in flight per load batch
-constexpr int kRwRawCap = 256;    // raw candidates (raw value >= x0) per row
+constexpr int kRwCandCap = 256;   // candidates (exact value >= tau) per row
+constexpr int kRwSlots = kRwCandCap / 32;
+constexpr int kRwRawCap = 384;    // raw candidates (raw value >= x0) per row
 
 // Per-warp shared memory.
 struct __align__(16) RwArea {
-    unsigned long long key[kCandCap];   // candidates in index order: okey(t) << 32 | id
-    unsigned long long srt[kCandCap];   // the same keys in ascending (value, id) order: position = rank
-    unsigned long long fx[kCandCap];    // softmax numerators by rank, fixed point round(e * 2^52)
+    unsigned long long key[kRwCandCap]; // candidates in index order: okey(t) << 32 | id
     union __align__(16) {
         struct {
             float v[kRwRawCap];          // raw candidates (raw value, id), index order
             int32_t id[kRwRawCap];
         } raw;
         struct {
-            unsigned long long tmp[kCandCap];   // bucket-sort scratch
-            double e[kCandCap];                 // softmax numerators by rank (fp64)
-        } s;
+            unsigned long long sv[64];   // survivors in index order (key as in `key`)
+            double e[64];                // their softmax numerators
+            unsigned long long f[64];    // the same in fixed point, round(e * 2^52)
+            uint32_t sk[64];             // survivors in ascending (value, index) order: (value - kth) << 6 | d
+            int32_t kept[64];            // survivor d kept by top-p
+            uint32_t blist[kRwCandCap];  // the values of the K-th largest's bucket
+        } sel;
         int32_t rflags[kCandCap];        // replay scratch
     } u;
     uint16_t vlist[kRwRawCap];          // marked vectors (global vector index), index order
     int32_t bcount[kRankBuckets];
-    int32_t bstart[kRankBuckets];
-    int32_t rank[kCandCap];             // rank of the candidate at index-order position c
 };
 static_assert(sizeof(RwArea) % 16 == 0, "RwArea alignment");
 
@@ -145,6 +147,8 @@ struct RwRow {
     int row_id, seg, opt, local;
     int V, kind, sup_lo, sup_hi, eos;
     bool eos_blocked, pen_on;
+    const int32_t* hist;     // the row's history ids (pen_on)
+    int hlen;
 };
 
 __device__ __forceinline__ bool bm_test(const uint32_t* bm, int id) { return (bm[id >> 5] >> (id & 31)) & 1u; }
@@ -210,8 +214,8 @@ __device__ bool rw_history(const int32_t* hist, int len, int V, uint32_t* bm, in
 // Steps 2-3 for one threshold: candidates (index order) into a.key, their number in C, the largest value in mx.
 // Returns false when the list overflows (too many marked vectors or raw candidates: the threshold is too low).
 template <int VW>
-__device__ bool rw_collect(const RwRow& r, const DevSegment& sg, float tau, float x0, const uint32_t* bm,
-                           RwArea& a, int lane, int& C, float& mx) {
+__device__ bool rw_collect(const RwRow& r, const DevSegment& sg, float tau, float x0, uint32_t* bm, bool& bm_ready,
+                           bool& hist_bad, RwArea& a, int lane, int& C, float& mx) {
     constexpr int vsh = VW == 4 ? 2 : 3;
     // marks, with the vectors holding suppressed ids (and EOS while it is blocked) always marked
     uint32_t mA = mark_part<VW>(r.row, 0, sg.va, sg.cpl_a, x0, lane);
@@ -268,6 +272,12 @@ __device__ bool rw_collect(const RwRow& r, const DevSegment& sg, float tau, floa
         R += tot;
     }
     __syncwarp();
+    // the history bitmap, built here so that its loads (prefetched into L2 at the row's start) are not waited for
+    // ahead of the pass above
+    if (r.pen_on && !bm_ready) {
+        hist_bad = rw_history(r.hist, r.hlen, r.V, bm, lane);
+        bm_ready = true;
+    }
     // exact values; the candidates are those >= tau
     int c = 0;
     float m = neg_inf();
@@ -284,7 +294,7 @@ __device__ bool rw_collect(const RwRow& r, const DevSegment& sg, float tau, floa
         const int pos = c + __popc(bal & ((1u << lane) - 1u));
         if (keep) {
             m = fmaxf(m, t);
-            if (pos < kCandCap) a.key[pos] = (static_cast<unsigned long long>(okey(t)) << 32) | static_cast<uint32_t>(id);
+            if (pos < kRwCandCap) a.key[pos] = (static_cast<unsigned long long>(okey(t)) << 32) | static_cast<uint32_t>(id);
         }
         c += __popc(bal);
     }
@@ -294,171 +304,243 @@ __device__ bool rw_collect(const RwRow& r, const DevSegment& sg, float tau, floa
     return true;
 }
 
-// Step 4: ranks of the C candidates (a.key, index order): a.srt[rank] = key, a.rank[c] = rank.  Counting sort over
-// 64 value buckets linear in [tau, mx] (non-decreasing in the value, so the buckets keep the key order), then a
-// count within the bucket.  Slot s of lane l holds position c = 32 s + l.
-__device__ void rw_rank(RwArea& a, int C, float tau, float mx, int lane) {
-    for (int b = lane; b < kRankBuckets; b += 32) a.bcount[b] = 0;
+// Step 4: the K-th largest value of the C candidates (a.key, index order; C <= 256, slot s of lane l holds
+// position 32 s + l), as an okey, and in `carry_val` an estimate of the value ranked `target` from the top (the next
+// row's threshold).  A 64-bucket count linear in [tau, mx] (non-decreasing in the value, so a higher bucket holds
+// only larger values) finds the bucket holding the K-th largest; that bucket's members are then ranked exactly.
+__device__ uint32_t rw_kth(RwArea& a, int C, int K, int target, float tau, float mx, int lane, float& carry_val) {
+    a.bcount[lane] = 0;
+    a.bcount[lane + 32] = 0;
     __syncwarp();
     const float span = __fsub_rn(mx, tau);
     const float scale = span > 0.0f ? __fdiv_rn(static_cast<float>(kRankBuckets), span) : 0.0f;
-    unsigned long long kk[4];
-    int bk[4], arr[4];
+    int bk[kRwSlots];
+    uint32_t vk[kRwSlots];
 #pragma unroll
-    for (int s = 0; s < 4; ++s) {
-        const int c = 32 * s + lane;
-        kk[s] = 0;
-        bk[s] = 0;
-        arr[s] = 0;
-        if (c < C) {
-            kk[s] = a.key[c];
-            const float x = okey_inv(static_cast<uint32_t>(kk[s] >> 32));
-            bk[s] = min(max(static_cast<int>(__fmul_rn(__fsub_rn(x, tau), scale)), 0), kRankBuckets - 1);
-            arr[s] = atomicAdd(&a.bcount[bk[s]], 1);
+    for (int s = 0; s < kRwSlots; ++s) {
+        bk[s] = -1;
+        vk[s] = 0;
+        if (32 * s < C) {
+            const int c = 32 * s + lane;
+            if (c < C) {
+                vk[s] = static_cast<uint32_t>(a.key[c] >> 32);
+                bk[s] = min(max(static_cast<int>(__fmul_rn(__fsub_rn(okey_inv(vk[s]), tau), scale)), 0),
+                            kRankBuckets - 1);
+                atomicAdd(&a.bcount[bk[s]], 1);
+            }
         }
     }
     __syncwarp();
-    {   // exclusive prefix of the 64 bucket counts (lane l: buckets 2l, 2l + 1)
-        const int c0 = a.bcount[2 * lane], c1 = a.bcount[2 * lane + 1];
-        int tot;
-        const int ex = warp_excl_i(c0 + c1, lane, tot);
-        a.bstart[2 * lane] = ex;
-        a.bstart[2 * lane + 1] = ex + c0;
+    // lane l holds buckets 63 - 2l and 62 - 2l, so the lane prefix runs from the top bucket down
+    const int b_hi = kRankBuckets - 1 - 2 * lane, b_lo = b_hi - 1;
+    const int n_hi = a.bcount[b_hi], n_lo = a.bcount[b_lo];
+    int tot;
+    const int above = warp_excl_i(n_hi + n_lo, lane, tot);   // candidates in the buckets above b_hi
+    int bstar = -1, need = 0;
+    if (above < K && K <= above + n_hi) {
+        bstar = b_hi;
+        need = K - above;
+    } else if (above + n_hi < K && K <= above + n_hi + n_lo) {
+        bstar = b_lo;
+        need = K - above - n_hi;
     }
-    __syncwarp();
+    const unsigned w1 = __ballot_sync(kFull, bstar >= 0);   // exactly one lane: 1 <= K <= C
+    bstar = __shfl_sync(kFull, bstar, __ffs(w1) - 1);
+    need = __shfl_sync(kFull, need, __ffs(w1) - 1);
+    // the next threshold: the value ranked `target` from the top, interpolated linearly by rank inside its bucket;
+    // with fewer candidates than that, tau moved down by the missing count at the density of the lowest 4 buckets
+    int bt = -1, nt = 0, at = 0;
+    if (above < target && target <= above + n_hi) {
+        bt = b_hi;
+        nt = n_hi;
+        at = target - above;
+    } else if (above + n_hi < target && target <= above + n_hi + n_lo) {
+        bt = b_lo;
+        nt = n_lo;
+        at = target - above - n_hi;
+    }
+    const unsigned w2 = __ballot_sync(kFull, bt >= 0);
+    const int n4 = warp_sum_i(lane >= 30 ? n_hi + n_lo : 0);   // buckets 3..0
+    if (scale == 0.0f) {
+        carry_val = tau;
+    } else if (w2) {
+        const int src = __ffs(w2) - 1;
+        bt = __shfl_sync(kFull, bt, src);
+        nt = __shfl_sync(kFull, nt, src);
+        at = __shfl_sync(kFull, at, src);
+        // bucket bt spans [tau + bt / scale, tau + (bt + 1) / scale); rank `at` of its nt members, from the top
+        const float frac = __fdiv_rn(static_cast<float>(at), static_cast<float>(nt + 1));
+        carry_val = __fadd_rn(tau, __fdiv_rn(__fsub_rn(static_cast<float>(bt + 1), frac), scale));
+    } else {
+        const float per = __fdiv_rn(4.0f, __fmul_rn(static_cast<float>(max(n4, 1)), scale));   // value per candidate
+        carry_val = __fsub_rn(tau, __fmul_rn(static_cast<float>(target - C), per));
+    }
+    // the members of bucket bstar, then the need-th largest of them (ties counted): #(> v) < need <= #(>= v)
+    int nb = 0;
 #pragma unroll
-    for (int s = 0; s < 4; ++s)
-        if (32 * s + lane < C) a.u.s.tmp[a.bstart[bk[s]] + arr[s]] = kk[s];
-    __syncwarp();
-#pragma unroll
-    for (int s = 0; s < 4; ++s) {
-        const int c = 32 * s + lane;
-        if (c < C) {
-            const int b0 = a.bstart[bk[s]], bn = a.bcount[bk[s]];
-            int lt = b0;
-            for (int j = b0; j < b0 + bn; ++j) lt += a.u.s.tmp[j] < kk[s] ? 1 : 0;
-            a.srt[lt] = kk[s];
-            a.rank[c] = lt;
+    for (int s = 0; s < kRwSlots; ++s) {
+        if (32 * s < C) {
+            const bool in = bk[s] == bstar;
+            const unsigned bal = __ballot_sync(kFull, in);
+            if (in) a.u.sel.blist[nb + __popc(bal & ((1u << lane) - 1u))] = vk[s];
+            nb += __popc(bal);
         }
     }
     __syncwarp();
+    uint32_t kth = 0;
+    bool found = false;
+    for (int j = lane; j < nb; j += 32) {
+        const uint32_t v = a.u.sel.blist[j];
+        int gt = 0, ge = 0;
+        for (int i = 0; i < nb; ++i) {
+            const uint32_t w = a.u.sel.blist[i];
+            gt += w > v ? 1 : 0;
+            ge += w >= v ? 1 : 0;
+        }
+        if (gt < need && need <= ge) {
+            kth = v;
+            found = true;
+        }
+    }
+    const unsigned w3 = __ballot_sync(kFull, found);
+    return __shfl_sync(kFull, kth, __ffs(w3) - 1);
 }
 
-// Step 5 on the ranked candidates: the id, or -1 when a decision lies inside the error band (the caller replays).
-// Follows the candidate logic of Sampler.cs:42-87: kth = the K-th largest value (ties kept), softmax numerators of
-// the survivors, the top-p cut over the ascending (probability, index) order with the last element never removed,
-// and the draw over the kept ids in index order.  Sums are exact 64-bit sums of round(e * 2^52); eta bounds their
-// difference from the reference's sequential fp64 sums.
-__device__ int rw_decide(RwArea& a, int C, int K, float top_p, double r, float mx, int V, double* out_probs,
+__device__ __forceinline__ unsigned long long warp_sum_ull(unsigned long long v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+    return v;
+}
+
+// Step 5: the id, or -1 when a decision lies inside the error band or the survivors do not fit this path (the
+// caller replays the row in the reference's order).  Follows Sampler.cs:48-87 on the survivors (the candidates >=
+// the K-th largest, ties kept): softmax numerators (libm exp, Sampler.cs:57) in fixed point round(e * 2^52), the
+// top-p cut over the ascending (probability, index) order with the last element never removed (:62-72), and the
+// inverse-CDF draw over the kept ids in index order (:77-87).  The fixed-point sums are exact; eta = (6 S + 128)
+// 2^-53 of the total bounds their difference from the reference's sequential fp64 sums, so a decision farther than
+// eta from its threshold is the reference's decision.  Survivor d (index order) sits in slot d >> 5 of lane d & 31.
+__device__ int rw_decide(RwArea& a, int C, uint32_t kth, float top_p, double r, float mx, int V, double* out_probs,
                          int lane) {
-    const uint32_t kth = static_cast<uint32_t>(a.srt[C - K] >> 32);   // Sampler.cs:45-47
-    // survivors are the ranks [first, C): the ranks whose value is >= kth (Sampler.cs:48)
-    int first = C;
+    // survivors in index order
+    int S = 0;
 #pragma unroll
-    for (int s = 3; s >= 0; --s) {
-        const int q = 32 * s + lane;
-        const bool sv = q < C && static_cast<uint32_t>(a.srt[q] >> 32) >= kth;
-        const unsigned b = __ballot_sync(kFull, sv);
-        if (b) first = 32 * s + __ffs(b) - 1;
-    }
-    const int S = C - first;
-    // numerators by rank, and the inclusive prefix of the survivor masses in rank order
-    unsigned long long f[4], inc[4];
-    unsigned long long carry = 0;
-#pragma unroll
-    for (int s = 0; s < 4; ++s) {
-        const int q = 32 * s + lane;
-        f[s] = 0;
-        if (q >= first && q < C) {
-            const double e = softmax_num(okey_inv(static_cast<uint32_t>(a.srt[q] >> 32)), mx);   // Sampler.cs:57
-            f[s] = __double2ull_rn(__dmul_rn(e, kFix52));
-            a.u.s.e[q] = e;
-        }
+    for (int s = 0; s < kRwSlots; ++s) {
         if (32 * s < C) {
-            const unsigned long long x = warp_incl_ull(f[s], lane);
-            inc[s] = carry + x;
-            carry += __shfl_sync(kFull, x, 31);
-        } else {
-            inc[s] = carry;
+            const int c = 32 * s + lane;
+            const bool sv = c < C && static_cast<uint32_t>(a.key[c] >> 32) >= kth;
+            const unsigned bal = __ballot_sync(kFull, sv);
+            const int pos = S + __popc(bal & ((1u << lane) - 1u));
+            if (sv && pos < 64) a.u.sel.sv[pos] = a.key[c];
+            S += __popc(bal);
         }
-        if (q < C) a.fx[q] = f[s];
     }
-    const unsigned long long tot = carry;
-    const double eta = (6.0 * S + 128.0) * kU;
+    if (S > 64) return -1;
     __syncwarp();
-    int cut = first;
+    unsigned long long f[2];
+    uint32_t vk[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int d = 32 * h + lane;
+        f[h] = 0;
+        vk[h] = 0;
+        if (d < S) {
+            vk[h] = static_cast<uint32_t>(a.u.sel.sv[d] >> 32);
+            const double e = softmax_num(okey_inv(vk[h]), mx);   // Sampler.cs:57
+            f[h] = __double2ull_rn(__dmul_rn(e, kFix52));
+            a.u.sel.e[d] = e;
+            a.u.sel.f[d] = f[h];
+        }
+    }
+    const unsigned long long tot = warp_sum_ull(f[0] + f[1]);
+    const double eta = (6.0 * S + 128.0) * kU;
+    bool kept[2] = {true, true};
     unsigned long long pre_cut = 0;
     if (top_p < 1.0f) {
-        // the element whose cumulative mass first exceeds (1 - TopP) of the total breaks the loop (Sampler.cs:67-72)
+        // ascending (value, index) order of the survivors = the reference's (probability, index) order, as long
+        // as the value groups next to the cut are apart in probability (checked below)
+        const uint32_t vmx = okey(mx);
+        if (vmx - kth >= (1u << 26)) return -1;   // the 32-bit sort key below would not hold the value
+        uint32_t sk[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int d = 32 * h + lane;
+            sk[h] = d < S ? (((vk[h] - kth) << 6) | static_cast<uint32_t>(d)) : 0xffffffffu;
+        }
+        warp_sort32<2>(sk, lane);   // position j = 32 h + lane
+#pragma unroll
+        for (int h = 0; h < 2; ++h) a.u.sel.sk[32 * h + lane] = sk[h];
+        __syncwarp();
+        unsigned long long fs[2], inc[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) fs[h] = (32 * h + lane) < S ? a.u.sel.f[sk[h] & 63u] : 0ull;
+        inc[0] = warp_incl_ull(fs[0], lane);
+        inc[1] = warp_incl_ull(fs[1], lane) + __shfl_sync(kFull, inc[0], 31);
         const double tot_d = static_cast<double>(tot);
-        const double thr = static_cast<double>(__fsub_rn(1.0f, top_p));
+        const double thr = static_cast<double>(__fsub_rn(1.0f, top_p));   // Sampler.cs:70, fp32 then widened
         const double T = __dmul_rn(thr, tot_d);
         const double band = __dmul_rn(eta, tot_d);
         int found = -1;
         bool amb = false;
         unsigned long long pc = 0;
 #pragma unroll
-        for (int s = 0; s < 4; ++s) {
-            const int q = 32 * s + lane;
-            if (q < first || q >= C) continue;
-            const double bd = static_cast<double>(inc[s] - f[s]);   // cum before this element
-            const double id = static_cast<double>(inc[s]);          // cum including it
-            const int pos = q - first;
-            const bool brk = pos <= S - 2 && !(bd > T) && id > T;
-            const bool last = pos == S - 1 && !(bd > T);
+        for (int h = 0; h < 2; ++h) {
+            const int j = 32 * h + lane;
+            if (j >= S) continue;
+            const double bd = static_cast<double>(inc[h] - fs[h]);   // cum before this element
+            const double id = static_cast<double>(inc[h]);           // cum including it
+            const bool brk = j <= S - 2 && !(bd > T) && id > T;
+            const bool last = j == S - 1 && !(bd > T);
             if (brk || last) {
-                found = q;
-                pc = inc[s] - f[s];
+                found = j;
+                pc = inc[h] - fs[h];
                 if (brk && !(__dsub_rn(id, T) > band)) amb = true;
                 if (bd > 0.0 && !(__dsub_rn(T, bd) > band)) amb = true;
                 // the value groups next to the cut must be strictly apart in probability (the reference orders by
                 // probability, then index)
-                const uint32_t vt = static_cast<uint32_t>(a.srt[q] >> 32);
-                const double et = a.u.s.e[q];
-                int qlo = q - 1;
-                while (qlo >= first && static_cast<uint32_t>(a.srt[qlo] >> 32) == vt) --qlo;
-                if (qlo >= first && !(a.u.s.e[qlo] < et * (1.0 - 32.0 * kU))) amb = true;
-                if (brk && qlo < q - 1) {   // the cut falls inside this value group: the group above matters too
-                    int qhi = q + 1;
-                    while (qhi < C && static_cast<uint32_t>(a.srt[qhi] >> 32) == vt) ++qhi;
-                    if (qhi < C && !(a.u.s.e[qhi] > et * (1.0 + 32.0 * kU))) amb = true;
+                const uint32_t vt = sk[h] >> 6;
+                const double et = a.u.sel.e[sk[h] & 63u];
+                int jlo = j - 1;
+                while (jlo >= 0 && (a.u.sel.sk[jlo] >> 6) == vt) --jlo;
+                if (jlo >= 0 && !(a.u.sel.e[a.u.sel.sk[jlo] & 63u] < et * (1.0 - 32.0 * kU))) amb = true;
+                if (brk && jlo < j - 1) {   // the cut falls inside this value group: the group above matters too
+                    int jhi = j + 1;
+                    while (jhi < S && (a.u.sel.sk[jhi] >> 6) == vt) ++jhi;
+                    if (jhi < S && !(a.u.sel.e[a.u.sel.sk[jhi] & 63u] > et * (1.0 + 32.0 * kU))) amb = true;
                 }
             }
         }
         const unsigned who = __ballot_sync(kFull, found >= 0);
         if (__popc(who) != 1 || __any_sync(kFull, amb)) return -1;
-        const int src = __ffs(who) - 1;
-        cut = __shfl_sync(kFull, found, src);
-        pre_cut = __shfl_sync(kFull, pc, src);
+        const int cut = __shfl_sync(kFull, found, __ffs(who) - 1);
+        pre_cut = __shfl_sync(kFull, pc, __ffs(who) - 1);
+        // kept: the survivors at sorted positions >= cut (Sampler.cs:69 zeroes the ones before)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+            if (32 * h + lane < S) a.u.sel.kept[sk[h] & 63u] = (32 * h + lane) >= cut ? 1 : 0;
+        __syncwarp();
+#pragma unroll
+        for (int h = 0; h < 2; ++h) kept[h] = (32 * h + lane) < S && a.u.sel.kept[32 * h + lane] != 0;
     }
-    const unsigned long long B = tot - pre_cut;   // mass of the kept candidates (Sampler.cs:73)
-    // inverse-CDF draw over the kept ids in index order (Sampler.cs:77-87): position c of a.key is index order
+    const unsigned long long B = tot - pre_cut;   // mass of the kept survivors (Sampler.cs:73)
+    // inverse-CDF draw over the kept ids in index order (Sampler.cs:77-87)
     const double Bd = static_cast<double>(B);
     const double rB = __dmul_rn(r, Bd);
     const double bandB = __dmul_rn(eta, Bd);
+    const unsigned long long fk0 = kept[0] ? f[0] : 0ull, fk1 = kept[1] ? f[1] : 0ull;
+    const unsigned long long x0 = warp_incl_ull(fk0, lane);
+    const unsigned long long x1 = warp_incl_ull(fk1, lane) + __shfl_sync(kFull, x0, 31);
     int hit = -1, hits = 0;
     bool amb = false;
-    unsigned long long run = 0;
 #pragma unroll
-    for (int s = 0; s < 4; ++s) {
-        if (32 * s >= C) break;
-        const int c = 32 * s + lane;
-        unsigned long long fc = 0;
-        int rk = -1;
-        if (c < C) {
-            rk = a.rank[c];
-            if (rk >= cut) fc = a.fx[rk];
-        }
-        const unsigned long long x = warp_incl_ull(fc, lane);
-        const unsigned long long hi = run + x, lo = hi - fc;
+    for (int h = 0; h < 2; ++h) {
+        const unsigned long long fc = h == 0 ? fk0 : fk1, hi = h == 0 ? x0 : x1, lo = hi - fc;
         const double lod = static_cast<double>(lo), hid = static_cast<double>(hi);
         if (fc > 0 && !(lod > rB) && hid > rB) {
             ++hits;
-            hit = static_cast<int>(static_cast<uint32_t>(a.srt[rk]));
+            hit = static_cast<int>(static_cast<uint32_t>(a.u.sel.sv[32 * h + lane]));
             if (!(__dsub_rn(hid, rB) > bandB)) amb = true;
             if (lo > 0 && !(__dsub_rn(rB, lod) > bandB)) amb = true;
         }
-        run += __shfl_sync(kFull, x, 31);
     }
     hits = warp_sum_i(hits);
     if (hits != 1 || __any_sync(kFull, amb)) return -1;
@@ -467,8 +549,10 @@ __device__ int rw_decide(RwArea& a, int C, int K, float top_p, double r, float m
         for (int i = lane; i < V; i += 32) out_probs[i] = 0.0;
         __syncwarp();
         const double scale = __dmul_rn(Bd, 1.0 / kFix52);
-        for (int q = cut + lane; q < C; q += 32)
-            out_probs[static_cast<uint32_t>(a.srt[q])] = __ddiv_rn(a.u.s.e[q], scale);
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+            if (kept[h] && 32 * h + lane < S)
+                out_probs[static_cast<uint32_t>(a.u.sel.sv[32 * h + lane])] = __ddiv_rn(a.u.sel.e[32 * h + lane], scale);
     }
     return res;
 }
@@ -551,54 +635,89 @@ __device__ int rw_argmax(const RwRow& r, const DevSegment& sg, const uint32_t* b
 // `carry` (per lane: segment `lane`'s threshold bits << 32 | option) is read and updated.
 template <int VW>
 __device__ int rw_sample_row(const LaunchParams& p, const RwRow& r, const DevSegment& sg, const DevOptions& o,
-                             RwArea& a, const uint32_t* bm, unsigned long long& carry, double* out_probs, int lane,
+                             RwArea& a, uint32_t* bm, bool& hist_bad, unsigned long long& carry, double* out_probs,
+                             int lane,
                              uint32_t& st_fast, uint32_t& st_exact, uint32_t& st_miss) {
     const int K = o.top_k;
     const unsigned long long cs = __shfl_sync(kFull, carry, r.seg);
     int C = 0;
     float mx = neg_inf(), tau = neg_inf();
-    bool ok = false;
+    bool ok = false, bm_ready = false, have = false;
     if (static_cast<uint32_t>(cs) == static_cast<uint32_t>(r.opt)) {
         tau = __uint_as_float(static_cast<uint32_t>(cs >> 32));
+        have = true;
+    } else if (p.guess_seed) {
+        // no threshold of this warp yet: the lower quartile of the ones the last call's warps left for this segment
+        // and option (robust to an atypical row)
+        const unsigned long long e = p.guess_seed[r.seg * kSeedSlots + lane];
+        const bool m = static_cast<uint32_t>(e) == static_cast<uint32_t>(r.opt) &&
+                       !isnan(__uint_as_float(static_cast<uint32_t>(e >> 32)));
+        uint32_t kk[1] = {m ? okey(__uint_as_float(static_cast<uint32_t>(e >> 32))) : 0xffffffffu};
+        const int n = __popc(__ballot_sync(kFull, m));
+        warp_sort32<1>(kk, lane);
+        if (n > 0) {
+            tau = okey_inv(__shfl_sync(kFull, kk[0], (n - 1) >> 2));
+            have = true;
+        }
+    }
+    if (have) {
         const float x0 = raw_threshold(tau, r.inv_t);
         if (fabsf(x0) < pos_inf())
-            ok = rw_collect<VW>(r, sg, tau, x0, bm, a, lane, C, mx) && C >= K && C <= kCandCap;
+            ok = rw_collect<VW>(r, sg, tau, x0, bm, bm_ready, hist_bad, a, lane, C, mx) && C >= K && C <= kRwCandCap;
     }
     if (!ok) {   // no usable carried threshold: rebuild it from this row
         ++st_miss;
+        if (r.pen_on && !bm_ready) {
+            hist_bad = rw_history(r.hist, r.hlen, r.V, bm, lane);
+            bm_ready = true;
+        }
         tau = rw_row_threshold<VW>(r, sg, bm, K, lane);
         if (is_neg_inf(tau)) return -2;   // fewer than K finite values in reach: the whole-row kernel decides
         const float x0 = raw_threshold(tau, r.inv_t);
         if (!(fabsf(x0) < pos_inf())) return -2;
-        ok = rw_collect<VW>(r, sg, tau, x0, bm, a, lane, C, mx) && C >= K && C <= kCandCap;
+        ok = rw_collect<VW>(r, sg, tau, x0, bm, bm_ready, hist_bad, a, lane, C, mx) && C >= K && C <= kRwCandCap;
         if (!ok) return -2;   // more than 128 candidates (flat rows, ties): the whole-row kernel decides
     }
-    rw_rank(a, C, tau, mx, lane);
-    int res = p.force_exact ? -1 : rw_decide(a, C, K, o.top_p, r.uniform, mx, r.V, out_probs, lane);
+    const int target = 2 * K + 8;
+    float gt = tau;
+    const uint32_t kth = rw_kth(a, C, K, target, tau, mx, lane, gt);
+    int res = p.force_exact ? -1 : rw_decide(a, C, kth, o.top_p, r.uniform, mx, r.V, out_probs, lane);
     if (res >= 0) {
         ++st_fast;
-    } else {   // a decision inside the error band: the reference's sequential order on the candidates
+    } else if (C <= kCandCap) {   // a decision inside the error band: the reference's order on the candidates
         res = replay_candidates(a.key, C, K, o, r.uniform, r.V, out_probs, a.u.rflags, lane);
         ++st_exact;
+    } else {
+        return -2;   // too many candidates for the warp's replay: the whole-row kernel decides the row
     }
-    // carry to the next row of this segment: the candidate ranked 1.5 K + 4 from the top, so that a similar row
-    // collects about that many; with fewer candidates, the lowest one moved down by the missing count times the
-    // mean gap of the lowest candidates
-    if (!p.force_exact) {
-        const int target = K + (K >> 1) + 4;
-        float gt;
-        if (C >= target) {
-            gt = okey_inv(static_cast<uint32_t>(a.srt[C - target] >> 32));
-        } else {
-            const int j = min(C - 1, 16);
-            const float lo = okey_inv(static_cast<uint32_t>(a.srt[0] >> 32));
-            const float hi = okey_inv(static_cast<uint32_t>(a.srt[j] >> 32));
-            gt = j > 0 ? lo - (hi - lo) * (static_cast<float>(target - C) / static_cast<float>(j)) : lo;
-        }
-        if (lane == r.seg && !is_neg_inf(gt) && !isnan(gt))
-            carry = (static_cast<unsigned long long>(__float_as_uint(gt)) << 32) | static_cast<uint32_t>(r.opt);
-    }
+    // carry to the next row of this segment: about the value ranked 2 K + 8 from the top, so that a similar row
+    // collects about that many candidates (rows differ: the window [K, 256] leaves room either way)
+    if (!p.force_exact && lane == r.seg && !is_neg_inf(gt) && !isnan(gt))
+        carry = (static_cast<unsigned long long>(__float_as_uint(gt)) << 32) | static_cast<uint32_t>(r.opt);
     return res;
+}
+
+__device__ __forceinline__ void prefetch_l2(const void* ptr) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
+}
+// Pulls row `row`'s active logit vectors (and its per-row words) into L2, one 128-byte line per lane at a time, so the
+// warp's later loads of that row hit L2 instead of waiting on HBM.
+__device__ void rw_prefetch_row(const LaunchParams& p, int row, int lane) {
+    int s = 0;
+    for (int i = 1; i < p.n_segs; ++i)
+        if (row >= p.seg[i].row_begin) s = i;
+    const DevSegment& sg = p.seg[s];
+    if (!sg.rw_ok) return;
+    const int local = row - sg.row_begin;
+    const unsigned char* base =
+        static_cast<const unsigned char*>(sg.logits) + static_cast<int64_t>(local) * sg.row_stride * (sg.dtype == 0 ? 4 : 2);
+    for (int b = lane * 128; b < sg.va * 16; b += 32 * 128) prefetch_l2(base + b);
+    for (int b = lane * 128; b < sg.vc * 16; b += 32 * 128) prefetch_l2(base + sg.c0 * 16 + b);
+    if (lane == 0 && sg.eosv >= 0) prefetch_l2(base + sg.eosv * 16);
+    if (lane == 1 && sg.opt_index) prefetch_l2(sg.opt_index + local);
+    if (lane == 2 && sg.uniforms) prefetch_l2(sg.uniforms + local);
+    if (lane == 3 && sg.kind == 0 && sg.hist_offsets) prefetch_l2(sg.hist_offsets + local);
+    if (lane == 4 && sg.kind == 0 && sg.steps) prefetch_l2(sg.steps + local);
 }
 
 // Shared memory of one warp: its RwArea, then its history bitmap ((vmax >> 5) + 1 words, padded to 16 bytes).
@@ -607,7 +726,7 @@ __host__ __device__ __forceinline__ size_t rw_warp_bytes(int vmax) {
     return sizeof(RwArea) + static_cast<size_t>(rw_bitmap_words(vmax)) * 4;
 }
 
-__global__ void __launch_bounds__(kRwWarps * 32, 6) row_warp_kernel(const __grid_constant__ LaunchParams p) {
+__global__ void __launch_bounds__(kRwWarps * 32, 7) row_warp_kernel(const __grid_constant__ LaunchParams p) {
     extern __shared__ __align__(128) unsigned char smem[];
     const int lane = threadIdx.x & 31;
     const int wib = threadIdx.x >> 5;
@@ -618,11 +737,10 @@ __global__ void __launch_bounds__(kRwWarps * 32, 6) row_warp_kernel(const __grid
     if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     const int G = gridDim.x * kRwWarps;
-    // carried thresholds: lane s holds segment s's (threshold bits << 32 | option); ~0: none
+    // carried thresholds: lane s holds segment s's (threshold bits << 32 | option); ~0: none yet
     unsigned long long carry = ~0ull;
-    if (p.guess_seed && lane < p.n_segs) carry = *reinterpret_cast<volatile unsigned long long*>(p.guess_seed + lane);
-    const unsigned long long carry0 = carry;
     uint32_t st_greedy = 0, st_fast = 0, st_exact = 0, st_overflow = 0, st_miss = 0;
+    if (blockIdx.x * kRwWarps + wib < p.total_rows) rw_prefetch_row(p, blockIdx.x * kRwWarps + wib, lane);
 
     for (int row = blockIdx.x * kRwWarps + wib; row < p.total_rows; row += G) {
         int s = 0;
@@ -669,8 +787,9 @@ __global__ void __launch_bounds__(kRwWarps * 32, 6) row_warp_kernel(const __grid
                                               static_cast<int64_t>(local) * sg.row_stride * (sg.dtype == 0 ? 4 : 2));
         r.uniform = uniform;
         r.pen = o.rep_penalty;
-        r.pen_rcp = pen_on ? __drcp_rn(static_cast<double>(o.rep_penalty)) : 1.0;
-        r.inv_t = sample ? __fdiv_rn(1.0f, o.temperature) : 1.0f;
+        const bool inl = p.n_opts <= kInlineOptions;
+        r.pen_rcp = !pen_on ? 1.0 : inl ? p.inl_pen_rcp[opt] : __drcp_rn(static_cast<double>(o.rep_penalty));
+        r.inv_t = !sample ? 1.0f : inl ? p.inl_inv_t[opt] : __fdiv_rn(1.0f, o.temperature);
         r.row_id = row;
         r.seg = s;
         r.opt = opt;
@@ -683,19 +802,27 @@ __global__ void __launch_bounds__(kRwWarps * 32, 6) row_warp_kernel(const __grid
         r.eos_blocked = sg.kind == 0 && step < sg.min_new;
         r.pen_on = pen_on;
         double* out_probs = sg.out_probs ? sg.out_probs + static_cast<int64_t>(local) * V : nullptr;
-        if (pen_on && rw_history(sg.hist_ids + hb, static_cast<int>(he - hb), V, bm, lane) && lane == 0)
-            atomicOr(p.err, kErrHistRange);
+        r.hist = sg.hist_ids + hb;
+        r.hlen = static_cast<int>(he - hb);
+        if (pen_on)   // into L2 now; read when the bitmap is built
+            for (int j = lane * 32; j < r.hlen; j += 32 * 32) prefetch_l2(r.hist + j);
+        if (row + G < p.total_rows) rw_prefetch_row(p, row + G, lane);   // this warp's next row
 
+        bool hist_bad = false;
         int res;
         if (!sample) {
+            if (pen_on) hist_bad = rw_history(r.hist, r.hlen, V, bm, lane);
             res = sg.dtype == 0 ? rw_argmax<4>(r, sg, bm, lane) : rw_argmax<8>(r, sg, bm, lane);
             if (out_probs)
                 for (int i = lane; i < V; i += 32) out_probs[i] = 0.0;
             ++st_greedy;
         } else {
-            res = sg.dtype == 0 ? rw_sample_row<4>(p, r, sg, o, a, bm, carry, out_probs, lane, st_fast, st_exact, st_miss)
-                                : rw_sample_row<8>(p, r, sg, o, a, bm, carry, out_probs, lane, st_fast, st_exact, st_miss);
+            res = sg.dtype == 0 ? rw_sample_row<4>(p, r, sg, o, a, bm, hist_bad, carry, out_probs, lane, st_fast,
+                                                   st_exact, st_miss)
+                                : rw_sample_row<8>(p, r, sg, o, a, bm, hist_bad, carry, out_probs, lane, st_fast,
+                                                   st_exact, st_miss);
         }
+        if (hist_bad && lane == 0) atomicOr(p.err, kErrHistRange);
         if (res == -2) {   // the whole-row kernel takes the row
             ++st_overflow;
             if (lane == 0) p.deferred_rows[atomicAdd(p.deferred_count, 1u)] = row;
@@ -704,7 +831,9 @@ __global__ void __launch_bounds__(kRwWarps * 32, 6) row_warp_kernel(const __grid
         }
         __syncwarp();   // the warp's shared area is reused by its next row
     }
-    if (p.guess_seed && lane < p.n_segs && carry != carry0) p.guess_seed[lane] = carry;   // seeds the next launch
+    // seeds the next call: this warp's threshold per segment, in the slot of its index
+    if (p.guess_seed && lane < p.n_segs && carry != ~0ull)
+        p.guess_seed[lane * kSeedSlots + ((blockIdx.x * kRwWarps + wib) & (kSeedSlots - 1))] = carry;
     if (p.stats && lane == 0) {
         const uint32_t v[4] = {st_greedy, st_fast, st_exact, st_overflow};
         const int idx[4] = {kStatGreedy, kStatFast, kStatFastReplayed, kStatOverflow};
