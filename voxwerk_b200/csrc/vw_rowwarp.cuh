@@ -92,13 +92,12 @@ template <int VW>
 __device__ __forceinline__ uint32_t mark_part(const uint4* row, int v0, int nv, int cpl, float x0, int lane) {
     uint32_t marks = 0u;
     const int q0 = lane * cpl;
-    for (int b0 = 0; b0 < cpl; b0 += kRwBatch) {
+    const int nmine = min(cpl, max(nv - q0, 0));   // this lane's vectors
+    const uint4* mine = row + v0 + q0;
+    for (int b0 = 0; b0 < nmine; b0 += kRwBatch) {
         uint4 v[kRwBatch];
 #pragma unroll
-        for (int i = 0; i < kRwBatch; ++i) {
-            const int it = b0 + i, q = q0 + it;
-            v[i] = (it < cpl && q < nv) ? __ldg(row + v0 + q) : neg_inf_vec(VW);
-        }
+        for (int i = 0; i < kRwBatch; ++i) v[i] = (b0 + i < nmine) ? __ldg(mine + b0 + i) : neg_inf_vec(VW);
         uint32_t m = 0u;
 #pragma unroll
         for (int i = 0; i < kRwBatch; ++i)
@@ -594,7 +593,7 @@ __device__ __forceinline__ void rw_for_each(const RwRow& r, const DevSegment& sg
 // largest (a subset of the row, so its K-th largest is <= the row's).  -inf when the row has fewer than K finite
 // values among them.
 template <int VW>
-__device__ float rw_row_threshold(const RwRow& r, const DevSegment& sg, const uint32_t* bm, int K, int lane) {
+__device__ __noinline__ float rw_row_threshold(const RwRow& r, const DevSegment& sg, const uint32_t* bm, int K, int lane) {
     float t1 = neg_inf(), t2 = neg_inf();
     rw_for_each<VW>(r, sg, lane, [&](float raw, int id) {
         const float t = rw_exact(raw, id, bm, r);
@@ -609,7 +608,7 @@ __device__ float rw_row_threshold(const RwRow& r, const DevSegment& sg, const ui
 
 // Greedy rows: first index of the maximum of the penalised, masked values (Sampler.cs:90-95); 0 when all are -inf.
 template <int VW>
-__device__ int rw_argmax(const RwRow& r, const DevSegment& sg, const uint32_t* bm, int lane) {
+__device__ __noinline__ int rw_argmax(const RwRow& r, const DevSegment& sg, const uint32_t* bm, int lane) {
     float bv = neg_inf();
     int bi = 0x7fffffff;
     rw_for_each<VW>(r, sg, lane, [&](float raw, int id) {
@@ -635,7 +634,8 @@ __device__ int rw_argmax(const RwRow& r, const DevSegment& sg, const uint32_t* b
 // `carry` (per lane: segment `lane`'s threshold bits << 32 | option) is read and updated.
 template <int VW>
 __device__ int rw_sample_row(const LaunchParams& p, const RwRow& r, const DevSegment& sg, const DevOptions& o,
-                             RwArea& a, uint32_t* bm, bool& hist_bad, unsigned long long& carry, double* out_probs,
+                             RwArea& a, uint32_t* bm, bool& hist_bad, unsigned long long& carry,
+                             const unsigned long long* seed, double* out_probs,
                              int lane,
                              uint32_t& st_fast, uint32_t& st_exact, uint32_t& st_miss) {
     const int K = o.top_k;
@@ -646,19 +646,10 @@ __device__ int rw_sample_row(const LaunchParams& p, const RwRow& r, const DevSeg
     if (static_cast<uint32_t>(cs) == static_cast<uint32_t>(r.opt)) {
         tau = __uint_as_float(static_cast<uint32_t>(cs >> 32));
         have = true;
-    } else if (p.guess_seed) {
-        // no threshold of this warp yet: the lower quartile of the ones the last call's warps left for this segment
-        // and option (robust to an atypical row)
-        const unsigned long long e = p.guess_seed[r.seg * kSeedSlots + lane];
-        const bool m = static_cast<uint32_t>(e) == static_cast<uint32_t>(r.opt) &&
-                       !isnan(__uint_as_float(static_cast<uint32_t>(e >> 32)));
-        uint32_t kk[1] = {m ? okey(__uint_as_float(static_cast<uint32_t>(e >> 32))) : 0xffffffffu};
-        const int n = __popc(__ballot_sync(kFull, m));
-        warp_sort32<1>(kk, lane);
-        if (n > 0) {
-            tau = okey_inv(__shfl_sync(kFull, kk[0], (n - 1) >> 2));
-            have = true;
-        }
+    } else if (static_cast<uint32_t>(seed[r.seg]) == static_cast<uint32_t>(r.opt)) {
+        // no threshold of this warp yet: the CTA's seed for this segment and option
+        tau = __uint_as_float(static_cast<uint32_t>(seed[r.seg] >> 32));
+        have = true;
     }
     if (have) {
         const float x0 = raw_threshold(tau, r.inv_t);
@@ -678,7 +669,7 @@ __device__ int rw_sample_row(const LaunchParams& p, const RwRow& r, const DevSeg
         ok = rw_collect<VW>(r, sg, tau, x0, bm, bm_ready, hist_bad, a, lane, C, mx) && C >= K && C <= kRwCandCap;
         if (!ok) return -2;   // more than 128 candidates (flat rows, ties): the whole-row kernel decides
     }
-    const int target = 2 * K + 8;
+    const int target = K + (K >> 1) + 4;
     float gt = tau;
     const uint32_t kth = rw_kth(a, C, K, target, tau, mx, lane, gt);
     int res = p.force_exact ? -1 : rw_decide(a, C, kth, o.top_p, r.uniform, mx, r.V, out_probs, lane);
@@ -690,7 +681,7 @@ __device__ int rw_sample_row(const LaunchParams& p, const RwRow& r, const DevSeg
     } else {
         return -2;   // too many candidates for the warp's replay: the whole-row kernel decides the row
     }
-    // carry to the next row of this segment: about the value ranked 2 K + 8 from the top, so that a similar row
+    // carry to the next row of this segment: about the value ranked 1.5 K + 4 from the top, so that a similar row
     // collects about that many candidates (rows differ: the window [K, 256] leaves room either way)
     if (!p.force_exact && lane == r.seg && !is_neg_inf(gt) && !isnan(gt))
         carry = (static_cast<unsigned long long>(__float_as_uint(gt)) << 32) | static_cast<uint32_t>(r.opt);
@@ -739,6 +730,23 @@ __global__ void __launch_bounds__(kRwWarps * 32, 7) row_warp_kernel(const __grid
     const int G = gridDim.x * kRwWarps;
     // carried thresholds: lane s holds segment s's (threshold bits << 32 | option); ~0: none yet
     unsigned long long carry = ~0ull;
+    // the CTA's seeds, one per segment: the lower quartile (robust to an atypical row) of the thresholds the last
+    // call's warps left in the table for that segment, among those of the option the segment's first slot holds
+    __shared__ unsigned long long seed[kMaxSegments];
+    if (wib < p.n_segs) {
+        unsigned long long e = p.guess_seed ? p.guess_seed[wib * kSeedSlots + lane] : ~0ull;
+        const uint32_t opt0 = __shfl_sync(kFull, static_cast<uint32_t>(e), 0);
+        const bool m = static_cast<uint32_t>(e) == opt0 && opt0 != 0xffffffffu &&
+                       !isnan(__uint_as_float(static_cast<uint32_t>(e >> 32)));
+        uint32_t kk[1] = {m ? okey(__uint_as_float(static_cast<uint32_t>(e >> 32))) : 0xffffffffu};
+        const int n = __popc(__ballot_sync(kFull, m));
+        warp_sort32<1>(kk, lane);
+        const uint32_t q = __shfl_sync(kFull, kk[0], max(n - 1, 0) >> 2);
+        if (lane == 0) seed[wib] = n > 0 ? ((static_cast<unsigned long long>(__float_as_uint(okey_inv(q))) << 32) | opt0) : ~0ull;
+    }
+    for (int s2 = kRwWarps + wib; s2 < p.n_segs; s2 += kRwWarps)   // more segments than warps: no seed
+        if (lane == 0) seed[s2] = ~0ull;
+    __syncthreads();
     uint32_t st_greedy = 0, st_fast = 0, st_exact = 0, st_overflow = 0, st_miss = 0;
     if (blockIdx.x * kRwWarps + wib < p.total_rows) rw_prefetch_row(p, blockIdx.x * kRwWarps + wib, lane);
 
@@ -817,9 +825,9 @@ __global__ void __launch_bounds__(kRwWarps * 32, 7) row_warp_kernel(const __grid
                 for (int i = lane; i < V; i += 32) out_probs[i] = 0.0;
             ++st_greedy;
         } else {
-            res = sg.dtype == 0 ? rw_sample_row<4>(p, r, sg, o, a, bm, hist_bad, carry, out_probs, lane, st_fast,
+            res = sg.dtype == 0 ? rw_sample_row<4>(p, r, sg, o, a, bm, hist_bad, carry, seed, out_probs, lane, st_fast,
                                                    st_exact, st_miss)
-                                : rw_sample_row<8>(p, r, sg, o, a, bm, hist_bad, carry, out_probs, lane, st_fast,
+                                : rw_sample_row<8>(p, r, sg, o, a, bm, hist_bad, carry, seed, out_probs, lane, st_fast,
                                                    st_exact, st_miss);
         }
         if (hist_bad && lane == 0) atomicOr(p.err, kErrHistRange);
