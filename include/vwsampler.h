@@ -180,6 +180,60 @@ vw_status vw_sample_static(int32_t device, const vw_segment* segments, int32_t n
                            int32_t err_msg_len);
 
 /*
+ * Device-resident generation state: TalkerGenerator.GenerateBatch's per-job state (TalkerGenerator.cs:322-455) kept
+ * in device memory, one slot per job, so that a generation step sends only logits and reads only ids.  Per slot: the
+ * talker ids generated so far (Active.History, :304), the step (Active.Step), MaxNewTokens, the job's two samplers
+ * (Sampler(Seed) for the talker and Sampler(Seed + 1) for the sub-talker, :345-346, System.Random restated on the
+ * device; their NextDouble() draws replace the per-row uniforms) and whether the job still runs.
+ *
+ * Row r of a step's logits belongs to slot r (row_stride elements apart, device memory).  Finished slots are not
+ * sampled (their id is -1) and draw nothing, like the retired jobs the reference drops from its active list.
+ * Steps are stream-ordered on `stream` (NULL: the handle's stream, and the call returns after the step with any
+ * device-side error); n_options <= 32.  A batch belongs to its handle and its host thread.
+ */
+typedef struct vw_batch vw_batch;
+
+typedef struct vw_slot_config {
+    int32_t talker_option;    /* index of the job's talker options (+ RepetitionPenalty) in each talker step's table */
+    int32_t sub_option;       /* index of the job's sub-talker options in each sub-talker step's table */
+    int32_t max_new_tokens;   /* GenerationOptions.MaxNewTokens */
+    int32_t seed;             /* GenerationOptions.Seed, when seeded != 0 */
+    int32_t seeded;           /* 0: an unseeded job (new Random(); the draws are not reproducible, as in voxwerk) */
+} vw_slot_config;
+
+/* n_slots jobs at most; vocab, eos_id, min_new_tokens and the suppress span as in vw_segment (voxwerk: 3072, 2150,
+ * 2, [2048, 3072)); max_history >= each job's initial history length + max_new_tokens. */
+vw_status vw_batch_create(vw_handle* handle, int32_t n_slots, int32_t vocab, int32_t max_history, int32_t eos_id,
+                          int32_t min_new_tokens, int32_t suppress_lo, int32_t suppress_hi, vw_batch** out_batch);
+vw_status vw_batch_destroy(vw_batch* batch);
+
+/* Starts a job in `slot` (the slot refill of TalkerGenerator.cs:336-358): step 0, running, the two samplers seeded,
+ * and the talker history set to history[0..history_len) (host memory; voxwerk starts from an empty one). */
+vw_status vw_batch_start(vw_batch* batch, int32_t slot, const vw_slot_config* config, const int32_t* history,
+                         int32_t history_len);
+
+/* Ends the job in `slot` early (the slot is not sampled again until the next vw_batch_start). */
+vw_status vw_batch_stop(vw_batch* batch, int32_t slot);
+
+/*
+ * One talker step for every running slot (TalkerGenerator.cs:366-385): repetition penalty over the slot's history,
+ * suppress mask, Select with the slot's options and its talker sampler's draw; then the id is appended to the
+ * history and the job ends when the id is EOS or its step is MaxNewTokens - 1 (out_done[slot] = 1), else its step
+ * advances.  logits: [n_slots, row_stride] of dtype; out_ids / out_done (nullable): [n_slots] int32, device memory.
+ */
+vw_status vw_batch_talker_step(vw_batch* batch, const void* logits, int64_t row_stride, int32_t dtype,
+                               const vw_options* options, int32_t n_options, int32_t* out_ids, int32_t* out_done,
+                               void* stream);
+
+/* One code-predictor group for every running slot (TalkerGenerator.cs:419-420): Select with the slot's sub-talker
+ * options and its sub-talker sampler's draw.  logits: [n_slots, row_stride], `vocab` ids (voxwerk: 2048). */
+vw_status vw_batch_sub_step(vw_batch* batch, const void* logits, int64_t row_stride, int32_t vocab, int32_t dtype,
+                            const vw_options* options, int32_t n_options, int32_t* out_ids, void* stream);
+
+/* A slot's step, history length and running flag (after the steps enqueued so far; synchronizes). */
+vw_status vw_batch_query(vw_batch* batch, int32_t slot, int32_t* step, int32_t* history_len, int32_t* active);
+
+/*
  * Single-row mirrors of the reference's Sampler methods, for callers that keep the reference's call shape.
  * Pointers follow `mem`; the calls are synchronous.
  */

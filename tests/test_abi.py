@@ -55,6 +55,9 @@ int main(void) {
   F(vw_segment, suppress_lo) F(vw_segment, suppress_hi) F(vw_segment, eos_id) F(vw_segment, min_new_tokens)
   F(vw_segment, max_hist_len) F(vw_segment, opt_index) F(vw_segment, uniforms) F(vw_segment, out_ids)
   F(vw_segment, out_probs)
+  printf("vw_slot_config %zu\n", sizeof(vw_slot_config));
+  F(vw_slot_config, talker_option) F(vw_slot_config, sub_option) F(vw_slot_config, max_new_tokens)
+  F(vw_slot_config, seed) F(vw_slot_config, seeded)
   return 0;
 }
 '''
@@ -72,7 +75,9 @@ def test_ctypes_structs_match_c_layout():
     assert lay["vw_options"] == ctypes.sizeof(_lib.VwOptions)
     assert lay["vw_segment"] == ctypes.sizeof(_lib.VwSegment)
     assert lay["vw_stats"] == ctypes.sizeof(_lib.VwStats)
-    for cls, cname in ((_lib.VwOptions, "vw_options"), (_lib.VwSegment, "vw_segment")):
+    assert lay["vw_slot_config"] == ctypes.sizeof(_lib.VwSlotConfig)
+    for cls, cname in ((_lib.VwOptions, "vw_options"), (_lib.VwSegment, "vw_segment"),
+                       (_lib.VwSlotConfig, "vw_slot_config")):
         for fname, _ in cls._fields_:
             key = "eos_id" if fname == "eos_id" else fname
             assert getattr(cls, fname).offset == lay[f"{cname}.{key}"], (cname, fname)
@@ -90,6 +95,9 @@ def test_null_handle_is_invalid_argument():
     assert L.vw_synchronize(None, None) == _lib.VW_ERR_INVALID_ARG
     assert L.vw_destroy(None) == _lib.VW_OK
     assert L.vw_last_error(None) == b""
+    assert L.vw_batch_destroy(None) == _lib.VW_OK
+    assert L.vw_batch_start(None, 0, None, None, 0) == _lib.VW_ERR_INVALID_ARG
+    assert L.vw_batch_talker_step(None, None, 0, 0, None, 0, None, None, None) == _lib.VW_ERR_INVALID_ARG
     out = ctypes.c_int32()
     assert L.vw_argmax(None, None, 1, 0, ctypes.byref(out)) == _lib.VW_ERR_INVALID_ARG
 

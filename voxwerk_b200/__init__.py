@@ -21,6 +21,7 @@ _NATIVE = {
                             "VwError", "VwInvalidArgument", "VwOutOfRange")},
     **{n: ".sampler" for n in ("Device", "GenerationOptions", "Sampler", "SamplingOptions", "Segment",
                                "TalkerBatchSampler", "sample_rows", "sample_rows_static", "vw_options")},
+    **{n: ".batch_state" for n in ("DeviceBatchState",)},
 }
 
 

@@ -42,6 +42,13 @@ EXPORTED = (
     "vw_argmax",
     "vw_sample_static",
     "vw_exp_diagnostic",
+    "vw_batch_create",
+    "vw_batch_destroy",
+    "vw_batch_start",
+    "vw_batch_stop",
+    "vw_batch_talker_step",
+    "vw_batch_sub_step",
+    "vw_batch_query",
 )
 
 
@@ -79,6 +86,18 @@ class VwSegment(ctypes.Structure):
         ("uniforms", ctypes.c_void_p),
         ("out_ids", ctypes.c_void_p),
         ("out_probs", ctypes.c_void_p),
+    ]
+
+
+class VwSlotConfig(ctypes.Structure):
+    """vw_slot_config: one job of a device-resident batch."""
+
+    _fields_ = [
+        ("talker_option", ctypes.c_int32),
+        ("sub_option", ctypes.c_int32),
+        ("max_new_tokens", ctypes.c_int32),
+        ("seed", ctypes.c_int32),
+        ("seeded", ctypes.c_int32),
     ]
 
 
@@ -153,6 +172,15 @@ def _load() -> ctypes.CDLL:
                                      ctypes.c_char_p, i32]
     lib.vw_exp_diagnostic.restype = ctypes.c_int
     lib.vw_exp_diagnostic.argtypes = [vp, vp, i64, vp, vp]
+    for name, args in (("vw_batch_create", [vp, i32, i32, i32, i32, i32, i32, i32, ctypes.POINTER(vp)]),
+                       ("vw_batch_destroy", [vp]),
+                       ("vw_batch_start", [vp, i32, ctypes.POINTER(VwSlotConfig), vp, i32]),
+                       ("vw_batch_stop", [vp, i32]),
+                       ("vw_batch_talker_step", [vp, vp, i64, i32, ctypes.POINTER(VwOptions), i32, vp, vp, vp]),
+                       ("vw_batch_sub_step", [vp, vp, i64, i32, i32, ctypes.POINTER(VwOptions), i32, vp, vp]),
+                       ("vw_batch_query", [vp, i32, vp, vp, vp])):
+        getattr(lib, name).restype = ctypes.c_int
+        getattr(lib, name).argtypes = args
     return lib
 
 

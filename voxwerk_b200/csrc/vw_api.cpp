@@ -2,6 +2,7 @@
 // callers, launch planning and error reporting.  No C++ exception crosses the boundary.
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstdint>
 #include <cstdlib>
@@ -374,8 +375,15 @@ vw_status read_device_error(vw_handle* h, cudaStream_t st) {
     return VW_OK;
 }
 
+// Layout of a device-resident batch's rows that vw_segment cannot express (see vw::DevSegment).
+struct SegExtra {
+    const int32_t* hist_lens;
+    int64_t hist_stride;
+    const int32_t* active;
+};
+
 vw_status sample_impl(vw_handle* h, const vw_segment* segs, int32_t n_segs, const vw_options* opts, int32_t n_opts,
-                      int32_t mem, void* stream) {
+                      int32_t mem, void* stream, const SegExtra* extra = nullptr) {
     if (!h) return VW_ERR_INVALID_ARG;
     h->last_error.clear();
     if (!segs || n_segs < 1 || n_segs > vw::kMaxSegments)
@@ -439,6 +447,11 @@ vw_status sample_impl(vw_handle* h, const vw_segment* segs, int32_t n_segs, cons
         const size_t es = s.dtype == VW_F32 ? 4 : 2;
         d.bulk_ok = aligned(s.logits, 16) && (s.row_stride * es) % 16 == 0 && (s.vocab * es) % 16 == 0;
         d.hist_aligned = d.hist_ids ? aligned(d.hist_ids, 16) : 0;
+        if (extra) {
+            d.hist_lens = extra[i].hist_lens;
+            d.hist_stride = extra[i].hist_stride;
+            d.active = extra[i].active;
+        }
         vw::fill_row_layout(d);
         row_begin += s.n_rows;
         vmax = std::max(vmax, s.vocab);
@@ -648,6 +661,258 @@ VW_EXPORT vw_status vw_get_stats(vw_handle* h, vw_stats* out, int32_t reset) {
     if (e != cudaSuccess) return cuda_fail(h, e, "vw_get_stats");
     out->h2d_bytes = h->h2d_bytes;   // host-side counter (the device word in that slot is unused)
     if (reset) h->h2d_bytes = 0;
+    return VW_OK;
+}
+
+// ------------------------------------------------------------------------------------- device-resident batches
+// One vw_batch per generation loop: TalkerGenerator.GenerateBatch's per-job state (TalkerGenerator.cs:322-455) in
+// device memory, one slot per job, so that a step sends only logits and reads only ids.
+struct vw_batch {
+    vw_handle* h = nullptr;
+    vw::BatchDevice d{};
+    double* d_uniforms = nullptr;   // [n_slots] the step's draws
+    void* mem = nullptr;            // one allocation for every array
+    int32_t vocab = 0, sup_lo = 0, sup_hi = 0, min_new = 0;
+};
+
+namespace {
+
+// System.Random(int seed)'s initial state: the published subtractive generator (Knuth, TAOCP Vol. 2 3.2.2;
+// Numerical Recipes ran3) with .NET's modulus 2^31 - 1, table spread in steps of 21 and four warm-up rounds.  C#
+// int arithmetic wraps, hence the unsigned differences.
+void dotnet_seed(int32_t seed, vw::DotNetRngState* g) {
+    constexpr int32_t kMBig = 2147483647, kMSeed = 161803398;
+    auto sub = [](int32_t a, int32_t b) {
+        return static_cast<int32_t>(static_cast<uint32_t>(a) - static_cast<uint32_t>(b));
+    };
+    const int32_t subtraction = seed == INT32_MIN ? kMBig : (seed < 0 ? -seed : seed);
+    int32_t mj = sub(kMSeed, subtraction);
+    g->seed[0] = 0;
+    g->seed[55] = mj;
+    int32_t mk = 1;
+    for (int i = 1; i < 55; ++i) {
+        const int ii = (21 * i) % 55;
+        g->seed[ii] = mk;
+        mk = sub(mj, mk);
+        if (mk < 0) mk += kMBig;
+        mj = g->seed[ii];
+    }
+    for (int k = 1; k < 5; ++k)
+        for (int i = 1; i < 56; ++i) {
+            int32_t v = sub(g->seed[i], g->seed[1 + (i + 30) % 55]);
+            if (v < 0) v += kMBig;
+            g->seed[i] = v;
+        }
+    g->inext = 0;
+    g->inextp = 21;
+}
+
+vw_status batch_check(vw_batch* b, const vw_options* options, int32_t n_options) {
+    if (!b || !b->h) return VW_ERR_INVALID_ARG;
+    b->h->last_error.clear();
+    if (!options || n_options < 1 || n_options > vw::kInlineOptions)
+        return fail(b->h, VW_ERR_INVALID_ARG, "batch steps take 1.." + std::to_string(vw::kInlineOptions) + " options");
+    return VW_OK;
+}
+
+std::vector<vw::DevOptions> dev_options(const vw_options* options, int32_t n) {
+    std::vector<vw::DevOptions> o(static_cast<size_t>(n));
+    std::memcpy(o.data(), options, sizeof(vw_options) * n);
+    return o;
+}
+
+// A talker or sub-talker step: draws, samples every slot (finished ones get id -1), commits talker ids.
+vw_status batch_step(vw_batch* b, int which, const void* logits, int64_t row_stride, int32_t vocab, int32_t dtype,
+                     const vw_options* options, int32_t n_options, int32_t* out_ids, int32_t* out_done,
+                     void* stream) {
+    vw_status r = batch_check(b, options, n_options);
+    if (r != VW_OK) return r;
+    vw_handle* h = b->h;
+    if (!logits || !out_ids) return fail(h, VW_ERR_INVALID_ARG, "logits and out_ids are required");
+    DeviceGuard guard(h->device);
+    if (!guard.ok()) return fail(h, VW_ERR_CUDA, "cudaSetDevice failed");
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+    const std::vector<vw::DevOptions> o = dev_options(options, n_options);
+    cudaError_t e = vw::launch_batch_draw(b->d, which, o.data(), n_options, b->d_uniforms, st);
+    if (e != cudaSuccess) return cuda_fail(h, e, "batch draw");
+    vw_segment sg;
+    std::memset(&sg, 0, sizeof sg);
+    sg.logits = logits;
+    sg.row_stride = row_stride;
+    sg.n_rows = b->d.n_slots;
+    sg.vocab = vocab;
+    sg.dtype = dtype;
+    sg.kind = which == 0 ? VW_ROWS_TALKER : VW_ROWS_SUB;
+    sg.opt_index = which == 0 ? b->d.opt_talker : b->d.opt_sub;
+    sg.uniforms = b->d_uniforms;
+    sg.out_ids = out_ids;
+    SegExtra ex{nullptr, 0, b->d.active};
+    if (which == 0) {
+        sg.hist_ids = b->d.history;
+        sg.steps = b->d.step;
+        sg.suppress_lo = b->sup_lo;
+        sg.suppress_hi = b->sup_hi;
+        sg.eos_id = b->d.eos;
+        sg.min_new_tokens = b->min_new;
+        sg.max_hist_len = b->d.max_history;
+        ex.hist_lens = b->d.hist_len;
+        ex.hist_stride = b->d.max_history;
+    }
+    r = sample_impl(h, &sg, 1, options, n_options, VW_MEM_DEVICE, st, &ex);
+    if (r != VW_OK) return r;
+    if (which == 0) {
+        e = vw::launch_batch_commit(b->d, out_ids, out_done, st);
+        if (e != cudaSuccess) return cuda_fail(h, e, "batch commit");
+    }
+    if (!stream) return read_device_error(h, st);
+    return VW_OK;
+}
+
+}  // namespace
+
+VW_EXPORT vw_status vw_batch_create(vw_handle* h, int32_t n_slots, int32_t vocab, int32_t max_history,
+                                    int32_t eos_id, int32_t min_new_tokens, int32_t suppress_lo, int32_t suppress_hi,
+                                    vw_batch** out) {
+    if (!h || !out) return VW_ERR_INVALID_ARG;
+    *out = nullptr;
+    h->last_error.clear();
+    if (n_slots < 1 || vocab < 1 || max_history < 1)
+        return fail(h, VW_ERR_INVALID_ARG, "n_slots, vocab and max_history must be >= 1");
+    DeviceGuard guard(h->device);
+    if (!guard.ok()) return fail(h, VW_ERR_CUDA, "cudaSetDevice failed");
+    vw_batch* b = new (std::nothrow) vw_batch;
+    if (!b) return fail(h, VW_ERR_CUDA, "out of host memory");
+    b->h = h;
+    b->vocab = vocab;
+    b->sup_lo = suppress_lo;
+    b->sup_hi = suppress_hi;
+    b->min_new = min_new_tokens;
+    const size_t n = static_cast<size_t>(n_slots);
+    const size_t hist = round_up(n * static_cast<size_t>(max_history) * 4, 256);
+    const size_t ints = round_up(n * 4, 256);
+    const size_t rng = round_up(n * sizeof(vw::DotNetRngState), 256);
+    const size_t total = hist + 6 * ints + 2 * rng + round_up(n * 8, 256);
+    cudaError_t e = cudaMalloc(&b->mem, total);
+    if (e == cudaSuccess) e = cudaMemset(b->mem, 0, total);
+    if (e != cudaSuccess) {
+        delete b;
+        return cuda_fail(h, e, "batch state");
+    }
+    char* p = static_cast<char*>(b->mem);
+    auto take = [&](size_t bytes) {
+        char* q = p;
+        p += bytes;
+        return q;
+    };
+    b->d.n_slots = n_slots;
+    b->d.max_history = max_history;
+    b->d.eos = eos_id;
+    b->d.history = reinterpret_cast<int32_t*>(take(hist));
+    b->d.hist_len = reinterpret_cast<int32_t*>(take(ints));
+    b->d.step = reinterpret_cast<int32_t*>(take(ints));
+    b->d.active = reinterpret_cast<int32_t*>(take(ints));
+    b->d.max_new = reinterpret_cast<int32_t*>(take(ints));
+    b->d.opt_talker = reinterpret_cast<int32_t*>(take(ints));
+    b->d.opt_sub = reinterpret_cast<int32_t*>(take(ints));
+    b->d.rng_talker = reinterpret_cast<vw::DotNetRngState*>(take(rng));
+    b->d.rng_sub = reinterpret_cast<vw::DotNetRngState*>(take(rng));
+    b->d_uniforms = reinterpret_cast<double*>(take(round_up(n * 8, 256)));
+    *out = b;
+    return VW_OK;
+}
+
+VW_EXPORT vw_status vw_batch_destroy(vw_batch* b) {
+    if (!b) return VW_OK;
+    if (b->h) {
+        DeviceGuard guard(b->h->device);
+        cudaStreamSynchronize(b->h->stream);
+        if (b->mem) cudaFree(b->mem);
+    }
+    delete b;
+    return VW_OK;
+}
+
+VW_EXPORT vw_status vw_batch_start(vw_batch* b, int32_t slot, const vw_slot_config* cfg, const int32_t* history,
+                                   int32_t history_len) {
+    if (!b || !b->h) return VW_ERR_INVALID_ARG;
+    vw_handle* h = b->h;
+    h->last_error.clear();
+    if (!cfg || slot < 0 || slot >= b->d.n_slots) return fail(h, VW_ERR_INVALID_ARG, "bad slot or config");
+    if (history_len < 0 || (history_len > 0 && !history)) return fail(h, VW_ERR_INVALID_ARG, "bad history");
+    if (cfg->max_new_tokens < 1) return fail(h, VW_ERR_INVALID_ARG, "max_new_tokens must be >= 1");
+    if (static_cast<int64_t>(history_len) + cfg->max_new_tokens > b->d.max_history)
+        return fail(h, VW_ERR_INVALID_ARG, "history_len + max_new_tokens exceeds the batch's max_history");
+    for (int32_t i = 0; i < history_len; ++i)
+        if (history[i] < 0 || history[i] >= b->vocab) return fail(h, VW_ERR_OUT_OF_RANGE, "history id outside [0, vocab)");
+    DeviceGuard guard(h->device);
+    if (!guard.ok()) return fail(h, VW_ERR_CUDA, "cudaSetDevice failed");
+    // Sampler(Seed) and Sampler(Seed + 1) (TalkerGenerator.cs:345-346); an unseeded job takes a host-drawn seed
+    // (the reference's unseeded Random is not reproducible either)
+    int32_t seed = cfg->seed;
+    if (!cfg->seeded) {
+        static std::mutex mu;
+        static uint64_t x = 0x9e3779b97f4a7c15ull;
+        std::lock_guard<std::mutex> lock(mu);
+        x ^= static_cast<uint64_t>(std::chrono::high_resolution_clock::now().time_since_epoch().count());
+        x = x * 6364136223846793005ull + 1442695040888963407ull;
+        seed = static_cast<int32_t>(x >> 33);
+    }
+    vw::DotNetRngState g[2];
+    dotnet_seed(seed, &g[0]);
+    dotnet_seed(static_cast<int32_t>(static_cast<uint32_t>(seed) + 1u), &g[1]);
+    const int32_t words[6] = {history_len, 0, 1, cfg->max_new_tokens, cfg->talker_option, cfg->sub_option};
+    int32_t* dst[6] = {b->d.hist_len, b->d.step, b->d.active, b->d.max_new, b->d.opt_talker, b->d.opt_sub};
+    cudaStream_t st = h->stream;
+    cudaError_t e = cudaSuccess;
+    for (int k = 0; k < 6 && e == cudaSuccess; ++k)
+        e = cudaMemcpyAsync(dst[k] + slot, &words[k], 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(b->d.rng_talker + slot, &g[0], sizeof g[0], cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(b->d.rng_sub + slot, &g[1], sizeof g[1], cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess && history_len > 0)
+        e = cudaMemcpyAsync(b->d.history + static_cast<int64_t>(slot) * b->d.max_history, history,
+                            static_cast<size_t>(history_len) * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_fail(h, e, "vw_batch_start");
+    return VW_OK;
+}
+
+VW_EXPORT vw_status vw_batch_stop(vw_batch* b, int32_t slot) {
+    if (!b || !b->h) return VW_ERR_INVALID_ARG;
+    if (slot < 0 || slot >= b->d.n_slots) return fail(b->h, VW_ERR_INVALID_ARG, "bad slot");
+    DeviceGuard guard(b->h->device);
+    const int32_t zero = 0;
+    cudaError_t e = cudaMemcpyAsync(b->d.active + slot, &zero, 4, cudaMemcpyHostToDevice, b->h->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(b->h->stream);
+    if (e != cudaSuccess) return cuda_fail(b->h, e, "vw_batch_stop");
+    return VW_OK;
+}
+
+VW_EXPORT vw_status vw_batch_talker_step(vw_batch* b, const void* logits, int64_t row_stride, int32_t dtype,
+                                         const vw_options* options, int32_t n_options, int32_t* out_ids,
+                                         int32_t* out_done, void* stream) {
+    return batch_step(b, 0, logits, row_stride, b ? b->vocab : 0, dtype, options, n_options, out_ids, out_done,
+                      stream);
+}
+
+VW_EXPORT vw_status vw_batch_sub_step(vw_batch* b, const void* logits, int64_t row_stride, int32_t vocab,
+                                      int32_t dtype, const vw_options* options, int32_t n_options, int32_t* out_ids,
+                                      void* stream) {
+    return batch_step(b, 1, logits, row_stride, vocab, dtype, options, n_options, out_ids, nullptr, stream);
+}
+
+VW_EXPORT vw_status vw_batch_query(vw_batch* b, int32_t slot, int32_t* step, int32_t* history_len, int32_t* active) {
+    if (!b || !b->h) return VW_ERR_INVALID_ARG;
+    if (slot < 0 || slot >= b->d.n_slots) return fail(b->h, VW_ERR_INVALID_ARG, "bad slot");
+    DeviceGuard guard(b->h->device);
+    int32_t v[3] = {0, 0, 0};
+    cudaError_t e = cudaStreamSynchronize(b->h->stream);
+    if (e == cudaSuccess) e = cudaMemcpy(&v[0], b->d.step + slot, 4, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(&v[1], b->d.hist_len + slot, 4, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(&v[2], b->d.active + slot, 4, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(b->h, e, "vw_batch_query");
+    if (step) *step = v[0];
+    if (history_len) *history_len = v[1];
+    if (active) *active = v[2];
     return VW_OK;
 }
 

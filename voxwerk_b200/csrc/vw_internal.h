@@ -75,10 +75,51 @@ struct DevSegment {
     int32_t va, c0, vc, eosv, spec_a, spec_b;
     int32_t cpl_a, cpl_c; // vectors per lane of parts A and C (lane l takes the contiguous vectors l * cpl ...)
     int32_t rw_ok;        // rows of this segment fit the warp-per-row kernel (aligned, <= 32 vectors per lane)
+    // ---- device-resident batches (vw_batch_*): histories in place, inactive rows skipped
+    const int32_t* hist_lens;   // non-null: row r's history is hist_ids[r * hist_stride, + hist_lens[r]) (no CSR)
+    int64_t hist_stride;
+    const int32_t* active;      // non-null: rows with active[r] == 0 are not sampled (their id is -1)
 };
 
 // Fills the warp-per-row layout fields of a segment whose other fields are set.
 void fill_row_layout(DevSegment& d);
+
+// Row r's history span [hb, he) in hist_ids: CSR offsets, or the strided layout of a device-resident batch.
+__host__ __device__ inline bool row_history(const DevSegment& sg, int local, int64_t& hb, int64_t& he) {
+    if (sg.kind != 0) return false;
+    if (sg.hist_lens) {
+        hb = static_cast<int64_t>(local) * sg.hist_stride;
+        he = hb + sg.hist_lens[local];
+        return true;
+    }
+    if (!sg.hist_offsets) return false;
+    hb = sg.hist_offsets[local];
+    he = sg.hist_offsets[local + 1];
+    return true;
+}
+
+// ---- device-resident generation state (vw_batch.cu)
+struct DotNetRngState {        // System.Random(int): the subtractive generator's table and its two indices
+    int32_t seed[56];
+    int32_t inext, inextp;
+};
+struct BatchDevice {
+    int32_t n_slots, max_history, eos;
+    int32_t* history;          // [n_slots, max_history] the talker ids generated so far (Active.History)
+    int32_t* hist_len;         // [n_slots]
+    int32_t* step;             // [n_slots] Active.Step
+    int32_t* active;           // [n_slots] 1 while the slot's job runs
+    int32_t* max_new;          // [n_slots] GenerationOptions.MaxNewTokens
+    int32_t* opt_talker;       // [n_slots] the slot's index into each talker step's options table
+    int32_t* opt_sub;          // [n_slots] ... into each sub-talker step's options table
+    DotNetRngState* rng_talker;   // [n_slots] Sampler(Seed)
+    DotNetRngState* rng_sub;      // [n_slots] Sampler(Seed + 1)
+};
+// One NextDouble() into uniforms[s] for every active slot whose option samples (which: 0 talker, 1 sub-talker).
+cudaError_t launch_batch_draw(const BatchDevice& b, int which, const DevOptions* opts, int n_opts, double* uniforms,
+                              cudaStream_t stream);
+// Appends ids[s] to every active slot's history, then retires the slot (EOS or last step) or advances its step.
+cudaError_t launch_batch_commit(const BatchDevice& b, const int32_t* ids, int32_t* out_done, cudaStream_t stream);
 
 struct LaunchParams {
     DevSegment seg[kMaxSegments];

@@ -707,7 +707,7 @@ __device__ void rw_prefetch_row(const LaunchParams& p, int row, int lane) {
     if (lane == 0 && sg.eosv >= 0) prefetch_l2(base + sg.eosv * 16);
     if (lane == 1 && sg.opt_index) prefetch_l2(sg.opt_index + local);
     if (lane == 2 && sg.uniforms) prefetch_l2(sg.uniforms + local);
-    if (lane == 3 && sg.kind == 0 && sg.hist_offsets) prefetch_l2(sg.hist_offsets + local);
+    if (lane == 3 && sg.kind == 0 && sg.hist_offsets && !sg.hist_lens) prefetch_l2(sg.hist_offsets + local);
     if (lane == 4 && sg.kind == 0 && sg.steps) prefetch_l2(sg.steps + local);
 }
 
@@ -756,14 +756,21 @@ __global__ void __launch_bounds__(kRwWarps * 32, 7) row_warp_kernel(const __grid
             if (row >= p.seg[i].row_begin) s = i;
         const DevSegment& sg = p.seg[s];
         const int local = row - sg.row_begin;
-        const bool talker_hist = sg.kind == 0 && sg.hist_offsets;
         // the row's own words, one lane each
         long long w = 0;
         if (lane == 0) w = sg.opt_index ? sg.opt_index[local] : 0;
         if (lane == 1) w = (sg.kind == 0 && sg.steps) ? sg.steps[local] : 0x7fffffff;
         if (lane == 2) w = sg.uniforms ? __double_as_longlong(sg.uniforms[local]) : 0;
-        if (lane == 3 && talker_hist) w = sg.hist_offsets[local];
-        if (lane == 4 && talker_hist) w = sg.hist_offsets[local + 1];
+        if (lane == 3 || lane == 4) {
+            int64_t b0 = 0, b1 = 0;
+            row_history(sg, local, b0, b1);
+            w = lane == 3 ? b0 : b1;
+        }
+        if (lane == 5) w = sg.active ? sg.active[local] : 1;
+        if (__shfl_sync(kFull, w, 5) == 0) {   // a device-resident batch's finished slot: no sample
+            if (lane == 0) sg.out_ids[local] = -1;
+            continue;
+        }
         const int opt = static_cast<int>(__shfl_sync(kFull, w, 0));
         const int step = static_cast<int>(__shfl_sync(kFull, w, 1));
         const double uniform = __longlong_as_double(__shfl_sync(kFull, w, 2));

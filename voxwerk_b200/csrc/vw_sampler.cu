@@ -1262,13 +1262,10 @@ __device__ RowMeta plan_row(const LaunchParams& p, int r, uint32_t& bytes, int& 
     m.step = sg.steps ? sg.steps[local] : 0x7fffffff;
     m.uniform = sg.uniforms ? sg.uniforms[local] : 0.0;
     int64_t hb = 0, he = 0;
-    if (sg.kind == 0 && sg.hist_offsets) {
-        hb = sg.hist_offsets[local];
-        he = sg.hist_offsets[local + 1];
-        if (hb < 0 || he < hb) {   // device-memory offsets are checked here: report, and read no history
-            atomicOr(p.err, kErrHistOffsets);
-            hb = he = 0;
-        }
+    if (row_history(sg, local, hb, he) && (hb < 0 || he < hb)) {
+        // device-memory offsets are checked here: report, and read no history
+        atomicOr(p.err, kErrHistOffsets);
+        hb = he = 0;
     }
     m.opt_ok = (opt_raw >= 0 && opt_raw < p.n_opts) ? 1 : 0;
     if (m.opt_ok) {
