@@ -13,8 +13,11 @@ no step reads another step's data from L2); K steps captured in one CUDA graph a
 launching stream.  e2e: the same metric through the public C-ABI call with host buffers (pinned host -> device
 copies of logits, histories and uniforms, and the ids back) inside the timed region.  cpu_baseline: the CPU
 restatement of voxwerk's Sampler (oracle/, "port": the C# reference cannot run here) on a bounded sample.
+`e2e_resident`: the same step through the device-resident batch API (vw_batch_*), where histories and samplers
+stay on the GPU and a step copies in only the logit columns the sampler reads.
 `parity`: every row of the timed batch against that restatement, with flips counted and attributed.
-At N = 1 `configs` holds the other four configurations (µs per call, rows/s, roofline fraction, parity).
+At N = 1 `configs` holds the other four configurations (µs per call, rows/s, roofline fraction, parity), and
+`frame_embedding` the next-input gather (vw_frame_embedding) for 1024 sequences.
 `--impl reference` times only the CPU implementation, with every host thread, and prints its own line; that
 process loads no GPU library of this repository.
 """
@@ -39,7 +42,7 @@ PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 TRAFFIC_PATH = os.path.join(ROOT, "profiles", "traffic.json")
 FALLBACK_HBM_GBS = 6650.0
 N_COPIES = 3
-LAUNCHES_PER_CALL = 2   # the candidate kernel and the whole-row kernel
+LAUNCHES_PER_CALL = 2   # the warp-per-row kernel and the whole-row kernel
 
 
 def host_threads() -> int:
@@ -264,6 +267,81 @@ def roofline(w, ms_per_step, peak, peak_kind):
             "peak_kind": peak_kind, "algorithmic_bytes_per_launch": alg}
 
 
+def e2e_resident(dev, w, steps, torch, barrier, rank):
+    """The talker step through the device-resident batch API (vw_batch_*): each slot keeps its history and its
+    sampler on the device, so a step copies in only the logit columns the sampler reads (pinned host -> device, one
+    2D copy) and copies the ids back.  Rows/s counts the slots sampled (every slot runs for the whole test)."""
+    from cuda.bindings import runtime as cudart
+    from voxwerk_b200 import DeviceBatchState, GenerationOptions, SamplingOptions
+    seg = w.segments[0]
+    n, V = seg.n_rows, seg.vocab
+    o = w.options[0]
+    hist = seg.hist_offsets
+    state = DeviceBatchState(dev, n, max_history=int(np.max(np.diff(hist))) + steps + 16, vocab=V)
+    for r in range(n):
+        job = GenerationOptions(seed=1000 * rank + r, max_new_tokens=steps + 8, repetition_penalty=o[4],
+                                talker=SamplingOptions(bool(o[0]), int(o[1]), float(o[2]), float(o[3])))
+        state.start(r, job, seg.hist_ids[hist[r]:hist[r + 1]].tolist())
+    lg = np.ascontiguousarray(seg.logits).copy()
+    lg[:, seg.eos_id] = -np.inf                  # keep every slot running for the whole measurement
+    cols = (seg.eos_id // 4 + 1) * 4             # the sampler reads [0, 2048) and the EOS vector: columns [0, 2152)
+    host = torch.from_numpy(np.ascontiguousarray(lg[:, :cols])).pin_memory()
+    dlog = torch.empty((n, V), dtype=torch.float32, device="cuda")
+    ids_host = torch.empty(n, dtype=torch.int32).pin_memory()
+    st = torch.cuda.Stream()
+
+    def step():
+        cudart.cudaMemcpy2DAsync(dlog.data_ptr(), V * 4, host.data_ptr(), cols * 4, cols * 4, n,
+                                 cudart.cudaMemcpyKind.cudaMemcpyHostToDevice, st.cuda_stream)
+        ids, _ = state.talker_step(dlog, stream=st.cuda_stream)
+        with torch.cuda.stream(st):
+            ids_host.copy_(ids, non_blocking=True)
+        st.synchronize()
+
+    for _ in range(2):
+        step()
+    if barrier:
+        barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    el = time.perf_counter() - t0
+    sampled = int((ids_host.numpy() >= 0).sum())
+    state.close()
+    return el, sampled, n * cols * 4, n * 4
+
+
+def frame_embedding_timing(dev, torch, peak, peak_kind, rows=1024, reps=50):
+    """vw_frame_embedding on `rows` sequences (config 3's stream count): Qwen3-TTS sizes (hidden 1024, 3072 + 15 x
+    2048 embedding rows), random codes and tables, CUDA events over `reps` calls."""
+    from voxwerk_b200 import frame_embedding
+    H, G = 1024, 16
+    g = torch.Generator(device="cuda").manual_seed(5)
+    codec = torch.randint(-20000, 20000, (3072, H), dtype=torch.int16, device="cuda", generator=g)
+    cps = [torch.randint(-20000, 20000, (2048, H), dtype=torch.int16, device="cuda", generator=g) for _ in range(G - 1)]
+    codes = torch.cat([torch.randint(0, 3072, (rows, 1), device="cuda", generator=g),
+                       torch.randint(0, 2048, (rows, G - 1), device="cuda", generator=g)], 1).to(torch.int32)
+    text = torch.randn((rows, H), device="cuda", generator=g)
+    out = torch.empty((rows, H), device="cuda")
+    st = torch.cuda.Stream()
+    for _ in range(3):
+        frame_embedding(dev, codes, codec, cps, text, out, stream=st.cuda_stream)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(st):
+        ev0.record(st)
+        for _ in range(reps):
+            frame_embedding(dev, codes, codec, cps, text, out, stream=st.cuda_stream)
+        ev1.record(st)
+    ev1.synchronize()
+    dev.synchronize(st.cuda_stream)
+    us = 1e3 * ev0.elapsed_time(ev1) / reps
+    alg = rows * (G * H * 2 + 2 * H * 4)   # the gathered bf16 rows, the text row in, the fp32 row out
+    achieved = alg / (us * 1e-6) / 1e9
+    return {"rows": rows, "hidden": H, "groups": G, "us_per_call": us,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_kind": peak_kind, "algorithmic_bytes_per_launch": alg}}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -347,6 +425,17 @@ def main():
     e2e_value = w.n_rows * world * args.e2e_steps / max_over_ranks(e2e_s, device="cuda")
     del host_arrays, hsegs
 
+    # ---- e2e through the device-resident batch API (histories and samplers stay on the GPU)
+    resident = None
+    if len(w.segments) == 1 and w.segments[0].kind == 0:
+        el, sampled, h2d_r, d2h_r = e2e_resident(dev, w, args.e2e_steps, torch, barrier, rank)
+        el_max = max_over_ranks(el, device="cuda")
+        sampled_all = int(sum_over_ranks(sampled, device="cuda"))
+        resident = {"value": sampled_all * args.e2e_steps / el_max, "unit": "rows/s", "h2d_bytes_per_step": h2d_r,
+                    "d2h_bytes_per_step": d2h_r, "steps": args.e2e_steps,
+                    "path": "vw_batch_talker_step: logits columns [0, 2152) copied from pinned host memory each step "
+                            "(one 2D copy), ids copied back; histories, steps and samplers stay on the device"}
+
     # ---- N > 1: config 2's one batch split over the ranks (strong scaling), and config 3 sharded by cost
     strong = cfg3 = None
     if world > 1 and not args.no_extra:
@@ -389,6 +478,8 @@ def main():
                                 "roofline": roofline(wc, per, peak, peak_kind), "parity": pc, "clocks": ck,
                                 "rows_by_path": pth}
 
+    gather = frame_embedding_timing(dev, torch, peak, peak_kind) if world == 1 and not args.no_extra else None
+
     line = None
     if rank == 0:
         need = w.needed_bytes()
@@ -410,11 +501,11 @@ def main():
         rl = roofline(w, ms_per_step, peak, peak_kind)
         rl.update({"traffic": traffic,
                    "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one full-size "
-                                     "candidate-kernel launch, read from profiles/traffic.json (not measured in "
+                                     "warp-per-row kernel launch, read from profiles/traffic.json (not measured in "
                                      "this run)",
                    "needed_bytes_per_launch": need,
                    "frac_of_needed_bytes": need / (ms_per_step * 1e-3) / 1e9 / peak,
-                   "kernel": "cand_kernel (the step: candidate kernel + whole-row kernel launch, CUDA events)"})
+                   "kernel": "row_warp_kernel (the step: warp-per-row kernel + whole-row kernel launch, CUDA events)"})
         line = {
             "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
@@ -425,6 +516,7 @@ def main():
                     "steps": args.e2e_steps,
                     "path": "vw_sample(VW_MEM_HOST) from pinned host buffers: logits (without the suppressed "
                             "span's columns), histories, steps, options, uniforms in; ids out"},
+            "e2e_resident": resident,
             "cpu_baseline": cpu,
             "clocks": clocks,
             "gpu_launches": LAUNCHES_PER_CALL * args.steps,
@@ -437,6 +529,8 @@ def main():
             line["cfg3_sharded"] = cfg3
         if configs is not None:
             line["configs"] = configs
+        if gather is not None:
+            line["frame_embedding"] = gather
         print(json.dumps(line), flush=True)
     dev.close()
     if world > 1:

@@ -234,6 +234,25 @@ vw_status vw_batch_sub_step(vw_batch* batch, const void* logits, int64_t row_str
 vw_status vw_batch_query(vw_batch* batch, int32_t slot, int32_t* step, int32_t* history_len, int32_t* active);
 
 /*
+ * The next talker input of n_rows sequences once their frames are sampled (TalkerGenerator.cs:428-439):
+ *   out[r] = FrameEmbedding(codes[r]) + text[r]     (TalkerModel.cs:114-118, TalkerGenerator.cs:437-438)
+ * i.e. the bf16 row codes[r][0] of the talker codec embedding widened to fp32, plus for g = 1..n_groups-1 the row
+ * codes[r][g] of code-predictor embedding g-1, plus the text row, each addition rounded once in that order, so the
+ * result equals the reference's bit for bit.
+ * codes: [n_rows, n_groups] int32 (n_groups <= 16; voxwerk: 16); a row whose codes[r][0] is -1 (a finished slot of
+ *   vw_batch_talker_step) is skipped and its output left as it was.
+ * codec_embedding: [vocab, hidden] bf16 bits; cp_embeddings: host array of n_groups-1 device pointers, each
+ *   [cp_vocab, hidden] bf16 bits (voxwerk: 3072 / 2048 ids, hidden 1024, a multiple of 8 here).
+ * text: [n_rows, hidden] fp32 (the step's trailing text row or tts_pad per sequence), or NULL to add nothing.
+ * out: [n_rows, hidden] fp32.  Device memory, 16-byte aligned.  A code outside its codebook returns
+ * VW_ERR_OUT_OF_RANGE (the reference throws, TalkerModel.cs:99, :106).  stream as in vw_sample.
+ */
+vw_status vw_frame_embedding(vw_handle* handle, const int32_t* codes, int32_t n_rows, int32_t n_groups,
+                             int32_t hidden, const uint16_t* codec_embedding, int32_t vocab,
+                             const uint16_t* const* cp_embeddings, int32_t cp_vocab, const float* text, float* out,
+                             void* stream);
+
+/*
  * Single-row mirrors of the reference's Sampler methods, for callers that keep the reference's call shape.
  * Pointers follow `mem`; the calls are synchronous.
  */

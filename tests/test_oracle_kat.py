@@ -259,3 +259,21 @@ def test_oracle_talker_row_matches_python_restatement(seed):
         row = pyref.suppress(row, lo, hi, eos, step)
         exp_id, _ = pyref.select(row, o[0], o[1], o[2], o[3], r)
         assert got == exp_id, (seed, case)
+
+
+def test_frame_embedding_restatement_known_answer():
+    """The gather restatement on a hand-checked row: bf16 bits widened exactly, fp32 adds in codebook order."""
+    from oracle.embedding import bf16_to_f32, frame_embedding
+    codec = np.array([[0x3F80, 0x4000], [0x3F00, 0xBF80]], dtype=np.uint16)      # rows (1, 2), (0.5, -1)
+    cp = [np.array([[0x3E80, 0x3F80]], dtype=np.uint16)]                           # row (0.25, 1)
+    codes = np.array([[1, 0], [-1, 0]], dtype=np.int32)
+    text = np.array([[1.0, 2.0], [7.0, 7.0]], dtype=np.float32)
+    out = frame_embedding(codes, codec, cp, text)
+    np.testing.assert_array_equal(out[0], np.array([0.5 + 0.25 + 1.0, -1.0 + 1.0 + 2.0], dtype=np.float32))
+    assert np.isnan(out[1]).all()
+    # the order of the fp32 additions is the reference's: 1 + 2^-24 + 2^-24 rounds to 1 in that order
+    big = np.array([[0x3F80]], dtype=np.uint16)
+    tiny = (np.array([2.0 ** -24], dtype=np.float32).view(np.uint32) >> 16).astype(np.uint16)
+    assert bf16_to_f32(tiny)[0] == np.float32(2.0 ** -24)
+    o = frame_embedding(np.array([[0, 0, 0]], np.int32), big, [tiny[None, :], tiny[None, :]], None)
+    assert o[0, 0] == np.float32(1.0)

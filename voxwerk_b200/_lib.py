@@ -49,6 +49,7 @@ EXPORTED = (
     "vw_batch_talker_step",
     "vw_batch_sub_step",
     "vw_batch_query",
+    "vw_frame_embedding",
 )
 
 
@@ -178,7 +179,8 @@ def _load() -> ctypes.CDLL:
                        ("vw_batch_stop", [vp, i32]),
                        ("vw_batch_talker_step", [vp, vp, i64, i32, ctypes.POINTER(VwOptions), i32, vp, vp, vp]),
                        ("vw_batch_sub_step", [vp, vp, i64, i32, i32, ctypes.POINTER(VwOptions), i32, vp, vp]),
-                       ("vw_batch_query", [vp, i32, vp, vp, vp])):
+                       ("vw_batch_query", [vp, i32, vp, vp, vp]),
+                       ("vw_frame_embedding", [vp, vp, i32, i32, i32, vp, i32, vp, i32, vp, vp, vp])):
         getattr(lib, name).restype = ctypes.c_int
         getattr(lib, name).argtypes = args
     return lib

@@ -372,6 +372,7 @@ vw_status read_device_error(vw_handle* h, cudaStream_t st) {
     if (bits & vw::kErrHistRange) return fail(h, VW_ERR_OUT_OF_RANGE, "a history id is outside [0, vocab)");
     if (bits & vw::kErrBadOption) return fail(h, VW_ERR_INVALID_ARG, "a row's opt_index is outside the options table");
     if (bits & vw::kErrHistOffsets) return fail(h, VW_ERR_INVALID_ARG, "hist_offsets are negative or decrease");
+    if (bits & vw::kErrCodeRange) return fail(h, VW_ERR_OUT_OF_RANGE, "a frame code is outside its codebook");
     return VW_OK;
 }
 
@@ -913,6 +914,37 @@ VW_EXPORT vw_status vw_batch_query(vw_batch* b, int32_t slot, int32_t* step, int
     if (step) *step = v[0];
     if (history_len) *history_len = v[1];
     if (active) *active = v[2];
+    return VW_OK;
+}
+
+VW_EXPORT vw_status vw_frame_embedding(vw_handle* h, const int32_t* codes, int32_t n_rows, int32_t n_groups,
+                                       int32_t hidden, const uint16_t* codec_embedding, int32_t vocab,
+                                       const uint16_t* const* cp_embeddings, int32_t cp_vocab, const float* text,
+                                       float* out, void* stream) {
+    if (!h) return VW_ERR_INVALID_ARG;
+    h->last_error.clear();
+    if (n_rows < 0 || n_groups < 1 || n_groups > vw::kMaxCodeGroups)
+        return fail(h, VW_ERR_INVALID_ARG, "n_rows >= 0 and 1 <= n_groups <= 16 are required");
+    if (hidden < 8 || hidden % 8 != 0) return fail(h, VW_ERR_INVALID_ARG, "hidden must be a positive multiple of 8");
+    if (vocab < 1 || (n_groups > 1 && cp_vocab < 1)) return fail(h, VW_ERR_INVALID_ARG, "vocab sizes must be >= 1");
+    if (n_rows == 0) return VW_OK;
+    const uint16_t* tables[vw::kMaxCodeGroups] = {codec_embedding};
+    if (n_groups > 1 && !cp_embeddings) return fail(h, VW_ERR_INVALID_ARG, "cp_embeddings is required");
+    for (int g = 1; g < n_groups; ++g) tables[g] = cp_embeddings[g - 1];
+    for (int g = 0; g < n_groups; ++g)
+        if (!tables[g] || !aligned(tables[g], 16))
+            return fail(h, VW_ERR_INVALID_ARG, "embedding tables must be non-NULL and 16-byte aligned");
+    if (!codes || !aligned(codes, 4) || !out || !aligned(out, 16) || (text && !aligned(text, 16)))
+        return fail(h, VW_ERR_INVALID_ARG, "codes, text and out must be aligned device arrays");
+    DeviceGuard guard(h->device);
+    if (!guard.ok()) return fail(h, VW_ERR_CUDA, "cudaSetDevice failed");
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+    cudaError_t e = stream ? cudaSuccess : cudaMemsetAsync(h->d_err, 0, sizeof(unsigned), st);
+    if (e == cudaSuccess)
+        e = vw::launch_frame_embedding(codes, n_rows, n_groups, hidden, tables, vocab, cp_vocab, text, out, h->d_err,
+                                       st);
+    if (e != cudaSuccess) return cuda_fail(h, e, "frame embedding");
+    if (!stream) return read_device_error(h, st);
     return VW_OK;
 }
 

@@ -39,7 +39,15 @@ enum : unsigned {
     kErrTimeout = 2u,     // an mbarrier wait gave up
     kErrBadOption = 4u,   // a row's option index outside the table
     kErrHistOffsets = 8u, // a row's history offsets negative or decreasing (the row is sampled without history)
+    kErrCodeRange = 16u,  // a frame code outside its codebook (vw_frame_embedding; the row is not written)
 };
+
+constexpr int kMaxCodeGroups = 16;     // codebooks per frame (Qwen3TtsConfig.NumCodeGroups)
+
+// The next talker input of n_rows sequences: sum of the frame's codebook embeddings plus the text row (vw_embed.cu).
+cudaError_t launch_frame_embedding(const int32_t* codes, int n_rows, int n_groups, int hidden,
+                                   const uint16_t* const* tables, int vocab, int cp_vocab, const float* text,
+                                   float* out, unsigned* err, cudaStream_t stream);
 
 struct DevOptions {       // same layout as vw_options
     int32_t do_sample;

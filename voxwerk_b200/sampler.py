@@ -364,3 +364,24 @@ class TalkerBatchSampler:
         """Active.Step++ for the jobs that produced a frame (TalkerGenerator.cs:440)."""
         for j in active:
             self.step[j] += 1
+
+
+def frame_embedding(device: Device, codes, codec_embedding, cp_embeddings: Sequence, text, out,
+                    stream: Optional[int] = None) -> None:
+    """vw_frame_embedding: out = FrameEmbedding(codes) + text (TalkerModel.cs:114-118, TalkerGenerator.cs:437-438).
+
+    CUDA tensors: codes [n, G] int32, codec_embedding [V, H] and each of cp_embeddings [CV, H] as bf16 (or int16 /
+    uint16 bits), text [n, H] float32 or None, out [n, H] float32.  Rows whose codes[r, 0] is -1 are left alone.
+    """
+    for t in [codes, codec_embedding, out, *cp_embeddings] + ([text] if text is not None else []):
+        if not _is_torch_cuda(t):
+            raise TypeError("frame_embedding takes CUDA tensors")
+    n, groups = int(codes.shape[0]), int(codes.shape[1])
+    ptrs = (ctypes.c_void_p * max(len(cp_embeddings), 1))(*[t.data_ptr() for t in cp_embeddings])
+    check(lib.vw_frame_embedding(device.handle, ctypes.c_void_p(codes.data_ptr()), n, groups,
+                                 int(codec_embedding.shape[1]), ctypes.c_void_p(codec_embedding.data_ptr()),
+                                 int(codec_embedding.shape[0]), ptrs,
+                                 int(cp_embeddings[0].shape[0]) if cp_embeddings else 0,
+                                 ctypes.c_void_p(text.data_ptr()) if text is not None else None,
+                                 ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(stream) if stream else None),
+          device.handle)
