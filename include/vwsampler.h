@@ -253,6 +253,22 @@ vw_status vw_frame_embedding(vw_handle* handle, const int32_t* codes, int32_t n_
                              void* stream);
 
 /*
+ * The vocabulary head and the sampler in one call: logits = hidden x weight^T (TalkerModel.CodecHead,
+ * TalkerModel.cs:133, or CodePredictorHead, :136-137) on the tcgen05 tensor cores (bf16 inputs, fp32 accumulation and
+ * output), then vw_sample over those logits, stream-ordered (the sampler reads the logits while they are in L2).
+ * hidden: [segment->n_rows, hidden_size] bf16 (row pitch hidden_stride elements); weight: [segment->vocab,
+ * hidden_size] bf16 (pitch weight_stride); both device memory, 16-byte aligned, sizes and pitches multiples of 8.
+ * segment: the rows as in vw_sample (histories, steps, mask, opt_index, uniforms, out_ids, out_probs); its logits,
+ *   row_stride and dtype are ignored.  vocab must be a multiple of 4.
+ * out_logits: optional [n_rows, vocab] fp32 that receives the GEMM's logits; NULL keeps them in a buffer of the
+ *   handle.  The ids equal the reference sampler's on these logits; the logits themselves are a bf16 GEMM's (the
+ *   reference's CPU GEMM sums in its own order).  Device memory; stream as in vw_sample.
+ */
+vw_status vw_head_sample(vw_handle* handle, const void* hidden, int64_t hidden_stride, int32_t hidden_size,
+                         const void* weight, int64_t weight_stride, const vw_segment* segment,
+                         const vw_options* options, int32_t n_options, float* out_logits, void* stream);
+
+/*
  * Single-row mirrors of the reference's Sampler methods, for callers that keep the reference's call shape.
  * Pointers follow `mem`; the calls are synchronous.
  */

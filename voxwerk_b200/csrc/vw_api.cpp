@@ -31,6 +31,8 @@ struct vw_handle {
     char* d_scratch = nullptr;      // general-path scratch, one slice per CTA
     size_t scratch_bytes = 0;
     char* d_stage = nullptr;        // VW_MEM_HOST: device copies of the caller's arrays
+    char* d_logits = nullptr;       // vw_head_sample: the GEMM's logits when the caller keeps none
+    size_t logits_bytes = 0;
     int32_t* d_defer = nullptr;     // four counters + the rows the warp-per-row kernel defers
     size_t defer_cap = 0;
     size_t stage_bytes = 0;
@@ -618,6 +620,7 @@ VW_EXPORT vw_status vw_destroy(vw_handle* h) {
         if (h->stream) cudaStreamSynchronize(h->stream);
         if (h->d_scratch) cudaFree(h->d_scratch);
         if (h->d_stage) cudaFree(h->d_stage);
+        if (h->d_logits) cudaFree(h->d_logits);
         if (h->d_opts) cudaFree(h->d_opts);
         if (h->h_opts) cudaFreeHost(h->h_opts);
         if (h->d_err) cudaFree(h->d_err);
@@ -944,6 +947,46 @@ VW_EXPORT vw_status vw_frame_embedding(vw_handle* h, const int32_t* codes, int32
         e = vw::launch_frame_embedding(codes, n_rows, n_groups, hidden, tables, vocab, cp_vocab, text, out, h->d_err,
                                        st);
     if (e != cudaSuccess) return cuda_fail(h, e, "frame embedding");
+    if (!stream) return read_device_error(h, st);
+    return VW_OK;
+}
+
+VW_EXPORT vw_status vw_head_sample(vw_handle* h, const void* hidden, int64_t hidden_stride, int32_t hidden_size,
+                                   const void* weight, int64_t weight_stride, const vw_segment* segment,
+                                   const vw_options* options, int32_t n_options, float* out_logits, void* stream) {
+    if (!h) return VW_ERR_INVALID_ARG;
+    h->last_error.clear();
+    if (!segment) return fail(h, VW_ERR_INVALID_ARG, "segment is required");
+    if (!hidden || !weight || hidden_size < 8 || hidden_size % 8 != 0 || hidden_stride < hidden_size ||
+        weight_stride < hidden_size || hidden_stride % 8 != 0 || weight_stride % 8 != 0 || !aligned(hidden, 16) ||
+        !aligned(weight, 16))
+        return fail(h, VW_ERR_INVALID_ARG,
+                    "hidden / weight: 16-byte aligned bf16 rows, hidden_size and strides multiples of 8");
+    vw_segment sg = *segment;
+    if (sg.vocab < 4 || sg.vocab % 4 != 0) return fail(h, VW_ERR_INVALID_ARG, "vocab must be a multiple of 4");
+    if (sg.n_rows < 0) return fail(h, VW_ERR_INVALID_ARG, "n_rows < 0");
+    if (sg.n_rows == 0) return VW_OK;
+    if (out_logits && !aligned(out_logits, 16)) return fail(h, VW_ERR_INVALID_ARG, "out_logits misaligned");
+    DeviceGuard guard(h->device);
+    if (!guard.ok()) return fail(h, VW_ERR_CUDA, "cudaSetDevice failed");
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+    float* logits = out_logits;
+    if (!logits) {
+        vw_status r = grow(h, &h->d_logits, &h->logits_bytes, static_cast<size_t>(sg.n_rows) * sg.vocab * 4,
+                           "logits buffer");
+        if (r != VW_OK) return r;
+        logits = reinterpret_cast<float*>(h->d_logits);
+    }
+    cudaError_t e = stream ? cudaSuccess : cudaMemsetAsync(h->d_err, 0, sizeof(unsigned), st);
+    if (e == cudaSuccess)
+        e = vw::launch_head_gemm(hidden, hidden_stride, weight, weight_stride, sg.n_rows, sg.vocab, hidden_size,
+                                 logits, sg.vocab, h->d_err, st);
+    if (e != cudaSuccess) return cuda_fail(h, e, "head GEMM");
+    sg.logits = logits;
+    sg.row_stride = sg.vocab;
+    sg.dtype = VW_F32;
+    vw_status r = sample_impl(h, &sg, 1, options, n_options, VW_MEM_DEVICE, st);
+    if (r != VW_OK) return r;
     if (!stream) return read_device_error(h, st);
     return VW_OK;
 }

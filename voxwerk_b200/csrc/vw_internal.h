@@ -201,6 +201,11 @@ cudaError_t static_scratch_address(char** ptr);
 cudaError_t launch_exp_diagnostic(const double* x, int64_t n, double* y_libm, double* y_cuda, int sm_count,
                                   cudaStream_t stream);
 
+// logits[M, N] (fp32, row pitch ldo) = A[M, K] x B[N, K]^T, A and B bf16 row-major (pitches lda, ldb elements,
+// multiples of 8), on the tcgen05 tensor cores (vw_head.cu).  err collects kErrTimeout.
+cudaError_t launch_head_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, int M, int N, int K, float* out,
+                             int64_t ldo, unsigned* err, cudaStream_t stream);
+
 // Sampler.ApplyRepetitionPenalty on one device row, in place.
 cudaError_t launch_apply_penalty(float* logits, int vocab, const int32_t* hist, int64_t hist_len, float penalty,
                                  unsigned* err, cudaStream_t stream);

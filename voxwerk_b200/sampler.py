@@ -172,8 +172,9 @@ class Segment:
     max_hist_len: int = 0
     out_probs: object = None
 
-    def to_c(self, mem: int) -> VwSegment:
-        shape = tuple(self.logits.shape)
+    def to_c(self, mem: int, shape: Optional[tuple] = None) -> VwSegment:
+        """The C struct; `shape` stands in for logits.shape when the logits come from vw_head_sample's GEMM."""
+        shape = tuple(self.logits.shape) if shape is None else tuple(shape)
         if len(shape) != 2:
             raise ValueError("logits must be 2-D [n_rows, row_stride]")
         n_rows, stride = int(shape[0]), int(shape[1])
@@ -183,8 +184,9 @@ class Segment:
             hi = vocab if self.suppress_hi is None else int(self.suppress_hi)
         else:
             lo = hi = 0
+        dtype = VW_F32 if self.logits is None else _dtype_code(self.logits)
         return VwSegment(
-            _ptr(self.logits, mem), stride, n_rows, vocab, _dtype_code(self.logits), int(self.kind),
+            _ptr(self.logits, mem), stride, n_rows, vocab, dtype, int(self.kind),
             _ptr(self.hist_offsets, mem), _ptr(self.hist_ids, mem), _ptr(self.steps, mem), lo, hi,
             int(self.eos_id), int(self.min_new_tokens), int(self.max_hist_len), _ptr(self.opt_index, mem),
             _ptr(self.uniforms, mem), _ptr(self.out_ids, mem), _ptr(self.out_probs, mem))
@@ -385,3 +387,32 @@ def frame_embedding(device: Device, codes, codec_embedding, cp_embeddings: Seque
                                  ctypes.c_void_p(text.data_ptr()) if text is not None else None,
                                  ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(stream) if stream else None),
           device.handle)
+
+
+def head_sample(device: Device, hidden, weight, segment: Segment, options: Sequence[VwOptions], out_logits=None,
+                stream: Optional[int] = None) -> None:
+    """vw_head_sample: logits = hidden x weight^T on the tensor cores (TalkerModel.CodecHead / CodePredictorHead,
+    TalkerModel.cs:133-137), then the sampler over them; ids land in ``segment.out_ids``.
+
+    CUDA tensors: hidden [n, H] and weight [V, H] bf16 (or raw int16 / uint16 bf16 bits), H a multiple of 8, V a
+    multiple of 4; ``segment`` carries the rows' histories, steps, options, uniforms and outputs (its ``logits`` is
+    ignored and may be None); ``out_logits`` [n, V] float32 optionally receives the GEMM's logits.
+    """
+    for t in [hidden, weight] + ([out_logits] if out_logits is not None else []):
+        if not _is_torch_cuda(t):
+            raise TypeError("head_sample takes CUDA tensors")
+    if hidden.dim() != 2 or weight.dim() != 2 or hidden.shape[1] != weight.shape[1]:
+        raise ValueError("hidden [n, H] and weight [V, H] must share H")
+    if hidden.stride(1) != 1 or weight.stride(1) != 1:
+        raise ValueError("hidden and weight rows must be contiguous")
+    n, v = int(hidden.shape[0]), int(weight.shape[0])
+    if out_logits is not None and (tuple(out_logits.shape) != (n, v) or not out_logits.is_contiguous()
+                                   or str(out_logits.dtype) != "torch.float32"):
+        raise ValueError("out_logits must be a contiguous float32 [n, V] tensor")
+    seg = segment.to_c(VW_MEM_DEVICE, shape=(n, v))
+    opts = (VwOptions * len(options))(*options)
+    check(lib.vw_head_sample(device.handle, ctypes.c_void_p(hidden.data_ptr()), int(hidden.stride(0)),
+                             int(hidden.shape[1]), ctypes.c_void_p(weight.data_ptr()), int(weight.stride(0)),
+                             ctypes.byref(seg), opts, len(options),
+                             ctypes.c_void_p(out_logits.data_ptr()) if out_logits is not None else None,
+                             ctypes.c_void_p(stream) if stream else None), device.handle)
