@@ -17,7 +17,8 @@ restatement of voxwerk's Sampler (oracle/, "port": the C# reference cannot run h
 stay on the GPU and a step copies in only the logit columns the sampler reads.
 `parity`: every row of the timed batch against that restatement, with flips counted and attributed.
 At N = 1 `configs` holds the other four configurations (µs per call, rows/s, roofline fraction, parity), and
-`frame_embedding` the next-input gather (vw_frame_embedding) for 1024 sequences.
+`frame_embedding` the next-input gather (vw_frame_embedding) for 1024 sequences, and `head` the vocabulary head
+(vw_head_logits, the tcgen05 GEMM; vw_head_sample, GEMM + sampler) against cuBLAS (+ vw_sample).
 `--impl reference` times only the CPU implementation, with every host thread, and prints its own line; that
 process loads no GPU library of this repository.
 """
@@ -41,6 +42,7 @@ METRIC = "sampled rows/s & HBM GB/s (B=4096,V=3072 talker step) at 1/2/4/8 B200"
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 TRAFFIC_PATH = os.path.join(ROOT, "profiles", "traffic.json")
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
 N_COPIES = 3
 LAUNCHES_PER_CALL = 2   # the warp-per-row kernel and the whole-row kernel
 
@@ -311,9 +313,38 @@ def e2e_resident(dev, w, steps, torch, barrier, rank):
     return el, sampled, n * cols * 4, n * 4
 
 
+def graph_us(torch, st, fn, reps):
+    """µs per call of fn(stream handle): `reps` calls captured in one CUDA graph (no host overhead in the timed
+    region), replayed untimed for at least 50 ms (so the SM clock has left its idle level), then the median of three
+    timed replays (CUDA events on the launching stream)."""
+    with torch.cuda.stream(st):
+        for _ in range(3):
+            fn(st.cuda_stream)
+    st.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=st):
+        for _ in range(reps):
+            fn(torch.cuda.current_stream().cuda_stream)
+    t_end = time.perf_counter() + 0.05
+    while time.perf_counter() < t_end:
+        graph.replay()
+        st.synchronize()
+    times = []
+    for _ in range(3):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(st):
+            e0.record(st)
+            graph.replay()
+            e1.record(st)
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+    del graph
+    return 1e3 * float(np.median(times)) / reps
+
+
 def frame_embedding_timing(dev, torch, peak, peak_kind, rows=1024, reps=50):
     """vw_frame_embedding on `rows` sequences (config 3's stream count): Qwen3-TTS sizes (hidden 1024, 3072 + 15 x
-    2048 embedding rows), random codes and tables, CUDA events over `reps` calls."""
+    2048 embedding rows), random codes and tables, `reps` calls in a CUDA graph (graph_us)."""
     from voxwerk_b200 import frame_embedding
     H, G = 1024, 16
     g = torch.Generator(device="cuda").manual_seed(5)
@@ -324,22 +355,96 @@ def frame_embedding_timing(dev, torch, peak, peak_kind, rows=1024, reps=50):
     text = torch.randn((rows, H), device="cuda", generator=g)
     out = torch.empty((rows, H), device="cuda")
     st = torch.cuda.Stream()
-    for _ in range(3):
-        frame_embedding(dev, codes, codec, cps, text, out, stream=st.cuda_stream)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(st):
-        ev0.record(st)
-        for _ in range(reps):
-            frame_embedding(dev, codes, codec, cps, text, out, stream=st.cuda_stream)
-        ev1.record(st)
-    ev1.synchronize()
+    us = graph_us(torch, st, lambda sp: frame_embedding(dev, codes, codec, cps, text, out, stream=sp), reps)
     dev.synchronize(st.cuda_stream)
-    us = 1e3 * ev0.elapsed_time(ev1) / reps
     alg = rows * (G * H * 2 + 2 * H * 4)   # the gathered bf16 rows, the text row in, the fp32 row out
     achieved = alg / (us * 1e-6) / 1e9
     return {"rows": rows, "hidden": H, "groups": G, "us_per_call": us,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": peak_kind, "algorithmic_bytes_per_launch": alg}}
+
+
+def tensor_peak():
+    try:
+        with open(PEAKS_PATH) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return FALLBACK_BF16_TFLOPS, "fallback"
+
+
+def head_timing(dev, torch, hbm, hbm_kind, reps=50, cases=((64, 3072), (1024, 3072), (4096, 3072), (1024, 2048))):
+    """The vocabulary head (hidden 1024) ahead of the sampler: vw_head_logits (tcgen05 GEMM) against cuBLAS
+    (torch.mm, bf16 in, fp32 out), and vw_head_sample (GEMM + sampler in one call) against cuBLAS followed by
+    vw_sample on its logits.  Talker rows (V 3072) carry config 2's histories and options; sub rows (V 2048) config
+    1's options.  CUDA events over `reps` calls on one stream; the weight (6 MB) stays in L2 between calls, as it
+    does between a model's steps."""
+    from tests.gpu_util import make_segment, options_table, to_device
+    from voxwerk_b200 import head_logits, head_sample, sample_rows
+    from voxwerk_b200 import workloads
+    tflops, t_kind = tensor_peak()
+    H = 1024
+    st = torch.cuda.Stream()
+    out = {}
+    for rows, V in cases:
+        w = workloads.make(2, rows) if V == 3072 else workloads.make(1)
+        sd = w.segments[0]
+        if sd.n_rows != rows:   # sub rows: config 1's options over `rows` rows with fresh draws
+            sd = workloads.SegData(np.zeros((rows, V), np.float32), workloads.F32, workloads.SUB, V,
+                                   np.random.default_rng(7).random(rows), np.zeros(rows, np.int32))
+        opts = options_table(w)
+        g = torch.Generator(device="cuda").manual_seed(rows + V)
+        hidden = torch.randn((rows, H), device="cuda", generator=g).to(torch.bfloat16)
+        weight = (torch.randn((V, H), device="cuda", generator=g) * 0.125).to(torch.bfloat16)
+        logits = torch.empty((rows, V), dtype=torch.float32, device="cuda")
+        arr = to_device(sd, torch)
+        arr["logits"] = None
+        seg_head = make_segment(sd, arr)
+        arr2 = dict(arr)
+        arr2["logits"] = logits
+        seg_lib = make_segment(sd, arr2)
+
+        def cublas(sp):
+            torch.mm(hidden, weight.t(), out_dtype=torch.float32, out=logits)
+
+        def lib_then_sample(sp):
+            cublas(sp)
+            sample_rows(dev, [seg_lib], opts, stream=sp)
+
+        def timed(fn):
+            return graph_us(torch, st, fn, reps)
+
+        def try_timed(fn):
+            try:
+                return timed(fn)
+            except Exception as e:   # torch without mm(out_dtype=...): no cuBLAS fp32-output baseline
+                return f"unavailable: {type(e).__name__}: {str(e)[:120]}"
+
+        t_ours = timed(lambda sp: head_logits(dev, hidden, weight, logits, stream=sp))
+        t_fused = timed(lambda sp: head_sample(dev, hidden, weight, seg_head, opts, stream=sp))
+        t_lib = try_timed(cublas)
+        t_lib_sample = try_timed(lib_then_sample)
+        head_logits(dev, hidden, weight, logits, stream=st.cuda_stream)
+        dev.synchronize(st.cuda_stream)
+        dev.stats(reset=True)
+        t_sample = timed(lambda sp: sample_rows(dev, [seg_lib], opts, stream=sp))
+        dev.synchronize(st.cuda_stream)
+        paths = dev.stats(reset=True)
+        s = st.cuda_stream
+        dev.synchronize(s)
+        flops = 2.0 * rows * V * H
+        alg = V * H * 2 + rows * H * 2 + rows * V * 4
+        t_flop, t_byte = flops / (tflops * 1e12), alg / (hbm * 1e9)
+        bound = "tensor" if t_flop >= t_byte else "hbm"
+        floor_us = 1e6 * max(t_flop, t_byte)
+        out[f"{rows}x{V}x{H}"] = {
+            "us_head_logits": t_ours, "us_cublas_mm": t_lib, "us_head_sample": t_fused,
+            "us_cublas_then_vw_sample": t_lib_sample, "us_vw_sample_on_head_logits": t_sample,
+            "sampler_rows_by_path": paths,
+            "roofline": {"bound": bound, "floor_us": floor_us, "frac": floor_us / t_ours,
+                         "achieved_tflops": flops / (t_ours * 1e-6) / 1e12, "tflops_peak": tflops,
+                         "tflops_peak_kind": t_kind, "achieved_gbs": alg / (t_ours * 1e-6) / 1e9, "hbm_peak": hbm,
+                         "hbm_peak_kind": hbm_kind, "algorithmic_bytes": alg, "flops": flops}}
+    return out
 
 
 def main():
@@ -479,6 +584,11 @@ def main():
                                 "rows_by_path": pth}
 
     gather = frame_embedding_timing(dev, torch, peak, peak_kind) if world == 1 and not args.no_extra else None
+    head = None
+    if world == 1 and not args.no_extra:
+        with ClockSampler(local) as cs:
+            head = head_timing(dev, torch, peak, peak_kind)
+        head["clocks"] = cs.summary()
 
     line = None
     if rank == 0:
@@ -531,6 +641,8 @@ def main():
             line["configs"] = configs
         if gather is not None:
             line["frame_embedding"] = gather
+        if head is not None:
+            line["head"] = head
         print(json.dumps(line), flush=True)
     dev.close()
     if world > 1:

@@ -253,6 +253,15 @@ vw_status vw_frame_embedding(vw_handle* handle, const int32_t* codes, int32_t n_
                              void* stream);
 
 /*
+ * The vocabulary head alone: out_logits[n_rows, vocab] (fp32, row pitch vocab) = hidden x weight^T -- the logits
+ * TalkerModel.CodecHead (TalkerModel.cs:133) and CodePredictorHead (:136-137) produce -- on the tcgen05 tensor cores
+ * (bf16 inputs, fp32 accumulation).  Operand rules as in vw_head_sample; out_logits 16-byte aligned device memory.
+ */
+vw_status vw_head_logits(vw_handle* handle, const void* hidden, int64_t hidden_stride, int32_t hidden_size,
+                         const void* weight, int64_t weight_stride, int32_t n_rows, int32_t vocab, float* out_logits,
+                         void* stream);
+
+/*
  * The vocabulary head and the sampler in one call: logits = hidden x weight^T (TalkerModel.CodecHead,
  * TalkerModel.cs:133, or CodePredictorHead, :136-137) on the tcgen05 tensor cores (bf16 inputs, fp32 accumulation and
  * output), then vw_sample over those logits, stream-ordered (the sampler reads the logits while they are in L2).

@@ -40,11 +40,14 @@ def _check_gemm(torch, hidden, weight, got):
     return worst
 
 
+# tile widths the host picks for these shapes: 32 (rows 1 .. 257), 64 (300), 96 (386), 128 (519), 192 (771),
+# 256 (1156, 4096); 4096 x 3072 and 8192 x 2048 give each persistent CTA several tiles (both accumulators reused)
 @pytest.mark.parametrize("n,V,H", [(1, 3072, 1024), (64, 3072, 1024), (130, 2048, 1024), (257, 1000, 1000),
-                                   (16, 3072, 2048), (300, 3072, 1024)])
+                                   (16, 3072, 2048), (300, 3072, 1024), (386, 3072, 1024), (519, 3072, 1024),
+                                   (771, 3072, 1024), (1156, 3072, 1024), (4096, 3072, 1024), (8192, 2048, 1024)])
 def test_head_gemm_matches_float64(device, n, V, H):
     import torch
-    from voxwerk_b200 import SamplingOptions, Segment, head_sample, vw_options
+    from voxwerk_b200 import SamplingOptions, Segment, head_logits, head_sample, vw_options
     hidden, weight = _operands(torch, n, V, H, seed=n * 7 + V)
     logits = torch.full((n, V), float("nan"), dtype=torch.float32, device="cuda")
     seg = Segment(None, kind=workloads.SUB, vocab=V, out_ids=torch.full((n,), -1, dtype=torch.int32, device="cuda"),
@@ -53,6 +56,9 @@ def test_head_gemm_matches_float64(device, n, V, H):
     head_sample(device, hidden, weight, seg, [vw_options(SamplingOptions.greedy())], out_logits=logits)
     assert not bool(torch.isnan(logits).any()), "the GEMM left logits unwritten"
     worst = _check_gemm(torch, hidden, weight, logits)
+    alone = torch.full((n, V), float("nan"), dtype=torch.float32, device="cuda")
+    head_logits(device, hidden, weight, alone)          # the GEMM-only entry writes the same logits
+    assert torch.equal(alone.view(torch.int32), logits.view(torch.int32))
     REPORT.append(f"head GEMM {n}x{V}x{H}: max error {worst:.2e} of sum|a*b|")
     # greedy ids are the argmax of the GEMM's logits (Sampler.ArgMax: first maximum)
     np.testing.assert_array_equal(seg.out_ids.cpu().numpy(), logits.cpu().numpy().argmax(axis=1))

@@ -20,7 +20,7 @@ _NATIVE = {
     **{n: "._lib" for n in ("VW_BF16", "VW_F32", "VW_MEM_DEVICE", "VW_MEM_HOST", "VW_ROWS_SUB", "VW_ROWS_TALKER",
                             "VwError", "VwInvalidArgument", "VwOutOfRange")},
     **{n: ".sampler" for n in ("Device", "GenerationOptions", "Sampler", "SamplingOptions", "Segment",
-                               "TalkerBatchSampler", "frame_embedding", "head_sample", "sample_rows", "sample_rows_static",
+                               "TalkerBatchSampler", "frame_embedding", "head_logits", "head_sample", "sample_rows", "sample_rows_static",
                                "vw_options")},
     **{n: ".batch_state" for n in ("DeviceBatchState",)},
 }

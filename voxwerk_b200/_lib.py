@@ -50,6 +50,7 @@ EXPORTED = (
     "vw_batch_sub_step",
     "vw_batch_query",
     "vw_frame_embedding",
+    "vw_head_logits",
     "vw_head_sample",
 )
 
@@ -182,6 +183,7 @@ def _load() -> ctypes.CDLL:
                        ("vw_batch_sub_step", [vp, vp, i64, i32, i32, ctypes.POINTER(VwOptions), i32, vp, vp]),
                        ("vw_batch_query", [vp, i32, vp, vp, vp]),
                        ("vw_frame_embedding", [vp, vp, i32, i32, i32, vp, i32, vp, i32, vp, vp, vp]),
+                       ("vw_head_logits", [vp, vp, i64, i32, vp, i64, i32, i32, vp, vp]),
                        ("vw_head_sample", [vp, vp, i64, i32, vp, i64, ctypes.POINTER(VwSegment),
                                            ctypes.POINTER(VwOptions), i32, vp, vp])):
         getattr(lib, name).restype = ctypes.c_int

@@ -951,19 +951,49 @@ VW_EXPORT vw_status vw_frame_embedding(vw_handle* h, const int32_t* codes, int32
     return VW_OK;
 }
 
+// hidden / weight checks shared by vw_head_logits and vw_head_sample
+static vw_status check_head_operands(vw_handle* h, const void* hidden, int64_t hidden_stride, int32_t hidden_size,
+                                     const void* weight, int64_t weight_stride, int32_t vocab) {
+    if (!hidden || !weight || hidden_size < 8 || hidden_size % 8 != 0 || hidden_stride < hidden_size ||
+        weight_stride < hidden_size || hidden_stride % 8 != 0 || weight_stride % 8 != 0 || !aligned(hidden, 16) ||
+        !aligned(weight, 16))
+        return fail(h, VW_ERR_INVALID_ARG,
+                    "hidden / weight: 16-byte aligned bf16 rows, hidden_size and strides multiples of 8");
+    if (vocab < 4 || vocab % 4 != 0) return fail(h, VW_ERR_INVALID_ARG, "vocab must be a multiple of 4");
+    return VW_OK;
+}
+
+VW_EXPORT vw_status vw_head_logits(vw_handle* h, const void* hidden, int64_t hidden_stride, int32_t hidden_size,
+                                   const void* weight, int64_t weight_stride, int32_t n_rows, int32_t vocab,
+                                   float* out_logits, void* stream) {
+    if (!h) return VW_ERR_INVALID_ARG;
+    h->last_error.clear();
+    vw_status r = check_head_operands(h, hidden, hidden_stride, hidden_size, weight, weight_stride, vocab);
+    if (r != VW_OK) return r;
+    if (n_rows < 0) return fail(h, VW_ERR_INVALID_ARG, "n_rows < 0");
+    if (!out_logits || !aligned(out_logits, 16)) return fail(h, VW_ERR_INVALID_ARG, "out_logits: 16-byte aligned");
+    if (n_rows == 0) return VW_OK;
+    DeviceGuard guard(h->device);
+    if (!guard.ok()) return fail(h, VW_ERR_CUDA, "cudaSetDevice failed");
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+    cudaError_t e = stream ? cudaSuccess : cudaMemsetAsync(h->d_err, 0, sizeof(unsigned), st);
+    if (e == cudaSuccess)
+        e = vw::launch_head_gemm(hidden, hidden_stride, weight, weight_stride, n_rows, vocab, hidden_size, out_logits,
+                                 vocab, h->d_err, st);
+    if (e != cudaSuccess) return cuda_fail(h, e, "head GEMM");
+    if (!stream) return read_device_error(h, st);
+    return VW_OK;
+}
+
 VW_EXPORT vw_status vw_head_sample(vw_handle* h, const void* hidden, int64_t hidden_stride, int32_t hidden_size,
                                    const void* weight, int64_t weight_stride, const vw_segment* segment,
                                    const vw_options* options, int32_t n_options, float* out_logits, void* stream) {
     if (!h) return VW_ERR_INVALID_ARG;
     h->last_error.clear();
     if (!segment) return fail(h, VW_ERR_INVALID_ARG, "segment is required");
-    if (!hidden || !weight || hidden_size < 8 || hidden_size % 8 != 0 || hidden_stride < hidden_size ||
-        weight_stride < hidden_size || hidden_stride % 8 != 0 || weight_stride % 8 != 0 || !aligned(hidden, 16) ||
-        !aligned(weight, 16))
-        return fail(h, VW_ERR_INVALID_ARG,
-                    "hidden / weight: 16-byte aligned bf16 rows, hidden_size and strides multiples of 8");
     vw_segment sg = *segment;
-    if (sg.vocab < 4 || sg.vocab % 4 != 0) return fail(h, VW_ERR_INVALID_ARG, "vocab must be a multiple of 4");
+    vw_status r = check_head_operands(h, hidden, hidden_stride, hidden_size, weight, weight_stride, sg.vocab);
+    if (r != VW_OK) return r;
     if (sg.n_rows < 0) return fail(h, VW_ERR_INVALID_ARG, "n_rows < 0");
     if (sg.n_rows == 0) return VW_OK;
     if (out_logits && !aligned(out_logits, 16)) return fail(h, VW_ERR_INVALID_ARG, "out_logits misaligned");
@@ -972,8 +1002,7 @@ VW_EXPORT vw_status vw_head_sample(vw_handle* h, const void* hidden, int64_t hid
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : h->stream;
     float* logits = out_logits;
     if (!logits) {
-        vw_status r = grow(h, &h->d_logits, &h->logits_bytes, static_cast<size_t>(sg.n_rows) * sg.vocab * 4,
-                           "logits buffer");
+        r = grow(h, &h->d_logits, &h->logits_bytes, static_cast<size_t>(sg.n_rows) * sg.vocab * 4, "logits buffer");
         if (r != VW_OK) return r;
         logits = reinterpret_cast<float*>(h->d_logits);
     }
@@ -985,7 +1014,7 @@ VW_EXPORT vw_status vw_head_sample(vw_handle* h, const void* hidden, int64_t hid
     sg.logits = logits;
     sg.row_stride = sg.vocab;
     sg.dtype = VW_F32;
-    vw_status r = sample_impl(h, &sg, 1, options, n_options, VW_MEM_DEVICE, st);
+    r = sample_impl(h, &sg, 1, options, n_options, VW_MEM_DEVICE, st);
     if (r != VW_OK) return r;
     if (!stream) return read_device_error(h, st);
     return VW_OK;

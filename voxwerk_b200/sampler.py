@@ -389,6 +389,30 @@ def frame_embedding(device: Device, codes, codec_embedding, cp_embeddings: Seque
           device.handle)
 
 
+def _head_operands(hidden, weight, *more) -> None:
+    for t in [hidden, weight, *[m for m in more if m is not None]]:
+        if not _is_torch_cuda(t):
+            raise TypeError("the head takes CUDA tensors")
+    if hidden.dim() != 2 or weight.dim() != 2 or hidden.shape[1] != weight.shape[1]:
+        raise ValueError("hidden [n, H] and weight [V, H] must share H")
+    if hidden.stride(1) != 1 or weight.stride(1) != 1:
+        raise ValueError("hidden and weight rows must be contiguous")
+
+
+def head_logits(device: Device, hidden, weight, out_logits, stream: Optional[int] = None) -> None:
+    """vw_head_logits: out_logits = hidden x weight^T (TalkerModel.CodecHead / CodePredictorHead, TalkerModel.cs:133-137)
+    on the tensor cores.  CUDA tensors: hidden [n, H], weight [V, H] bf16 (or int16 / uint16 bits), out_logits a
+    contiguous float32 [n, V]."""
+    _head_operands(hidden, weight, out_logits)
+    n, v = int(hidden.shape[0]), int(weight.shape[0])
+    if tuple(out_logits.shape) != (n, v) or not out_logits.is_contiguous() or str(out_logits.dtype) != "torch.float32":
+        raise ValueError("out_logits must be a contiguous float32 [n, V] tensor")
+    check(lib.vw_head_logits(device.handle, ctypes.c_void_p(hidden.data_ptr()), int(hidden.stride(0)),
+                             int(hidden.shape[1]), ctypes.c_void_p(weight.data_ptr()), int(weight.stride(0)), n, v,
+                             ctypes.c_void_p(out_logits.data_ptr()), ctypes.c_void_p(stream) if stream else None),
+          device.handle)
+
+
 def head_sample(device: Device, hidden, weight, segment: Segment, options: Sequence[VwOptions], out_logits=None,
                 stream: Optional[int] = None) -> None:
     """vw_head_sample: logits = hidden x weight^T on the tensor cores (TalkerModel.CodecHead / CodePredictorHead,
@@ -398,13 +422,7 @@ def head_sample(device: Device, hidden, weight, segment: Segment, options: Seque
     multiple of 4; ``segment`` carries the rows' histories, steps, options, uniforms and outputs (its ``logits`` is
     ignored and may be None); ``out_logits`` [n, V] float32 optionally receives the GEMM's logits.
     """
-    for t in [hidden, weight] + ([out_logits] if out_logits is not None else []):
-        if not _is_torch_cuda(t):
-            raise TypeError("head_sample takes CUDA tensors")
-    if hidden.dim() != 2 or weight.dim() != 2 or hidden.shape[1] != weight.shape[1]:
-        raise ValueError("hidden [n, H] and weight [V, H] must share H")
-    if hidden.stride(1) != 1 or weight.stride(1) != 1:
-        raise ValueError("hidden and weight rows must be contiguous")
+    _head_operands(hidden, weight, out_logits)
     n, v = int(hidden.shape[0]), int(weight.shape[0])
     if out_logits is not None and (tuple(out_logits.shape) != (n, v) or not out_logits.is_contiguous()
                                    or str(out_logits.dtype) != "torch.float32"):
