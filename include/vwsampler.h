@@ -205,6 +205,9 @@ typedef struct vw_slot_config {
  * 2, [2048, 3072)); max_history >= each job's initial history length + max_new_tokens. */
 vw_status vw_batch_create(vw_handle* handle, int32_t n_slots, int32_t vocab, int32_t max_history, int32_t eos_id,
                           int32_t min_new_tokens, int32_t suppress_lo, int32_t suppress_hi, vw_batch** out_batch);
+/* Frees the batch.  vw_destroy of its handle releases the device memory of every batch still alive on it; the
+ * caller then still calls vw_batch_destroy (which only frees the host object), and every other call on such a batch
+ * returns VW_ERR_INVALID_ARG. */
 vw_status vw_batch_destroy(vw_batch* batch);
 
 /* Starts a job in `slot` (the slot refill of TalkerGenerator.cs:336-358): step 0, running, the two samplers seeded,
@@ -232,6 +235,43 @@ vw_status vw_batch_sub_step(vw_batch* batch, const void* logits, int64_t row_str
 
 /* A slot's step, history length and running flag (after the steps enqueued so far; synchronizes). */
 vw_status vw_batch_query(vw_batch* batch, int32_t slot, int32_t* step, int32_t* history_len, int32_t* active);
+
+/*
+ * The per-frame loop of GenerateBatch (TalkerGenerator.cs:362-439) on the device, around the caller's transformer
+ * steps.  The batch keeps the frame being built, codes[n_slots][16] (keepFrames, :382, :420): a talker step records
+ * code 0 of every slot that goes on to the code predictor and -1 for the others (idle, or retired at this step by
+ * EOS or MaxNewTokens); sub-talker head step `group` records codebook `group`.  Per frame:
+ *   vw_batch_talker_head_step                 codebook 0 from the talker's last hidden rows      (:366-385, :443)
+ *   vw_batch_code_embedding(group 0)          CodecEmbedding(code0), the code predictor's 2nd input row (:411)
+ *   for group = 1..15:
+ *     vw_batch_sub_head_step(group)           CodePredictorHead(group) + SubSampler.Select          (:418-420)
+ *     vw_batch_code_embedding(group)          CodePredictorEmbedding(group, code), next input    (:422)
+ *   vw_batch_frame_embedding                  FrameEmbedding(frame) + text, the next talker input (:428-439)
+ * Head steps: hidden [n_slots, hidden_size] and weight [vocab, hidden_size] bf16 as in vw_head_logits (rows of
+ * idle slots are multiplied but not sampled); the logits live in a buffer of the batch.  The ids come out as in
+ * vw_batch_talker_step / vw_batch_sub_step (out_ids [n_slots], -1 for slots that did not sample).  All calls are
+ * stream-ordered and allocate nothing after a batch's first head step of the largest vocab, so a frame can be
+ * captured in a CUDA graph.
+ */
+vw_status vw_batch_talker_head_step(vw_batch* batch, const void* hidden, int64_t hidden_stride, int32_t hidden_size,
+                                    const void* weight, int64_t weight_stride, const vw_options* options,
+                                    int32_t n_options, int32_t* out_ids, int32_t* out_done, void* stream);
+vw_status vw_batch_sub_head_step(vw_batch* batch, int32_t group, const void* hidden, int64_t hidden_stride,
+                                 int32_t hidden_size, const void* weight, int64_t weight_stride, int32_t vocab,
+                                 const vw_options* options, int32_t n_options, int32_t* out_ids, void* stream);
+/* out[s] (row pitch out_stride floats) = bf16 -> fp32 of table row codes[s][group] for every slot whose frame goes
+ * on (codes[s][0] >= 0); other rows are left alone.  table: [table_rows, hidden] bf16 bits (group 0: the talker
+ * codec embedding, vocab rows; group g: code-predictor embedding g-1).  A code outside the table returns
+ * VW_ERR_OUT_OF_RANGE. */
+vw_status vw_batch_code_embedding(vw_batch* batch, int32_t group, const void* table, int32_t table_rows,
+                                  int32_t hidden, float* out, int64_t out_stride, void* stream);
+/* vw_frame_embedding over the batch's codes table (n_slots rows, 16 groups); slots with codes[s][0] == -1 are
+ * skipped. */
+vw_status vw_batch_frame_embedding(vw_batch* batch, int32_t hidden, const uint16_t* codec_embedding,
+                                   const uint16_t* const* cp_embeddings, int32_t cp_vocab, const float* text,
+                                   float* out, void* stream);
+/* Copies the codes table [n_slots, 16] int32 to host memory (after the handle's stream drains). */
+vw_status vw_batch_get_codes(vw_batch* batch, int32_t* out);
 
 /*
  * The next talker input of n_rows sequences once their frames are sampled (TalkerGenerator.cs:428-439):

@@ -52,6 +52,11 @@ EXPORTED = (
     "vw_frame_embedding",
     "vw_head_logits",
     "vw_head_sample",
+    "vw_batch_talker_head_step",
+    "vw_batch_sub_head_step",
+    "vw_batch_code_embedding",
+    "vw_batch_frame_embedding",
+    "vw_batch_get_codes",
 )
 
 
@@ -184,6 +189,13 @@ def _load() -> ctypes.CDLL:
                        ("vw_batch_query", [vp, i32, vp, vp, vp]),
                        ("vw_frame_embedding", [vp, vp, i32, i32, i32, vp, i32, vp, i32, vp, vp, vp]),
                        ("vw_head_logits", [vp, vp, i64, i32, vp, i64, i32, i32, vp, vp]),
+                       ("vw_batch_talker_head_step", [vp, vp, i64, i32, vp, i64, ctypes.POINTER(VwOptions), i32, vp,
+                                                      vp, vp]),
+                       ("vw_batch_sub_head_step", [vp, i32, vp, i64, i32, vp, i64, i32, ctypes.POINTER(VwOptions), i32,
+                                                   vp, vp]),
+                       ("vw_batch_code_embedding", [vp, i32, vp, i32, i32, vp, i64, vp]),
+                       ("vw_batch_frame_embedding", [vp, i32, vp, vp, i32, vp, vp, vp]),
+                       ("vw_batch_get_codes", [vp, vp]),
                        ("vw_head_sample", [vp, vp, i64, i32, vp, i64, ctypes.POINTER(VwSegment),
                                            ctypes.POINTER(VwOptions), i32, vp, vp])):
         getattr(lib, name).restype = ctypes.c_int

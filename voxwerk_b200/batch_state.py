@@ -8,6 +8,16 @@ A step then moves only logits in and ids out:
     ids, done = state.talker_step(talker_logits)             # :366-385, history append and retirement :374-380
     for g in range(1, 16): state.sub_step(cp_logits[g])      # :416-420
 
+or, with the vocabulary heads on the tensor cores and the frame kept on the device (hidden rows from the caller's
+transformer steps):
+
+    ids, done = state.talker_head_step(last_hidden, codec_head)          # :366-385 over CodecHead (:443)
+    state.code_embedding(0, codec_embedding, cp_input)                   # :411
+    for g in range(1, 16):
+        state.sub_head_step(g, cp_hidden, cp_heads[g - 1])               # :418-420
+        state.code_embedding(g, cp_embeddings[g - 1], cp_input)          # :422
+    state.frame_embedding(codec_embedding, cp_embeddings, text, step_input)   # :428-439
+
 Logits are CUDA tensors [n_slots, V] (row r belongs to slot r); ids and done flags come back as CUDA int32 tensors.
 Finished slots are not sampled (id -1).  Each step's options table is built from the jobs' options, so slots with
 different options share one call.
@@ -107,6 +117,60 @@ class DeviceBatchState:
                                     ctypes.c_void_p(self.sub_ids.data_ptr()),
                                     ctypes.c_void_p(stream) if stream else None), self.device.handle)
         return self.sub_ids
+
+    # ---- the frame loop around the caller's transformer steps (vw_batch_*_head_step, include/vwsampler.h)
+    def _head(self, hidden, weight):
+        for t in (hidden, weight):
+            if not t.is_cuda or t.dim() != 2 or t.stride(1) != 1:
+                raise ValueError("hidden and weight must be 2-D CUDA tensors with contiguous rows")
+        if hidden.shape[0] != self.n_slots or hidden.shape[1] != weight.shape[1]:
+            raise ValueError("hidden must be [n_slots, H] and weight [V, H]")
+        return (ctypes.c_void_p(hidden.data_ptr()), int(hidden.stride(0)), int(hidden.shape[1]),
+                ctypes.c_void_p(weight.data_ptr()), int(weight.stride(0)))
+
+    def talker_head_step(self, hidden, weight, stream: Optional[int] = None):
+        """Codebook 0 from the talker's last hidden rows: logits = hidden x weight^T (CodecHead,
+        TalkerGenerator.cs:443) on the tensor cores, then talker_step over them; (ids, done)."""
+        opts = (VwOptions * len(self._talker_opts))(*self._talker_opts)
+        check(lib.vw_batch_talker_head_step(self._b, *self._head(hidden, weight), opts, len(self._talker_opts),
+                                            ctypes.c_void_p(self.ids.data_ptr()),
+                                            ctypes.c_void_p(self.done.data_ptr()),
+                                            ctypes.c_void_p(stream) if stream else None), self.device.handle)
+        return self.ids, self.done
+
+    def sub_head_step(self, group: int, hidden, weight, stream: Optional[int] = None):
+        """Codebook `group` (1..15): CodePredictorHead(group) then SubSampler.Select (TalkerGenerator.cs:418-420);
+        the ids are also recorded in the batch's frame (codes())."""
+        opts = (VwOptions * len(self._sub_opts))(*self._sub_opts)
+        check(lib.vw_batch_sub_head_step(self._b, int(group), *self._head(hidden, weight), int(weight.shape[0]),
+                                         opts, len(self._sub_opts), ctypes.c_void_p(self.sub_ids.data_ptr()),
+                                         ctypes.c_void_p(stream) if stream else None), self.device.handle)
+        return self.sub_ids
+
+    def code_embedding(self, group: int, table, out, stream: Optional[int] = None) -> None:
+        """out[s] = table[codes[s][group]] widened to fp32 for every slot whose frame goes on (CodecEmbedding for
+        group 0, CodePredictorEmbedding for 1..15: TalkerGenerator.cs:411, :422).  table [rows, H] bf16 (or int16
+        bits), out [n_slots, H'] float32 with H' >= H."""
+        check(lib.vw_batch_code_embedding(self._b, int(group), ctypes.c_void_p(table.data_ptr()), int(table.shape[0]),
+                                          int(table.shape[1]), ctypes.c_void_p(out.data_ptr()), int(out.stride(0)),
+                                          ctypes.c_void_p(stream) if stream else None), self.device.handle)
+
+    def frame_embedding(self, codec_embedding, cp_embeddings, text, out, stream: Optional[int] = None) -> None:
+        """FrameEmbedding(frame) + text of every continuing slot (TalkerGenerator.cs:428-439) from the batch's frame."""
+        ptrs = (ctypes.c_void_p * len(cp_embeddings))(*[t.data_ptr() for t in cp_embeddings])
+        check(lib.vw_batch_frame_embedding(self._b, int(codec_embedding.shape[1]),
+                                           ctypes.c_void_p(codec_embedding.data_ptr()), ptrs,
+                                           int(cp_embeddings[0].shape[0]),
+                                           ctypes.c_void_p(text.data_ptr()) if text is not None else None,
+                                           ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(stream) if stream else None),
+              self.device.handle)
+
+    def codes(self):
+        """The frame being built, [n_slots, 16] int32 on the host (-1: not sampled / slot not continuing)."""
+        import numpy as np
+        out = np.empty((self.n_slots, 16), dtype=np.int32)
+        check(lib.vw_batch_get_codes(self._b, out.ctypes.data), self.device.handle)
+        return out
 
     def query(self, slot: int):
         """(step, history length, running) of `slot`."""

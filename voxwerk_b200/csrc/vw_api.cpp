@@ -45,8 +45,13 @@ struct vw_handle {
     int force_exact = 0;                     // VW_FORCE_EXACT at creation
     int test_stall_row = -1;                 // VW_TEST_STALL_ROW at creation (first vw_sample call only)
     unsigned long long h2d_bytes = 0;        // host -> device input bytes of VW_MEM_HOST calls (vw_stats.h2d_bytes)
+    std::vector<vw_batch*> batches;          // live batches created on this handle (released by vw_destroy)
     std::string last_error;
 };
+
+namespace {
+void orphan_batch(vw_batch* b);   // frees a batch's device memory and detaches it from its handle
+}  // namespace
 
 namespace vw {
 
@@ -618,6 +623,8 @@ VW_EXPORT vw_status vw_destroy(vw_handle* h) {
     {
         DeviceGuard guard(h->device);
         if (h->stream) cudaStreamSynchronize(h->stream);
+        for (vw_batch* b : h->batches) orphan_batch(b);   // the caller still owns (and destroys) the structs
+        h->batches.clear();
         if (h->d_scratch) cudaFree(h->d_scratch);
         if (h->d_stage) cudaFree(h->d_stage);
         if (h->d_logits) cudaFree(h->d_logits);
@@ -668,6 +675,18 @@ VW_EXPORT vw_status vw_get_stats(vw_handle* h, vw_stats* out, int32_t reset) {
     return VW_OK;
 }
 
+// hidden / weight checks shared by vw_head_logits and vw_head_sample
+static vw_status check_head_operands(vw_handle* h, const void* hidden, int64_t hidden_stride, int32_t hidden_size,
+                                     const void* weight, int64_t weight_stride, int32_t vocab) {
+    if (!hidden || !weight || hidden_size < 8 || hidden_size % 8 != 0 || hidden_stride < hidden_size ||
+        weight_stride < hidden_size || hidden_stride % 8 != 0 || weight_stride % 8 != 0 || !aligned(hidden, 16) ||
+        !aligned(weight, 16))
+        return fail(h, VW_ERR_INVALID_ARG,
+                    "hidden / weight: 16-byte aligned bf16 rows, hidden_size and strides multiples of 8");
+    if (vocab < 4 || vocab % 4 != 0) return fail(h, VW_ERR_INVALID_ARG, "vocab must be a multiple of 4");
+    return VW_OK;
+}
+
 // ------------------------------------------------------------------------------------- device-resident batches
 // One vw_batch per generation loop: TalkerGenerator.GenerateBatch's per-job state (TalkerGenerator.cs:322-455) in
 // device memory, one slot per job, so that a step sends only logits and reads only ids.
@@ -676,10 +695,21 @@ struct vw_batch {
     vw::BatchDevice d{};
     double* d_uniforms = nullptr;   // [n_slots] the step's draws
     void* mem = nullptr;            // one allocation for every array
+    float* d_logits = nullptr;      // head steps: [n_slots, vocab] logits of the batch's own GEMM
+    size_t logits_bytes = 0;
     int32_t vocab = 0, sup_lo = 0, sup_hi = 0, min_new = 0;
 };
 
 namespace {
+
+void orphan_batch(vw_batch* b) {
+    if (b->mem) cudaFree(b->mem);
+    if (b->d_logits) cudaFree(b->d_logits);
+    b->mem = nullptr;
+    b->d_logits = nullptr;
+    b->logits_bytes = 0;
+    b->h = nullptr;   // every later call on the batch returns VW_ERR_INVALID_ARG
+}
 
 // System.Random(int seed)'s initial state: the published subtractive generator (Knuth, TAOCP Vol. 2 3.2.2;
 // Numerical Recipes ran3) with .NET's modulus 2^31 - 1, table spread in steps of 21 and four warm-up rounds.  C#
@@ -795,7 +825,8 @@ VW_EXPORT vw_status vw_batch_create(vw_handle* h, int32_t n_slots, int32_t vocab
     const size_t hist = round_up(n * static_cast<size_t>(max_history) * 4, 256);
     const size_t ints = round_up(n * 4, 256);
     const size_t rng = round_up(n * sizeof(vw::DotNetRngState), 256);
-    const size_t total = hist + 6 * ints + 2 * rng + round_up(n * 8, 256);
+    const size_t codes = round_up(n * vw::kMaxCodeGroups * 4, 256);
+    const size_t total = hist + 6 * ints + 2 * rng + round_up(n * 8, 256) + codes;
     cudaError_t e = cudaMalloc(&b->mem, total);
     if (e == cudaSuccess) e = cudaMemset(b->mem, 0, total);
     if (e != cudaSuccess) {
@@ -821,16 +852,26 @@ VW_EXPORT vw_status vw_batch_create(vw_handle* h, int32_t n_slots, int32_t vocab
     b->d.rng_talker = reinterpret_cast<vw::DotNetRngState*>(take(rng));
     b->d.rng_sub = reinterpret_cast<vw::DotNetRngState*>(take(rng));
     b->d_uniforms = reinterpret_cast<double*>(take(round_up(n * 8, 256)));
+    b->d.codes = reinterpret_cast<int32_t*>(take(codes));
+    e = cudaMemset(b->d.codes, 0xff, n * vw::kMaxCodeGroups * 4);   // every code -1: no frame yet
+    if (e != cudaSuccess) {
+        cudaFree(b->mem);
+        delete b;
+        return cuda_fail(h, e, "batch state");
+    }
+    h->batches.push_back(b);
     *out = b;
     return VW_OK;
 }
 
 VW_EXPORT vw_status vw_batch_destroy(vw_batch* b) {
     if (!b) return VW_OK;
-    if (b->h) {
-        DeviceGuard guard(b->h->device);
-        cudaStreamSynchronize(b->h->stream);
-        if (b->mem) cudaFree(b->mem);
+    if (b->h) {   // otherwise vw_destroy of its handle has already released the device memory
+        vw_handle* h = b->h;
+        DeviceGuard guard(h->device);
+        cudaStreamSynchronize(h->stream);
+        h->batches.erase(std::remove(h->batches.begin(), h->batches.end(), b), h->batches.end());
+        orphan_batch(b);
     }
     delete b;
     return VW_OK;
@@ -904,6 +945,112 @@ VW_EXPORT vw_status vw_batch_sub_step(vw_batch* b, const void* logits, int64_t r
     return batch_step(b, 1, logits, row_stride, vocab, dtype, options, n_options, out_ids, nullptr, stream);
 }
 
+namespace {
+
+// The head GEMM into the batch's logits buffer (all n_slots rows), then a talker (which 0) or sub-talker step over
+// those logits; a sub-talker step records its ids as codebook `group` of each slot's frame.
+vw_status batch_head_step(vw_batch* b, int which, int group, const void* hidden, int64_t hidden_stride,
+                          int32_t hidden_size, const void* weight, int64_t weight_stride, int32_t vocab,
+                          const vw_options* options, int32_t n_options, int32_t* out_ids, int32_t* out_done,
+                          void* stream) {
+    vw_status r = batch_check(b, options, n_options);
+    if (r != VW_OK) return r;
+    vw_handle* h = b->h;
+    r = check_head_operands(h, hidden, hidden_stride, hidden_size, weight, weight_stride, vocab);
+    if (r != VW_OK) return r;
+    if (!out_ids) return fail(h, VW_ERR_INVALID_ARG, "out_ids is required");
+    if (which == 1 && (group < 1 || group >= vw::kMaxCodeGroups))
+        return fail(h, VW_ERR_INVALID_ARG, "group must be in [1, 15]");
+    DeviceGuard guard(h->device);
+    if (!guard.ok()) return fail(h, VW_ERR_CUDA, "cudaSetDevice failed");
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+    const size_t need = static_cast<size_t>(b->d.n_slots) * static_cast<size_t>(vocab) * 4;
+    if (need > b->logits_bytes) {
+        cudaError_t e = cudaStreamSynchronize(st);   // an earlier step may still read the old buffer
+        if (e == cudaSuccess && b->d_logits) e = cudaFree(b->d_logits);
+        b->d_logits = nullptr;
+        b->logits_bytes = 0;
+        if (e == cudaSuccess) e = cudaMalloc(&b->d_logits, need);
+        if (e != cudaSuccess) return cuda_fail(h, e, "batch logits buffer");
+        b->logits_bytes = need;
+    }
+    cudaError_t e = stream ? cudaSuccess : cudaMemsetAsync(h->d_err, 0, sizeof(unsigned), st);
+    if (e == cudaSuccess)
+        e = vw::launch_head_gemm(hidden, hidden_stride, weight, weight_stride, b->d.n_slots, vocab, hidden_size,
+                                 b->d_logits, vocab, h->d_err, st);
+    if (e != cudaSuccess) return cuda_fail(h, e, "head GEMM");
+    r = batch_step(b, which, b->d_logits, vocab, vocab, VW_F32, options, n_options, out_ids, out_done, st);
+    if (r != VW_OK) return r;
+    if (which == 1) {
+        e = vw::launch_batch_record_codes(b->d, out_ids, group, st);
+        if (e != cudaSuccess) return cuda_fail(h, e, "record codes");
+    }
+    if (!stream) return read_device_error(h, st);
+    return VW_OK;
+}
+
+}  // namespace
+
+VW_EXPORT vw_status vw_batch_talker_head_step(vw_batch* b, const void* hidden, int64_t hidden_stride,
+                                              int32_t hidden_size, const void* weight, int64_t weight_stride,
+                                              const vw_options* options, int32_t n_options, int32_t* out_ids,
+                                              int32_t* out_done, void* stream) {
+    return batch_head_step(b, 0, 0, hidden, hidden_stride, hidden_size, weight, weight_stride, b ? b->vocab : 0,
+                           options, n_options, out_ids, out_done, stream);
+}
+
+VW_EXPORT vw_status vw_batch_sub_head_step(vw_batch* b, int32_t group, const void* hidden, int64_t hidden_stride,
+                                           int32_t hidden_size, const void* weight, int64_t weight_stride,
+                                           int32_t vocab, const vw_options* options, int32_t n_options,
+                                           int32_t* out_ids, void* stream) {
+    return batch_head_step(b, 1, group, hidden, hidden_stride, hidden_size, weight, weight_stride, vocab, options,
+                           n_options, out_ids, nullptr, stream);
+}
+
+VW_EXPORT vw_status vw_batch_code_embedding(vw_batch* b, int32_t group, const void* table, int32_t table_rows,
+                                            int32_t hidden, float* out, int64_t out_stride, void* stream) {
+    if (!b || !b->h) return VW_ERR_INVALID_ARG;
+    vw_handle* h = b->h;
+    h->last_error.clear();
+    if (group < 0 || group >= vw::kMaxCodeGroups) return fail(h, VW_ERR_INVALID_ARG, "group must be in [0, 15]");
+    if (!table || !out || table_rows < 1 || hidden < 8 || hidden % 8 != 0 || out_stride < hidden ||
+        out_stride % 4 != 0 || !aligned(table, 16) || !aligned(out, 16))
+        return fail(h, VW_ERR_INVALID_ARG, "16-byte aligned table and out, hidden a multiple of 8");
+    DeviceGuard guard(h->device);
+    if (!guard.ok()) return fail(h, VW_ERR_CUDA, "cudaSetDevice failed");
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+    cudaError_t e = stream ? cudaSuccess : cudaMemsetAsync(h->d_err, 0, sizeof(unsigned), st);
+    if (e == cudaSuccess)
+        e = vw::launch_batch_code_embedding(b->d, group, static_cast<const uint16_t*>(table), table_rows, hidden, out,
+                                            out_stride, h->d_err, st);
+    if (e != cudaSuccess) return cuda_fail(h, e, "code embedding");
+    if (!stream) return read_device_error(h, st);
+    return VW_OK;
+}
+
+VW_EXPORT vw_status vw_batch_frame_embedding(vw_batch* b, int32_t hidden, const uint16_t* codec_embedding,
+                                             const uint16_t* const* cp_embeddings, int32_t cp_vocab,
+                                             const float* text, float* out, void* stream) {
+    if (!b || !b->h) return VW_ERR_INVALID_ARG;
+    return vw_frame_embedding(b->h, b->d.codes, b->d.n_slots, vw::kMaxCodeGroups, hidden, codec_embedding, b->vocab,
+                              cp_embeddings, cp_vocab, text, out, stream);
+}
+
+VW_EXPORT vw_status vw_batch_get_codes(vw_batch* b, int32_t* out) {
+    if (!b || !b->h) return VW_ERR_INVALID_ARG;
+    vw_handle* h = b->h;
+    h->last_error.clear();
+    if (!out) return fail(h, VW_ERR_INVALID_ARG, "NULL out");
+    DeviceGuard guard(h->device);
+    if (!guard.ok()) return fail(h, VW_ERR_CUDA, "cudaSetDevice failed");
+    cudaError_t e = cudaStreamSynchronize(h->stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpy(out, b->d.codes, static_cast<size_t>(b->d.n_slots) * vw::kMaxCodeGroups * 4,
+                       cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(h, e, "vw_batch_get_codes");
+    return VW_OK;
+}
+
 VW_EXPORT vw_status vw_batch_query(vw_batch* b, int32_t slot, int32_t* step, int32_t* history_len, int32_t* active) {
     if (!b || !b->h) return VW_ERR_INVALID_ARG;
     if (slot < 0 || slot >= b->d.n_slots) return fail(b->h, VW_ERR_INVALID_ARG, "bad slot");
@@ -948,18 +1095,6 @@ VW_EXPORT vw_status vw_frame_embedding(vw_handle* h, const int32_t* codes, int32
                                        st);
     if (e != cudaSuccess) return cuda_fail(h, e, "frame embedding");
     if (!stream) return read_device_error(h, st);
-    return VW_OK;
-}
-
-// hidden / weight checks shared by vw_head_logits and vw_head_sample
-static vw_status check_head_operands(vw_handle* h, const void* hidden, int64_t hidden_stride, int32_t hidden_size,
-                                     const void* weight, int64_t weight_stride, int32_t vocab) {
-    if (!hidden || !weight || hidden_size < 8 || hidden_size % 8 != 0 || hidden_stride < hidden_size ||
-        weight_stride < hidden_size || hidden_stride % 8 != 0 || weight_stride % 8 != 0 || !aligned(hidden, 16) ||
-        !aligned(weight, 16))
-        return fail(h, VW_ERR_INVALID_ARG,
-                    "hidden / weight: 16-byte aligned bf16 rows, hidden_size and strides multiples of 8");
-    if (vocab < 4 || vocab % 4 != 0) return fail(h, VW_ERR_INVALID_ARG, "vocab must be a multiple of 4");
     return VW_OK;
 }
 

@@ -9,7 +9,9 @@
 //     Sampler.Select takes at Sampler.cs:77; greedy slots draw nothing, as the reference's Select returns first);
 //   * the sampler kernels read each slot's history in place (row r = slot r);
 //   * commit_kernel: appends the talker id to the slot's history (:374), then retires the slot on EOS or on the
-//     last step, or advances its step (:375-380, :440).
+//     last step, or advances its step (:375-380, :440), and records code 0 of the frame the slot goes on with;
+//   * record_codes_kernel / code_embedding_kernel: each code-predictor group's codes into the frame (:420), and the
+//     embedding row of a group's code, the next code-predictor input (:411, :422).
 // System.Random(int) is restated from the published subtractive generator (Knuth, TAOCP Vol. 2 3.2.2; Numerical
 // Recipes ran3) with .NET's modulus 2^31 - 1 and second tap 21; its state is seeded on the host (vw_api.cpp).
 
@@ -70,6 +72,37 @@ __global__ void commit_kernel(BatchDevice b, const int32_t* ids, int32_t* out_do
         }
     }
     if (out_done) out_done[s] = done;
+    // f[0] = code0 for the jobs that go on to the code predictor (:382-384)
+    b.codes[static_cast<int64_t>(s) * kMaxCodeGroups] = (b.active[s] && !done) ? ids[s] : -1;
+}
+
+__global__ void record_codes_kernel(BatchDevice b, const int32_t* ids, int group) {
+    const int s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s < b.n_slots) b.codes[static_cast<int64_t>(s) * kMaxCodeGroups + group] = ids[s];   // keepFrames[i][g] (:420)
+}
+
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }   // Bf16.cs:13
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// one CTA per slot, 8 bf16 per thread and step (AddRow with add: false, TalkerModel.cs:120-125)
+__global__ void __launch_bounds__(128) code_embedding_kernel(BatchDevice b, int group, const uint16_t* table,
+                                                             int table_rows, int hidden, float* out,
+                                                             int64_t out_stride, unsigned* err) {
+    const int s = blockIdx.x;
+    const int64_t base = static_cast<int64_t>(s) * kMaxCodeGroups;
+    if (b.codes[base] < 0) return;   // the slot is idle or retired at this frame's talker step
+    const int code = b.codes[base + group];
+    if (static_cast<unsigned>(code) >= static_cast<unsigned>(table_rows)) {
+        if (threadIdx.x == 0) atomicOr(err, kErrCodeRange);   // ArgumentOutOfRangeException (TalkerModel.cs:102,109)
+        return;
+    }
+    const uint16_t* src = table + static_cast<int64_t>(code) * hidden;
+    float* dst = out + static_cast<int64_t>(s) * out_stride;
+    for (int i0 = threadIdx.x * 8; i0 < hidden; i0 += blockDim.x * 8) {
+        const uint4 u = *reinterpret_cast<const uint4*>(src + i0);
+        *reinterpret_cast<float4*>(dst + i0) = make_float4(bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y));
+        *reinterpret_cast<float4*>(dst + i0 + 4) = make_float4(bf16_lo(u.z), bf16_hi(u.z), bf16_lo(u.w), bf16_hi(u.w));
+    }
 }
 
 }  // namespace
@@ -87,6 +120,19 @@ cudaError_t launch_batch_draw(const BatchDevice& b, int which, const DevOptions*
 cudaError_t launch_batch_commit(const BatchDevice& b, const int32_t* ids, int32_t* out_done, cudaStream_t stream) {
     const int threads = 128, blocks = (b.n_slots + threads - 1) / threads;
     commit_kernel<<<blocks, threads, 0, stream>>>(b, ids, out_done);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_batch_record_codes(const BatchDevice& b, const int32_t* ids, int group, cudaStream_t stream) {
+    const int threads = 128, blocks = (b.n_slots + threads - 1) / threads;
+    record_codes_kernel<<<blocks, threads, 0, stream>>>(b, ids, group);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_batch_code_embedding(const BatchDevice& b, int group, const uint16_t* table, int table_rows,
+                                        int hidden, float* out, int64_t out_stride, unsigned* err,
+                                        cudaStream_t stream) {
+    code_embedding_kernel<<<b.n_slots, 128, 0, stream>>>(b, group, table, table_rows, hidden, out, out_stride, err);
     return cudaGetLastError();
 }
 

@@ -27,16 +27,19 @@ __global__ void __launch_bounds__(128) frame_embedding_kernel(const int32_t* cod
                                                               EmbedTables t, int vocab, int cp_vocab,
                                                               const float* text, float* out, unsigned* err) {
     const int row = blockIdx.x;
+    const int32_t* rc = codes + static_cast<int64_t>(row) * n_groups;
+    // a sequence without a frame (a finished slot of vw_batch_talker_step: code 0 is -1); its other codes are not
+    // looked at
+    if (rc[0] == -1) return;
     __shared__ int32_t code[kMaxCodeGroups];
     __shared__ int skip;
     if (threadIdx.x == 0) skip = 0;
     __syncthreads();
     if (threadIdx.x < n_groups) {
-        const int c = codes[static_cast<int64_t>(row) * n_groups + threadIdx.x];
+        const int c = rc[threadIdx.x];
         code[threadIdx.x] = c;
-        if (threadIdx.x == 0 && c == -1) skip = 1;   // a finished sequence (vw_batch_talker_step id -1)
         const int lim = threadIdx.x == 0 ? vocab : cp_vocab;
-        if (!(threadIdx.x == 0 && c == -1) && static_cast<unsigned>(c) >= static_cast<unsigned>(lim)) {
+        if (static_cast<unsigned>(c) >= static_cast<unsigned>(lim)) {
             atomicOr(err, kErrCodeRange);   // the reference throws ArgumentOutOfRangeException (TalkerModel.cs:99)
             skip = 1;
         }

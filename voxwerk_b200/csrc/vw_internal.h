@@ -122,12 +122,22 @@ struct BatchDevice {
     int32_t* opt_sub;          // [n_slots] ... into each sub-talker step's options table
     DotNetRngState* rng_talker;   // [n_slots] Sampler(Seed)
     DotNetRngState* rng_sub;      // [n_slots] Sampler(Seed + 1)
+    int32_t* codes;               // [n_slots, kMaxCodeGroups] the frame being built (keepFrames); codes[s][0] is -1
+                                  // unless slot s continues past its last talker step
 };
 // One NextDouble() into uniforms[s] for every active slot whose option samples (which: 0 talker, 1 sub-talker).
 cudaError_t launch_batch_draw(const BatchDevice& b, int which, const DevOptions* opts, int n_opts, double* uniforms,
                               cudaStream_t stream);
-// Appends ids[s] to every active slot's history, then retires the slot (EOS or last step) or advances its step.
+// Appends ids[s] to every active slot's history, then retires the slot (EOS or last step) or advances its step;
+// records code 0 of the frame of every slot that continues (-1 for the others).
 cudaError_t launch_batch_commit(const BatchDevice& b, const int32_t* ids, int32_t* out_done, cudaStream_t stream);
+// codes[s][group] = ids[s] for every slot (a code-predictor group's ids; -1 where the slot did not sample).
+cudaError_t launch_batch_record_codes(const BatchDevice& b, const int32_t* ids, int group, cudaStream_t stream);
+// out[s] = bf16 -> fp32 of table row codes[s][group] for every continuing slot (TalkerModel.CodecEmbedding for
+// group 0, CodePredictorEmbedding for groups 1..15); other rows are left alone.  err collects kErrCodeRange.
+cudaError_t launch_batch_code_embedding(const BatchDevice& b, int group, const uint16_t* table, int table_rows,
+                                        int hidden, float* out, int64_t out_stride, unsigned* err,
+                                        cudaStream_t stream);
 
 struct LaunchParams {
     DevSegment seg[kMaxSegments];
