@@ -18,7 +18,8 @@ stay on the GPU and a step copies in only the logit columns the sampler reads.
 `parity`: every row of the timed batch against that restatement, with flips counted and attributed.
 At N = 1 `configs` holds the other four configurations (µs per call, rows/s, roofline fraction, parity), and
 `frame_embedding` the next-input gather (vw_frame_embedding) for 1024 sequences, and `head` the vocabulary head
-(vw_head_logits, the tcgen05 GEMM; vw_head_sample, GEMM + sampler) against cuBLAS (+ vw_sample).
+(vw_head_logits, the tcgen05 GEMM; vw_head_sample, GEMM + sampler) against cuBLAS (+ vw_sample), with
+`head.frame_loop` one whole device frame of the batch loop (every sampling step of a frame for 1024 sequences).
 `--impl reference` times only the CPU implementation, with every host thread, and prints its own line; that
 process loads no GPU library of this repository.
 """
@@ -447,6 +448,51 @@ def head_timing(dev, torch, hbm, hbm_kind, reps=50, cases=((64, 3072), (1024, 30
     return out
 
 
+def frame_loop_timing(dev, torch, streams=1024, reps=10):
+    """One frame of the device loop for `streams` sequences (config 3's stream count; hidden 1024, Qwen3-TTS
+    vocabularies): vw_batch_talker_head_step, code embedding 0, 15 x (vw_batch_sub_head_step + code embedding),
+    vw_batch_frame_embedding -- everything of TalkerGenerator.cs:362-439 except the transformer steps, whose hidden
+    rows are fixed random inputs here.  Talker options as config 3 (top-k 50, top-p 0.8, rp 1.05, 1024-id
+    histories), sub-talker top-k 50; `reps` frames in one CUDA graph (graph_us)."""
+    from voxwerk_b200 import DeviceBatchState, GenerationOptions, SamplingOptions
+    H, V, CV, G = 1024, 3072, 2048, 16
+    g = torch.Generator(device="cuda").manual_seed(11)
+    bf = lambda *shape, s=1.0: (torch.randn(shape, device="cuda", generator=g) * s).to(torch.bfloat16)
+    codec_head, cp_heads = bf(V, H, s=0.125), [bf(CV, H, s=0.125) for _ in range(G - 1)]
+    codec_head[2150].zero_()   # EOS logit 0, far below the top-50 cut: no sequence retires while timing
+    codec_emb, cp_emb = bf(V, H), [bf(CV, H) for _ in range(G - 1)]
+    last, cp_hidden = bf(streams, H), bf(streams, H)
+    text = torch.randn((streams, H), device="cuda", generator=g)
+    cp_in = torch.empty((streams, H), device="cuda")
+    step_in = torch.empty((streams, H), device="cuda")
+    # 1024-id starting histories (config 3); jobs long enough that no slot reaches MaxNewTokens while timing
+    state = DeviceBatchState(dev, streams, max_history=1024 + 50000)
+    job = GenerationOptions(seed=42, max_new_tokens=50000, repetition_penalty=1.05,
+                            talker=SamplingOptions(top_k=50, top_p=0.8), sub_talker=SamplingOptions(top_k=50))
+    hist = np.random.default_rng(3).integers(0, 2048, (streams, 1024))
+    for s in range(streams):
+        state.start(s, job, hist[s].tolist())
+
+    def frame(sp):
+        state.talker_head_step(last, codec_head, stream=sp)
+        state.code_embedding(0, codec_emb, cp_in, stream=sp)
+        for grp in range(1, G):
+            state.sub_head_step(grp, cp_hidden, cp_heads[grp - 1], stream=sp)
+            state.code_embedding(grp, cp_emb[grp - 1], cp_in, stream=sp)
+        state.frame_embedding(codec_emb, cp_emb, text, step_in, stream=sp)
+
+    st = torch.cuda.Stream()
+    us = graph_us(torch, st, frame, reps)
+    dev.synchronize(st.cuda_stream)
+    steps = state.query(0)[0]
+    state.close()
+    # kernels per frame: talker (GEMM, draw, 2 sampler, commit) + code embedding + 15 x (GEMM, draw, 2 sampler,
+    # record, code embedding) + frame embedding
+    return {"streams": streams, "hidden": H, "us_per_frame": us, "frames_per_s": 1e6 / us,
+            "sampled_rows_per_s": streams * G / (us * 1e-6), "kernels_per_frame": 5 + 1 + 15 * 6 + 1,
+            "slot0_steps_after_timing": steps, "note": "talker EOS logit held at 0 (no slot retires while timing)"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -589,6 +635,7 @@ def main():
         with ClockSampler(local) as cs:
             head = head_timing(dev, torch, peak, peak_kind)
         head["clocks"] = cs.summary()
+        head["frame_loop"] = frame_loop_timing(dev, torch)
 
     line = None
     if rank == 0:
