@@ -214,29 +214,32 @@ def timed_graph(dev, copies, opts, steps, warmup, stream, torch, barrier=None, c
     with torch.cuda.graph(graph, stream=stream):
         for i in range(steps):
             sample_rows(dev, copies[i % len(copies)][0], opts, stream=torch.cuda.current_stream().cuda_stream)
-    for _ in range(2):
-        graph.replay()
-    torch.cuda.synchronize()
-    dev.stats(reset=True)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if barrier:
-        barrier()
-    torch.cuda.synchronize()
-    clocks = None
-    if clocks_gpu is not None:
-        with ClockSampler(clocks_gpu) as cs:
-            with torch.cuda.stream(stream):
-                ev0.record(stream)
-                graph.replay()
-                ev1.record(stream)
-            ev1.synchronize()
-        clocks = cs.summary()
-    else:
+    cs = ClockSampler(clocks_gpu) if clocks_gpu is not None else None
+    if cs is not None:
+        cs.__enter__()   # nvidia-smi samples from here on (its start-up pause comes before the warm replays)
+    try:
+        # untimed replays for at least 50 ms (two at least), right before the timed one, so the SM clock has left
+        # its idle level
+        t_end = time.perf_counter() + 0.05
+        n_warm = 0
+        while n_warm < 2 or time.perf_counter() < t_end:
+            graph.replay()
+            torch.cuda.synchronize()
+            n_warm += 1
+        dev.stats(reset=True)
+        if barrier:
+            barrier()
+        torch.cuda.synchronize()
         with torch.cuda.stream(stream):
             ev0.record(stream)
             graph.replay()
             ev1.record(stream)
         ev1.synchronize()
+    finally:
+        if cs is not None:
+            cs.__exit__(None, None, None)
+    clocks = cs.summary() if cs is not None else None
     torch.cuda.synchronize()
     ms = ev0.elapsed_time(ev1)
     dev.synchronize(sp)   # raises if the kernel latched an error

@@ -22,6 +22,8 @@
 
 constexpr int kRwWarps = 4;       // warps per CTA, each on its own rows
 constexpr int kRwBatch = 8;       // 16-byte vectors per lane in flight per load batch
+constexpr int kRwPre = 4;         // re-read vectors per lane in flight (marked vectors, 32 per step)
+constexpr int kRwHistBatch = 8;   // 16-byte history loads per lane in flight
 constexpr int kRwCandCap = 256;   // candidates (exact value >= tau) per row
 constexpr int kRwSlots = kRwCandCap / 32;
 constexpr int kRwRawCap = 384;    // raw candidates (raw value >= x0) per row
@@ -188,15 +190,15 @@ __device__ bool rw_history(const int32_t* hist, int len, int V, uint32_t* bm, in
     if (lane < head) put(hist[lane]);
     const int4* h4 = reinterpret_cast<const int4*>(hist + head);
     const int n4 = (len - head) >> 2;
-    for (int j0 = 0; j0 < n4; j0 += 4 * 32) {
-        int4 w[4];
+    for (int j0 = 0; j0 < n4; j0 += kRwHistBatch * 32) {
+        int4 w[kRwHistBatch];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
+        for (int k = 0; k < kRwHistBatch; ++k) {
             const int j = j0 + k * 32 + lane;
             w[k] = j < n4 ? __ldg(h4 + j) : make_int4(0, 0, 0, 0);
         }
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
+        for (int k = 0; k < kRwHistBatch; ++k) {
             if (j0 + k * 32 + lane >= n4) continue;
             put(w[k].x);
             put(w[k].y);
@@ -242,33 +244,44 @@ __device__ bool rw_collect(const RwRow& r, const DevSegment& sg, float tau, floa
             a.vlist[o++] = static_cast<uint16_t>(sg.c0 + lane * sg.cpl_c + __ffs(m) - 1);
     }
     __syncwarp();
-    // raw candidates: elements >= x0 of the listed vectors (every element of a vector with suppressed ids)
+    // raw candidates: elements >= x0 of the listed vectors (every element of a vector with suppressed ids); the
+    // re-reads of up to kRwPre * 32 listed vectors are all in flight before the first is used
     int R = 0;
-    for (int e0 = 0; e0 < M; e0 += 32) {
-        const int e = e0 + lane;
-        uint32_t bits = 0u;
-        uint4 u = neg_inf_vec(VW);
-        int gv = 0;
-        if (e < M) {
-            gv = a.vlist[e];
-            u = __ldg(r.row + gv);
-            const bool spec = (gv >= sg.spec_a && gv <= sg.spec_b) || gv == ev;
+    for (int e00 = 0; e00 < M; e00 += 32 * kRwPre) {
+        uint4 uu[kRwPre];
+        int gg[kRwPre];
 #pragma unroll
-            for (int k = 0; k < VW; ++k)
-                if (spec || vec_elem<VW>(u, k) >= x0) bits |= 1u << k;
+        for (int t = 0; t < kRwPre; ++t) {
+            const int e = e00 + 32 * t + lane;
+            gg[t] = e < M ? a.vlist[e] : 0;
+            uu[t] = e < M ? __ldg(r.row + gg[t]) : neg_inf_vec(VW);
         }
-        int tot;
-        int o = R + warp_excl_i(__popc(bits), lane, tot);
-        if (R + tot > kRwRawCap) return false;
 #pragma unroll
-        for (int k = 0; k < VW; ++k) {
-            if ((bits >> k) & 1u) {
-                a.u.raw.v[o] = vec_elem<VW>(u, k);
-                a.u.raw.id[o] = (gv << vsh) + k;
-                ++o;
+        for (int t = 0; t < kRwPre; ++t) {
+            if (e00 + 32 * t >= M) break;   // warp-uniform
+            const int e = e00 + 32 * t + lane;
+            const uint4 u = uu[t];
+            const int gv = gg[t];
+            uint32_t bits = 0u;
+            if (e < M) {
+                const bool spec = (gv >= sg.spec_a && gv <= sg.spec_b) || gv == ev;
+#pragma unroll
+                for (int k = 0; k < VW; ++k)
+                    if (spec || vec_elem<VW>(u, k) >= x0) bits |= 1u << k;
             }
+            int tot;
+            int o = R + warp_excl_i(__popc(bits), lane, tot);
+            if (R + tot > kRwRawCap) return false;
+#pragma unroll
+            for (int k = 0; k < VW; ++k) {
+                if ((bits >> k) & 1u) {
+                    a.u.raw.v[o] = vec_elem<VW>(u, k);
+                    a.u.raw.id[o] = (gv << vsh) + k;
+                    ++o;
+                }
+            }
+            R += tot;
         }
-        R += tot;
     }
     __syncwarp();
     // the history bitmap, built here so that its loads (prefetched into L2 at the row's start) are not waited for
@@ -556,26 +569,26 @@ __device__ int rw_decide(RwArea& a, int C, uint32_t kth, float top_p, double r, 
     return res;
 }
 
-// Calls f(raw, id) for every active element of the row: parts A and C (lane l: its contiguous vectors) and the EOS
-// vector (lane 0).  Used by greedy rows and by the threshold rebuild, which need every element's exact value.
+// Calls f(raw, id) for every active element of the row: parts A and C (lane l: vectors l, l + 32, ...) and the EOS
+// vector (lane 0).  Used by greedy rows and by the threshold rebuild, which need every element's exact value and do
+// not depend on the order of the calls.
 template <int VW, class F>
 __device__ __forceinline__ void rw_for_each(const RwRow& r, const DevSegment& sg, int lane, F f) {
     constexpr int vsh = VW == 4 ? 2 : 3;
 #pragma unroll 1
     for (int part = 0; part < 2; ++part) {
-        const int v0 = part == 0 ? 0 : sg.c0, nv = part == 0 ? sg.va : sg.vc, cpl = part == 0 ? sg.cpl_a : sg.cpl_c;
-        const int q0 = lane * cpl;
-        for (int b0 = 0; b0 < cpl; b0 += kRwBatch) {
+        const int v0 = part == 0 ? 0 : sg.c0, nv = part == 0 ? sg.va : sg.vc;
+        for (int j0 = 0; j0 < nv; j0 += 32 * kRwBatch) {
             uint4 v[kRwBatch];
 #pragma unroll
             for (int i = 0; i < kRwBatch; ++i) {
-                const int it = b0 + i, q = q0 + it;
-                v[i] = (it < cpl && q < nv) ? __ldg(r.row + v0 + q) : neg_inf_vec(VW);
+                const int q = j0 + 32 * i + lane;
+                v[i] = q < nv ? __ldg(r.row + v0 + q) : neg_inf_vec(VW);
             }
 #pragma unroll
             for (int i = 0; i < kRwBatch; ++i) {
-                const int q = q0 + b0 + i;
-                if (b0 + i < cpl && q < nv) {
+                const int q = j0 + 32 * i + lane;
+                if (q < nv) {
 #pragma unroll
                     for (int k = 0; k < VW; ++k) f(vec_elem<VW>(v[i], k), ((v0 + q) << vsh) + k);
                 }
@@ -837,6 +850,10 @@ __global__ void __launch_bounds__(kRwWarps * 32, 7) row_warp_kernel(const __grid
                                 : rw_sample_row<8>(p, r, sg, o, a, bm, hist_bad, carry, seed, out_probs, lane, st_fast,
                                                    st_exact, st_miss);
         }
+        // seeds the next call: slot j of segment s holds the threshold carried out of row j of s (one writer per
+        // slot, so the table is the same whatever order the warps finish in)
+        if (sample && p.guess_seed && local < kSeedSlots && lane == s && carry != ~0ull)
+            p.guess_seed[lane * kSeedSlots + local] = carry;
         if (hist_bad && lane == 0) atomicOr(p.err, kErrHistRange);
         if (res == -2) {   // the whole-row kernel takes the row
             ++st_overflow;
@@ -846,9 +863,6 @@ __global__ void __launch_bounds__(kRwWarps * 32, 7) row_warp_kernel(const __grid
         }
         __syncwarp();   // the warp's shared area is reused by its next row
     }
-    // seeds the next call: this warp's threshold per segment, in the slot of its index
-    if (p.guess_seed && lane < p.n_segs && carry != ~0ull)
-        p.guess_seed[lane * kSeedSlots + ((blockIdx.x * kRwWarps + wib) & (kSeedSlots - 1))] = carry;
     if (p.stats && lane == 0) {
         const uint32_t v[4] = {st_greedy, st_fast, st_exact, st_overflow};
         const int idx[4] = {kStatGreedy, kStatFast, kStatFastReplayed, kStatOverflow};
