@@ -739,6 +739,8 @@ __global__ void __launch_bounds__(kRwWarps * 32, 7) row_warp_kernel(const __grid
     uint32_t* bm = reinterpret_cast<uint32_t*>(mine + sizeof(RwArea));
     // the whole-row kernel may be scheduled now; it waits (griddepcontrol.wait) until this grid has finished
     if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // the first row's logits and per-row words start towards L2 before the seed table is read
+    if (blockIdx.x * kRwWarps + wib < p.total_rows) rw_prefetch_row(p, blockIdx.x * kRwWarps + wib, lane);
 
     const int G = gridDim.x * kRwWarps;
     // carried thresholds: lane s holds segment s's (threshold bits << 32 | option); ~0: none yet
@@ -761,7 +763,6 @@ __global__ void __launch_bounds__(kRwWarps * 32, 7) row_warp_kernel(const __grid
         if (lane == 0) seed[s2] = ~0ull;
     __syncthreads();
     uint32_t st_greedy = 0, st_fast = 0, st_exact = 0, st_overflow = 0, st_miss = 0;
-    if (blockIdx.x * kRwWarps + wib < p.total_rows) rw_prefetch_row(p, blockIdx.x * kRwWarps + wib, lane);
 
     for (int row = blockIdx.x * kRwWarps + wib; row < p.total_rows; row += G) {
         int s = 0;
