@@ -40,11 +40,15 @@ def _check_gemm(torch, hidden, weight, got):
     return worst
 
 
-# tile widths the host picks for these shapes: 32 (rows 1 .. 257), 64 (300), 96 (386), 128 (519), 192 (771),
-# 256 (1156, 4096); 4096 x 3072 and 8192 x 2048 give each persistent CTA several tiles (both accumulators reused)
+# tile widths the host picks for these shapes (148 SMs): 32 (rows 1 .. 257, 6 x 3072 x 256, 1 x 1024, 1 x 2048),
+# 64 (300, 273 x 3072 x 512, 137), 96 (386, 392 x 3072 x 2048), 128 (519, 8192 x 2048), 192 (771), 256 (1156, 4096);
+# 4096 x 3072 and 8192 x 2048 give each persistent CTA several tiles (both accumulators reused); 257 x 1000 x 1000 is
+# ragged in N and K
 @pytest.mark.parametrize("n,V,H", [(1, 3072, 1024), (64, 3072, 1024), (130, 2048, 1024), (257, 1000, 1000),
                                    (16, 3072, 2048), (300, 3072, 1024), (386, 3072, 1024), (519, 3072, 1024),
-                                   (771, 3072, 1024), (1156, 3072, 1024), (4096, 3072, 1024), (8192, 2048, 1024)])
+                                   (771, 3072, 1024), (1156, 3072, 1024), (4096, 3072, 1024), (8192, 2048, 1024),
+                                   (6, 3072, 256), (1, 1024, 1024), (273, 3072, 512), (1, 2048, 1024),
+                                   (137, 3072, 1024), (392, 3072, 2048)])
 def test_head_gemm_matches_float64(device, n, V, H):
     import torch
     from voxwerk_b200 import SamplingOptions, Segment, head_logits, head_sample, vw_options
