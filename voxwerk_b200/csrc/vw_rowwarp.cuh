@@ -3,15 +3,16 @@
 //
 // One warp per row and no block barrier: warp g of the grid takes rows g, g + G, g + 2G, ... (G = warps launched),
 // so the warps of a CTA never wait for one another.  A row is read with 16-byte vector loads straight from
-// global memory (the skipped suppress span is never read); lane l owns the contiguous vectors [l * cpl, (l+1) *
-// cpl) of each part, so lane order is index order everywhere below.  Per sampling row with 0 < K <= 64:
+// global memory (the skipped suppress span is never read).  Per sampling row with 0 < K <= 64:
 //   1. history ids -> a bitmap of the ids (Distinct(), Sampler.cs:28);
-//   2. mark pass: a vector is marked when its largest raw value is >= x0, the smallest raw value whose
-//      temperature-scaled value reaches the carried threshold tau (a penalty > 1 only lowers values, so raw >= x0 is
-//      necessary for a candidate); vectors holding suppressed ids or EOS are always marked;
-//   3. the marked vectors are listed in index order and re-read (L1 / L2); each element with raw >= x0 becomes a
-//      raw candidate, and each raw candidate's exact value (penalty, mask, temperature: Sampler.cs:31,
-//      TalkerGenerator.cs:247-248, Sampler.cs:40) is kept when >= tau: the candidates, in index order;
+//   2. mark pass: lane l reads vectors l, l + 32, ... of each part (every warp load is 512 contiguous bytes); a
+//      vector is marked when its largest raw value is >= x0, the smallest raw value whose temperature-scaled value
+//      reaches the threshold tau (a penalty > 1 only lowers values, so raw >= x0 is necessary for a candidate);
+//      vectors holding suppressed ids or EOS are always marked;
+//   3. the marked vectors are listed in index order (one ballot per step of 32 vectors) and re-read (L1 / L2); each
+//      element with raw >= x0 becomes a raw candidate, and each raw candidate's exact value (penalty, mask,
+//      temperature: Sampler.cs:31, TalkerGenerator.cs:247-248, Sampler.cs:40) is kept when >= tau: the candidates,
+//      in index order (lane l holds positions l, l + 32, ... from here on);
 //   4. with K <= C <= 256 candidates the K-th largest value is >= tau, so the candidates hold every survivor of the
 //      top-k cut (Sampler.cs:42-49); a count over value buckets finds the K-th largest;
 //   5. softmax numerators (libm exp, Sampler.cs:57) in 64-bit fixed point, the top-p cut over the ascending order
@@ -88,36 +89,43 @@ __device__ __forceinline__ uint4 neg_inf_vec(int VW) {
     return make_uint4(n, n, n, n);
 }
 
-// Mark pass over one part (global vectors [v0, v0 + nv), lane l taking [l * cpl, (l + 1) * cpl)): bit i of the
-// result is set when vector l * cpl + i holds a raw value >= x0.
+// Mark pass over one part (global vectors [v0, v0 + nv), lane l taking vectors l, l + 32, ...: each warp load is 512
+// contiguous bytes): bit i of the result is set when vector v0 + 32 i + l holds a raw value >= x0, or holds
+// suppressed ids ([spec_a, spec_b]) or the blocked EOS (ev).
 template <int VW>
-__device__ __forceinline__ uint32_t mark_part(const uint4* row, int v0, int nv, int cpl, float x0, int lane) {
+__device__ __forceinline__ uint32_t mark_part(const uint4* row, int v0, int nv, float x0, int spec_a, int spec_b, int ev,
+                                              int lane) {
     uint32_t marks = 0u;
-    const int q0 = lane * cpl;
-    const int nmine = min(cpl, max(nv - q0, 0));   // this lane's vectors
-    const uint4* mine = row + v0 + q0;
-    for (int b0 = 0; b0 < nmine; b0 += kRwBatch) {
+    const int steps = (nv + 31) >> 5;
+    for (int b0 = 0; b0 < steps; b0 += kRwBatch) {
         uint4 v[kRwBatch];
 #pragma unroll
-        for (int i = 0; i < kRwBatch; ++i) v[i] = (b0 + i < nmine) ? __ldg(mine + b0 + i) : neg_inf_vec(VW);
+        for (int i = 0; i < kRwBatch; ++i) {
+            const int q = ((b0 + i) << 5) + lane;
+            v[i] = q < nv ? __ldg(row + v0 + q) : neg_inf_vec(VW);
+        }
         uint32_t m = 0u;
 #pragma unroll
-        for (int i = 0; i < kRwBatch; ++i)
-            if (vec_max<VW>(v[i]) >= x0) m |= 1u << i;
+        for (int i = 0; i < kRwBatch; ++i) {
+            const int q = ((b0 + i) << 5) + lane, gv = v0 + q;
+            const bool spec = q < nv && ((gv >= spec_a && gv <= spec_b) || gv == ev);
+            if (spec || vec_max<VW>(v[i]) >= x0) m |= 1u << i;
+        }
         marks |= m << b0;
     }
     return marks;
 }
 
-// Bits of lane l's chunk [l * cpl, ...) of a part starting at global vector v0 that fall in [a, b] (global).
-__device__ __forceinline__ uint32_t chunk_bits(int v0, int nv, int cpl, int a, int b, int lane) {
-    const int lo = v0 + lane * cpl;
-    const int hi = min(lo + cpl, v0 + nv) - 1;   // inclusive
-    const int x = max(a, lo), y = min(b, hi);
-    if (x > y) return 0u;
-    const int n = y - x + 1;
-    const uint32_t ones = n >= 32 ? 0xffffffffu : ((1u << n) - 1u);
-    return ones << (x - lo);
+// Lists the marked vectors of one part (bit i of lane l: vector v0 + 32 i + l) in index order at a.vlist[o..].
+__device__ __forceinline__ void list_part(uint32_t marks, int v0, int nv, uint16_t* vlist, int o, int lane) {
+    const int steps = (nv + 31) >> 5;
+    const uint32_t lt = (1u << lane) - 1u;
+    for (int i = 0; i < steps; ++i) {
+        const bool on = (marks >> i) & 1u;
+        const unsigned bal = __ballot_sync(kFull, on);
+        if (on) vlist[o + __popc(bal & lt)] = static_cast<uint16_t>(v0 + (i << 5) + lane);
+        o += __popc(bal);
+    }
 }
 
 // Exclusive prefix of v over the lanes; `total` = the sum over all lanes.
@@ -219,30 +227,17 @@ __device__ bool rw_collect(const RwRow& r, const DevSegment& sg, float tau, floa
                            bool& hist_bad, RwArea& a, int lane, int& C, float& mx) {
     constexpr int vsh = VW == 4 ? 2 : 3;
     // marks, with the vectors holding suppressed ids (and EOS while it is blocked) always marked
-    uint32_t mA = mark_part<VW>(r.row, 0, sg.va, sg.cpl_a, x0, lane);
-    uint32_t mC = sg.vc > 0 ? mark_part<VW>(r.row, sg.c0, sg.vc, sg.cpl_c, x0, lane) : 0u;
-    mA |= chunk_bits(0, sg.va, sg.cpl_a, sg.spec_a, sg.spec_b, lane);
-    if (sg.vc > 0) mC |= chunk_bits(sg.c0, sg.vc, sg.cpl_c, sg.spec_a, sg.spec_b, lane);
     const int ev = (r.kind == 0 && r.eos_blocked && r.eos >= 0 && r.eos < r.V) ? (r.eos >> vsh) : -1;
-    if (ev >= 0) {
-        mA |= chunk_bits(0, sg.va, sg.cpl_a, ev, ev, lane);
-        if (sg.vc > 0) mC |= chunk_bits(sg.c0, sg.vc, sg.cpl_c, ev, ev, lane);
-    }
+    const uint32_t mA = mark_part<VW>(r.row, 0, sg.va, x0, sg.spec_a, sg.spec_b, ev, lane);
+    const uint32_t mC = sg.vc > 0 ? mark_part<VW>(r.row, sg.c0, sg.vc, x0, sg.spec_a, sg.spec_b, ev, lane) : 0u;
     // list in index order: part A, the EOS vector, part C
-    int tA, tC;
-    const int oA = warp_excl_i(__popc(mA), lane, tA);
-    const int oC = warp_excl_i(__popc(mC), lane, tC);
+    const int tA = __reduce_add_sync(kFull, __popc(mA)), tC = __reduce_add_sync(kFull, __popc(mC));
     const int ne = sg.eosv >= 0 ? 1 : 0;
     const int M = tA + ne + tC;
     if (M > kRwRawCap) return false;
-    {
-        int o = oA;
-        for (uint32_t m = mA; m; m &= m - 1u) a.vlist[o++] = static_cast<uint16_t>(lane * sg.cpl_a + __ffs(m) - 1);
-        if (ne && lane == 0) a.vlist[tA] = static_cast<uint16_t>(sg.eosv);
-        o = tA + ne + oC;
-        for (uint32_t m = mC; m; m &= m - 1u)
-            a.vlist[o++] = static_cast<uint16_t>(sg.c0 + lane * sg.cpl_c + __ffs(m) - 1);
-    }
+    list_part(mA, 0, sg.va, a.vlist, 0, lane);
+    if (ne && lane == 0) a.vlist[tA] = static_cast<uint16_t>(sg.eosv);
+    if (sg.vc > 0) list_part(mC, sg.c0, sg.vc, a.vlist, tA + ne, lane);
     __syncwarp();
     // raw candidates: elements >= x0 of the listed vectors (every element of a vector with suppressed ids); the
     // re-reads of up to kRwPre * 32 listed vectors are all in flight before the first is used
