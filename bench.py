@@ -453,7 +453,7 @@ def head_timing(dev, torch, hbm, hbm_kind, reps=50, cases=((64, 3072), (1024, 30
 
 def frame_loop_timing(dev, torch, streams=1024, reps=10):
     """One frame of the device loop for `streams` sequences (config 3's stream count; hidden 1024, Qwen3-TTS
-    vocabularies): vw_batch_talker_head_step, code embedding 0, 15 x (vw_batch_sub_head_step + code embedding),
+    vocabularies): vw_batch_talker_head_step, 15 x vw_batch_sub_head_step (each with its next-input gather),
     vw_batch_frame_embedding -- everything of TalkerGenerator.cs:362-439 except the transformer steps, whose hidden
     rows are fixed random inputs here.  Talker options as config 3 (top-k 50, top-p 0.8, rp 1.05, 1024-id
     histories), sub-talker top-k 50; `reps` frames in one CUDA graph (graph_us)."""
@@ -476,12 +476,10 @@ def frame_loop_timing(dev, torch, streams=1024, reps=10):
     for s in range(streams):
         state.start(s, job, hist[s].tolist())
 
-    def frame(sp):
-        state.talker_head_step(last, codec_head, stream=sp)
-        state.code_embedding(0, codec_emb, cp_in, stream=sp)
+    def frame(sp):   # the next-input gathers ride along with the head steps
+        state.talker_head_step(last, codec_head, codec_emb, cp_in, stream=sp)
         for grp in range(1, G):
-            state.sub_head_step(grp, cp_hidden, cp_heads[grp - 1], stream=sp)
-            state.code_embedding(grp, cp_emb[grp - 1], cp_in, stream=sp)
+            state.sub_head_step(grp, cp_hidden, cp_heads[grp - 1], cp_emb[grp - 1], cp_in, stream=sp)
         state.frame_embedding(codec_emb, cp_emb, text, step_in, stream=sp)
 
     st = torch.cuda.Stream()
@@ -489,10 +487,10 @@ def frame_loop_timing(dev, torch, streams=1024, reps=10):
     dev.synchronize(st.cuda_stream)
     steps = state.query(0)[0]
     state.close()
-    # kernels per frame: talker (GEMM, draw, 2 sampler, commit) + code embedding + 15 x (GEMM, draw, 2 sampler,
-    # record, code embedding) + frame embedding
+    # kernels per frame: talker (GEMM, draw, 2 sampler, commit + gather) + 15 x (GEMM, draw, 2 sampler,
+    # record + gather) + frame embedding
     return {"streams": streams, "hidden": H, "us_per_frame": us, "frames_per_s": 1e6 / us,
-            "sampled_rows_per_s": streams * G / (us * 1e-6), "kernels_per_frame": 5 + 1 + 15 * 6 + 1,
+            "sampled_rows_per_s": streams * G / (us * 1e-6), "kernels_per_frame": 5 + 15 * 5 + 1,
             "slot0_steps_after_timing": steps, "note": "talker EOS logit held at 0 (no slot retires while timing)"}
 
 

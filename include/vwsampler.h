@@ -242,10 +242,11 @@ vw_status vw_batch_query(vw_batch* batch, int32_t slot, int32_t* step, int32_t* 
  * code 0 of every slot that goes on to the code predictor and -1 for the others (idle, or retired at this step by
  * EOS or MaxNewTokens); sub-talker head step `group` records codebook `group`.  Per frame:
  *   vw_batch_talker_head_step                 codebook 0 from the talker's last hidden rows      (:366-385, :443)
- *   vw_batch_code_embedding(group 0)          CodecEmbedding(code0), the code predictor's 2nd input row (:411)
+ *                                             + CodecEmbedding(code0), the code predictor's 2nd input row (:411)
  *   for group = 1..15:
  *     vw_batch_sub_head_step(group)           CodePredictorHead(group) + SubSampler.Select          (:418-420)
- *     vw_batch_code_embedding(group)          CodePredictorEmbedding(group, code), next input    (:422)
+ *                                             + CodePredictorEmbedding(group, code), the next input (:422)
+ * (the gathers ride along with a vw_embed_out; vw_batch_code_embedding does them alone)
  *   vw_batch_frame_embedding                  FrameEmbedding(frame) + text, the next talker input (:428-439)
  * Head steps: hidden [n_slots, hidden_size] and weight [vocab, hidden_size] bf16 as in vw_head_logits (rows of
  * idle slots are multiplied but not sampled); the logits live in a buffer of the batch.  The ids come out as in
@@ -253,12 +254,27 @@ vw_status vw_batch_query(vw_batch* batch, int32_t slot, int32_t* step, int32_t* 
  * stream-ordered and allocate nothing after a batch's first head step of the largest vocab, so a frame can be
  * captured in a CUDA graph.
  */
+/* Where a head step also writes the next input row of each slot whose frame goes on: out[s] (row pitch out_stride
+ * floats) = bf16 -> fp32 of table[code] -- CodecEmbedding(code0) for the talker step (TalkerGenerator.cs:411),
+ * CodePredictorEmbedding(group, code) for a sub-talker step (:422).  table: [table_rows, hidden] bf16 bits, hidden a
+ * multiple of 8 (the talker's hidden size in voxwerk, which the code predictor's embeddings share); 16-byte aligned
+ * device memory.  The same as a vw_batch_code_embedding call after the step, in the step's last kernel. */
+typedef struct vw_embed_out {
+    const void* table;
+    int32_t table_rows;
+    int32_t hidden;
+    float* out;
+    int64_t out_stride;
+} vw_embed_out;
+
 vw_status vw_batch_talker_head_step(vw_batch* batch, const void* hidden, int64_t hidden_stride, int32_t hidden_size,
                                     const void* weight, int64_t weight_stride, const vw_options* options,
-                                    int32_t n_options, int32_t* out_ids, int32_t* out_done, void* stream);
+                                    int32_t n_options, int32_t* out_ids, int32_t* out_done,
+                                    const vw_embed_out* embed /* NULL: no gather */, void* stream);
 vw_status vw_batch_sub_head_step(vw_batch* batch, int32_t group, const void* hidden, int64_t hidden_stride,
                                  int32_t hidden_size, const void* weight, int64_t weight_stride, int32_t vocab,
-                                 const vw_options* options, int32_t n_options, int32_t* out_ids, void* stream);
+                                 const vw_options* options, int32_t n_options, int32_t* out_ids,
+                                 const vw_embed_out* embed /* NULL: no gather */, void* stream);
 /* out[s] (row pitch out_stride floats) = bf16 -> fp32 of table row codes[s][group] for every slot whose frame goes
  * on (codes[s][0] >= 0); other rows are left alone.  table: [table_rows, hidden] bf16 bits (group 0: the talker
  * codec embedding, vocab rows; group g: code-predictor embedding g-1).  A code outside the table returns

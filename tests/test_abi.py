@@ -58,6 +58,9 @@ int main(void) {
   printf("vw_slot_config %zu\n", sizeof(vw_slot_config));
   F(vw_slot_config, talker_option) F(vw_slot_config, sub_option) F(vw_slot_config, max_new_tokens)
   F(vw_slot_config, seed) F(vw_slot_config, seeded)
+  printf("vw_embed_out %zu\n", sizeof(vw_embed_out));
+  F(vw_embed_out, table) F(vw_embed_out, table_rows) F(vw_embed_out, hidden) F(vw_embed_out, out)
+  F(vw_embed_out, out_stride)
   return 0;
 }
 '''
@@ -76,8 +79,9 @@ def test_ctypes_structs_match_c_layout():
     assert lay["vw_segment"] == ctypes.sizeof(_lib.VwSegment)
     assert lay["vw_stats"] == ctypes.sizeof(_lib.VwStats)
     assert lay["vw_slot_config"] == ctypes.sizeof(_lib.VwSlotConfig)
+    assert lay["vw_embed_out"] == ctypes.sizeof(_lib.VwEmbedOut)
     for cls, cname in ((_lib.VwOptions, "vw_options"), (_lib.VwSegment, "vw_segment"),
-                       (_lib.VwSlotConfig, "vw_slot_config")):
+                       (_lib.VwSlotConfig, "vw_slot_config"), (_lib.VwEmbedOut, "vw_embed_out")):
         for fname, _ in cls._fields_:
             key = "eos_id" if fname == "eos_id" else fname
             assert getattr(cls, fname).offset == lay[f"{cname}.{key}"], (cname, fname)

@@ -1,7 +1,8 @@
 """The device frame loop (vw_batch_*_head_step, vw_batch_code_embedding, vw_batch_frame_embedding) against the
 reference's GenerateBatch frame (TalkerGenerator.cs:362-439) run on the host with the CPU oracle.
 
-The caller's transformer steps are replaced by a fixed stand-in (next hidden rows = bf16 of the previous step's
+Even frames gather the next code-predictor inputs inside the head steps (vw_embed_out), odd frames with separate
+vw_batch_code_embedding calls.  The caller's transformer steps are replaced by a fixed stand-in (next hidden rows = bf16 of the previous step's
 input rows), applied identically on both sides.  Per frame the host side: samples codebook 0 of every running job
 (oracle, the job's Random(Seed) draws) from CodecHead's logits, appends it, retires on EOS / MaxNewTokens; for the
 survivors gathers CodecEmbedding(code0), then for g = 1..15 samples from CodePredictorHead(g)'s logits (Random(Seed + 1)
@@ -83,7 +84,8 @@ def test_device_frame_loop_matches_generate_batch(device):
         logits = torch.empty((n, V), dtype=torch.float32, device="cuda")
         head_logits(device, hidden, codec_head, logits)
         lg = logits.cpu().numpy()
-        ids, done = state.talker_head_step(hidden, codec_head)
+        fused = frame % 2 == 0   # even frames: the gathers ride along with the head steps
+        ids, done = state.talker_head_step(hidden, codec_head, *((codec_emb, cp_in) if fused else ()))
         ids, done = ids.cpu().numpy(), done.cpu().numpy()
         going = []
         for s, job in enumerate(host):
@@ -103,7 +105,8 @@ def test_device_frame_loop_matches_generate_batch(device):
             frame_codes[s, 0] = ids[s]
         np.testing.assert_array_equal(state.codes()[:, 0], frame_codes[:, 0])
 
-        state.code_embedding(0, codec_emb, cp_in)                     # CodecEmbedding(code0), :411
+        if not fused:
+            state.code_embedding(0, codec_emb, cp_in)                 # CodecEmbedding(code0), :411
         for s in going:
             ref_cp_in[s] = _widen(codec_emb_bits[frame_codes[s, 0]])
         for g in range(1, G):
@@ -113,13 +116,15 @@ def test_device_frame_loop_matches_generate_batch(device):
             cl = torch.empty((n, CV), dtype=torch.float32, device="cuda")
             head_logits(device, cp_hidden, cp_heads[g - 1], cl)
             cl = cl.cpu().numpy()
-            sub = state.sub_head_step(g, cp_hidden, cp_heads[g - 1]).cpu().numpy()
+            sub = state.sub_head_step(g, cp_hidden, cp_heads[g - 1],
+                                      *((cp_emb[g - 1], cp_in) if fused else ())).cpu().numpy()
             for s, job in enumerate(host):
                 want = _sub_ref(job, cl[s]) if s in going else -1
                 assert sub[s] == want, (frame, g, s, int(sub[s]), want)
                 if s in going:
                     frame_codes[s, g] = want
-            state.code_embedding(g, cp_emb[g - 1], cp_in)             # CodePredictorEmbedding(g, code), :422
+            if not fused:
+                state.code_embedding(g, cp_emb[g - 1], cp_in)         # CodePredictorEmbedding(g, code), :422
             for s in going:
                 ref_cp_in[s] = _widen(cp_emb_bits[g - 1][frame_codes[s, g]])
         codes = state.codes()

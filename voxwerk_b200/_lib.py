@@ -109,6 +109,18 @@ class VwSlotConfig(ctypes.Structure):
     ]
 
 
+class VwEmbedOut(ctypes.Structure):
+    """vw_embed_out: the next input row a head step also gathers for each continuing slot."""
+
+    _fields_ = [
+        ("table", ctypes.c_void_p),
+        ("table_rows", ctypes.c_int32),
+        ("hidden", ctypes.c_int32),
+        ("out", ctypes.c_void_p),
+        ("out_stride", ctypes.c_int64),
+    ]
+
+
 class VwStats(ctypes.Structure):
     """vw_stats: rows sampled per path."""
 
@@ -190,9 +202,9 @@ def _load() -> ctypes.CDLL:
                        ("vw_frame_embedding", [vp, vp, i32, i32, i32, vp, i32, vp, i32, vp, vp, vp]),
                        ("vw_head_logits", [vp, vp, i64, i32, vp, i64, i32, i32, vp, vp]),
                        ("vw_batch_talker_head_step", [vp, vp, i64, i32, vp, i64, ctypes.POINTER(VwOptions), i32, vp,
-                                                      vp, vp]),
+                                                      vp, ctypes.POINTER(VwEmbedOut), vp]),
                        ("vw_batch_sub_head_step", [vp, i32, vp, i64, i32, vp, i64, i32, ctypes.POINTER(VwOptions), i32,
-                                                   vp, vp]),
+                                                   vp, ctypes.POINTER(VwEmbedOut), vp]),
                        ("vw_batch_code_embedding", [vp, i32, vp, i32, i32, vp, i64, vp]),
                        ("vw_batch_frame_embedding", [vp, i32, vp, vp, i32, vp, vp, vp]),
                        ("vw_batch_get_codes", [vp, vp]),

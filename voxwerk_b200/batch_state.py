@@ -11,12 +11,10 @@ A step then moves only logits in and ids out:
 or, with the vocabulary heads on the tensor cores and the frame kept on the device (hidden rows from the caller's
 transformer steps):
 
-    ids, done = state.talker_head_step(last_hidden, codec_head)          # :366-385 over CodecHead (:443)
-    state.code_embedding(0, codec_embedding, cp_input)                   # :411
+    ids, done = state.talker_head_step(last_hidden, codec_head, codec_embedding, cp_input)   # :366-385, :411, :443
     for g in range(1, 16):
-        state.sub_head_step(g, cp_hidden, cp_heads[g - 1])               # :418-420
-        state.code_embedding(g, cp_embeddings[g - 1], cp_input)          # :422
-    state.frame_embedding(codec_embedding, cp_embeddings, text, step_input)   # :428-439
+        state.sub_head_step(g, cp_hidden, cp_heads[g - 1], cp_embeddings[g - 1], cp_input)     # :418-422
+    state.frame_embedding(codec_embedding, cp_embeddings, text, step_input)                # :428-439
 
 Logits are CUDA tensors [n_slots, V] (row r belongs to slot r); ids and done flags come back as CUDA int32 tensors.
 Finished slots are not sampled (id -1).  Each step's options table is built from the jobs' options, so slots with
@@ -29,7 +27,7 @@ import ctypes
 from typing import List, Optional, Sequence
 
 from . import _lib
-from ._lib import VW_BF16, VW_F32, VwOptions, VwSlotConfig, check, lib
+from ._lib import VW_BF16, VW_F32, VwEmbedOut, VwOptions, VwSlotConfig, check, lib
 from .qwen3_tts import CODEC_EOS_ID, CP_VOCAB_SIZE, MIN_NEW_TOKENS, SUPPRESS_SPAN, VOCAB_SIZE
 from .sampler import Device, GenerationOptions, vw_options
 
@@ -128,22 +126,33 @@ class DeviceBatchState:
         return (ctypes.c_void_p(hidden.data_ptr()), int(hidden.stride(0)), int(hidden.shape[1]),
                 ctypes.c_void_p(weight.data_ptr()), int(weight.stride(0)))
 
-    def talker_head_step(self, hidden, weight, stream: Optional[int] = None):
+    @staticmethod
+    def _embed(table, out):
+        if table is None:
+            return None
+        return ctypes.byref(VwEmbedOut(table.data_ptr(), int(table.shape[0]), int(table.shape[1]), out.data_ptr(),
+                                       int(out.stride(0))))
+
+    def talker_head_step(self, hidden, weight, embed_table=None, embed_out=None, stream: Optional[int] = None):
         """Codebook 0 from the talker's last hidden rows: logits = hidden x weight^T (CodecHead,
-        TalkerGenerator.cs:443) on the tensor cores, then talker_step over them; (ids, done)."""
+        TalkerGenerator.cs:443) on the tensor cores, then talker_step over them; (ids, done).  With embed_table (the
+        codec embedding) each continuing slot's CodecEmbedding(code0) row also goes to embed_out (:411)."""
         opts = (VwOptions * len(self._talker_opts))(*self._talker_opts)
         check(lib.vw_batch_talker_head_step(self._b, *self._head(hidden, weight), opts, len(self._talker_opts),
                                             ctypes.c_void_p(self.ids.data_ptr()),
-                                            ctypes.c_void_p(self.done.data_ptr()),
+                                            ctypes.c_void_p(self.done.data_ptr()), self._embed(embed_table, embed_out),
                                             ctypes.c_void_p(stream) if stream else None), self.device.handle)
         return self.ids, self.done
 
-    def sub_head_step(self, group: int, hidden, weight, stream: Optional[int] = None):
+    def sub_head_step(self, group: int, hidden, weight, embed_table=None, embed_out=None,
+                      stream: Optional[int] = None):
         """Codebook `group` (1..15): CodePredictorHead(group) then SubSampler.Select (TalkerGenerator.cs:418-420);
-        the ids are also recorded in the batch's frame (codes())."""
+        the ids are also recorded in the batch's frame (codes()).  With embed_table (code-predictor embedding
+        group - 1) each continuing slot's CodePredictorEmbedding(group, code) row also goes to embed_out (:422)."""
         opts = (VwOptions * len(self._sub_opts))(*self._sub_opts)
         check(lib.vw_batch_sub_head_step(self._b, int(group), *self._head(hidden, weight), int(weight.shape[0]),
                                          opts, len(self._sub_opts), ctypes.c_void_p(self.sub_ids.data_ptr()),
+                                         self._embed(embed_table, embed_out),
                                          ctypes.c_void_p(stream) if stream else None), self.device.handle)
         return self.sub_ids
 

@@ -758,7 +758,7 @@ std::vector<vw::DevOptions> dev_options(const vw_options* options, int32_t n) {
 // A talker or sub-talker step: draws, samples every slot (finished ones get id -1), commits talker ids.
 vw_status batch_step(vw_batch* b, int which, const void* logits, int64_t row_stride, int32_t vocab, int32_t dtype,
                      const vw_options* options, int32_t n_options, int32_t* out_ids, int32_t* out_done,
-                     void* stream) {
+                     void* stream, const vw::EmbedOut* emb = nullptr) {
     vw_status r = batch_check(b, options, n_options);
     if (r != VW_OK) return r;
     vw_handle* h = b->h;
@@ -795,7 +795,7 @@ vw_status batch_step(vw_batch* b, int which, const void* logits, int64_t row_str
     r = sample_impl(h, &sg, 1, options, n_options, VW_MEM_DEVICE, st, &ex);
     if (r != VW_OK) return r;
     if (which == 0) {
-        e = vw::launch_batch_commit(b->d, out_ids, out_done, st);
+        e = vw::launch_batch_commit(b->d, out_ids, out_done, emb, h->d_err, st);
         if (e != cudaSuccess) return cuda_fail(h, e, "batch commit");
     }
     if (!stream) return read_device_error(h, st);
@@ -947,12 +947,23 @@ VW_EXPORT vw_status vw_batch_sub_step(vw_batch* b, const void* logits, int64_t r
 
 namespace {
 
+// A caller's vw_embed_out as the kernels take it; false (with the handle's error set) when it is malformed.
+bool embed_out(vw_handle* h, const vw_embed_out* in, vw::EmbedOut* out) {
+    if (!in->table || !in->out || in->table_rows < 1 || in->hidden < 8 || in->hidden % 8 != 0 ||
+        in->out_stride < in->hidden || in->out_stride % 4 != 0 || !aligned(in->table, 16) || !aligned(in->out, 16)) {
+        fail(h, VW_ERR_INVALID_ARG, "embed: 16-byte aligned table and out, hidden a multiple of 8, out_stride >= hidden");
+        return false;
+    }
+    *out = vw::EmbedOut{static_cast<const uint16_t*>(in->table), in->table_rows, in->hidden, in->out, in->out_stride};
+    return true;
+}
+
 // The head GEMM into the batch's logits buffer (all n_slots rows), then a talker (which 0) or sub-talker step over
 // those logits; a sub-talker step records its ids as codebook `group` of each slot's frame.
 vw_status batch_head_step(vw_batch* b, int which, int group, const void* hidden, int64_t hidden_stride,
                           int32_t hidden_size, const void* weight, int64_t weight_stride, int32_t vocab,
                           const vw_options* options, int32_t n_options, int32_t* out_ids, int32_t* out_done,
-                          void* stream) {
+                          const vw_embed_out* embed, void* stream) {
     vw_status r = batch_check(b, options, n_options);
     if (r != VW_OK) return r;
     vw_handle* h = b->h;
@@ -961,6 +972,8 @@ vw_status batch_head_step(vw_batch* b, int which, int group, const void* hidden,
     if (!out_ids) return fail(h, VW_ERR_INVALID_ARG, "out_ids is required");
     if (which == 1 && (group < 1 || group >= vw::kMaxCodeGroups))
         return fail(h, VW_ERR_INVALID_ARG, "group must be in [1, 15]");
+    vw::EmbedOut emb{};
+    if (embed && !embed_out(h, embed, &emb)) return VW_ERR_INVALID_ARG;
     DeviceGuard guard(h->device);
     if (!guard.ok()) return fail(h, VW_ERR_CUDA, "cudaSetDevice failed");
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : h->stream;
@@ -979,10 +992,11 @@ vw_status batch_head_step(vw_batch* b, int which, int group, const void* hidden,
         e = vw::launch_head_gemm(hidden, hidden_stride, weight, weight_stride, b->d.n_slots, vocab, hidden_size,
                                  b->d_logits, vocab, h->d_err, st);
     if (e != cudaSuccess) return cuda_fail(h, e, "head GEMM");
-    r = batch_step(b, which, b->d_logits, vocab, vocab, VW_F32, options, n_options, out_ids, out_done, st);
+    r = batch_step(b, which, b->d_logits, vocab, vocab, VW_F32, options, n_options, out_ids, out_done, st,
+                   embed ? &emb : nullptr);
     if (r != VW_OK) return r;
     if (which == 1) {
-        e = vw::launch_batch_record_codes(b->d, out_ids, group, st);
+        e = vw::launch_batch_record_codes(b->d, out_ids, group, embed ? &emb : nullptr, h->d_err, st);
         if (e != cudaSuccess) return cuda_fail(h, e, "record codes");
     }
     if (!stream) return read_device_error(h, st);
@@ -994,17 +1008,17 @@ vw_status batch_head_step(vw_batch* b, int which, int group, const void* hidden,
 VW_EXPORT vw_status vw_batch_talker_head_step(vw_batch* b, const void* hidden, int64_t hidden_stride,
                                               int32_t hidden_size, const void* weight, int64_t weight_stride,
                                               const vw_options* options, int32_t n_options, int32_t* out_ids,
-                                              int32_t* out_done, void* stream) {
+                                              int32_t* out_done, const vw_embed_out* embed, void* stream) {
     return batch_head_step(b, 0, 0, hidden, hidden_stride, hidden_size, weight, weight_stride, b ? b->vocab : 0,
-                           options, n_options, out_ids, out_done, stream);
+                           options, n_options, out_ids, out_done, embed, stream);
 }
 
 VW_EXPORT vw_status vw_batch_sub_head_step(vw_batch* b, int32_t group, const void* hidden, int64_t hidden_stride,
                                            int32_t hidden_size, const void* weight, int64_t weight_stride,
                                            int32_t vocab, const vw_options* options, int32_t n_options,
-                                           int32_t* out_ids, void* stream) {
+                                           int32_t* out_ids, const vw_embed_out* embed, void* stream) {
     return batch_head_step(b, 1, group, hidden, hidden_stride, hidden_size, weight, weight_stride, vocab, options,
-                           n_options, out_ids, nullptr, stream);
+                           n_options, out_ids, nullptr, embed, stream);
 }
 
 VW_EXPORT vw_status vw_batch_code_embedding(vw_batch* b, int32_t group, const void* table, int32_t table_rows,
@@ -1013,16 +1027,15 @@ VW_EXPORT vw_status vw_batch_code_embedding(vw_batch* b, int32_t group, const vo
     vw_handle* h = b->h;
     h->last_error.clear();
     if (group < 0 || group >= vw::kMaxCodeGroups) return fail(h, VW_ERR_INVALID_ARG, "group must be in [0, 15]");
-    if (!table || !out || table_rows < 1 || hidden < 8 || hidden % 8 != 0 || out_stride < hidden ||
-        out_stride % 4 != 0 || !aligned(table, 16) || !aligned(out, 16))
-        return fail(h, VW_ERR_INVALID_ARG, "16-byte aligned table and out, hidden a multiple of 8");
+    const vw_embed_out in{table, table_rows, hidden, out, out_stride};
+    vw::EmbedOut emb{};
+    if (!embed_out(h, &in, &emb)) return VW_ERR_INVALID_ARG;
     DeviceGuard guard(h->device);
     if (!guard.ok()) return fail(h, VW_ERR_CUDA, "cudaSetDevice failed");
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : h->stream;
     cudaError_t e = stream ? cudaSuccess : cudaMemsetAsync(h->d_err, 0, sizeof(unsigned), st);
     if (e == cudaSuccess)
-        e = vw::launch_batch_code_embedding(b->d, group, static_cast<const uint16_t*>(table), table_rows, hidden, out,
-                                            out_stride, h->d_err, st);
+        e = vw::launch_batch_code_embedding(b->d, group, emb, h->d_err, st);
     if (e != cudaSuccess) return cuda_fail(h, e, "code embedding");
     if (!stream) return read_device_error(h, st);
     return VW_OK;

@@ -53,9 +53,28 @@ __global__ void draw_kernel(BatchDevice b, int which, OptTable t, double* unifor
     uniforms[s] = u;
 }
 
-__global__ void commit_kernel(BatchDevice b, const int32_t* ids, int32_t* out_done) {
-    const int s = blockIdx.x * blockDim.x + threadIdx.x;
-    if (s >= b.n_slots) return;
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }   // Bf16.cs:13
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// out[s] = bf16 -> fp32 of table row `code` (AddRow with add: false, TalkerModel.cs:120-125): the CTA's threads take 8
+// values each per step.  A code outside the table sets kErrCodeRange (ArgumentOutOfRangeException, TalkerModel.cs:102,
+// 109) and writes nothing.
+__device__ __forceinline__ void gather_row(const EmbedOut& e, int s, int code, unsigned* err) {
+    if (static_cast<unsigned>(code) >= static_cast<unsigned>(e.table_rows)) {
+        if (threadIdx.x == 0) atomicOr(err, kErrCodeRange);
+        return;
+    }
+    const uint16_t* src = e.table + static_cast<int64_t>(code) * e.hidden;
+    float* dst = e.out + static_cast<int64_t>(s) * e.out_stride;
+    for (int i0 = threadIdx.x * 8; i0 < e.hidden; i0 += blockDim.x * 8) {
+        const uint4 u = *reinterpret_cast<const uint4*>(src + i0);
+        *reinterpret_cast<float4*>(dst + i0) = make_float4(bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y));
+        *reinterpret_cast<float4*>(dst + i0 + 4) = make_float4(bf16_lo(u.z), bf16_hi(u.z), bf16_lo(u.w), bf16_hi(u.w));
+    }
+}
+
+// The talker step's bookkeeping for slot s; returns code 0 of the frame slot s goes on with, or -1.
+__device__ __forceinline__ int32_t commit_slot(const BatchDevice& b, int s, const int32_t* ids, int32_t* out_done) {
     int32_t done = 0;
     if (b.active[s]) {
         const int32_t id = ids[s];
@@ -73,7 +92,25 @@ __global__ void commit_kernel(BatchDevice b, const int32_t* ids, int32_t* out_do
     }
     if (out_done) out_done[s] = done;
     // f[0] = code0 for the jobs that go on to the code predictor (:382-384)
-    b.codes[static_cast<int64_t>(s) * kMaxCodeGroups] = (b.active[s] && !done) ? ids[s] : -1;
+    const int32_t c0 = (b.active[s] && !done) ? ids[s] : -1;
+    b.codes[static_cast<int64_t>(s) * kMaxCodeGroups] = c0;
+    return c0;
+}
+
+__global__ void commit_kernel(BatchDevice b, const int32_t* ids, int32_t* out_done) {
+    const int s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s < b.n_slots) commit_slot(b, s, ids, out_done);
+}
+
+// commit_kernel and, for every slot that goes on, its CodecEmbedding(code0) row (TalkerGenerator.cs:411): one CTA
+// per slot
+__global__ void __launch_bounds__(128) commit_embed_kernel(BatchDevice b, const int32_t* ids, int32_t* out_done,
+                                                           EmbedOut e, unsigned* err) {
+    const int s = blockIdx.x;
+    __shared__ int32_t code;
+    if (threadIdx.x == 0) code = commit_slot(b, s, ids, out_done);
+    __syncthreads();
+    if (code >= 0) gather_row(e, s, code, err);
 }
 
 __global__ void record_codes_kernel(BatchDevice b, const int32_t* ids, int group) {
@@ -81,28 +118,24 @@ __global__ void record_codes_kernel(BatchDevice b, const int32_t* ids, int group
     if (s < b.n_slots) b.codes[static_cast<int64_t>(s) * kMaxCodeGroups + group] = ids[s];   // keepFrames[i][g] (:420)
 }
 
-__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }   // Bf16.cs:13
-__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+// record_codes_kernel and, for every slot whose frame goes on, the CodePredictorEmbedding(group, code) row
+// (TalkerGenerator.cs:422): one CTA per slot
+__global__ void __launch_bounds__(128) record_embed_kernel(BatchDevice b, const int32_t* ids, int group, EmbedOut e,
+                                                           unsigned* err) {
+    const int s = blockIdx.x;
+    const int64_t base = static_cast<int64_t>(s) * kMaxCodeGroups;
+    const int32_t id = ids[s];
+    if (threadIdx.x == 0) b.codes[base + group] = id;
+    if (b.codes[base] < 0 || id < 0) return;   // the slot is idle or retired at this frame's talker step
+    gather_row(e, s, id, err);
+}
 
-// one CTA per slot, 8 bf16 per thread and step (AddRow with add: false, TalkerModel.cs:120-125)
-__global__ void __launch_bounds__(128) code_embedding_kernel(BatchDevice b, int group, const uint16_t* table,
-                                                             int table_rows, int hidden, float* out,
-                                                             int64_t out_stride, unsigned* err) {
+// the gather alone, from the codes table (one CTA per slot)
+__global__ void __launch_bounds__(128) code_embedding_kernel(BatchDevice b, int group, EmbedOut e, unsigned* err) {
     const int s = blockIdx.x;
     const int64_t base = static_cast<int64_t>(s) * kMaxCodeGroups;
     if (b.codes[base] < 0) return;   // the slot is idle or retired at this frame's talker step
-    const int code = b.codes[base + group];
-    if (static_cast<unsigned>(code) >= static_cast<unsigned>(table_rows)) {
-        if (threadIdx.x == 0) atomicOr(err, kErrCodeRange);   // ArgumentOutOfRangeException (TalkerModel.cs:102,109)
-        return;
-    }
-    const uint16_t* src = table + static_cast<int64_t>(code) * hidden;
-    float* dst = out + static_cast<int64_t>(s) * out_stride;
-    for (int i0 = threadIdx.x * 8; i0 < hidden; i0 += blockDim.x * 8) {
-        const uint4 u = *reinterpret_cast<const uint4*>(src + i0);
-        *reinterpret_cast<float4*>(dst + i0) = make_float4(bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y));
-        *reinterpret_cast<float4*>(dst + i0 + 4) = make_float4(bf16_lo(u.z), bf16_hi(u.z), bf16_lo(u.w), bf16_hi(u.w));
-    }
+    gather_row(e, s, b.codes[base + group], err);
 }
 
 }  // namespace
@@ -117,22 +150,31 @@ cudaError_t launch_batch_draw(const BatchDevice& b, int which, const DevOptions*
     return cudaGetLastError();
 }
 
-cudaError_t launch_batch_commit(const BatchDevice& b, const int32_t* ids, int32_t* out_done, cudaStream_t stream) {
-    const int threads = 128, blocks = (b.n_slots + threads - 1) / threads;
-    commit_kernel<<<blocks, threads, 0, stream>>>(b, ids, out_done);
+cudaError_t launch_batch_commit(const BatchDevice& b, const int32_t* ids, int32_t* out_done, const EmbedOut* e,
+                                unsigned* err, cudaStream_t stream) {
+    if (e) {
+        commit_embed_kernel<<<b.n_slots, 128, 0, stream>>>(b, ids, out_done, *e, err);
+    } else {
+        const int threads = 128, blocks = (b.n_slots + threads - 1) / threads;
+        commit_kernel<<<blocks, threads, 0, stream>>>(b, ids, out_done);
+    }
     return cudaGetLastError();
 }
 
-cudaError_t launch_batch_record_codes(const BatchDevice& b, const int32_t* ids, int group, cudaStream_t stream) {
-    const int threads = 128, blocks = (b.n_slots + threads - 1) / threads;
-    record_codes_kernel<<<blocks, threads, 0, stream>>>(b, ids, group);
+cudaError_t launch_batch_record_codes(const BatchDevice& b, const int32_t* ids, int group, const EmbedOut* e,
+                                      unsigned* err, cudaStream_t stream) {
+    if (e) {
+        record_embed_kernel<<<b.n_slots, 128, 0, stream>>>(b, ids, group, *e, err);
+    } else {
+        const int threads = 128, blocks = (b.n_slots + threads - 1) / threads;
+        record_codes_kernel<<<blocks, threads, 0, stream>>>(b, ids, group);
+    }
     return cudaGetLastError();
 }
 
-cudaError_t launch_batch_code_embedding(const BatchDevice& b, int group, const uint16_t* table, int table_rows,
-                                        int hidden, float* out, int64_t out_stride, unsigned* err,
+cudaError_t launch_batch_code_embedding(const BatchDevice& b, int group, const EmbedOut& e, unsigned* err,
                                         cudaStream_t stream) {
-    code_embedding_kernel<<<b.n_slots, 128, 0, stream>>>(b, group, table, table_rows, hidden, out, out_stride, err);
+    code_embedding_kernel<<<b.n_slots, 128, 0, stream>>>(b, group, e, err);
     return cudaGetLastError();
 }
 

@@ -128,15 +128,26 @@ struct BatchDevice {
 // One NextDouble() into uniforms[s] for every active slot whose option samples (which: 0 talker, 1 sub-talker).
 cudaError_t launch_batch_draw(const BatchDevice& b, int which, const DevOptions* opts, int n_opts, double* uniforms,
                               cudaStream_t stream);
+// Where a slot's gathered embedding row goes: out[s] (row pitch out_stride floats) = bf16 -> fp32 of table row code
+// (table [table_rows, hidden] bf16 bits, hidden a multiple of 8, 16-byte aligned rows).
+struct EmbedOut {
+    const uint16_t* table;
+    int table_rows, hidden;
+    float* out;
+    int64_t out_stride;
+};
 // Appends ids[s] to every active slot's history, then retires the slot (EOS or last step) or advances its step;
-// records code 0 of the frame of every slot that continues (-1 for the others).
-cudaError_t launch_batch_commit(const BatchDevice& b, const int32_t* ids, int32_t* out_done, cudaStream_t stream);
-// codes[s][group] = ids[s] for every slot (a code-predictor group's ids; -1 where the slot did not sample).
-cudaError_t launch_batch_record_codes(const BatchDevice& b, const int32_t* ids, int group, cudaStream_t stream);
-// out[s] = bf16 -> fp32 of table row codes[s][group] for every continuing slot (TalkerModel.CodecEmbedding for
-// group 0, CodePredictorEmbedding for groups 1..15); other rows are left alone.  err collects kErrCodeRange.
-cudaError_t launch_batch_code_embedding(const BatchDevice& b, int group, const uint16_t* table, int table_rows,
-                                        int hidden, float* out, int64_t out_stride, unsigned* err,
+// records code 0 of the frame of every slot that continues (-1 for the others) and, with `e`, gathers that code's
+// row of e->table for it.  err collects kErrCodeRange.
+cudaError_t launch_batch_commit(const BatchDevice& b, const int32_t* ids, int32_t* out_done, const EmbedOut* e,
+                                unsigned* err, cudaStream_t stream);
+// codes[s][group] = ids[s] for every slot (a code-predictor group's ids; -1 where the slot did not sample) and, with
+// `e`, the row of e->table for each slot whose frame goes on.
+cudaError_t launch_batch_record_codes(const BatchDevice& b, const int32_t* ids, int group, const EmbedOut* e,
+                                      unsigned* err, cudaStream_t stream);
+// The row of e.table at codes[s][group] for every continuing slot (TalkerModel.CodecEmbedding for group 0,
+// CodePredictorEmbedding for groups 1..15); other rows are left alone.
+cudaError_t launch_batch_code_embedding(const BatchDevice& b, int group, const EmbedOut& e, unsigned* err,
                                         cudaStream_t stream);
 
 struct LaunchParams {
