@@ -733,6 +733,8 @@ __global__ void __launch_bounds__(kRwWarps * 32, 7) row_warp_kernel(const __grid
     unsigned char* mine = smem + static_cast<size_t>(wib) * rw_warp_bytes(p.vmax);
     RwArea& a = *reinterpret_cast<RwArea*>(mine);
     uint32_t* bm = reinterpret_cast<uint32_t*>(mine + sizeof(RwArea));
+    // launched as a programmatic dependent of the stream's previous kernel: its results are visible from here on
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     // the whole-row kernel may be scheduled now; it waits (griddepcontrol.wait) until this grid has finished
     if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     // the first row's logits and per-row words start towards L2 before the seed table is read

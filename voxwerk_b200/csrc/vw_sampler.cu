@@ -1811,9 +1811,21 @@ bool plan_launch(LaunchParams& p, int sm_count, int max_grid_general, LaunchPlan
 }
 
 cudaError_t launch_sampler(const LaunchParams& p, const LaunchPlan& plan, cudaStream_t stream) {
-    row_warp_kernel<<<plan.grid, kRwWarps * 32, plan.smem_cand, stream>>>(p);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+    cudaError_t e;
+    {   // a programmatic dependent of the stream's previous kernel (the kernel waits for it before reading anything)
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(plan.grid);
+        cfg.blockDim = dim3(kRwWarps * 32);
+        cfg.dynamicSmemBytes = plan.smem_cand;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, row_warp_kernel, p);
+        if (e != cudaSuccess) return e;
+    }
     // programmatic dependent launch: the whole-row grid is scheduled while the candidate grid drains, instead of
     // after it (its kernel waits for the first grid's completion before reading the deferred list)
     cudaLaunchConfig_t cfg = {};
