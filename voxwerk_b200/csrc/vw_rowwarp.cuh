@@ -726,6 +726,9 @@ __host__ __device__ __forceinline__ size_t rw_warp_bytes(int vmax) {
     return sizeof(RwArea) + static_cast<size_t>(rw_bitmap_words(vmax)) * 4;
 }
 
+// VWK: 4 when every segment of the call holds fp32 rows, 8 when every one holds bf16 rows (the other row path is
+// then not compiled into the instance, so the warps fetch half the code), 0 for a mix.
+template <int VWK>
 __global__ void __launch_bounds__(kRwWarps * 32, 7) row_warp_kernel(const __grid_constant__ LaunchParams p) {
     extern __shared__ __align__(128) unsigned char smem[];
     const int lane = threadIdx.x & 31;
@@ -839,12 +842,13 @@ __global__ void __launch_bounds__(kRwWarps * 32, 7) row_warp_kernel(const __grid
         int res;
         if (!sample) {
             if (pen_on) hist_bad = rw_history(r.hist, r.hlen, V, bm, lane);
-            res = sg.dtype == 0 ? rw_argmax<4>(r, sg, bm, lane) : rw_argmax<8>(r, sg, bm, lane);
+            res = (VWK == 4 || (VWK == 0 && sg.dtype == 0)) ? rw_argmax<4>(r, sg, bm, lane) : rw_argmax<8>(r, sg, bm, lane);
             if (out_probs)
                 for (int i = lane; i < V; i += 32) out_probs[i] = 0.0;
             ++st_greedy;
         } else {
-            res = sg.dtype == 0 ? rw_sample_row<4>(p, r, sg, o, a, bm, hist_bad, carry, seed, out_probs, lane, st_fast,
+            res = (VWK == 4 || (VWK == 0 && sg.dtype == 0))
+                      ? rw_sample_row<4>(p, r, sg, o, a, bm, hist_bad, carry, seed, out_probs, lane, st_fast,
                                                    st_exact, st_miss)
                                 : rw_sample_row<8>(p, r, sg, o, a, bm, hist_bad, carry, seed, out_probs, lane, st_fast,
                                                    st_exact, st_miss);

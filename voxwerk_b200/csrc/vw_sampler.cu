@@ -1784,7 +1784,7 @@ int ctas_per_sm(const void* fn, int which, int threads, size_t smem) {
 }  // namespace
 
 bool plan_launch(LaunchParams& p, int sm_count, int max_grid_general, LaunchPlan* plan) {
-    const void* fw = reinterpret_cast<const void*>(&row_warp_kernel);
+    const void* fw = reinterpret_cast<const void*>(&row_warp_kernel<0>);   // the instances share resources
     const void* fg = reinterpret_cast<const void*>(&whole_row_kernel);
     // the whole-row kernel's stage count: the one that keeps the most of its CTAs resident (ties: the deeper ring)
     int best_stages = 0, best_cg = 0;
@@ -1823,7 +1823,14 @@ cudaError_t launch_sampler(const LaunchParams& p, const LaunchPlan& plan, cudaSt
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, row_warp_kernel, p);
+        // one row path compiled in when every segment has the same dtype
+        bool all_f32 = true, all_bf16 = true;
+        for (int i = 0; i < p.n_segs; ++i) {
+            all_f32 = all_f32 && p.seg[i].dtype == 0;
+            all_bf16 = all_bf16 && p.seg[i].dtype != 0;
+        }
+        e = all_f32 ? cudaLaunchKernelEx(&cfg, row_warp_kernel<4>, p)
+                    : all_bf16 ? cudaLaunchKernelEx(&cfg, row_warp_kernel<8>, p) : cudaLaunchKernelEx(&cfg, row_warp_kernel<0>, p);
         if (e != cudaSuccess) return e;
     }
     // programmatic dependent launch: the whole-row grid is scheduled while the candidate grid drains, instead of
