@@ -1411,6 +1411,8 @@ constexpr int kRankBuckets = 64;   // value buckets of the candidate counting so
 // top-k off or K > 64, rows whose candidates overflowed, and rows of more than 3072 staged ids.  CTA b takes list
 // entries b, b + grid, ...; each row is held in registers (24 values per thread) for the binned top-k / top-p
 // searches, and rows whose decisions fall inside the error band are replayed in the reference's order.
+// VWK as for row_warp_kernel: 4 / 8 when every segment holds fp32 / bf16 rows (one row path compiled in), 0 for a mix.
+template <int VWK>
 __global__ void __launch_bounds__(kBlockThreads, 3) whole_row_kernel(const __grid_constant__ LaunchParams p) {
     extern __shared__ __align__(128) unsigned char smem[];
     const int tid = threadIdx.x;
@@ -1476,7 +1478,7 @@ __global__ void __launch_bounds__(kBlockThreads, 3) whole_row_kernel(const __gri
         const RowMeta& m = metas[rp.meta(S_)];
         const int32_t* sh = reinterpret_cast<const int32_t*>(sl + p.stage_logit_bytes);
         const int V = m.V;
-        const int dtype = m.dtype;
+        const int dtype = VWK == 4 ? 0 : VWK == 8 ? 1 : m.dtype;
         const int VWe = dtype == 0 ? 4 : 8;
         const RowMap mp{m.lo_al, m.kvw, m.kbase, m.hi_al};
         const int NA = m.lo_al + m.kvw + (V - m.hi_al);
@@ -1760,9 +1762,10 @@ int64_t sampler_gscratch_stride(int vmax) {
 }
 
 namespace {
-// Resident CTAs per SM of `fn` at `threads` x `smem`; raises the kernel's dynamic shared-memory limit on the current
-// device first when it needs more than the default 48 KB (once per device and size).
-int ctas_per_sm(const void* fn, int which, int threads, size_t smem) {
+// Resident CTAs per SM of fns[0] at `threads` x `smem`; raises the dynamic shared-memory limit of every instance in
+// fns (they share their resources) on the current device first when it needs more than the default 48 KB (once per
+// device and size).
+int ctas_per_sm(const void* const (&fns)[3], int which, int threads, size_t smem) {
     constexpr int kMaxDevices = 64;
     static std::mutex mu;
     static size_t configured[kMaxDevices][2] = {};
@@ -1771,21 +1774,26 @@ int ctas_per_sm(const void* fn, int which, int threads, size_t smem) {
     if (smem > 48 * 1024) {
         std::lock_guard<std::mutex> lock(mu);
         if (smem > configured[dev][which]) {
-            if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
-                cudaSuccess)
-                return 0;
+            for (const void* fn : fns)
+                if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+                    cudaSuccess)
+                    return 0;
             configured[dev][which] = smem;
         }
     }
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, threads, smem) != cudaSuccess) return 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fns[0], threads, smem) != cudaSuccess) return 0;
     return n;
 }
 }  // namespace
 
 bool plan_launch(LaunchParams& p, int sm_count, int max_grid_general, LaunchPlan* plan) {
-    const void* fw = reinterpret_cast<const void*>(&row_warp_kernel<0>);   // the instances share resources
-    const void* fg = reinterpret_cast<const void*>(&whole_row_kernel);
+    const void* const fw[3] = {reinterpret_cast<const void*>(&row_warp_kernel<0>),
+                               reinterpret_cast<const void*>(&row_warp_kernel<4>),
+                               reinterpret_cast<const void*>(&row_warp_kernel<8>)};
+    const void* const fg[3] = {reinterpret_cast<const void*>(&whole_row_kernel<0>),
+                               reinterpret_cast<const void*>(&whole_row_kernel<4>),
+                               reinterpret_cast<const void*>(&whole_row_kernel<8>)};
     // the whole-row kernel's stage count: the one that keeps the most of its CTAs resident (ties: the deeper ring)
     int best_stages = 0, best_cg = 0;
     for (int stages = kStages; stages >= 2; --stages) {
@@ -1811,6 +1819,12 @@ bool plan_launch(LaunchParams& p, int sm_count, int max_grid_general, LaunchPlan
 }
 
 cudaError_t launch_sampler(const LaunchParams& p, const LaunchPlan& plan, cudaStream_t stream) {
+    // one row path compiled into the kernels when every segment has the same dtype
+    bool all_f32 = true, all_bf16 = true;
+    for (int i = 0; i < p.n_segs; ++i) {
+        all_f32 = all_f32 && p.seg[i].dtype == 0;
+        all_bf16 = all_bf16 && p.seg[i].dtype != 0;
+    }
     cudaError_t e;
     {   // a programmatic dependent of the stream's previous kernel (the kernel waits for it before reading anything)
         cudaLaunchConfig_t cfg = {};
@@ -1823,12 +1837,6 @@ cudaError_t launch_sampler(const LaunchParams& p, const LaunchPlan& plan, cudaSt
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        // one row path compiled in when every segment has the same dtype
-        bool all_f32 = true, all_bf16 = true;
-        for (int i = 0; i < p.n_segs; ++i) {
-            all_f32 = all_f32 && p.seg[i].dtype == 0;
-            all_bf16 = all_bf16 && p.seg[i].dtype != 0;
-        }
         e = all_f32 ? cudaLaunchKernelEx(&cfg, row_warp_kernel<4>, p)
                     : all_bf16 ? cudaLaunchKernelEx(&cfg, row_warp_kernel<8>, p) : cudaLaunchKernelEx(&cfg, row_warp_kernel<0>, p);
         if (e != cudaSuccess) return e;
@@ -1845,7 +1853,8 @@ cudaError_t launch_sampler(const LaunchParams& p, const LaunchPlan& plan, cudaSt
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, whole_row_kernel, p);
+    e = all_f32 ? cudaLaunchKernelEx(&cfg, whole_row_kernel<4>, p)
+                : all_bf16 ? cudaLaunchKernelEx(&cfg, whole_row_kernel<8>, p) : cudaLaunchKernelEx(&cfg, whole_row_kernel<0>, p);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
