@@ -216,6 +216,26 @@ def test_carried_threshold_misses_and_overflow(device):
     assert st["rows_overflow"] > 0 and st["rows_fast"] > 0
 
 
+def test_short_threshold_lowered_and_collected_again(device):
+    """A call seeds the threshold table from config 2's rows; the next call samples the same rows with every logit
+    scaled by 0.85, so at the seeded threshold most rows collect a few candidates fewer than K.  Those rows lower the
+    threshold by the missing count and collect once more: ids stay bit-exact, and the rows stay in the warp kernel
+    (a lowered threshold that still missed would hand the row to the whole-row kernel)."""
+    import copy
+    w = workloads.make(2, 1024)
+    run_workload(device, w)
+    w2 = copy.deepcopy(w)
+    w2.segments[0].logits = (w.segments[0].logits * np.float32(0.85)).astype(np.float32)
+    device.stats(reset=True)
+    got = run_workload(device, w2)
+    st = device.stats(reset=True)
+    assert_ids_equal(w2, got, oracle_ids(w2))
+    REPORT.append(f"lowered thresholds: {st['rows_threshold_miss']} of {w2.n_rows} rows missed at the seed, "
+                  f"{st['rows_overflow']} went to the whole-row kernel")
+    assert st["rows_threshold_miss"] > w2.n_rows // 4, st
+    assert st["rows_overflow"] * 20 < st["rows_threshold_miss"], st
+
+
 def test_history_out_of_range_raises(device):
     from voxwerk_b200 import VwOutOfRange
     w = workloads.make(0)

@@ -18,7 +18,8 @@
 //   5. softmax numerators (libm exp, Sampler.cs:57) in 64-bit fixed point, the top-p cut over the ascending order
 //      (Sampler.cs:62-72) and the inverse-CDF draw over index order (Sampler.cs:77-87), each decision certified
 //      against the error band of the parallel sums, else the warp replays the row in the reference's order.
-// A threshold that misses (C outside [K, 256]) is rebuilt from the row's own values; rows the kernel does not take
+// A threshold that misses (C outside [K, 256]) is rebuilt from the row's own values, except that one a few
+// candidates short is first lowered by the missing count at the density just above it; rows the kernel does not take
 // (top-k off or > 64, a penalty < 1, unaligned rows, too many candidates) go to the whole-row kernel.
 
 constexpr int kRwWarps = 4;       // warps per CTA, each on its own rows
@@ -597,6 +598,19 @@ __device__ __forceinline__ void rw_for_each(const RwRow& r, const DevSegment& sg
     }
 }
 
+// A lower threshold for a row that collected 0 < C < K candidates (exact values >= tau, largest mx, in a.key): tau
+// moved down by the target - C missing candidates at the density of the lowest sixteenth of [tau, mx].  Any
+// threshold with at least K candidates gives the same decision, so this is only a guess: the caller collects again
+// and rebuilds the threshold from the row when the guess is still short.
+__device__ float rw_lowered(const RwArea& a, int C, int target, float tau, float mx, int lane) {
+    const float band = __fadd_rn(tau, __fmul_rn(__fsub_rn(mx, tau), 0.0625f));
+    int n = 0;
+    for (int c = lane; c < C; c += 32) n += okey_inv(static_cast<uint32_t>(a.key[c] >> 32)) <= band ? 1 : 0;
+    n = warp_sum_i(n);
+    const float per = __fdiv_rn(__fsub_rn(band, tau), static_cast<float>(max(n, 1)));   // value per candidate
+    return __fsub_rn(tau, __fmul_rn(static_cast<float>(target - C), per));
+}
+
 // A threshold tau with at least K exact values >= tau: the K-th largest of the 64 values formed by each lane's two
 // largest (a subset of the row, so its K-th largest is <= the row's).  -inf when the row has fewer than K finite
 // values among them.
@@ -650,7 +664,7 @@ __device__ int rw_sample_row(const LaunchParams& p, const RwRow& r, const DevSeg
     const unsigned long long cs = __shfl_sync(kFull, carry, r.seg);
     int C = 0;
     float mx = neg_inf(), tau = neg_inf();
-    bool ok = false, bm_ready = false, have = false;
+    bool bm_ready = false, have = false;
     if (static_cast<uint32_t>(seed[r.seg]) == static_cast<uint32_t>(r.opt)) {
         // the CTA's seed for this segment and option: the lower quartile of 32 rows' thresholds, which misses far
         // less often than the single row this warp sampled last (that one is the fallback for other options)
@@ -660,23 +674,35 @@ __device__ int rw_sample_row(const LaunchParams& p, const RwRow& r, const DevSeg
         tau = __uint_as_float(static_cast<uint32_t>(cs >> 32));
         have = true;
     }
+    bool ok = false, got = false;
     if (have) {
         const float x0 = raw_threshold(tau, r.inv_t);
-        if (fabsf(x0) < pos_inf())
-            ok = rw_collect<VW>(r, sg, tau, x0, bm, bm_ready, hist_bad, a, lane, C, mx) && C >= K && C <= kRwCandCap;
-    }
-    if (!ok) {   // no usable carried threshold: rebuild it from this row
-        ++st_miss;
-        if (r.pen_on && !bm_ready) {
-            hist_bad = rw_history(r.hist, r.hlen, r.V, bm, lane);
-            bm_ready = true;
+        if (fabsf(x0) < pos_inf()) {
+            got = rw_collect<VW>(r, sg, tau, x0, bm, bm_ready, hist_bad, a, lane, C, mx);
+            ok = got && C >= K && C <= kRwCandCap;
         }
-        tau = rw_row_threshold<VW>(r, sg, bm, K, lane);
-        if (is_neg_inf(tau)) return -2;   // fewer than K finite values in reach: the whole-row kernel decides
+    }
+    if (!ok) {   // no usable threshold yet: one more collection, at a threshold that should reach K
+        ++st_miss;
+        // a few candidates short: the threshold lowered by the missing count at the density just above it (no pass
+        // over the row); otherwise (no threshold, too many candidates) rebuilt from the row's own values.  A lowered
+        // threshold that still misses sends the row to the whole-row kernel, so the collection exists twice in the
+        // code, not three times.
+        const float t2 = got && C > 0 && C < K ? rw_lowered(a, C, K + (K >> 1) + 4, tau, mx, lane) : tau;
+        if (t2 < tau) {
+            tau = t2;
+        } else {
+            if (r.pen_on && !bm_ready) {
+                hist_bad = rw_history(r.hist, r.hlen, r.V, bm, lane);
+                bm_ready = true;
+            }
+            tau = rw_row_threshold<VW>(r, sg, bm, K, lane);
+            if (is_neg_inf(tau)) return -2;   // fewer than K finite values in reach: the whole-row kernel decides
+        }
         const float x0 = raw_threshold(tau, r.inv_t);
         if (!(fabsf(x0) < pos_inf())) return -2;
         ok = rw_collect<VW>(r, sg, tau, x0, bm, bm_ready, hist_bad, a, lane, C, mx) && C >= K && C <= kRwCandCap;
-        if (!ok) return -2;   // more than 128 candidates (flat rows, ties): the whole-row kernel decides
+        if (!ok) return -2;   // still outside [K, 256] (flat rows, ties): the whole-row kernel decides
     }
     const int target = K + (K >> 1) + 4;
     float gt = tau;
