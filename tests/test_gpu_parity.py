@@ -236,6 +236,64 @@ def test_short_threshold_lowered_and_collected_again(device):
     assert st["rows_overflow"] * 20 < st["rows_threshold_miss"], st
 
 
+def _topk_off_workload(seed, n=256):
+    """Top-k off rows of every shape the whole-row kernel's general path must decide: integer-valued rows (large tie
+    groups at the top-p break), near-flat rows, N(0, 16) rows, rows with one dominant id under a small top-p (only the
+    max stays);
+    options with K = 0 and K = V, with and without a top-p cut; talker rows with the suppress mask and, on early
+    steps, the EOS blocked; and a bf16 code-predictor segment."""
+    rng = np.random.default_rng(seed)
+    V = 3072
+    x = np.empty((n, V), np.float32)
+    q = n // 4
+    x[0::4] = rng.integers(0, 16, size=(q, V)).astype(np.float32) - np.float32(7.5)
+    x[1::4] = rng.normal(0.0, 0.01, size=(q, V)).astype(np.float32)
+    x[2::4] = rng.normal(0.0, 4.0, size=(q, V)).astype(np.float32)
+    x[3::4] = rng.normal(0.0, 1.0, size=(q, V)).astype(np.float32)
+    x[np.arange(3, n, 4), rng.integers(0, 2048, size=q)] += np.float32(30.0)
+    hlen = 512
+    ho = np.arange(n + 1, dtype=np.int64) * hlen
+    hi = rng.integers(0, V, size=n * hlen).astype(np.int32)
+    opt = np.zeros(n, np.int32)
+    opt[3::4] = 1                      # top-p 0.05: only the max stays
+    opt[2::8] = 2                      # K = 0, no top-p cut
+    opt[np.arange(n) % 16 == 5] = 3    # K = V, top-p 0.95, penalty 1 (history ignored)
+    steps = np.where(np.arange(n) % 3 == 0, 0, 7).astype(np.int32)   # EOS blocked below MIN_NEW_TOKENS
+    talker = SegData(x, 0, 0, V, workloads._uniforms(seed, n), opt, ho, hi, steps,
+                     suppress_lo=V - 1024, suppress_hi=V)
+    ns, CV = n // 2, 2048
+    xs = rng.normal(0.0, 3.0, size=(ns, CV)).astype(np.float32)
+    xs[::2] = np.round(xs[::2])
+    sub = SegData(workloads._bf16_rne(xs), 1, 1, CV, workloads._uniforms(seed + 1, ns), np.full(ns, 4, np.int32))
+    return Workload("topk_off_mix", 2, [talker, sub],
+                    [(1, V, 0.6, 0.9, 1.3), (1, 0, 0.05, 0.8, 1.1), (1, 0, 1.0, 0.7, 1.2), (1, V, 0.95, 1.1, 1.0),
+                     (1, CV, 0.7, 0.9, 1.0)])
+
+
+def test_topk_off_rows_of_every_shape(device):
+    """Top-k off rows take the whole-row kernel: ids bit-exact against the oracle, and nearly all of them decided in
+    parallel (within the error bands) rather than replayed."""
+    w = _topk_off_workload(91)
+    device.stats(reset=True)
+    got = run_workload(device, w)
+    st = device.stats(reset=True)
+    assert_ids_equal(w, got, oracle_ids(w))
+    n = sum(s.n_rows for s in w.segments)
+    REPORT.append(f"top-k off mix: {n} rows, general {st['rows_general']}, replayed {st['rows_general_replayed']}")
+    assert st["rows_general"] + st["rows_general_replayed"] == n, st
+    assert st["rows_general_replayed"] * 20 < n, st
+
+
+def test_topk_off_rows_probabilities(device):
+    w = _topk_off_workload(92, n=64)
+    got_ids, got_p = run_workload(device, w, want_probs=True)
+    ref = oracle_ids(w, want_probs=True)
+    for (gi, gp), (ri, rp) in zip(zip(got_ids, got_p), ref):
+        np.testing.assert_array_equal(gi, ri)
+        assert ((gp == 0) == (rp == 0)).all(), "different sets of ids carry probability"
+        np.testing.assert_allclose(gp, rp, rtol=PROB_RTOL, atol=0)
+
+
 def test_history_out_of_range_raises(device):
     from voxwerk_b200 import VwOutOfRange
     w = workloads.make(0)

@@ -19,7 +19,7 @@
 //      (Sampler.cs:62-72) and the inverse-CDF draw over index order (Sampler.cs:77-87), each decision certified
 //      against the error band of the parallel sums, else the warp replays the row in the reference's order.
 // A threshold that misses (C outside [K, 256]) is rebuilt from the row's own values, except that one a few
-// candidates short is first lowered by the missing count at the density just above it; rows the kernel does not take
+// candidates short is first lowered along the tail its candidates show; rows the kernel does not take
 // (top-k off or > 64, a penalty < 1, unaligned rows, too many candidates) go to the whole-row kernel.
 
 constexpr int kRwWarps = 4;       // warps per CTA, each on its own rows
@@ -598,17 +598,20 @@ __device__ __forceinline__ void rw_for_each(const RwRow& r, const DevSegment& sg
     }
 }
 
-// A lower threshold for a row that collected 0 < C < K candidates (exact values >= tau, largest mx, in a.key): tau
-// moved down by the target - C missing candidates at the density of the lowest sixteenth of [tau, mx].  Any
-// threshold with at least K candidates gives the same decision, so this is only a guess: the caller collects again
-// and rebuilds the threshold from the row when the guess is still short.
-__device__ float rw_lowered(const RwArea& a, int C, int target, float tau, float mx, int lane) {
-    const float band = __fadd_rn(tau, __fmul_rn(__fsub_rn(mx, tau), 0.0625f));
-    int n = 0;
-    for (int c = lane; c < C; c += 32) n += okey_inv(static_cast<uint32_t>(a.key[c] >> 32)) <= band ? 1 : 0;
-    n = warp_sum_i(n);
-    const float per = __fdiv_rn(__fsub_rn(band, tau), static_cast<float>(max(n, 1)));   // value per candidate
-    return __fsub_rn(tau, __fmul_rn(static_cast<float>(target - C), per));
+// A lower threshold for a row that collected 0 < C < K candidates (exact values >= tau, in a.key; C < 64), aimed at
+// `target` candidates.  Near tau the counts follow a tail: #(values >= x) ~ C exp((tau - x) / s), with the scale s
+// fitted so that the median candidate holds (half of the C above it); tau moves down by s ln(target / C).  (A linear
+// step at the density of the smallest candidates overshoots: the density keeps growing below tau.)  Any threshold
+// with at least K candidates gives the same decision, so this is only a guess: a row still outside [K, 256] at it goes
+// to the whole-row kernel.  Out of line: it runs on misses only.
+__device__ __noinline__ float rw_lowered(const RwArea& a, int C, int target, float tau, int lane) {
+    uint32_t k[2] = {lane < C ? static_cast<uint32_t>(a.key[lane] >> 32) : 0xffffffffu,
+                     lane + 32 < C ? static_cast<uint32_t>(a.key[lane + 32] >> 32) : 0xffffffffu};
+    warp_sort32<2>(k, lane);   // ascending values, position p at slot p / 32 of lane p % 32
+    const int m = max(1, C >> 1);                                        // m - 1 <= 30: slot 0
+    const float gap = okey_inv(__shfl_sync(kFull, k[0], m - 1)) - tau;   // the m-th smallest candidate, above tau
+    const float sc = C > m ? gap / logf(static_cast<float>(C) / static_cast<float>(C - m)) : gap;
+    return tau - sc * logf(static_cast<float>(target) / static_cast<float>(C));
 }
 
 // A threshold tau with at least K exact values >= tau: the K-th largest of the 64 values formed by each lane's two
@@ -684,11 +687,11 @@ __device__ int rw_sample_row(const LaunchParams& p, const RwRow& r, const DevSeg
     }
     if (!ok) {   // no usable threshold yet: one more collection, at a threshold that should reach K
         ++st_miss;
-        // a few candidates short: the threshold lowered by the missing count at the density just above it (no pass
-        // over the row); otherwise (no threshold, too many candidates) rebuilt from the row's own values.  A lowered
+        // a few candidates short: the threshold lowered along the tail the candidates show (no pass over the
+        // row); otherwise (no threshold, too many candidates) rebuilt from the row's own values.  A lowered
         // threshold that still misses sends the row to the whole-row kernel, so the collection exists twice in the
         // code, not three times.
-        const float t2 = got && C > 0 && C < K ? rw_lowered(a, C, K + (K >> 1) + 4, tau, mx, lane) : tau;
+        const float t2 = got && C > 0 && C < K ? rw_lowered(a, C, K + (K >> 1) + 4, tau, lane) : tau;
         if (t2 < tau) {
             tau = t2;
         } else {
