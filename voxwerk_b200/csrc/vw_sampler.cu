@@ -52,7 +52,8 @@ namespace {
 
 constexpr unsigned kFull = 0xffffffffu;
 constexpr double kU = 1.1102230246251565e-16;      // 2^-53
-constexpr double kFix = 2251799813685248.0;         // 2^51: fixed-point scale of histogram masses (e <= 1)
+constexpr double kFix = 1099511627776.0;            // 2^40: fixed-point scale of histogram masses (e <= 1): two
+                                                    // 20-bit parts, each bin's sum of 3072 parts fits 32 bits
 constexpr int kProducerWarp = kWarps;              // warp 4
 constexpr int kBlockThreads = (kWarps + 1) * 32;   // 160
 
@@ -705,8 +706,8 @@ __device__ int exact_block_path(const RowCtx& c, const DevOptions& o, double r, 
 // ---------------------------------------------------------------- binned search (element threads)
 // Ascending search over the values x[j] whose bit j is set in `live`: finds the value v* at which the running
 // weight, from the smallest value up, first exceeds `target` (weights: counts, or fixed-point masses
-// round(ev(j) * 2^51) when kMass).  On return `below` is the weight of the live values < v* and `cnt` the number
-// of live values equal to v*.  Each pass bins the live values linearly over [min, max] (monotone in the value),
+// round(ev(j) * 2^40) when kMass, binned without counts: two shared atomics per value).  On return `below` is the
+// weight of the live values < v* and `cnt` the number of live values equal to v*.  Each pass bins the live values linearly over [min, max] (monotone in the value),
 // keeps the bin holding the crossing, and stops when one value is left.  Returns false (the caller replays the
 // row) when the span is not a finite positive float or eight passes do not isolate a value.
 template <bool kMass, typename EvFn>
@@ -729,23 +730,29 @@ __device__ bool binned_search(const float (&x)[kRegElems], uint32_t live, EvFn e
     for (int pass = 0; pass < 8; ++pass) {
         if (lo == hi) {
             vstar = lo;
+            if (kMass && pass > 0) {   // the mass passes keep no counts: the members left, counted once
+                int nl = 0;
+#pragma unroll
+                for (int j = 0; j < kRegElems; ++j) nl += (live >> j) & 1u;
+                cnt = block_sum_i(nl, m, 4, lane, warp);
+            }
             return true;
         }
         const float scale = __fdiv_rn(256.0f, __fsub_rn(hi, lo));
         if (!(scale > 0.0f) || !(scale < pos_inf())) return false;
-        uint32_t* bw = &m.u.bins.cnt[0];
-        for (int i = tid; i < 4 * 256; i += kThreads) bw[i] = 0u;
+        uint32_t* bw = kMass ? &m.u.bins.m[0][0] : &m.u.bins.cnt[0];
+        for (int i = tid; i < (kMass ? 2 : 1) * 256; i += kThreads) bw[i] = 0u;
         cbar();
 #pragma unroll
         for (int j = 0; j < kRegElems; ++j) {
             if ((live >> j) & 1u) {
                 const int b = min(255, static_cast<int>(__fmul_rn(__fsub_rn(x[j], lo), scale)));
-                atomicAdd(&m.u.bins.cnt[b], 1u);
                 if (kMass) {
-                    const unsigned long long f = __double2ull_rn(__dmul_rn(ev(j), kFix));
+                    const unsigned long long f = __double2ull_rn(__dmul_rn(ev(j), kFix));   // <= 2^40
                     atomicAdd(&m.u.bins.m[0][b], static_cast<uint32_t>(f & 0xfffffull));
-                    atomicAdd(&m.u.bins.m[1][b], static_cast<uint32_t>((f >> 20) & 0xfffffull));
-                    atomicAdd(&m.u.bins.m[2][b], static_cast<uint32_t>(f >> 40));
+                    atomicAdd(&m.u.bins.m[1][b], static_cast<uint32_t>(f >> 20));
+                } else {
+                    atomicAdd(&m.u.bins.cnt[b], 1u);
                 }
             }
         }
@@ -756,8 +763,7 @@ __device__ bool binned_search(const float (&x)[kRegElems], uint32_t live, EvFn e
             for (int b = 0; b < 8; ++b) {
                 const int bb = lane * 8 + b;
                 w8[b] = kMass ? (static_cast<unsigned long long>(m.u.bins.m[0][bb]) +
-                                 (static_cast<unsigned long long>(m.u.bins.m[1][bb]) << 20) +
-                                 (static_cast<unsigned long long>(m.u.bins.m[2][bb]) << 40))
+                                 (static_cast<unsigned long long>(m.u.bins.m[1][bb]) << 20))
                               : static_cast<unsigned long long>(m.u.bins.cnt[bb]);
                 loc += w8[b];
             }
@@ -789,7 +795,7 @@ __device__ bool binned_search(const float (&x)[kRegElems], uint32_t live, EvFn e
                 const unsigned long long ab = __shfl_sync(kFull, acc_before, src);
                 if (lane == 0) {
                     m.bc_i[1] = d;
-                    m.bc_i[2] = static_cast<int>(m.u.bins.cnt[d]);
+                    m.bc_i[2] = kMass ? 0 : static_cast<int>(m.u.bins.cnt[d]);
                     m.bc_u[0] = ab;
                 }
             }
@@ -864,7 +870,7 @@ __device__ int general_parallel(const float (&x)[kRegElems], int nvec, const Row
     }
     const double total = block_sum_d(lsum, m, 0, lane, warp);
     const int nsurv = block_sum_i(__popc(surv), m, 1, lane, warp);
-    const double eta = (8.0 * nsurv + 128.0) * kU;   // also covers the 2^-52-per-value histogram rounding
+    const double eta = (8.0 * nsurv + 128.0) * kU;
     uint32_t removed = 0;   // bit j: element j removed by top-p
     if (o.top_p < 1.0f) {
         const double thr = static_cast<double>(__fsub_rn(1.0f, o.top_p));
@@ -901,14 +907,16 @@ __device__ int general_parallel(const float (&x)[kRegElems], int nvec, const Row
             int ng;
             if (!binned_search<true>(x, surv, ev, tfx, m, tid, lane, warp, xs, below_fx, ng)) return -1;
             const double below = __dmul_rn(static_cast<double>(below_fx), 1.0 / kFix);
+            // `below` sums masses rounded to 2^-40 each: within nsurv * 2^-41 of the exact sum, on top of the band
+            const double bandm = __dadd_rn(band, static_cast<double>(nsurv + 1) * 0x1p-41);
             const double es = softmax_num(xs, mx);
             const double q = __ddiv_rn(__dsub_rn(T, below), es);
             if (!(q >= 0.0) || !(q < static_cast<double>(ng))) return -1;
             const int jrem = static_cast<int>(floor(q));   // group members removed (lowest ids first)
             const double last_removed = __dadd_rn(below, __dmul_rn(static_cast<double>(jrem), es));
             const double brk = __dadd_rn(below, __dmul_rn(static_cast<double>(jrem + 1), es));
-            if (!(__dsub_rn(brk, T) > band)) return -1;
-            if (last_removed > 0.0 && !(__dsub_rn(T, last_removed) > band)) return -1;
+            if (!(__dsub_rn(brk, T) > bandm)) return -1;
+            if (last_removed > 0.0 && !(__dsub_rn(T, last_removed) > bandm)) return -1;
             // neighbours: the reference orders by probability, so the groups next to x* must be strictly apart
             float lo_n = neg_inf(), hi_n = pos_inf();
 #pragma unroll
