@@ -101,8 +101,9 @@ typedef struct vw_stats {
     uint64_t rows_general_replayed;  /* whole-row rows replayed in the reference's order */
     uint64_t rows_large;             /* rows of more than 3072 active ids (always replayed) */
     uint64_t rows_overflow;          /* top-k <= 64 rows whose candidates overflowed (counted in rows_general*) */
-    uint64_t rows_threshold_miss;    /* top-k <= 64 rows whose carried candidate threshold missed and was rebuilt
-                                        from the row (extra work, same result) */
+    uint64_t rows_threshold_miss;    /* top-k <= 64 rows whose carried candidate threshold missed: lowered (a few
+                                        candidates short) or rebuilt from the row, then collected once more (extra
+                                        work, same result; a row still missing counts in rows_overflow) */
     uint64_t h2d_bytes;              /* bytes VW_MEM_HOST calls copied host -> device (inputs only: the logit
                                         columns of a suppressed span are not copied, no kernel reads them) */
 } vw_stats;

@@ -29,7 +29,7 @@ enum : int {
     kStatGeneralReplayed = 4,  // whole-row rows replayed in the reference's order
     kStatLarge = 5,            // rows of more than 3072 active ids (always replayed)
     kStatOverflow = 6,         // candidate-eligible rows that took the whole-row path
-    kStatThresholdMiss = 7,    // candidate rows whose carried threshold missed (rebuilt from the row)
+    kStatThresholdMiss = 7,    // candidate rows whose carried threshold missed (lowered or rebuilt)
     kNumStats = 9,             // slot 8 is vw_stats.h2d_bytes, kept on the host
 };
 
