@@ -516,10 +516,11 @@ vw_status sample_impl(vw_handle* h, const vw_segment* segs, int32_t n_segs, cons
     p.test_stall_row = h->test_stall_row;
     h->test_stall_row = -1;   // one call only
 
-    // When every segment fits the warp-per-row kernel and every sampling option is a small top-k (0 < K <= 64, K < V,
-    // penalty >= 1), rows reach the whole-row kernel only when their candidates overflow, which is rare: one CTA per SM
-    // is enough then, and the launch that usually finds nothing to do costs less (config 2: 29.1 -> 28.6 us per call).
-    // A batch whose rows mostly overflow (all ties) runs at a third of the full grid's whole-row throughput.
+    // When every segment fits the warp-per-row kernel, no option has a penalty below 1 and every sampling option is a
+    // small top-k (0 < K <= 64, K < V), rows reach the whole-row kernel only when their candidates overflow, which is
+    // rare: one CTA per SM is enough then, and the launch that usually finds nothing to do costs less (config 2:
+    // 29.1 -> 28.6 us per call).  A batch whose rows mostly overflow (all ties) runs at a third of the full grid's
+    // whole-row throughput.
     bool rare_defer = true;
     int vmin = INT32_MAX;
     for (int i = 0; i < nd; ++i) {
@@ -527,9 +528,8 @@ vw_status sample_impl(vw_handle* h, const vw_segment* segs, int32_t n_segs, cons
         vmin = std::min(vmin, p.seg[i].vocab);
     }
     for (int i = 0; i < n_opts && rare_defer; ++i)
-        if (opts[i].do_sample)
-            rare_defer = opts[i].top_k > 0 && opts[i].top_k <= vw::kSmallK && opts[i].top_k < vmin &&
-                         opts[i].repetition_penalty >= 1.0f;
+        rare_defer = opts[i].repetition_penalty >= 1.0f &&
+                     (!opts[i].do_sample || (opts[i].top_k > 0 && opts[i].top_k <= vw::kSmallK && opts[i].top_k < vmin));
     vw::LaunchPlan plan;
     if (!vw::plan_launch(p, h->sm_count, rare_defer ? h->sm_count : INT32_MAX, &plan))
         return fail(h, VW_ERR_INVALID_ARG, "rows too large for shared memory");
