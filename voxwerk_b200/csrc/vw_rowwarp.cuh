@@ -669,7 +669,7 @@ __device__ int rw_sample_row(const LaunchParams& p, const RwRow& r, const DevSeg
     float mx = neg_inf(), tau = neg_inf();
     bool bm_ready = false, have = false;
     if (static_cast<uint32_t>(seed[r.seg]) == static_cast<uint32_t>(r.opt)) {
-        // the CTA's seed for this segment and option: the lower quartile of 32 rows' thresholds, which misses far
+        // the CTA's seed for this segment and option: the lower eighth of 32 rows' thresholds, which misses far
         // less often than the single row this warp sampled last (that one is the fallback for other options)
         tau = __uint_as_float(static_cast<uint32_t>(seed[r.seg] >> 32));
         have = true;
@@ -775,8 +775,9 @@ __global__ void __launch_bounds__(kRwWarps * 32, 7) row_warp_kernel(const __grid
     const int G = gridDim.x * kRwWarps;
     // carried thresholds: lane s holds segment s's (threshold bits << 32 | option); ~0: none yet
     unsigned long long carry = ~0ull;
-    // the CTA's seeds, one per segment: the lower quartile (robust to an atypical row) of the thresholds the last
-    // call's warps left in the table for that segment, among those of the option the segment's first slot holds
+    // the CTA's seeds, one per segment: the lower eighth (the 4th lowest of 32: robust to an atypical row, and low
+    // enough that rows a little below the typical one still reach K) of the thresholds the last call's warps left in
+    // the table for that segment, among those of the option the segment's first slot holds
     __shared__ unsigned long long seed[kMaxSegments];
     if (wib < p.n_segs) {
         unsigned long long e = p.guess_seed ? p.guess_seed[wib * kSeedSlots + lane] : ~0ull;
@@ -786,7 +787,7 @@ __global__ void __launch_bounds__(kRwWarps * 32, 7) row_warp_kernel(const __grid
         uint32_t kk[1] = {m ? okey(__uint_as_float(static_cast<uint32_t>(e >> 32))) : 0xffffffffu};
         const int n = __popc(__ballot_sync(kFull, m));
         warp_sort32<1>(kk, lane);
-        const uint32_t q = __shfl_sync(kFull, kk[0], max(n - 1, 0) >> 2);
+        const uint32_t q = __shfl_sync(kFull, kk[0], max(n - 1, 0) >> 3);
         if (lane == 0) seed[wib] = n > 0 ? ((static_cast<unsigned long long>(__float_as_uint(okey_inv(q))) << 32) | opt0) : ~0ull;
     }
     for (int s2 = kRwWarps + wib; s2 < p.n_segs; s2 += kRwWarps)   // more segments than warps: no seed
